@@ -1,0 +1,61 @@
+// combine.cu — weighted combine of the routed expert outputs, plus the shared expert and
+// the residual, in the reference's operation order:
+//   routed = 0; for k: routed += w[t,k] * y_k        (src/attention.cpp:296-298)
+//   moe    = shared + routed                         (src/attention.cpp:306-309)
+//   out    = residual + moe                          (src/decoder_layer.cpp:42)
+// Each element is a chain of separately rounded IEEE multiplies and adds in that order.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace hymoe {
+
+namespace {
+
+__global__ __launch_bounds__(256) void combine_kernel(const float* __restrict__ y,
+                                                      const int* __restrict__ slot_pos,
+                                                      const float* __restrict__ topk_w,
+                                                      const int* __restrict__ goff,
+                                                      const float* resid, float* out, int T,
+                                                      int H, int E, int K) {
+    __shared__ int pos[9];
+    __shared__ float w[8];
+    const int t = blockIdx.y;
+    if (threadIdx.x < K) {
+        pos[threadIdx.x] = slot_pos[t * K + threadIdx.x];
+        w[threadIdx.x] = topk_w[t * K + threadIdx.x];
+    }
+    if (threadIdx.x == 0) pos[8] = goff[E] + t;
+    __syncthreads();
+    const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (j >= H) return;
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < K; ++k) {
+        const float4 v = *reinterpret_cast<const float4*>(y + static_cast<size_t>(pos[k]) * H + j);
+        const float wk = w[k];
+        r.x = __fadd_rn(r.x, __fmul_rn(wk, v.x));
+        r.y = __fadd_rn(r.y, __fmul_rn(wk, v.y));
+        r.z = __fadd_rn(r.z, __fmul_rn(wk, v.z));
+        r.w = __fadd_rn(r.w, __fmul_rn(wk, v.w));
+    }
+    const float4 s = *reinterpret_cast<const float4*>(y + static_cast<size_t>(pos[8]) * H + j);
+    float4 o = make_float4(__fadd_rn(s.x, r.x), __fadd_rn(s.y, r.y), __fadd_rn(s.z, r.z),
+                           __fadd_rn(s.w, r.w));
+    if (resid != nullptr) {
+        const float4 h = *reinterpret_cast<const float4*>(resid + static_cast<size_t>(t) * H + j);
+        o = make_float4(__fadd_rn(h.x, o.x), __fadd_rn(h.y, o.y), __fadd_rn(h.z, o.z),
+                        __fadd_rn(h.w, o.w));
+    }
+    *reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H + j) = o;
+}
+
+}  // namespace
+
+cudaError_t launch_combine(const float* y, const int* slot_pos, const float* topk_w,
+                           const int* goff, const float* resid, float* out, int T, int H, int E,
+                           int K, cudaStream_t st) {
+    dim3 grid((H / 4 + 255) / 256, T);
+    combine_kernel<<<grid, 256, 0, st>>>(y, slot_pos, topk_w, goff, resid, out, T, H, E, K);
+    return cudaGetLastError();
+}
+
+}  // namespace hymoe

@@ -1,0 +1,365 @@
+// gemm_tc.cu — grouped expert GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Replaces the per-(token, expert) matrix-vector loops of swiglu_ffn_f32
+// (src/rms_norm.cpp:55-63 gate_up, :81-89 down) with one persistent grouped GEMM per
+// projection over all experts (and the shared expert as one more group).
+//
+// Orientation ("swap AB"): the weight slab is the MMA's A operand (M = 128 weight rows)
+// and the group's token rows are B (N = 16..256 tokens, multiple of 16), so a group's last,
+// ragged token tile costs at most 15 padding columns instead of a padded 128-row M tile.
+//   D[128 weight rows, N tokens] (fp32, TMEM) += A[128, 64] (fp16, smem) * B[N, 64]^T (fp16)
+// per 64-wide K stage, as four K=16 tcgen05.mma.cta_group::1.kind::f16 instructions.
+//
+// Warp roles (448 threads, one CTA per SM, persistent over the work list):
+//   warp 0      TMA producer: 2-D tiled load of the B tile (fp16 token rows, 128B swizzle)
+//               and one 1-D bulk copy of the raw GGUF weight tile, both on full[s]
+//   warp 1      TMEM allocator + MMA issuer (one thread), commits to empty[s] / acc_full[b]
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (each warp its 32-lane quarter),
+//               transpose through shared memory, SwiGLU -> fp16 (gate_up) or fp32 (down)
+//   warps 6..13 dequantisers: GGUF Q4_0/Q8_0/F16 tile -> fp16 A tile in the canonical
+//               K-major 128B-swizzled layout, one (row, GGUF block) per thread
+// Pipelines: STAGES-deep ring (full/a_ready/empty mbarriers) for K stages; two TMEM
+// accumulators (2 x 256 columns) so the epilogue of one tile overlaps the next tile's MMAs.
+// Every mbarrier wait is bounded in time; on expiry the CTA records an error code and
+// unwinds (and still releases its tensor memory).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace hymoe {
+
+namespace {
+
+constexpr int kThreads = 448;
+constexpr int kBRows = 256;                     // B tile rows (TMA box height)
+constexpr int kABytes = kTileRows * 128;        // 16 KB fp16 A stage
+constexpr int kBBytes = kBRows * 128;           // 32 KB fp16 B stage
+constexpr int kStageLd = 33;                    // epilogue staging row stride (floats)
+constexpr int kAccCols = 256;
+constexpr int kTmemCols = 512;
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ bool named_bar_and(int id, int n, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\t"
+        "setp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.and.pred po, %2, %3, pi;\n\t"
+        "selp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(p)), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// ---- dequantisers: entry e = 2 r + b of the raw tile -> row r, chunks 4b..4b+3 of A.
+
+template <int WT>
+__device__ __forceinline__ void dequant_entry(const uint8_t* raw, uint8_t* A, int e);
+
+template <>
+__device__ __forceinline__ void dequant_entry<W_Q4_0>(const uint8_t* raw, uint8_t* A, int e) {
+    const int r = e >> 1, b = e & 1;
+    const __half2 d2 = __half2half2(*reinterpret_cast<const __half*>(raw + 2 * e));
+    const uint4 q = *reinterpret_cast<const uint4*>(raw + 512 + 16 * e);
+    const __half2 off = __float2half2_rn(1032.0f);  // 1024 magic + 8 offset
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    uint32_t lo[8], hi[8];  // half2 pairs of elements (2i, 2i+1) and (16+2i, 17+2i)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t p0 = __byte_perm(w[i], 0, 0x4140);  // bytes 4i, 4i+1 -> halves
+        const uint32_t p1 = __byte_perm(w[i], 0, 0x4342);  // bytes 4i+2, 4i+3
+        lo[2 * i] = (p0 & 0x000F000Fu) | 0x64006400u;
+        hi[2 * i] = ((p0 >> 4) & 0x000F000Fu) | 0x64006400u;
+        lo[2 * i + 1] = (p1 & 0x000F000Fu) | 0x64006400u;
+        hi[2 * i + 1] = ((p1 >> 4) & 0x000F000Fu) | 0x64006400u;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        lo[i] = h2_bits(__hmul2(__hsub2(bits_h2(lo[i]), off), d2));
+        hi[i] = h2_bits(__hmul2(__hsub2(bits_h2(hi[i]), off), d2));
+    }
+    uint8_t* row = A;
+    *reinterpret_cast<uint4*>(row + sw128_offset(r, 4 * b + 0)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(row + sw128_offset(r, 4 * b + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+    *reinterpret_cast<uint4*>(row + sw128_offset(r, 4 * b + 2)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(row + sw128_offset(r, 4 * b + 3)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+}
+
+template <>
+__device__ __forceinline__ void dequant_entry<W_Q8_0>(const uint8_t* raw, uint8_t* A, int e) {
+    const int r = e >> 1, b = e & 1;
+    const __half2 d2 = __half2half2(*reinterpret_cast<const __half*>(raw + 2 * e));
+    const uint4* qp = reinterpret_cast<const uint4*>(raw + 512 + 32 * e);
+    const uint4 q0 = qp[0], q1 = qp[1];
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const __half2 off = __float2half2_rn(1152.0f);  // 1024 magic + 128 sign offset
+    uint32_t h[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t p0 = __byte_perm(w[i], 0, 0x4140) ^ 0x64806480u;
+        const uint32_t p1 = __byte_perm(w[i], 0, 0x4342) ^ 0x64806480u;
+        h[2 * i] = h2_bits(__hmul2(__hsub2(bits_h2(p0), off), d2));
+        h[2 * i + 1] = h2_bits(__hmul2(__hsub2(bits_h2(p1), off), d2));
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(A + sw128_offset(r, 4 * b + c)) =
+            make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+}
+
+template <>
+__device__ __forceinline__ void dequant_entry<W_F16>(const uint8_t* raw, uint8_t* A, int e) {
+    const int r = e >> 1, b = e & 1;
+    const uint4* src = reinterpret_cast<const uint4*>(raw + r * 128 + b * 64);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(A + sw128_offset(r, 4 * b + c)) = src[c];
+}
+
+// Time-bounded wait that ignores the error word: used only to let copies already in
+// flight land before the CTA exits.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) return;
+}
+
+template <int WT, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
+    constexpr int RAW = tile_bytes(WT);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = sA + STAGES * kABytes;
+    uint8_t* sRaw = sB + STAGES * kBBytes;
+    float* sStage = reinterpret_cast<float*>(sRaw + STAGES * RAW);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + kTileRows * kStageLd);
+    uint64_t* full = bars;
+    uint64_t* aready = full + STAGES;
+    uint64_t* empty = aready + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* mma_done = acc_empty + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&aready[s], 8);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(mma_done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+    const int n_items = *a.n_items;
+    int* err = a.err;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+                const int4 item = a.items[w];
+                const uint8_t* wt = a.wtiles[item.x] + static_cast<size_t>(item.y) * a.n_ks * RAW;
+                for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!mbar_wait(&empty[s], ph ^ 1, err, DEVERR_TIMEOUT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], kBBytes + RAW);
+                    tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], ks * kTileK, item.z);
+                    bulk_load(sRaw + s * RAW, wt + static_cast<size_t>(ks) * RAW, RAW, &full[s]);
+                }
+            }
+            // Let every copy this CTA issued land before shared memory goes away.
+            const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0;
+            for (uint32_t j = first; j < it; ++j) mbar_drain(&full[j % STAGES], (j / STAGES) & 1);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t it = 0, tc = 0;
+            bool ok = true;
+            for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++tc) {
+                const int4 item = a.items[w];
+                int n = ((item.w + 15) / 16) * 16;
+                n = n < 16 ? 16 : (n > kAccCols ? kAccCols : n);
+                const uint32_t idesc = idesc_f16_f32(kTileRows, n);
+                const uint32_t ab = tc & 1, aph = (tc >> 1) & 1;
+                if (!mbar_wait(&acc_empty[ab], aph ^ 1, err, DEVERR_TIMEOUT_MMA)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + ab * kAccCols;
+                for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!mbar_wait(&aready[s], ph, err, DEVERR_TIMEOUT_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sA + s * kABytes);
+                    const uint32_t b_addr = smem_u32(sB + s * kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kTileK / 16; ++kk)
+                        mma_f16_ss(d_tmem, sw128_kmajor_desc(a_addr + kk * 32),
+                                   sw128_kmajor_desc(b_addr + kk * 32), idesc,
+                                   (ks | kk) != 0 ? 1u : 0u);
+                    mma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&acc_full[ab]);
+            }
+            // All MMAs issued by this thread complete before tensor memory is released.
+            mma_commit(mma_done);
+            mbar_drain(mma_done, 0);
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;            // TMEM lane quarter this warp may access
+        const int et = tid - 64;           // 0..127
+        const int tok = et >> 2, seg = et & 3;
+        uint32_t tc = 0;
+        for (int w = blockIdx.x; w < n_items; w += gridDim.x, ++tc) {
+            const int4 item = a.items[w];
+            const int rb = item.y, row0 = item.z, nrows = item.w;
+            const uint32_t ab = tc & 1, aph = (tc >> 1) & 1;
+            const bool got = mbar_wait(&acc_full[ab], aph, err, DEVERR_TIMEOUT_EPILOGUE);
+            if (!named_bar_and(1, 128, got)) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem + ab * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
+            const int nchunks = (nrows + 31) / 32;
+            for (int ch = 0; ch < nchunks; ++ch) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(d_tmem + ch * 32, v);
+                tmem_ld_wait();
+                if (ch == nchunks - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[ab]);
+                }
+                float* srow = sStage + (q * 32 + lane) * kStageLd;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) srow[j] = __uint_as_float(v[j]);
+                named_bar_sync(1, 128);
+                const int c = ch * 32 + tok;
+                if (c < nrows) {
+                    const size_t row = static_cast<size_t>(row0 + c);
+                    if (a.glu) {
+                        uint32_t hv[8];
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj) {
+                            const int j = seg * 16 + 2 * jj;
+                            const float h0 = silu_mul(sStage[j * kStageLd + tok],
+                                                      sStage[(kGluHalf + j) * kStageLd + tok]);
+                            const float h1 = silu_mul(sStage[(j + 1) * kStageLd + tok],
+                                                      sStage[(kGluHalf + j + 1) * kStageLd + tok]);
+                            hv[jj] = h2_bits(__floats2half2_rn(h0, h1));
+                        }
+                        uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) +
+                                                            row * a.out_ld + rb * kGluHalf +
+                                                            seg * 16);
+                        o[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                        o[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+                    } else {
+                        float4* o = reinterpret_cast<float4*>(static_cast<float*>(a.out) +
+                                                              row * a.out_ld + rb * kTileRows +
+                                                              seg * 32);
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj) {
+                            const int n0 = seg * 32 + 4 * jj;
+                            o[jj] = make_float4(sStage[n0 * kStageLd + tok],
+                                                sStage[(n0 + 1) * kStageLd + tok],
+                                                sStage[(n0 + 2) * kStageLd + tok],
+                                                sStage[(n0 + 3) * kStageLd + tok]);
+                        }
+                    }
+                }
+                named_bar_sync(1, 128);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ dequantisers
+        const int e = tid - 192;  // 0..255
+        uint32_t it = 0;
+        bool ok = true;
+        for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+            for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
+                const int s = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1;
+                if (!mbar_wait(&full[s], ph, err, DEVERR_TIMEOUT_DEQUANT)) {
+                    ok = false;
+                    break;
+                }
+                dequant_entry<WT>(sRaw + s * RAW, sA + s * kABytes, e);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&aready[s]);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+template <int WT, int STAGES>
+constexpr size_t smem_bytes() {
+    return 1024 + STAGES * (kABytes + kBBytes + tile_bytes(WT)) + kTileRows * kStageLd * 4 +
+           (3 * STAGES + 5) * 8 + 16;
+}
+
+template <int WT, int STAGES>
+cudaError_t launch_typed(const CUtensorMap& tmap_b, const GemmArgs& a, int n_sms,
+                         cudaStream_t st) {
+    constexpr size_t smem = smem_bytes<WT, STAGES>();
+    static_assert(smem <= 232448, "shared memory budget");
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<WT, STAGES>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    gemm_tc_kernel<WT, STAGES><<<n_sms, kThreads, smem, st>>>(tmap_b, a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_tc(const CUtensorMap& tmap_b, const GemmArgs& a, int n_sms,
+                           cudaStream_t st) {
+    switch (a.wtype) {
+        case W_Q4_0: return launch_typed<W_Q4_0, 3>(tmap_b, a, n_sms, st);
+        case W_Q8_0: return launch_typed<W_Q8_0, 3>(tmap_b, a, n_sms, st);
+        case W_F16: return launch_typed<W_F16, 3>(tmap_b, a, n_sms, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace hymoe

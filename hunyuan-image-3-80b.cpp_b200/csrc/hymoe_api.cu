@@ -1,0 +1,553 @@
+// hymoe_api.cu — the C ABI (include/hymoe.h): context, device weight store, and the
+// per-call orchestration of the MoE block on one GPU.
+//
+// Forward pipeline for one layer call (all on the context's stream):
+//   [H2D x, residual]        (HYMOE_HOST_PTRS only)
+//   router_kernel            logits / softmax / top-K / renorm + per-chunk expert counts
+//   plan_kernel              prefix scan -> group offsets, chunk bases, GEMM work lists
+//   scatter_gather_kernel    stable counting sort of (token, rank) pairs; fp16 rows -> xp
+//   gate_up GEMM             tcgen05 grouped GEMM + SwiGLU epilogue -> h (fp16)
+//                            (grouped GEMV when n_tokens <= 8: decode regime)
+//   down GEMM                -> y (fp32), one row per (token, expert) pair + shared rows
+//   combine_kernel           out = residual + shared + sum_k w_k y_k
+//   [D2H out, debug]         (HYMOE_HOST_PTRS only)
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/hymoe.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace hymoe;
+
+namespace {
+
+thread_local std::string g_create_error;
+
+struct LayerStore {
+    bool loaded = false;
+    int wtype = -1;                    // device tile type (Q4_0 / Q8_0 / F16)
+    float* router = nullptr;           // [E, H] f32
+    uint8_t* gu = nullptr;             // groups x gate_up tiles
+    uint8_t* dn = nullptr;             // groups x down tiles
+    const uint8_t** d_gu_ptrs = nullptr;  // device [groups] tile bases
+    const uint8_t** d_dn_ptrs = nullptr;
+};
+
+size_t gguf_nbytes(int type, int64_t n) {
+    switch (type) {
+        case HYMOE_TYPE_F32: return static_cast<size_t>(n) * 4;
+        case HYMOE_TYPE_F16: return static_cast<size_t>(n) * 2;
+        case HYMOE_TYPE_Q4_0: return static_cast<size_t>(n / 32) * 18;
+        case HYMOE_TYPE_Q8_0: return static_cast<size_t>(n / 32) * 34;
+        default: return 0;
+    }
+}
+
+int tile_type_for(int ggml_type) {
+    return ggml_type == HYMOE_TYPE_Q4_0 ? W_Q4_0 : ggml_type == HYMOE_TYPE_Q8_0 ? W_Q8_0 : W_F16;
+}
+
+using EncodeTiledFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+}  // namespace
+
+struct hymoe_ctx {
+    hymoe_config cfg{};
+    std::string err;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int n_sms = 148;
+    int H = 0, I = 0, E = 0, K = 0;
+    int groups = 0;           // local routed experts + shared
+    int e_local = 0, e_first = 0;
+    size_t gu_group_bytes = 0, dn_group_bytes = 0;
+    std::vector<LayerStore> layers;
+
+    // scratch (sized for max_tokens at create; expert-parallel receive side included)
+    size_t rows_cap = 0;
+    int max_items = 0;
+    float *x_dev = nullptr, *resid_dev = nullptr, *out_dev = nullptr;
+    float *logits = nullptr, *probs = nullptr, *topk_w = nullptr;
+    int *topk_idx = nullptr, *chunk_counts = nullptr, *chunk_base = nullptr, *goff = nullptr;
+    int *slot_pos = nullptr, *n_items = nullptr, *err_word = nullptr;
+    int4 *items_gu = nullptr, *items_dn = nullptr;
+    __half *xp = nullptr, *hbuf = nullptr;
+    float* y = nullptr;
+    uint8_t* tmp = nullptr;   // load / synthesis staging of one GGUF tensor
+    size_t tmp_bytes = 0;
+    CUtensorMap tmap_xp{}, tmap_h{};
+
+    float* bias_dev = nullptr;
+
+    hymoe_status fail(hymoe_status st, const char* fmt, ...) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof(buf), fmt, ap);
+        va_end(ap);
+        err = buf;
+        return st;
+    }
+    hymoe_status cuda_fail(cudaError_t e, const char* what) {
+        return fail(e == cudaErrorMemoryAllocation ? HYMOE_ERR_OOM : HYMOE_ERR_CUDA,
+                    "%s: %s", what, cudaGetErrorString(e));
+    }
+};
+
+#define HY_CUDA(ctx, call)                                          \
+    do {                                                            \
+        cudaError_t _e = (call);                                    \
+        if (_e != cudaSuccess) return (ctx)->cuda_fail(_e, #call);  \
+    } while (0)
+
+namespace {
+
+template <typename T>
+cudaError_t dalloc(T** p, size_t count) {
+    return cudaMalloc(reinterpret_cast<void**>(p), sizeof(T) * (count ? count : 1));
+}
+
+hymoe_status make_tmap(hymoe_ctx* c, CUtensorMap* map, void* base, uint64_t K, uint64_t rows) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return c->fail(HYMOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {K, rows};
+    cuuint64_t strides[1] = {K * 2};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), 256u};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return c->fail(HYMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", r);
+    return HYMOE_OK;
+}
+
+void free_layer(LayerStore& L) {
+    cudaFree(L.router);
+    cudaFree(L.gu);
+    cudaFree(L.dn);
+    cudaFree(L.d_gu_ptrs);
+    cudaFree(L.d_dn_ptrs);
+    L = LayerStore{};
+}
+
+hymoe_status ensure_layer(hymoe_ctx* c, uint32_t layer, int wtype) {
+    LayerStore& L = c->layers[layer];
+    const int TB = tile_bytes(wtype);
+    const size_t gu_bytes = static_cast<size_t>(2 * c->I / kTileRows) * (c->H / kTileK) * TB;
+    const size_t dn_bytes = static_cast<size_t>(c->H / kTileRows) * (c->I / kTileK) * TB;
+    if (L.gu && L.wtype == wtype) return HYMOE_OK;
+    free_layer(L);
+    L.wtype = wtype;
+    c->gu_group_bytes = gu_bytes;
+    c->dn_group_bytes = dn_bytes;
+    HY_CUDA(c, dalloc(&L.router, static_cast<size_t>(c->E) * c->H));
+    HY_CUDA(c, dalloc(&L.gu, gu_bytes * c->groups));
+    HY_CUDA(c, dalloc(&L.dn, dn_bytes * c->groups));
+    HY_CUDA(c, dalloc(&L.d_gu_ptrs, c->groups));
+    HY_CUDA(c, dalloc(&L.d_dn_ptrs, c->groups));
+    std::vector<const uint8_t*> gp(c->groups), dp(c->groups);
+    for (int g = 0; g < c->groups; ++g) {
+        gp[g] = L.gu + gu_bytes * g;
+        dp[g] = L.dn + dn_bytes * g;
+    }
+    HY_CUDA(c, cudaMemcpy(L.d_gu_ptrs, gp.data(), sizeof(void*) * c->groups, cudaMemcpyHostToDevice));
+    HY_CUDA(c, cudaMemcpy(L.d_dn_ptrs, dp.data(), sizeof(void*) * c->groups, cudaMemcpyHostToDevice));
+    return HYMOE_OK;
+}
+
+bool tensor_ok(const hymoe_tensor* t, int64_t rows, int64_t cols, int want_type) {
+    if (!t || !t->data) return false;
+    if (t->ne[0] != cols || t->ne[1] != rows) return false;
+    if (want_type >= 0 && t->ggml_type != want_type) return false;
+    const size_t nb = gguf_nbytes(t->ggml_type, rows * cols);
+    return nb != 0 && t->nbytes == nb;
+}
+
+// Copies (if on host) and re-tiles one expert matrix into `dst`.
+hymoe_status load_matrix(hymoe_ctx* c, const hymoe_tensor* t, uint8_t* dst, int dst_type,
+                         int rows, int K, int glu_I, bool host) {
+    const uint8_t* src = static_cast<const uint8_t*>(t->data);
+    if (host) {
+        HY_CUDA(c, cudaMemcpyAsync(c->tmp, t->data, t->nbytes, cudaMemcpyHostToDevice, c->stream));
+        src = c->tmp;
+    }
+    HY_CUDA(c, launch_repack(src, t->ggml_type, dst, dst_type, rows, K, glu_I, c->stream));
+    if (host) HY_CUDA(c, cudaStreamSynchronize(c->stream));  // tmp is reused by the next tensor
+    return HYMOE_OK;
+}
+
+}  // namespace
+
+// ============================================================================ C ABI
+
+extern "C" {
+
+const char* hymoe_version(void) { return "hymoe 0.1 (sm_100a)"; }
+
+hymoe_status hymoe_nccl_unique_id(void* out128) {
+    if (!out128) return HYMOE_ERR_INVALID_ARG;
+    return HYMOE_ERR_UNSUPPORTED;
+}
+
+const char* hymoe_last_error(const hymoe_ctx* ctx) {
+    return ctx ? ctx->err.c_str() : g_create_error.c_str();
+}
+
+hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
+    g_create_error.clear();
+    if (!cfg || !out) {
+        g_create_error = "null argument";
+        return HYMOE_ERR_INVALID_ARG;
+    }
+    *out = nullptr;
+    const uint32_t H = cfg->hidden_size, I = cfg->moe_intermediate_size, E = cfg->num_experts,
+                   K = cfg->moe_topk;
+    if (H == 0 || H % 128 || I == 0 || I % 64 || E < 1 || E > 64 || K < 1 || K > 8 || K > E ||
+        cfg->max_tokens == 0 || cfg->num_layers == 0 || cfg->ep_size < 1 ||
+        cfg->ep_rank < 0 || cfg->ep_rank >= cfg->ep_size || E % cfg->ep_size) {
+        g_create_error =
+            "unsupported shape: need H%128==0, I%64==0, 1<=E<=64, 1<=K<=8, K<=E, E%ep_size==0";
+        return HYMOE_ERR_INVALID_ARG;
+    }
+    if (cudaSetDevice(cfg->device) != cudaSuccess) {
+        g_create_error = "cudaSetDevice failed";
+        return HYMOE_ERR_CUDA;
+    }
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, cfg->device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, cfg->device);
+    if (major != 10 || minor != 0) {
+        g_create_error = "this build targets sm_100a (B200); device is not compute capability 10.0";
+        return HYMOE_ERR_UNSUPPORTED;
+    }
+    hymoe_ctx* c = new hymoe_ctx();
+    c->cfg = *cfg;
+    c->H = H;
+    c->I = I;
+    c->E = E;
+    c->K = K;
+    c->e_local = E / cfg->ep_size;
+    c->e_first = cfg->ep_rank * c->e_local;
+    c->groups = c->e_local + 1;
+    c->layers.resize(cfg->num_layers);
+    cudaDeviceGetAttribute(&c->n_sms, cudaDevAttrMultiProcessorCount, cfg->device);
+
+    auto bail = [&](hymoe_status st) {
+        g_create_error = c->err;
+        hymoe_destroy(c);
+        return st;
+    };
+    if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(c->fail(HYMOE_ERR_CUDA, "cudaStreamCreate failed"));
+    c->stream = c->own_stream;
+
+    const size_t T = cfg->max_tokens;
+    // Rows of the expert-sorted activation matrix: local pairs + shared rows, plus (for
+    // expert parallelism) rows received from other ranks.
+    size_t rows = T * (K + 1);
+    c->rows_cap = rows;
+    const size_t n_chunks = (T + kRouterTok - 1) / kRouterTok;
+    const int n_rb = std::max<int>(2 * I / kTileRows, H / kTileRows);
+    c->max_items = n_rb * static_cast<int>(rows / 256 + c->groups + 2);
+    cudaError_t e = cudaSuccess;
+    auto A = [&](cudaError_t r) {
+        if (e == cudaSuccess) e = r;
+    };
+    A(dalloc(&c->x_dev, T * H));
+    A(dalloc(&c->resid_dev, T * H));
+    A(dalloc(&c->out_dev, T * H));
+    A(dalloc(&c->logits, T * E));
+    A(dalloc(&c->probs, T * E));
+    A(dalloc(&c->topk_w, T * K));
+    A(dalloc(&c->topk_idx, T * K));
+    A(dalloc(&c->chunk_counts, n_chunks * E));
+    A(dalloc(&c->chunk_base, n_chunks * E));
+    A(dalloc(&c->goff, E + 2));
+    A(dalloc(&c->bias_dev, E));
+    A(dalloc(&c->slot_pos, T * K));
+    A(dalloc(&c->n_items, 2));
+    A(dalloc(&c->err_word, 1));
+    A(dalloc(&c->items_gu, c->max_items));
+    A(dalloc(&c->items_dn, c->max_items));
+    A(dalloc(&c->xp, rows * H));
+    A(dalloc(&c->hbuf, rows * I));
+    A(dalloc(&c->y, rows * H));
+    c->tmp_bytes = static_cast<size_t>(2 * I) * H * 4;  // largest GGUF tensor (F32 gate_up)
+    A(dalloc(&c->tmp, c->tmp_bytes));
+    if (e != cudaSuccess) return bail(c->cuda_fail(e, "scratch allocation"));
+    if (cudaMemset(c->err_word, 0, sizeof(int)) != cudaSuccess)
+        return bail(c->fail(HYMOE_ERR_CUDA, "cudaMemset failed"));
+    hymoe_status st = make_tmap(c, &c->tmap_xp, c->xp, H, rows);
+    if (st == HYMOE_OK) st = make_tmap(c, &c->tmap_h, c->hbuf, I, rows);
+    if (st != HYMOE_OK) return bail(st);
+    if (cfg->ep_size > 1)
+        return bail(c->fail(HYMOE_ERR_UNSUPPORTED, "expert parallelism not available"));
+    *out = c;
+    return HYMOE_OK;
+}
+
+void hymoe_destroy(hymoe_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->cfg.device);
+    if (c->own_stream) cudaStreamSynchronize(c->own_stream);
+    for (auto& L : c->layers) free_layer(L);
+    cudaFree(c->x_dev);
+    cudaFree(c->resid_dev);
+    cudaFree(c->out_dev);
+    cudaFree(c->logits);
+    cudaFree(c->probs);
+    cudaFree(c->topk_w);
+    cudaFree(c->topk_idx);
+    cudaFree(c->chunk_counts);
+    cudaFree(c->chunk_base);
+    cudaFree(c->goff);
+    cudaFree(c->bias_dev);
+    cudaFree(c->slot_pos);
+    cudaFree(c->n_items);
+    cudaFree(c->err_word);
+    cudaFree(c->items_gu);
+    cudaFree(c->items_dn);
+    cudaFree(c->xp);
+    cudaFree(c->hbuf);
+    cudaFree(c->y);
+    cudaFree(c->tmp);
+    if (c->own_stream) cudaStreamDestroy(c->own_stream);
+    delete c;
+}
+
+hymoe_status hymoe_set_stream(hymoe_ctx* c, void* stream) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own_stream;
+    return HYMOE_OK;
+}
+
+hymoe_status hymoe_synchronize(hymoe_ctx* c) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    HY_CUDA(c, cudaStreamSynchronize(c->stream));
+    int word = 0;
+    HY_CUDA(c, cudaMemcpy(&word, c->err_word, sizeof(int), cudaMemcpyDeviceToHost));
+    if (word != 0) {
+        cudaMemset(c->err_word, 0, sizeof(int));
+        return c->fail(HYMOE_ERR_TIMEOUT, "device-side bounded wait expired (code 0x%x)", word);
+    }
+    return HYMOE_OK;
+}
+
+hymoe_status hymoe_load_layer(hymoe_ctx* c, uint32_t layer, const hymoe_tensor* router,
+                              const hymoe_tensor* shared_gate_up, const hymoe_tensor* shared_down,
+                              const hymoe_tensor* experts_gate_up,
+                              const hymoe_tensor* experts_down, int flags) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
+    HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    const int H = c->H, I = c->I, E = c->E;
+    if (!tensor_ok(router, E, H, HYMOE_TYPE_F32))
+        return c->fail(HYMOE_ERR_INVALID_ARG, "router must be F32 [E=%d, H=%d]", E, H);
+    if (!shared_gate_up || !shared_down || !experts_gate_up || !experts_down)
+        return c->fail(HYMOE_ERR_INVALID_ARG, "null tensor array");
+    const int gt = shared_gate_up->ggml_type;
+    if (gt != HYMOE_TYPE_F32 && gt != HYMOE_TYPE_F16 && gt != HYMOE_TYPE_Q4_0 && gt != HYMOE_TYPE_Q8_0)
+        return c->fail(HYMOE_ERR_INVALID_ARG, "unsupported GGUF type %d", gt);
+    if (!tensor_ok(shared_gate_up, 2 * I, H, gt) || !tensor_ok(shared_down, H, I, gt))
+        return c->fail(HYMOE_ERR_INVALID_ARG, "shared expert tensors: bad shape/type/size");
+    for (int le = 0; le < c->e_local; ++le) {
+        const int ge = c->e_first + le;
+        if (!tensor_ok(&experts_gate_up[ge], 2 * I, H, gt) || !tensor_ok(&experts_down[ge], H, I, gt))
+            return c->fail(HYMOE_ERR_INVALID_ARG,
+                           "expert %d tensors: bad shape/size or type differs from the shared expert", ge);
+    }
+    const int wt = tile_type_for(gt);
+    hymoe_status st = ensure_layer(c, layer, wt);
+    if (st != HYMOE_OK) return st;
+    LayerStore& L = c->layers[layer];
+    L.loaded = false;
+    const bool host = (flags & HYMOE_HOST_PTRS) != 0;
+    HY_CUDA(c, cudaMemcpyAsync(L.router, router->data, router->nbytes,
+                               host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, c->stream));
+    for (int g = 0; g < c->groups; ++g) {
+        const bool shared = g == c->e_local;
+        const hymoe_tensor* tg = shared ? shared_gate_up : &experts_gate_up[c->e_first + g];
+        const hymoe_tensor* td = shared ? shared_down : &experts_down[c->e_first + g];
+        st = load_matrix(c, tg, L.gu + c->gu_group_bytes * g, wt, 2 * I, H, I, host);
+        if (st == HYMOE_OK) st = load_matrix(c, td, L.dn + c->dn_group_bytes * g, wt, H, I, 0, host);
+        if (st != HYMOE_OK) return st;
+    }
+    HY_CUDA(c, cudaStreamSynchronize(c->stream));
+    L.loaded = true;
+    return HYMOE_OK;
+}
+
+hymoe_status hymoe_synth_layer(hymoe_ctx* c, uint32_t layer, int32_t ggml_type, uint64_t seed,
+                               float stddev) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
+    if (ggml_type != HYMOE_TYPE_F32 && ggml_type != HYMOE_TYPE_F16 && ggml_type != HYMOE_TYPE_Q4_0 &&
+        ggml_type != HYMOE_TYPE_Q8_0)
+        return c->fail(HYMOE_ERR_INVALID_ARG, "unsupported GGUF type %d", ggml_type);
+    HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    const int H = c->H, I = c->I, E = c->E;
+    const int wt = tile_type_for(ggml_type);
+    hymoe_status st = ensure_layer(c, layer, wt);
+    if (st != HYMOE_OK) return st;
+    LayerStore& L = c->layers[layer];
+    L.loaded = false;
+    // c = float(stddev * sqrt(1.5) / 65536), computed in double as the CPU generator does.
+    const float scale = static_cast<float>(static_cast<double>(stddev) * 1.2247448713915890491 / 65536.0);
+    auto sid = [&](int kind, int index) {
+        return (static_cast<uint64_t>(layer) << 32) | (static_cast<uint64_t>(kind) << 16) |
+               static_cast<uint64_t>(index);
+    };
+    HY_CUDA(c, launch_synth_f32(L.router, static_cast<uint64_t>(E) * H, seed, sid(1, 0), scale, c->stream));
+    for (int g = 0; g < c->groups; ++g) {
+        const bool shared = g == c->e_local;
+        const int idx = shared ? 0xFFFF : c->e_first + g;
+        HY_CUDA(c, launch_synth_gguf(c->tmp, ggml_type, static_cast<uint64_t>(2 * I) * H, seed,
+                                     sid(2, idx), scale, c->stream));
+        HY_CUDA(c, launch_repack(c->tmp, ggml_type, L.gu + c->gu_group_bytes * g, wt, 2 * I, H, I,
+                                 c->stream));
+        HY_CUDA(c, launch_synth_gguf(c->tmp, ggml_type, static_cast<uint64_t>(H) * I, seed,
+                                     sid(3, idx), scale, c->stream));
+        HY_CUDA(c, launch_repack(c->tmp, ggml_type, L.dn + c->dn_group_bytes * g, wt, H, I, 0,
+                                 c->stream));
+    }
+    HY_CUDA(c, cudaStreamSynchronize(c->stream));
+    L.loaded = true;
+    return HYMOE_OK;
+}
+
+hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const float* residual,
+                           float* out, uint32_t n_tokens, const float* router_bias,
+                           hymoe_debug* dbg, int flags) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    if (layer >= c->layers.size() || !c->layers[layer].loaded)
+        return c->fail(HYMOE_ERR_STATE, "layer %u not loaded", layer);
+    if (n_tokens > c->cfg.max_tokens)
+        return c->fail(HYMOE_ERR_INVALID_ARG, "n_tokens %u exceeds max_tokens %u", n_tokens,
+                       c->cfg.max_tokens);
+    if ((!x || !out) && n_tokens > 0) return c->fail(HYMOE_ERR_INVALID_ARG, "null x/out");
+    HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    const LayerStore& L = c->layers[layer];
+    const int T = static_cast<int>(n_tokens), H = c->H, I = c->I, E = c->E, K = c->K;
+    const bool host = (flags & HYMOE_HOST_PTRS) != 0;
+    cudaStream_t st = c->stream;
+    const size_t xbytes = static_cast<size_t>(T) * H * sizeof(float);
+
+    const float* dx = x;
+    const float* dres = residual;
+    float* dout = out;
+    const float* dbias = router_bias;
+    float* dlog = dbg ? dbg->router_logits : nullptr;
+    float* dprob = dbg ? dbg->router_probs : nullptr;
+    if (host) {
+        if (T > 0) HY_CUDA(c, cudaMemcpyAsync(c->x_dev, x, xbytes, cudaMemcpyHostToDevice, st));
+        dx = c->x_dev;
+        if (residual && T > 0) {
+            HY_CUDA(c, cudaMemcpyAsync(c->resid_dev, residual, xbytes, cudaMemcpyHostToDevice, st));
+            dres = c->resid_dev;
+        }
+        dout = c->out_dev;
+        if (router_bias) {
+            HY_CUDA(c, cudaMemcpyAsync(c->bias_dev, router_bias, sizeof(float) * E,
+                                       cudaMemcpyHostToDevice, st));
+            dbias = c->bias_dev;
+        }
+        if (dlog) dlog = c->logits;
+        if (dprob) dprob = c->probs;
+    }
+
+    if (T > 0) {
+        const int n_chunks = (T + kRouterTok - 1) / kRouterTok;
+        HY_CUDA(c, launch_router(dx, T, H, L.router, E, K, dbias, dlog, dprob, c->topk_w,
+                                 c->topk_idx, c->chunk_counts, st));
+        const bool gemv = T <= kGemvMaxRows;
+        PlanArgs pa{};
+        pa.chunk_counts = c->chunk_counts;
+        pa.n_chunks = n_chunks;
+        pa.T = T;
+        pa.E = E;
+        pa.K = K;
+        pa.n_rb_gu = 2 * I / kTileRows;
+        pa.n_rb_dn = H / kTileRows;
+        pa.tile_n = 256;
+        pa.gemv = gemv ? 1 : 0;
+        pa.goff = c->goff;
+        pa.chunk_base = c->chunk_base;
+        pa.items_gu = c->items_gu;
+        pa.items_dn = c->items_dn;
+        pa.n_items = c->n_items;
+        HY_CUDA(c, launch_plan(pa, st));
+        HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->goff,
+                                         c->slot_pos, c->xp, st));
+        if (gemv) {
+            const int active = std::min(E, T * K) + 1;
+            HY_CUDA(c, launch_gemv(c->items_gu, c->n_items, pa.n_rb_gu * active, L.d_gu_ptrs,
+                                   L.wtype, H / kTileK, 1, c->xp, H, c->hbuf, I, st));
+            HY_CUDA(c, launch_gemv(c->items_dn, c->n_items + 1, pa.n_rb_dn * active, L.d_dn_ptrs,
+                                   L.wtype, I / kTileK, 0, c->hbuf, I, c->y, H, st));
+        } else {
+            GemmArgs ga{};
+            ga.items = c->items_gu;
+            ga.n_items = c->n_items;
+            ga.wtiles = L.d_gu_ptrs;
+            ga.wtype = L.wtype;
+            ga.n_ks = H / kTileK;
+            ga.glu = 1;
+            ga.out = c->hbuf;
+            ga.out_ld = I;
+            ga.err = c->err_word;
+            HY_CUDA(c, launch_gemm_tc(c->tmap_xp, ga, c->n_sms, st));
+            ga.items = c->items_dn;
+            ga.n_items = c->n_items + 1;
+            ga.wtiles = L.d_dn_ptrs;
+            ga.n_ks = I / kTileK;
+            ga.glu = 0;
+            ga.out = c->y;
+            ga.out_ld = H;
+            HY_CUDA(c, launch_gemm_tc(c->tmap_h, ga, c->n_sms, st));
+        }
+        HY_CUDA(c, launch_combine(c->y, c->slot_pos, c->topk_w, c->goff, dres, dout, T, H, E, K, st));
+        if (dbg) {
+            const cudaMemcpyKind kd = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+            if (dbg->topk_weights)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->topk_weights, c->topk_w, sizeof(float) * T * K, kd, st));
+            if (dbg->topk_indices)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->topk_indices, c->topk_idx, sizeof(int) * T * K, kd, st));
+            if (host && dlog)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->router_logits, dlog, sizeof(float) * T * E, kd, st));
+            if (host && dprob)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->router_probs, dprob, sizeof(float) * T * E, kd, st));
+        }
+    }
+    if (host) {
+        if (T > 0) HY_CUDA(c, cudaMemcpyAsync(out, dout, xbytes, cudaMemcpyDeviceToHost, st));
+        return hymoe_synchronize(c);
+    }
+    return HYMOE_OK;
+}
+
+}  // extern "C"

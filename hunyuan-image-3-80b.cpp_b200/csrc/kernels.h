@@ -1,0 +1,75 @@
+// kernels.h — host-side launchers of the hymoe CUDA kernels (internal to libhymoe.so).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hymoe {
+
+// ---- weights.cu
+// Re-tiles one GGUF matrix [rows, K] (device bytes, type src_type) into the device tile
+// format (dst_type: the same quantised type, or F16 for F32/F16 sources).  glu_I > 0
+// selects the gate_up row interleave (rows 0..I-1 gate, I..2I-1 up).
+cudaError_t launch_repack(const uint8_t* src, int src_type, uint8_t* dst, int dst_type, int rows,
+                          int K, int glu_I, cudaStream_t st);
+// Synthetic GGUF tensor of n elements into dst (GGUF bytes of `type`).
+cudaError_t launch_synth_gguf(uint8_t* dst, int type, uint64_t n, uint64_t seed, uint64_t stream,
+                              float scale, cudaStream_t st);
+// Synthetic F32 values.
+cudaError_t launch_synth_f32(float* dst, uint64_t n, uint64_t seed, uint64_t stream, float scale,
+                             cudaStream_t st);
+
+// ---- router.cu
+constexpr int kRouterTok = 16;  // tokens per router CTA (= dispatch chunk)
+cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
+                          const float* bias, float* logits, float* probs, float* topk_w,
+                          int* topk_idx, int* chunk_counts, cudaStream_t st);
+
+// ---- dispatch.cu
+struct PlanArgs {
+    const int* chunk_counts;  // [n_chunks][E]
+    int n_chunks, T, E, K;
+    int n_rb_gu, n_rb_dn;     // row blocks of gate_up / down matrices
+    int tile_n;               // token rows per GEMM work item (tensor-core path)
+    int gemv;                 // 1: one work item per (group, row block)
+    int* goff;                // [E + 2] group row offsets (group E = shared expert)
+    int* chunk_base;          // [n_chunks][E]
+    int4* items_gu;           // {group, row block, row start, rows}
+    int4* items_dn;
+    int* n_items;             // [2]: gate_up, down
+};
+cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
+
+cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
+                                  const int* chunk_base, const int* goff, int* slot_pos,
+                                  __half* xp, cudaStream_t st);
+
+// ---- gemm_tc.cu (tcgen05 grouped GEMM)
+struct GemmArgs {
+    const int4* items;
+    const int* n_items;
+    const uint8_t* const* wtiles;  // [groups] tile base per group
+    int wtype;
+    int n_ks;                      // K / 64
+    int glu;                       // 1: gate_up + SwiGLU epilogue -> fp16; 0: down -> fp32
+    void* out;                     // [rows, out_ld]
+    int out_ld;
+    int* err;
+};
+// tmap_b: tensor map over the token operand (fp16 [rows, K], box {64, 256}, SW128).
+cudaError_t launch_gemm_tc(const CUtensorMap& tmap_b, const GemmArgs& a, int n_sms,
+                           cudaStream_t st);
+
+// ---- gemv.cu (decode path, CUDA cores)
+constexpr int kGemvMaxRows = 8;
+cudaError_t launch_gemv(const int4* items, const int* n_items, int max_items,
+                        const uint8_t* const* wtiles, int wtype, int n_ks, int glu,
+                        const __half* act, int act_ld, void* out, int out_ld, cudaStream_t st);
+
+// ---- combine.cu
+cudaError_t launch_combine(const float* y, const int* slot_pos, const float* topk_w,
+                           const int* goff, const float* resid, float* out, int T, int H, int E,
+                           int K, cudaStream_t st);
+
+}  // namespace hymoe

@@ -1,0 +1,186 @@
+"""ctypes bindings of libhymoe.so (the C ABI in include/hymoe.h).
+
+This is how the test-suite and bench.py drive the library; a C++ host uses the header
+directly (see the adapter in csrc/adapter/).  The module fails loudly when the CUDA
+library is missing: there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libhymoe.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "hymoe.h")
+
+TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0 = 0, 1, 2, 8
+HOST_PTRS = 1
+
+STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OOM", 4: "UNSUPPORTED", 5: "NCCL",
+          6: "TIMEOUT", 7: "STATE"}
+
+# Every function include/hymoe.h declares.
+EXPORTS = ["hymoe_version", "hymoe_nccl_unique_id", "hymoe_create", "hymoe_destroy",
+           "hymoe_last_error", "hymoe_set_stream", "hymoe_synchronize", "hymoe_load_layer",
+           "hymoe_synth_layer", "hymoe_forward"]
+
+
+class Config(C.Structure):
+    _fields_ = [("hidden_size", C.c_uint32), ("moe_intermediate_size", C.c_uint32),
+                ("num_experts", C.c_uint32), ("moe_topk", C.c_uint32), ("num_layers", C.c_uint32),
+                ("max_tokens", C.c_uint32), ("device", C.c_int32), ("ep_rank", C.c_int32),
+                ("ep_size", C.c_int32), ("nccl_unique_id", C.c_void_p)]
+
+
+class Tensor(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("ggml_type", C.c_int32), ("ne", C.c_int64 * 2),
+                ("nbytes", C.c_size_t)]
+
+
+class Debug(C.Structure):
+    _fields_ = [("router_logits", C.c_void_p), ("router_probs", C.c_void_p),
+                ("topk_weights", C.c_void_p), ("topk_indices", C.c_void_p)]
+
+
+class HymoeError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"hymoe {STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-C", HERE, "-j8"], check=True)
+
+
+_LIB = None
+
+
+def lib() -> C.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is not built (run make -C {HERE})")
+        L = C.CDLL(LIB_PATH)
+        vp, i32, u32, u64 = C.c_void_p, C.c_int32, C.c_uint32, C.c_uint64
+        L.hymoe_version.restype = C.c_char_p
+        L.hymoe_nccl_unique_id.argtypes = [vp]
+        L.hymoe_create.argtypes = [C.POINTER(Config), C.POINTER(vp)]
+        L.hymoe_destroy.argtypes = [vp]
+        L.hymoe_destroy.restype = None
+        L.hymoe_last_error.argtypes = [vp]
+        L.hymoe_last_error.restype = C.c_char_p
+        L.hymoe_set_stream.argtypes = [vp, vp]
+        L.hymoe_synchronize.argtypes = [vp]
+        L.hymoe_load_layer.argtypes = [vp, u32, C.POINTER(Tensor), C.POINTER(Tensor),
+                                       C.POINTER(Tensor), C.POINTER(Tensor), C.POINTER(Tensor),
+                                       C.c_int]
+        L.hymoe_synth_layer.argtypes = [vp, u32, i32, u64, C.c_float]
+        L.hymoe_forward.argtypes = [vp, u32, vp, vp, vp, u32, vp, C.POINTER(Debug), C.c_int]
+        for f in EXPORTS:
+            if f not in ("hymoe_version", "hymoe_destroy", "hymoe_last_error"):
+                getattr(L, f).restype = C.c_int
+        _LIB = L
+    return _LIB
+
+
+def nccl_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    st = lib().hymoe_nccl_unique_id(buf)
+    if st != 0:
+        raise HymoeError(st, "hymoe_nccl_unique_id failed")
+    return buf.raw
+
+
+def gguf_nbytes(t: int, n: int) -> int:
+    return {TYPE_F32: 4 * n, TYPE_F16: 2 * n, TYPE_Q4_0: n // 32 * 18, TYPE_Q8_0: n // 32 * 34}[t]
+
+
+def _tensor(arr, t: int, rows: int, cols: int) -> Tensor:
+    """arr: numpy uint8/float32 host array (GGUF bytes) or None."""
+    if arr is None:
+        return Tensor(None, t, (C.c_int64 * 2)(cols, rows), 0)
+    return Tensor(arr.ctypes.data, t, (C.c_int64 * 2)(cols, rows), arr.nbytes)
+
+
+class MoE:
+    """One hymoe context: shapes of HunyuanConfig, layer slots, scratch for max_tokens."""
+
+    def __init__(self, H=4096, I=3072, E=64, K=8, num_layers=1, max_tokens=4096, device=0,
+                 ep_rank=0, ep_size=1, nccl_id: bytes | None = None):
+        self.L = lib()
+        self.H, self.I, self.E, self.K = H, I, E, K
+        self._id = C.create_string_buffer(nccl_id, 128) if nccl_id else None
+        cfg = Config(H, I, E, K, num_layers, max_tokens, device, ep_rank, ep_size,
+                     C.cast(self._id, C.c_void_p) if self._id else None)
+        h = C.c_void_p()
+        st = self.L.hymoe_create(C.byref(cfg), C.byref(h))
+        if st != 0:
+            raise HymoeError(st, self.L.hymoe_last_error(None).decode())
+        self.h = h
+
+    def _check(self, st: int) -> None:
+        if st != 0:
+            raise HymoeError(st, self.L.hymoe_last_error(self.h).decode())
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.L.hymoe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_ptr: int | None) -> None:
+        self._check(self.L.hymoe_set_stream(self.h, stream_ptr))
+
+    def synchronize(self) -> None:
+        self._check(self.L.hymoe_synchronize(self.h))
+
+    def load_layer(self, layer: int, router, shared_gu, shared_dn, experts_gu, experts_dn,
+                   wtype: int) -> None:
+        """Host numpy arrays: router float32 [E, H]; the others GGUF bytes of `wtype`
+        (entries of experts_* may be None for experts another rank owns)."""
+        H, I, E = self.H, self.I, self.E
+        r = _tensor(router, TYPE_F32, E, H)
+        sg = _tensor(shared_gu, wtype, 2 * I, H)
+        sd = _tensor(shared_dn, wtype, H, I)
+        eg = (Tensor * E)(*[_tensor(a, wtype, 2 * I, H) for a in experts_gu])
+        ed = (Tensor * E)(*[_tensor(a, wtype, H, I) for a in experts_dn])
+        self._check(self.L.hymoe_load_layer(self.h, layer, C.byref(r), C.byref(sg), C.byref(sd),
+                                            eg, ed, HOST_PTRS))
+
+    def synth_layer(self, layer: int, wtype: int, seed: int, std: float = 0.02) -> None:
+        self._check(self.L.hymoe_synth_layer(self.h, layer, wtype, seed, std))
+
+    def forward_host(self, layer: int, x, resid=None, bias=None, debug: bool = False) -> dict:
+        """x (and resid) float32 [T, H] numpy; returns numpy outputs."""
+        import numpy as np
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T = x.shape[0]
+        out = np.empty_like(x)
+        res = {"out": out}
+        dbg = None
+        if debug:
+            res.update(logits=np.empty((T, self.E), np.float32),
+                       probs=np.empty((T, self.E), np.float32),
+                       w=np.empty((T, self.K), np.float32), idx=np.empty((T, self.K), np.int32))
+            dbg = Debug(res["logits"].ctypes.data, res["probs"].ctypes.data,
+                        res["w"].ctypes.data, res["idx"].ctypes.data)
+        r = None if resid is None else np.ascontiguousarray(resid, dtype=np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        self._check(self.L.hymoe_forward(self.h, layer, x.ctypes.data,
+                                         None if r is None else r.ctypes.data, out.ctypes.data, T,
+                                         None if b is None else b.ctypes.data,
+                                         C.byref(dbg) if dbg else None, HOST_PTRS))
+        return res
+
+    def forward_device(self, layer: int, x_ptr: int, out_ptr: int, T: int, resid_ptr=None,
+                       bias_ptr=None, dbg: Debug | None = None, host: bool = False) -> None:
+        """Raw pointers (device memory unless host=True); asynchronous on the set stream."""
+        self._check(self.L.hymoe_forward(self.h, layer, x_ptr, resid_ptr, out_ptr, T, bias_ptr,
+                                         C.byref(dbg) if dbg else None,
+                                         HOST_PTRS if host else 0))

@@ -1,0 +1,157 @@
+/* hymoe.h — C ABI of the B200 (sm_100a) MoE block library, libhymoe.so.
+ *
+ * Drop-in for the MoE step of the reference's decoder layer:
+ *   void moe_forward_cpu(const float* hidden_states, const MoEWeights& w, uint32_t n_tokens,
+ *                        const HunyuanConfig& cfg, float* output,
+ *                        float* debug_router_logits, float* debug_router_weights,
+ *                        int32_t* debug_router_indices)
+ *   (declared src/hunyuan_model.h:147-156, defined src/attention.cpp:191-313,
+ *    called from src/decoder_layer.cpp:38 with the residual added at :42)
+ * and of the per-layer weight load it consumes
+ *   HunyuanGGUFLoader::load_layer_weights (src/hunyuan_gguf_loader.cpp:229-281,
+ *   tensor names blk.N.ffn_gate / ffn_shared_{gate_up,down} / ffn_expert_E_{gate_up,down}).
+ *
+ * Plain C types only.  Every call returns an hymoe_status; nothing aborts the process.
+ * One context per host thread (calls on one context are serialised by the caller).
+ */
+#ifndef HYMOE_H
+#define HYMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    HYMOE_OK = 0,
+    HYMOE_ERR_INVALID_ARG = 1, /* bad pointer, size, type or shape */
+    HYMOE_ERR_CUDA = 2,        /* a CUDA runtime/driver call failed */
+    HYMOE_ERR_OOM = 3,         /* device allocation failed */
+    HYMOE_ERR_UNSUPPORTED = 4, /* configuration this build does not implement */
+    HYMOE_ERR_NCCL = 5,        /* NCCL communicator error (expert-parallel mode) */
+    HYMOE_ERR_TIMEOUT = 6,     /* a bounded device-side or collective wait expired */
+    HYMOE_ERR_STATE = 7        /* call out of order (e.g. layer not loaded) */
+} hymoe_status;
+
+/* GGUF tensor types (GGUF numbering, as the reference's ggml_type at
+ * src/hunyuan_gguf_loader.cpp:172-177). */
+enum {
+    HYMOE_TYPE_F32 = 0,
+    HYMOE_TYPE_F16 = 1,
+    HYMOE_TYPE_Q4_0 = 2, /* 32-element blocks: fp16 d, 16 bytes of nibbles; x = (q-8)*d */
+    HYMOE_TYPE_Q8_0 = 8  /* 32-element blocks: fp16 d, 32 int8;            x = q*d     */
+};
+
+/* flags for hymoe_load_layer / hymoe_forward */
+enum {
+    HYMOE_HOST_PTRS = 1 /* pointers are host memory (copied H2D / D2H inside the call) */
+};
+
+typedef struct hymoe_ctx hymoe_ctx;
+
+/* Shapes mirror HunyuanConfig (src/hunyuan_model.h:13-45). */
+typedef struct {
+    uint32_t hidden_size;           /* H, 4096 (hidden_size, :14); multiple of 128        */
+    uint32_t moe_intermediate_size; /* I, 3072 (moe_intermediate_size, :20); multiple of 64 */
+    uint32_t num_experts;           /* E, 64 (num_experts, :21); 8..64                    */
+    uint32_t moe_topk;              /* K, 8 (moe_topk, :22); 1..8                         */
+    uint32_t num_layers;            /* layer slots this context holds                     */
+    uint32_t max_tokens;            /* largest n_tokens of one hymoe_forward (this rank)  */
+    int32_t device;                 /* CUDA device ordinal                                */
+    /* Expert parallelism: ep_size ranks each own num_experts/ep_size consecutive
+     * experts.  ep_size == 1 runs everything locally.  For ep_size > 1,
+     * nccl_unique_id points at the 128-byte id from hymoe_nccl_unique_id() on rank 0. */
+    int32_t ep_rank;
+    int32_t ep_size;
+    const void* nccl_unique_id;
+} hymoe_config;
+
+/* One GGUF tensor: raw GGUF bytes exactly as stored in the file.
+ * ne[0] = input features (contiguous, blocks run along it), ne[1] = output rows,
+ * i.e. PyTorch [out, in] row-major (scripts/convert_to_gguf.py:196-200 writes no
+ * transpose).  nbytes must equal the GGUF size for (type, ne). */
+typedef struct {
+    const void* data;
+    int32_t ggml_type;
+    int64_t ne[2];
+    size_t nbytes;
+} hymoe_tensor;
+
+/* Optional router outputs, any member may be NULL.  Same memory kind as x. */
+typedef struct {
+    float* router_logits; /* [T, E] pre-softmax logits (+bias)                          */
+    float* router_probs;  /* [T, E] softmax; what moe_forward_cpu writes into its
+                             debug_router_logits argument (src/attention.cpp:224-240,278) */
+    float* topk_weights;  /* [T, K] renormalised (debug_router_weights)                  */
+    int32_t* topk_indices;/* [T, K] rank order (debug_router_indices)                    */
+} hymoe_debug;
+
+/* Library version string. */
+const char* hymoe_version(void);
+
+/* Writes the 128-byte NCCL unique id that rank 0 hands to every rank. */
+hymoe_status hymoe_nccl_unique_id(void* out128);
+
+/* Creates a context on cfg->device; allocates the per-call scratch for max_tokens.
+ * Expert-parallel contexts join the NCCL communicator here (collective across ranks). */
+hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out);
+
+/* Destroys the context and frees all device memory it owns. */
+void hymoe_destroy(hymoe_ctx* ctx);
+
+/* Message of the last failing call on this context ("" when none).  With ctx == NULL,
+ * the last failure of hymoe_create on this thread. */
+const char* hymoe_last_error(const hymoe_ctx* ctx);
+
+/* Makes subsequent work run on `stream` (a cudaStream_t; NULL = the context's own). */
+hymoe_status hymoe_set_stream(hymoe_ctx* ctx, void* stream);
+
+/* Waits for all work of the context and reports device-side errors (bounded waits that
+ * expired, NCCL failures) as a status. */
+hymoe_status hymoe_synchronize(hymoe_ctx* ctx);
+
+/* Loads one layer's MoE weights (replaces HunyuanGGUFLoader::load_layer_weights for the
+ * MoE tensors, src/hunyuan_gguf_loader.cpp:259-276).
+ *   router        blk.N.ffn_gate.weight               [E, H], must be F32
+ *   shared_gate_up blk.N.ffn_shared_gate_up.weight    [2I, H]  F32/F16/Q4_0/Q8_0
+ *   shared_down    blk.N.ffn_shared_down.weight       [H, I]
+ *   experts_gate_up[E] blk.N.ffn_expert_E_gate_up.weight [2I, H]
+ *   experts_down[E]    blk.N.ffn_expert_E_down.weight    [H, I]
+ * Rows 0..I-1 of gate_up are the gate (SiLU'd), rows I..2I-1 the up projection
+ * (src/rms_norm.cpp:70-74).  The bytes are copied to the device and re-tiled there;
+ * the caller's buffers may be freed on return.  F32 expert weights are rounded to
+ * F16 on the device.  In expert-parallel mode a rank reads only the experts it owns;
+ * the other entries may have data == NULL. */
+hymoe_status hymoe_load_layer(hymoe_ctx* ctx, uint32_t layer, const hymoe_tensor* router,
+                              const hymoe_tensor* shared_gate_up,
+                              const hymoe_tensor* shared_down,
+                              const hymoe_tensor* experts_gate_up,
+                              const hymoe_tensor* experts_down, int flags);
+
+/* Fills a layer with synthetic weights generated on the device: every tensor ~N(0,std)
+ * by the library's Philox4x32-10 / Irwin-Hall generator (stream layout documented in
+ * DESIGN.md), quantised to `ggml_type` with the GGUF rule.  The router stays F32.
+ * Bit-identical to the CPU generator of the test oracle.  No reference counterpart:
+ * it exists so benchmarks can build 40+ GB of weights without a host round trip. */
+hymoe_status hymoe_synth_layer(hymoe_ctx* ctx, uint32_t layer, int32_t ggml_type,
+                               uint64_t seed, float stddev);
+
+/* The MoE block of one decoder layer for n_tokens tokens:
+ *   out[t] = residual[t] + shared(x[t]) + sum_k w[t,k] * expert_{idx[t,k]}(x[t])
+ * (src/attention.cpp:191-313; residual add of src/decoder_layer.cpp:42 when residual
+ * is non-NULL; out may alias residual).  x, residual and out are [n_tokens, H] F32
+ * row-major.  router_bias [E] (nullable) is added to the router logits before the
+ * softmax (no reference counterpart; 0 reproduces the reference).  In expert-parallel
+ * mode every rank calls this with its own tokens (n_tokens may differ per rank).
+ * With HYMOE_HOST_PTRS the call copies in, computes and copies out before returning;
+ * otherwise it is asynchronous on the context's stream. */
+hymoe_status hymoe_forward(hymoe_ctx* ctx, uint32_t layer, const float* x,
+                           const float* residual, float* out, uint32_t n_tokens,
+                           const float* router_bias, hymoe_debug* dbg, int flags);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HYMOE_H */

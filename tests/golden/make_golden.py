@@ -1,0 +1,73 @@
+"""Generate the golden fixtures under tests/golden/ by running the REFERENCE's own
+moe_forward_cpu (src/attention.cpp:191-313), compiled from the reference sources into
+oracle/_ref/libhyref.so by oracle/Makefile.
+
+Inputs are never stored for the full-shape cases: weights and activations are
+regenerated from (seed, layer, stream) by the synthetic generator (Philox4x32-10 +
+Irwin-Hall), whose known-answer vectors tests/test_oracle.py pins.  Each fixture
+records the case parameters, the reference outputs and a checksum of the inputs so a
+drifting generator is caught.
+
+Run (needs the reference tree, i.e. only in the build container):
+    python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import os
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+import oracle as O  # noqa: E402
+
+# name, H, I, E, K, T, weight type, seed
+CASES = [
+    ("small_f32", 256, 192, 64, 8, 16, O.F32, 0),
+    ("small_q4_0", 512, 384, 64, 8, 32, O.Q4_0, 1),
+    ("small_q8_0", 512, 256, 64, 8, 24, O.Q8_0, 2),
+    ("ragged_q4_0", 384, 128, 16, 8, 7, O.Q4_0, 3),
+    ("multitile_q8_0", 256, 128, 8, 8, 300, O.Q8_0, 4),
+    ("topk4_f16", 256, 64, 32, 4, 40, O.F16, 5),
+    ("full_f32_t2", 4096, 3072, 64, 8, 2, O.F32, 0),
+    ("full_q4_0_t2", 4096, 3072, 64, 8, 2, O.Q4_0, 0),
+    ("full_q8_0_t1", 4096, 3072, 64, 8, 1, O.Q8_0, 0),
+]
+
+
+def input_checksum(x: np.ndarray, rw: np.ndarray) -> np.ndarray:
+    return np.array([np.float64(x).sum(), np.float64(np.abs(x)).sum(), np.float64(rw).sum()])
+
+
+def run_case(orc: O.Oracle, ref: O.RefMoE, name, H, I, E, K, T, wt, seed):
+    x = O.synth_x(orc, seed, T, H)
+    rw = orc.fill_normal(E * H, seed, O.stream_id(0, O.KIND_ROUTER), 0.02).reshape(E, H)
+    _, _, _, ti = orc.router(x, rw, K)
+    rw, sgu, sdn, egu, edn = O.synth_layer_f32(orc, seed, 0, H, I, E, wt,
+                                               experts=np.unique(ti))
+    h = ref.weights(H, I, rw, sgu, sdn, egu, edn)
+    t0 = time.time()
+    r = ref.moe_forward(x, h, E, H, I, K)
+    dt = time.time() - t0
+    ref.free(h)
+    meta = np.array([H, I, E, K, T, wt, seed], dtype=np.int64)
+    path = os.path.join(HERE, f"{name}.npz")
+    np.savez_compressed(path, meta=meta, out=r["out"], probs=r["probs"], w=r["w"], idx=r["idx"],
+                        checksum=input_checksum(x, rw))
+    print(f"{name}: reference {dt:.2f}s -> {os.path.getsize(path)} bytes")
+
+
+def main():
+    orc = O.Oracle()
+    ref = O.RefMoE()
+    only = set(sys.argv[1:])
+    for c in CASES:
+        if not only or c[0] in only:
+            run_case(orc, ref, *c)
+
+
+if __name__ == "__main__":
+    main()
