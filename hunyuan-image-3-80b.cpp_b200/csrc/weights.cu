@@ -94,10 +94,10 @@ __device__ __forceinline__ float synth_value(uint64_t i, uint64_t seed, uint64_t
     return __fmul_rn(static_cast<float>(s - 262140), c);
 }
 
+// One 16-bit store: every GGUF block (18 / 34 / 64 bytes) starts on an even offset of a
+// cudaMalloc'd buffer, so the fp16 field is 2-byte aligned.
 __device__ __forceinline__ void put_half(uint8_t* p, float v) {
-    const uint16_t h = __half_as_ushort(__float2half_rn(v));
-    p[0] = static_cast<uint8_t>(h);
-    p[1] = static_cast<uint8_t>(h >> 8);
+    *reinterpret_cast<__half*>(p) = __float2half_rn(v);
 }
 
 // One thread per 32-element GGUF block.
