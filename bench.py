@@ -1,0 +1,429 @@
+#!/usr/bin/env python
+"""bench.py — MoE-layer tokens/s of the B200 MoE block (BASELINE metric), plus the decode
+HBM bandwidth sub-metric.
+
+Default workload (N=1): one HunyuanImage-3.0 MoE block (H=4096, I=3072, 64 routed + 1
+shared SwiGLU expert, top-8), GGUF Q4_0 expert weights, 4096 tokens per step,
+activations ~N(0,1), router bias ~N(0,0.5) (seeded synthetic data, random-init weights
+generated on the device).  A step is one hymoe_forward over the 4096 tokens.
+
+  value  tokens/s with inputs resident in HBM, device time by CUDA events, L2 flushed
+         between steps (a 256 MiB write outside the timed events)
+  e2e    the same call through the C ABI with pinned HOST buffers: H2D of x and the bias,
+         compute, D2H of the output inside the timed region
+  roofline  the dominant kernel (grouped gate_up GEMM): algorithmic FLOP per launch /
+         its CUDA-event duration, against MEASURED_PEAKS.json bf16 (sustained)
+  cpu_baseline  the reference's own moe_forward_cpu (oracle/_ref, compiled from the
+         reference sources) on a bounded token sample, one host core as written
+
+--impl reference times the reference's CPU implementation with all host cores (token
+sharded over processes; the MoE is per-token independent) on the same workload.
+Under torchrun (N > 1) every rank runs an independent replica of the layer on its own
+4096 tokens (expert parallelism arrives with the EP runtime).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "hunyuan-image-3-80b.cpp_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+sys.path.insert(0, PKG)
+
+H, I, E, K = 4096, 3072, 64, 8
+FLOP_PER_PAIR_GU = 2 * 2 * I * H      # gate_up, per (token, expert) row
+FLOP_PER_PAIR_DN = 2 * H * I          # down
+FLOP_ROUTER_PER_TOKEN = 2 * E * H
+FFN_BYTES = {2: 2 * I * H // 32 * 18 + H * I // 32 * 18, 8: 2 * I * H // 32 * 34 + H * I // 32 * 34}
+METRIC = "MoE-layer tokens/s (Q4_0, 4096 tok) at 1/2/4/8 B200; decode HBM GB/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return dict(hbm=d["hbm_gbs"], tf=d["bf16_tflops"], tf_sus=d["bf16_tflops_sustained"],
+                    src="measured")
+    return dict(hbm=6650.0, tf=1590.0, tf_sus=1400.0, src="fallback")
+
+
+def ncu_traffic():
+    p = os.path.join(ROOT, "profiles", "ncu_summary.json")
+    if os.path.exists(p):
+        return json.load(open(p))
+    return {}
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, dev: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-i", str(dev), "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4)
+                          if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- GPU arm
+
+def run_gpu(args, rank: int, world: int, local_rank: int):
+    import numpy as np
+    import torch
+    import hymoe
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    T = args.tokens
+    m = hymoe.MoE(H, I, E, K, 1, T, device=local_rank)
+    m.synth_layer(0, hymoe.TYPE_Q4_0, args.seed, 0.02)
+    stream = torch.cuda.current_stream()
+    m.set_stream(stream.cuda_stream)
+    g = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank)
+    x = torch.randn(T, H, device=dev, generator=g, dtype=torch.float32)
+    bias = (torch.randn(E, device=dev, generator=g) * 0.5).contiguous()
+    out = torch.empty_like(x)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        m.forward_device(0, x.data_ptr(), out.data_ptr(), T, bias_ptr=bias.data_ptr())
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # routing statistics of this workload (for the algorithmic FLOP count)
+    dbg_idx = torch.empty(T, K, dtype=torch.int32, device=dev)
+    dbg = hymoe.Debug(None, None, None, dbg_idx.data_ptr())
+    m.forward_device(0, x.data_ptr(), out.data_ptr(), T, bias_ptr=bias.data_ptr(), dbg=dbg)
+    torch.cuda.synchronize()
+    counts = torch.bincount(dbg_idx.flatten().long(), minlength=E).cpu().numpy()
+    rows = T * K + T
+    flop_gu = rows * FLOP_PER_PAIR_GU
+    flop_dn = rows * FLOP_PER_PAIR_DN
+    flop_total = flop_gu + flop_dn + T * FLOP_ROUTER_PER_TOKEN
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local_rank)
+    m.profile(True)
+    for s in range(args.steps):
+        flush.zero_()
+        ev[s][0].record(stream)
+        step()
+        ev[s][1].record(stream)
+    torch.cuda.synchronize()
+    m.profile(False)
+    prof = m.profile_read()
+    clk = clocks.stop()
+    if world > 1:
+        torch.distributed.barrier()
+    dev_ms = sum(a.elapsed_time(b) for a, b in ev)
+    t_max = dev_ms
+    if world > 1:
+        tt = torch.tensor([dev_ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        t_max = float(tt.item())
+    ms_per_step = t_max / args.steps
+    value = world * T * args.steps / (t_max / 1e3)
+
+    # ---- e2e through the C ABI with pinned host buffers
+    xh = x.cpu().pin_memory()
+    bh = bias.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    for _ in range(2):
+        m.forward_device(0, xh.data_ptr(), oh.data_ptr(), T, bias_ptr=bh.data_ptr(), host=True)
+    e2e_ms = 0.0
+    for s in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        m.forward_device(0, xh.data_ptr(), oh.data_ptr(), T, bias_ptr=bh.data_ptr(), host=True)
+        b.record(stream)
+        b.synchronize()
+        e2e_ms += a.elapsed_time(b)
+    if world > 1:
+        tt = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+
+    pk = peaks()
+    gu_ms, gu_n = prof["gate_up"]
+    gu_launch_ms = gu_ms / max(gu_n, 1)
+    achieved = flop_gu / (gu_launch_ms / 1e3) / 1e12
+    tr = ncu_traffic().get("gate_up_q4_0_t4096", {})
+    roofline = {"kernel": "gemm_tc_kernel<Q4_0> (grouped gate_up + SwiGLU)", "bound": "tensor",
+                "achieved": round(achieved, 1), "peak": pk["tf_sus"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["tf_sus"], 4),
+                "peak_src": f"{pk['src']} bf16 sustained (burst {pk['tf']})",
+                "traffic": tr.get("dram_bytes_per_launch"),
+                "algorithmic_flop_per_launch": flop_gu}
+    phases = {k: round(v[0] / args.steps, 4) for k, v in prof.items() if v[1]}
+    launches = sum(v[1] for v in prof.values())
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded; random-init Q4_0 weights generated on device)",
+        "config": {"workload": "cfg3: one MoE block, Q4_0 experts, 4096 tokens/step/GPU, "
+                               "router bias ~N(0,0.5)",
+                   "model": "HunyuanImage-3.0 MoE block H=4096 I=3072 E=64+1 shared top-8",
+                   "global_batch": T * world, "seq_len": T,
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "flushed between steps (256 MiB write outside the timed events)"},
+        "tflops_total": round(flop_total / (ms_per_step / 1e3) / 1e12, 1),
+        "frac_of_peak_total": round(flop_total / (ms_per_step / 1e3) / 1e12 / pk["tf_sus"], 4),
+        "phases_ms_per_step": phases,
+        "roofline": roofline,
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": xh.numel() * 4 + bh.numel() * 4,
+                "d2h_bytes_per_step": oh.numel() * 4, "ms_per_step": round(e2e_ms / args.steps, 4)},
+        "gpu_launches": launches,
+        "clocks": clk,
+        "expert_load": {"max": int(counts.max()), "min": int(counts.min()),
+                        "mean": float(counts.mean())},
+    }
+    m.close()
+    if args.decode and rank == 0:
+        res["decode"] = run_decode(args, local_rank)
+    return res
+
+
+def run_decode(args, local_rank: int) -> dict:
+    """cfg2: Q8_0 weights, T = 1/8/64 tokens per step, HBM-bound grouped GEMV/GEMM."""
+    import torch
+    import hymoe
+
+    dev = torch.device("cuda", local_rank)
+    m = hymoe.MoE(H, I, E, K, 1, 64, device=local_rank)
+    m.synth_layer(0, hymoe.TYPE_Q8_0, args.seed, 0.02)
+    stream = torch.cuda.current_stream()
+    m.set_stream(stream.cuda_stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    pk = peaks()
+    res = {}
+    for T in (1, 8, 64):
+        g = torch.Generator(device=dev).manual_seed(args.seed + T)
+        x = torch.randn(T, H, device=dev, generator=g)
+        out = torch.empty_like(x)
+        idx = torch.empty(T, K, dtype=torch.int32, device=dev)
+        dbg = hymoe.Debug(None, None, None, idx.data_ptr())
+        m.forward_device(0, x.data_ptr(), out.data_ptr(), T, dbg=dbg)
+        torch.cuda.synchronize()
+        distinct = int(torch.unique(idx).numel())
+        nbytes = (distinct + 1) * FFN_BYTES[8] + E * H * 4 + 2 * T * H * 4
+        for _ in range(max(args.warmup, 3)):
+            m.forward_device(0, x.data_ptr(), out.data_ptr(), T)
+        steps = max(args.steps, 20)
+        tot = 0.0
+        m.profile(True)
+        for _ in range(steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            m.forward_device(0, x.data_ptr(), out.data_ptr(), T)
+            b.record(stream)
+            b.synchronize()
+            tot += a.elapsed_time(b)
+        m.profile(False)
+        prof = m.profile_read()
+        ms = tot / steps
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[f"T{T}"] = {"ms_per_step": round(ms, 4), "algorithmic_bytes": nbytes,
+                        "distinct_experts": distinct, "achieved_GBps": round(gbs, 1),
+                        "frac_hbm": round(gbs / pk["hbm"], 4),
+                        "phases_ms": {k: round(v[0] / steps, 4) for k, v in prof.items() if v[1]}}
+    m.close()
+    res["peak_GBps"] = pk["hbm"]
+    res["weights"] = "Q8_0"
+    return res
+
+
+# --------------------------------------------------------------------------- CPU reference
+
+def _cpu_inputs(n_tokens: int, seed: int):
+    """Full-shape Q4_0 layer as the reference consumes it (F32), restricted to the
+    experts the sample tokens select; x ~N(0,1).  moe_forward_cpu has no router-bias
+    input, so the CPU runs route without it; the per-token cost (shared + 8 experts) is
+    the same either way."""
+    sys.path.insert(0, ORACLE)
+    import numpy as np
+    import oracle as O
+    orc = O.Oracle()
+    x = O.synth_x(orc, seed, n_tokens, H)
+    rw = orc.fill_normal(E * H, seed, O.stream_id(0, O.KIND_ROUTER), 0.02).reshape(E, H)
+    _, _, _, ti = orc.router(x, rw, K)
+    w = O.synth_layer_f32(orc, seed, 0, H, I, E, O.Q4_0, experts=np.unique(ti))
+    return O, orc, x, w
+
+
+def cpu_baseline_single(seed: int, n_tokens: int = 12) -> dict:
+    """The reference's own moe_forward_cpu, one core (as written), on a token sample."""
+    O, orc, x, w = _cpu_inputs(n_tokens, seed)
+    if O.RefMoE.available():
+        ref = O.RefMoE()
+        h = ref.weights(H, I, *w)
+        t0 = time.perf_counter()
+        ref.moe_forward(x, h, E, H, I, K)
+        dt = time.perf_counter() - t0
+        ref.free(h)
+        kind = "reference"
+    else:
+        one = O.Oracle(nthreads=1)
+        t0 = time.perf_counter()
+        one.moe_forward(x, *w, K, I)
+        dt = time.perf_counter() - t0
+        kind = "port"
+    return {"value": round(n_tokens / dt, 3), "unit": "tokens/s", "cores": 1, "kind": kind,
+            "sample": f"{n_tokens} tokens of the cfg3 workload through moe_forward_cpu "
+                      f"(src/attention.cpp:191-313), F32-dequantised Q4_0 weights, no router bias "
+                      f"(the reference has none; same per-token cost), "
+                      f"{dt:.2f} s; host has {os.cpu_count()} cores"}
+
+
+def run_reference(args, rank: int, world: int) -> dict | None:
+    """Reference arm: the reference's CPU path with every host core (persistent workers
+    forked after the weight build, each running moe_forward_cpu on its token slice)."""
+    if rank != 0:
+        return None
+    P = len(os.sched_getaffinity(0))
+    per = 2
+    S = P * per
+    O, orc, x, w = _cpu_inputs(S, args.seed)
+    use_ref = O.RefMoE.available()
+    if use_ref:
+        ref = O.RefMoE()
+        handle = ref.weights(H, I, *w)
+    pipes = []
+    for p in range(P):
+        r_go, w_go = os.pipe()
+        r_done, w_done = os.pipe()
+        pid = os.fork()
+        if pid == 0:
+            os.close(w_go)
+            os.close(r_done)
+            xs = x[p * per:(p + 1) * per].copy()
+            one = O.Oracle(nthreads=1)
+            while True:
+                b = os.read(r_go, 1)
+                if not b or b == b"q":
+                    os._exit(0)
+                if use_ref:
+                    ref.moe_forward(xs, handle, E, H, I, K)
+                else:
+                    one.moe_forward(xs, *w, K, I)
+                os.write(w_done, b"d")
+        os.close(r_go)
+        os.close(w_done)
+        pipes.append((pid, w_go, r_done))
+
+    def step():
+        t0 = time.perf_counter()
+        for _, wg, _ in pipes:
+            os.write(wg, b"g")
+        for _, _, rd in pipes:
+            os.read(rd, 1)
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        step()
+    tot = sum(step() for _ in range(args.steps))
+    for pid, wg, rd in pipes:
+        os.write(wg, b"q")
+        os.waitpid(pid, 0)
+    value = S * args.steps / tot
+    kind = "reference" if use_ref else "port"
+    sample = (f"{S} tokens per step ({per} per process x {P} processes) of the cfg3 workload, "
+              f"F32-dequantised Q4_0 weights, no router bias (moe_forward_cpu has none; same "
+              f"per-token cost)")
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "impl": "reference",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(tot / args.steps * 1e3, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": "cfg3: one MoE block, Q4_0 experts (dequantised to F32 as the "
+                               "reference holds them), router bias ~N(0,0.5)",
+                   "model": "HunyuanImage-3.0 MoE block H=4096 I=3072 E=64+1 shared top-8",
+                   "global_batch": S, "seq_len": S, "parallelism": f"{P} CPU processes"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": P, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+# --------------------------------------------------------------------------- main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="hymoe", choices=["hymoe", "reference"])
+    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu", dest="cpu", action="store_false")
+    ap.add_argument("--no-decode", dest="decode", action="store_false")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+
+        import torch
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    res = run_gpu(args, rank, world, local_rank)
+    if rank == 0:
+        if args.cpu and world == 1:
+            res["cpu_baseline"] = cpu_baseline_single(args.seed)
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -103,6 +103,46 @@ struct hymoe_ctx {
 
     float* bias_dev = nullptr;
 
+    // per-phase profiling (hymoe_profile)
+    bool prof = false;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> prof_ev[HYMOE_NUM_PHASES];
+    int prof_launches[HYMOE_NUM_PHASES] = {};
+    std::vector<cudaEvent_t> ev_pool;
+    cudaEvent_t prof_open = nullptr;
+    cudaEvent_t take_event() {
+        cudaEvent_t e = nullptr;
+        if (!ev_pool.empty()) {
+            e = ev_pool.back();
+            ev_pool.pop_back();
+        } else {
+            cudaEventCreate(&e);
+        }
+        return e;
+    }
+    void phase_begin() {
+        if (!prof) return;
+        prof_open = take_event();
+        cudaEventRecord(prof_open, stream);
+    }
+    void phase_end(int phase, int launches = 1) {
+        if (!prof || !prof_open) return;
+        cudaEvent_t e = take_event();
+        cudaEventRecord(e, stream);
+        prof_ev[phase].emplace_back(prof_open, e);
+        prof_launches[phase] += launches;
+        prof_open = nullptr;
+    }
+    void prof_clear() {
+        for (auto& v : prof_ev) {
+            for (auto& pr : v) {
+                ev_pool.push_back(pr.first);
+                ev_pool.push_back(pr.second);
+            }
+            v.clear();
+        }
+        for (int& n : prof_launches) n = 0;
+    }
+
     hymoe_status fail(hymoe_status st, const char* fmt, ...) {
         char buf[512];
         va_list ap;
@@ -335,6 +375,8 @@ void hymoe_destroy(hymoe_ctx* c) {
     cudaFree(c->hbuf);
     cudaFree(c->y);
     cudaFree(c->tmp);
+    c->prof_clear();
+    for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
     delete c;
 }
@@ -482,8 +524,10 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
 
     if (T > 0) {
         const int n_chunks = (T + kRouterTok - 1) / kRouterTok;
+        c->phase_begin();
         HY_CUDA(c, launch_router(dx, T, H, L.router, E, K, dbias, dlog, dprob, c->topk_w,
                                  c->topk_idx, c->chunk_counts, st));
+        c->phase_end(HYMOE_PHASE_ROUTER);
         const bool gemv = T <= kGemvMaxRows;
         PlanArgs pa{};
         pa.chunk_counts = c->chunk_counts;
@@ -500,15 +544,23 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         pa.items_gu = c->items_gu;
         pa.items_dn = c->items_dn;
         pa.n_items = c->n_items;
+        c->phase_begin();
         HY_CUDA(c, launch_plan(pa, st));
+        c->phase_end(HYMOE_PHASE_PLAN);
+        c->phase_begin();
         HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->goff,
                                          c->slot_pos, c->xp, st));
+        c->phase_end(HYMOE_PHASE_DISPATCH);
         if (gemv) {
             const int active = std::min(E, T * K) + 1;
+            c->phase_begin();
             HY_CUDA(c, launch_gemv(c->items_gu, c->n_items, pa.n_rb_gu * active, L.d_gu_ptrs,
                                    L.wtype, H / kTileK, 1, c->xp, H, c->hbuf, I, st));
+            c->phase_end(HYMOE_PHASE_GATE_UP);
+            c->phase_begin();
             HY_CUDA(c, launch_gemv(c->items_dn, c->n_items + 1, pa.n_rb_dn * active, L.d_dn_ptrs,
                                    L.wtype, I / kTileK, 0, c->hbuf, I, c->y, H, st));
+            c->phase_end(HYMOE_PHASE_DOWN);
         } else {
             GemmArgs ga{};
             ga.items = c->items_gu;
@@ -520,7 +572,9 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             ga.out = c->hbuf;
             ga.out_ld = I;
             ga.err = c->err_word;
+            c->phase_begin();
             HY_CUDA(c, launch_gemm_tc(c->tmap_xp, ga, c->n_sms, st));
+            c->phase_end(HYMOE_PHASE_GATE_UP);
             ga.items = c->items_dn;
             ga.n_items = c->n_items + 1;
             ga.wtiles = L.d_dn_ptrs;
@@ -528,9 +582,13 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             ga.glu = 0;
             ga.out = c->y;
             ga.out_ld = H;
+            c->phase_begin();
             HY_CUDA(c, launch_gemm_tc(c->tmap_h, ga, c->n_sms, st));
+            c->phase_end(HYMOE_PHASE_DOWN);
         }
+        c->phase_begin();
         HY_CUDA(c, launch_combine(c->y, c->slot_pos, c->topk_w, c->goff, dres, dout, T, H, E, K, st));
+        c->phase_end(HYMOE_PHASE_COMBINE);
         if (dbg) {
             const cudaMemcpyKind kd = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
             if (dbg->topk_weights)
@@ -546,6 +604,30 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     if (host) {
         if (T > 0) HY_CUDA(c, cudaMemcpyAsync(out, dout, xbytes, cudaMemcpyDeviceToHost, st));
         return hymoe_synchronize(c);
+    }
+    return HYMOE_OK;
+}
+
+hymoe_status hymoe_profile(hymoe_ctx* c, int enable) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    if (enable) c->prof_clear();
+    c->prof = enable != 0;
+    return HYMOE_OK;
+}
+
+hymoe_status hymoe_profile_read(hymoe_ctx* c, float* total_ms, int32_t* launches, int n) {
+    if (!c || n < 0 || n > HYMOE_NUM_PHASES) return HYMOE_ERR_INVALID_ARG;
+    HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    HY_CUDA(c, cudaStreamSynchronize(c->stream));
+    for (int p = 0; p < n; ++p) {
+        float tot = 0.f;
+        for (auto& pr : c->prof_ev[p]) {
+            float ms = 0.f;
+            HY_CUDA(c, cudaEventElapsedTime(&ms, pr.first, pr.second));
+            tot += ms;
+        }
+        if (total_ms) total_ms[p] = tot;
+        if (launches) launches[p] = c->prof_launches[p];
     }
     return HYMOE_OK;
 }

@@ -23,7 +23,10 @@ STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OOM", 4: "UNSUPPORTED", 5: "
 # Every function include/hymoe.h declares.
 EXPORTS = ["hymoe_version", "hymoe_nccl_unique_id", "hymoe_create", "hymoe_destroy",
            "hymoe_last_error", "hymoe_set_stream", "hymoe_synchronize", "hymoe_load_layer",
-           "hymoe_synth_layer", "hymoe_forward"]
+           "hymoe_synth_layer", "hymoe_forward", "hymoe_profile", "hymoe_profile_read"]
+
+PHASES = ["router", "plan", "dispatch", "gate_up", "down", "combine", "ep_dispatch",
+          "ep_combine"]
 
 
 class Config(C.Structure):
@@ -77,6 +80,8 @@ def lib() -> C.CDLL:
                                        C.c_int]
         L.hymoe_synth_layer.argtypes = [vp, u32, i32, u64, C.c_float]
         L.hymoe_forward.argtypes = [vp, u32, vp, vp, vp, u32, vp, C.POINTER(Debug), C.c_int]
+        L.hymoe_profile.argtypes = [vp, C.c_int]
+        L.hymoe_profile_read.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(C.c_int32), C.c_int]
         for f in EXPORTS:
             if f not in ("hymoe_version", "hymoe_destroy", "hymoe_last_error"):
                 getattr(L, f).restype = C.c_int
@@ -139,6 +144,17 @@ class MoE:
 
     def synchronize(self) -> None:
         self._check(self.L.hymoe_synchronize(self.h))
+
+    def profile(self, enable: bool) -> None:
+        self._check(self.L.hymoe_profile(self.h, 1 if enable else 0))
+
+    def profile_read(self) -> dict:
+        """{phase: (total_ms, launches)} recorded since profile(True)."""
+        n = len(PHASES)
+        ms = (C.c_float * n)()
+        cnt = (C.c_int32 * n)()
+        self._check(self.L.hymoe_profile_read(self.h, ms, cnt, n))
+        return {p: (float(ms[i]), int(cnt[i])) for i, p in enumerate(PHASES)}
 
     def load_layer(self, layer: int, router, shared_gu, shared_dn, experts_gu, experts_dn,
                    wtype: int) -> None:

@@ -151,6 +151,28 @@ hymoe_status hymoe_forward(hymoe_ctx* ctx, uint32_t layer, const float* x,
                            const float* residual, float* out, uint32_t n_tokens,
                            const float* router_bias, hymoe_debug* dbg, int flags);
 
+/* Per-phase device timing for benchmarks and tracing: while enabled, hymoe_forward
+ * brackets each phase with CUDA events on the context's stream.  No reference
+ * counterpart (the reference has no timers). */
+enum {
+    HYMOE_PHASE_ROUTER = 0,   /* router GEMV + softmax + top-K               */
+    HYMOE_PHASE_PLAN = 1,     /* prefix scan + work lists                    */
+    HYMOE_PHASE_DISPATCH = 2, /* scatter / gather of token rows              */
+    HYMOE_PHASE_GATE_UP = 3,  /* grouped gate_up GEMM + SwiGLU               */
+    HYMOE_PHASE_DOWN = 4,     /* grouped down GEMM                           */
+    HYMOE_PHASE_COMBINE = 5,  /* weighted combine + residual                 */
+    HYMOE_PHASE_EP_DISPATCH = 6, /* expert-parallel token exchange (NCCL)    */
+    HYMOE_PHASE_EP_COMBINE = 7,  /* expert-parallel result exchange (NCCL)   */
+    HYMOE_NUM_PHASES = 8
+};
+
+/* enable != 0 clears the accumulators and starts recording; 0 stops. */
+hymoe_status hymoe_profile(hymoe_ctx* ctx, int enable);
+
+/* Waits for the context's stream, then writes for each of the first n phases the total
+ * device milliseconds and the number of kernel launches recorded since recording began. */
+hymoe_status hymoe_profile_read(hymoe_ctx* ctx, float* total_ms, int32_t* launches, int n);
+
 #ifdef __cplusplus
 }
 #endif
