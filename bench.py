@@ -105,7 +105,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     T = args.tokens
     m = hymoe.MoE(H, I, E, K, 1, T, device=local_rank)
     m.synth_layer(0, hymoe.TYPE_Q4_0, args.seed, 0.02)
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: torch's default stream has handle 0, which the C ABI reads as
+    # "the context's own stream".  Every torch op and event below runs on this stream.
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
     m.set_stream(stream.cuda_stream)
     g = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank)
     x = torch.randn(T, H, device=dev, generator=g, dtype=torch.float32)
@@ -228,7 +231,8 @@ def run_decode(args, local_rank: int) -> dict:
     dev = torch.device("cuda", local_rank)
     m = hymoe.MoE(H, I, E, K, 1, 64, device=local_rank)
     m.synth_layer(0, hymoe.TYPE_Q8_0, args.seed, 0.02)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
     m.set_stream(stream.cuda_stream)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     pk = peaks()

@@ -131,10 +131,12 @@ def test_device_pointers_and_aliased_residual(orc):
     resid = O.synth_x(orc, seed + 1, T, H)
     m = _ctx(H, I, E, K, T)
     _load(m, lay, wt)
-    xd = torch.from_numpy(x).cuda()
-    rd = torch.from_numpy(resid).cuda()
-    m.set_stream(torch.cuda.current_stream().cuda_stream)
-    m.forward_device(0, xd.data_ptr(), rd.data_ptr(), T, resid_ptr=rd.data_ptr())  # in place
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        xd = torch.from_numpy(x).cuda()
+        rd = torch.from_numpy(resid).cuda()
+        m.set_stream(st.cuda_stream)
+        m.forward_device(0, xd.data_ptr(), rd.data_ptr(), T, resid_ptr=rd.data_ptr())  # in place
     m.synchronize()
     o = _oracle(orc, lay, x, K, I, resid=resid)
     assert rel_l2(rd.cpu().numpy(), o["out"]) <= REL_L2_TOL
