@@ -75,6 +75,10 @@ EncodeTiledFn get_encode_fn() {
 
 }  // namespace
 
+namespace hymoe {
+void set_thread_error(const char* msg) { g_create_error = msg ? msg : ""; }
+}  // namespace hymoe
+
 struct hymoe_ctx {
     hymoe_config cfg{};
     std::string err;

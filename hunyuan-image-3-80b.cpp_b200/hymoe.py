@@ -23,7 +23,8 @@ STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OOM", 4: "UNSUPPORTED", 5: "
 # Every function include/hymoe.h declares.
 EXPORTS = ["hymoe_version", "hymoe_nccl_unique_id", "hymoe_create", "hymoe_destroy",
            "hymoe_last_error", "hymoe_set_stream", "hymoe_synchronize", "hymoe_load_layer",
-           "hymoe_synth_layer", "hymoe_forward", "hymoe_profile", "hymoe_profile_read"]
+           "hymoe_synth_layer", "hymoe_forward", "hymoe_profile", "hymoe_profile_read",
+           "hymoe_ffn_noalloc"]
 
 PHASES = ["router", "plan", "dispatch", "gate_up", "down", "combine", "ep_dispatch",
           "ep_combine"]
@@ -81,6 +82,7 @@ def lib() -> C.CDLL:
         L.hymoe_synth_layer.argtypes = [vp, u32, i32, u64, C.c_float]
         L.hymoe_forward.argtypes = [vp, u32, vp, vp, vp, u32, vp, C.POINTER(Debug), C.c_int]
         L.hymoe_profile.argtypes = [vp, C.c_int]
+        L.hymoe_ffn_noalloc.argtypes = [C.POINTER(Tensor), C.POINTER(Tensor), vp, vp, u32, vp]
         L.hymoe_profile_read.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(C.c_int32), C.c_int]
         for f in EXPORTS:
             if f not in ("hymoe_version", "hymoe_destroy", "hymoe_last_error"):

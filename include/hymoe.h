@@ -104,6 +104,7 @@ void hymoe_destroy(hymoe_ctx* ctx);
 /* Message of the last failing call on this context ("" when none).  With ctx == NULL,
  * the last failure of hymoe_create on this thread. */
 const char* hymoe_last_error(const hymoe_ctx* ctx);
+/* (With ctx == NULL it also reports the last failure of hymoe_ffn_noalloc on this thread.) */
 
 /* Makes subsequent work run on `stream` (a cudaStream_t; NULL = the context's own). */
 hymoe_status hymoe_set_stream(hymoe_ctx* ctx, void* stream);
@@ -172,6 +173,29 @@ hymoe_status hymoe_profile(hymoe_ctx* ctx, int enable);
 /* Waits for the context's stream, then writes for each of the first n phases the total
  * device milliseconds and the number of kernel launches recorded since recording began. */
 hymoe_status hymoe_profile_read(hymoe_ctx* ctx, float* total_ms, int32_t* launches, int n);
+
+/* Limits of hymoe_ffn_noalloc: its scratch is one fixed array per device. */
+#define HYMOE_NOALLOC_MAX_TOKENS 8
+#define HYMOE_NOALLOC_MAX_INTERMEDIATE 16384
+
+/* One SwiGLU expert FFN for up to 8 tokens that allocates no device memory.
+ * No counterpart in the reference: it exists for callers that cannot call cudaMalloc,
+ * e.g. code running inside CUDA stream capture (allocation calls are not permitted
+ * there), engines whose device memory belongs to another allocator or pool, or decode
+ * loops that must not allocate per step.  Needs no context.
+ *   y[t] = down( silu(gate_up[0:I] x[t]) * gate_up[I:2I] x[t] )   (src/rms_norm.cpp:39-91)
+ * gate_up [2I, H] and down [H, I] are standard GGUF tensors (F32/F16/Q4_0/Q8_0, one
+ * type) whose data, like x [n_tokens, H] and y [n_tokens, H] (F32), are DEVICE pointers
+ * owned by the caller, 16-byte aligned.  n_tokens <= HYMOE_NOALLOC_MAX_TOKENS,
+ * I <= HYMOE_NOALLOC_MAX_INTERMEDIATE; larger sizes are rejected with
+ * HYMOE_ERR_INVALID_ARG.  The intermediate activation lives in a 512 KiB static device
+ * array that every GPU loading the library holds until process exit.  The first call on
+ * a device looks up that array's device address (cudaGetSymbolAddress) with the device
+ * current; make that first call before any stream capture.  Asynchronous on `stream`
+ * (a cudaStream_t, NULL = legacy default stream).  All calls share the array: calls
+ * that overlap on the GPU (unordered streams) race and give wrong results. */
+hymoe_status hymoe_ffn_noalloc(const hymoe_tensor* gate_up, const hymoe_tensor* down,
+                               const float* x, float* y, uint32_t n_tokens, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,77 @@
+"""GPU test of hymoe_ffn_noalloc, the entry point for callers that cannot allocate device
+memory (code inside CUDA stream capture, engines whose device memory belongs to another
+allocator, decode loops that must not allocate per step).  It must give the same answer as
+the regular entry point.
+
+Comparison: a layer whose routed experts are all zero makes hymoe_forward return exactly
+the shared expert's SwiGLU FFN, which is what hymoe_ffn_noalloc computes from the same
+GGUF bytes.  Two calls in a row are checked, so a call that depends on what the previous
+call left in the shared static scratch array would be caught.  This file is collected
+last and builds everything it needs itself, so it passes alone in a fresh process too.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import hymoe
+import oracle as O
+from moe_cases import REL_L2_TOL, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _device_tensor(torch, raw: np.ndarray, wt: int, rows: int, cols: int):
+    d = torch.from_numpy(raw).cuda()
+    return d, hymoe.Tensor(d.data_ptr(), wt, (C.c_int64 * 2)(cols, rows), raw.nbytes)
+
+
+@pytest.mark.parametrize("wt", [O.Q4_0, O.Q8_0])
+def test_ffn_noalloc_matches_hymoe_forward(orc, wt):
+    torch = pytest.importorskip("torch")
+    H, I, E, K, T, seed = 512, 256, 16, 8, 6, 31
+    rw = orc.fill_normal(E * H, seed, O.stream_id(0, O.KIND_ROUTER), 0.02).reshape(E, H)
+    sgu = orc.synth_tensor(wt, 2 * I * H, seed, O.stream_id(0, O.KIND_GATE_UP, O.SHARED_INDEX), 0.02)
+    sdn = orc.synth_tensor(wt, H * I, seed, O.stream_id(0, O.KIND_DOWN, O.SHARED_INDEX), 0.02)
+    zgu = orc.quantize(wt, np.zeros(2 * I * H, np.float32))
+    zdn = orc.quantize(wt, np.zeros(H * I, np.float32))
+    m = hymoe.MoE(H, I, E, K, 1, 16)
+    m.load_layer(0, rw, sgu, sdn, [zgu] * E, [zdn] * E, wt)
+
+    L = hymoe.lib()
+    gu_d, tg = _device_tensor(torch, sgu, wt, 2 * I, H)
+    dn_d, td = _device_tensor(torch, sdn, wt, H, I)
+    for call in range(2):
+        x = O.synth_x(orc, seed + call, T, H)
+        want = m.forward_host(0, x)["out"]
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.full_like(xd, float("nan"))
+        torch.cuda.synchronize()
+        st = L.hymoe_ffn_noalloc(C.byref(tg), C.byref(td), xd.data_ptr(), yd.data_ptr(), T, None)
+        assert st == 0, L.hymoe_last_error(None)
+        torch.cuda.synchronize()
+        err = rel_l2(yd.cpu().numpy(), want)
+        assert err <= REL_L2_TOL, f"call {call}: rel L2 {err:.3e}"
+    m.close()
+
+
+def test_ffn_noalloc_rejects_sizes_beyond_its_scratch(orc):
+    torch = pytest.importorskip("torch")
+    L = hymoe.lib()
+    H, I, wt = 256, 128, O.Q8_0
+    gu_d, tg = _device_tensor(torch, orc.quantize(wt, np.zeros(2 * I * H, np.float32)), wt, 2 * I, H)
+    dn_d, td = _device_tensor(torch, orc.quantize(wt, np.zeros(H * I, np.float32)), wt, H, I)
+    x = torch.zeros(16, H, device="cuda")
+    y = torch.zeros(16, H, device="cuda")
+    st = L.hymoe_ffn_noalloc(C.byref(tg), C.byref(td), x.data_ptr(), y.data_ptr(),
+                             9, None)
+    assert st == 1 and b"HYMOE_NOALLOC_MAX_TOKENS" in L.hymoe_last_error(None)
+    big_i = 16384 + 32  # claims an intermediate size larger than the static array
+    tbig = hymoe.Tensor(gu_d.data_ptr(), wt, (C.c_int64 * 2)(H, 2 * big_i),
+                        2 * big_i * H // 32 * 34)
+    dbig = hymoe.Tensor(dn_d.data_ptr(), wt, (C.c_int64 * 2)(big_i, H), big_i * H // 32 * 34)
+    st = L.hymoe_ffn_noalloc(C.byref(tbig), C.byref(dbig), x.data_ptr(), y.data_ptr(), 1, None)
+    assert st == 1 and b"HYMOE_NOALLOC_MAX_INTERMEDIATE" in L.hymoe_last_error(None)
+    xh = np.zeros((1, H), np.float32)
+    st = L.hymoe_ffn_noalloc(C.byref(tg), C.byref(td), xh.ctypes.data, y.data_ptr(), 1, None)
+    assert st == 1 and b"device memory" in L.hymoe_last_error(None)
