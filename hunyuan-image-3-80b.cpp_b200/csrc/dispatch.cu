@@ -14,40 +14,50 @@ namespace hymoe {
 
 namespace {
 
-// One CTA of 1024 threads: (expert, part) = (tid / 16, tid % 16) owns a contiguous run of
-// router chunks for the column scan.
+// One CTA of 1024 threads.  (expert, part) = (tid / 16, tid % 16) owns a contiguous run of
+// at most kMaxChunksPerPart router chunks; its counts stay in registers between the column
+// sum and the base write-out.
+constexpr int kMaxChunksPerPart = 32;  // 16 parts x 32 chunks x 16 tokens = 8192 tokens
+
 __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
     __shared__ int part_sum[64][17];
-    __shared__ int gcnt[66], goff_s[66], ioff_gu[66], ioff_dn[66];
+    __shared__ int gcnt[66], goff_s[67], ioff_gu[67], ioff_dn[67], ntt_s[66];
     const int tid = threadIdx.x;
     const int e = tid >> 4, part = tid & 15;
     const int cpp = (a.n_chunks + 15) / 16;
     const int c_lo = min(a.n_chunks, part * cpp), c_hi = min(a.n_chunks, c_lo + cpp);
+    int cnt[kMaxChunksPerPart];
     int s = 0;
-    if (e < a.E)
-        for (int c = c_lo; c < c_hi; ++c) s += a.chunk_counts[c * a.E + e];
+#pragma unroll
+    for (int i = 0; i < kMaxChunksPerPart; ++i) {
+        const int c = c_lo + i;
+        cnt[i] = (e < a.E && c < c_hi) ? a.chunk_counts[c * a.E + e] : 0;
+        s += cnt[i];
+    }
     part_sum[e][part] = s;
     __syncthreads();
+    if (tid < 64) {
+        int tot = 0;
+        for (int p = 0; p < 16; ++p) tot += part_sum[tid][p];
+        gcnt[tid] = tid < a.E ? tot : 0;
+    }
+    __syncthreads();
     if (tid == 0) {
-        int off = 0;
-        for (int g = 0; g < a.E; ++g) {
-            int tot = 0;
-            for (int p = 0; p < 16; ++p) tot += part_sum[g][p];
-            goff_s[g] = off;
-            gcnt[g] = tot;
-            off += tot;
-        }
-        goff_s[a.E] = off;  // == T * K
-        gcnt[a.E] = a.T;
-        goff_s[a.E + 1] = off + a.T;
-        int ngu = 0, ndn = 0;
+        gcnt[a.E] = a.T;  // shared expert: every token
+        int off = 0, ngu = 0, ndn = 0;
         for (int g = 0; g <= a.E; ++g) {
+            goff_s[g] = off;
+            off += gcnt[g];
             const int ntt = a.gemv ? (gcnt[g] > 0) : (gcnt[g] + a.tile_n - 1) / a.tile_n;
+            ntt_s[g] = ntt;
             ioff_gu[g] = ngu;
             ioff_dn[g] = ndn;
             ngu += ntt * a.n_rb_gu;
             ndn += ntt * a.n_rb_dn;
         }
+        goff_s[a.E + 1] = off;
+        ioff_gu[a.E + 1] = ngu;
+        ioff_dn[a.E + 1] = ndn;
         a.n_items[0] = ngu;
         a.n_items[1] = ndn;
     }
@@ -56,26 +66,34 @@ __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
     if (e < a.E) {
         int base = goff_s[e];
         for (int p = 0; p < part; ++p) base += part_sum[e][p];
-        for (int c = c_lo; c < c_hi; ++c) {
-            a.chunk_base[c * a.E + e] = base;
-            base += a.chunk_counts[c * a.E + e];
+#pragma unroll
+        for (int i = 0; i < kMaxChunksPerPart; ++i) {
+            const int c = c_lo + i;
+            if (c < c_hi) a.chunk_base[c * a.E + e] = base;
+            base += cnt[i];
         }
     }
     // Work items, group-major then row block then token tile: consecutive items share a
-    // weight tile, so concurrently running CTAs hit it in L2.
-    for (int g = 0; g <= a.E; ++g) {
-        const int cnt = gcnt[g];
-        if (cnt == 0) continue;
-        const int tn = a.gemv ? cnt : a.tile_n;
-        const int ntt = a.gemv ? 1 : (cnt + tn - 1) / tn;
-        for (int which = 0; which < 2; ++which) {
-            const int nrb = which ? a.n_rb_dn : a.n_rb_gu;
-            int4* items = which ? a.items_dn : a.items_gu;
-            const int base = which ? ioff_dn[g] : ioff_gu[g];
-            for (int i = tid; i < nrb * ntt; i += blockDim.x) {
-                const int rb = i / ntt, tt = i % ntt;
-                items[base + i] = make_int4(g, rb, goff_s[g] + tt * tn, min(tn, cnt - tt * tn));
+    // weight tile, so concurrently running CTAs hit it in L2.  Flat loop over all items;
+    // the group of an item is found by binary search over the item offsets.
+    for (int which = 0; which < 2; ++which) {
+        const int* ioff = which ? ioff_dn : ioff_gu;
+        const int nrb = which ? a.n_rb_dn : a.n_rb_gu;
+        int4* items = which ? a.items_dn : a.items_gu;
+        const int total = ioff[a.E + 1];
+        for (int i = tid; i < total; i += blockDim.x) {
+            int lo = 0, hi = a.E;  // find g with ioff[g] <= i < ioff[g + 1]
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (ioff[mid] <= i) lo = mid;
+                else hi = mid - 1;
             }
+            const int g = lo, local = i - ioff[g];
+            const int ntt = ntt_s[g];
+            const int rb = local / ntt, tt = local - rb * ntt;
+            const int tn = a.gemv ? gcnt[g] : a.tile_n;
+            items[i] = make_int4(g, rb, goff_s[g] + tt * tn, min(tn, gcnt[g] - tt * tn));
+            (void)nrb;
         }
     }
 }

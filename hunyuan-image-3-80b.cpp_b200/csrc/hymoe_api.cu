@@ -271,10 +271,11 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     const uint32_t H = cfg->hidden_size, I = cfg->moe_intermediate_size, E = cfg->num_experts,
                    K = cfg->moe_topk;
     if (H == 0 || H % 128 || I == 0 || I % 64 || E < 1 || E > 64 || K < 1 || K > 8 || K > E ||
-        cfg->max_tokens == 0 || cfg->num_layers == 0 || cfg->ep_size < 1 ||
+        cfg->max_tokens == 0 || cfg->max_tokens > 8192 || cfg->num_layers == 0 || cfg->ep_size < 1 ||
         cfg->ep_rank < 0 || cfg->ep_rank >= cfg->ep_size || E % cfg->ep_size) {
         g_create_error =
-            "unsupported shape: need H%128==0, I%64==0, 1<=E<=64, 1<=K<=8, K<=E, E%ep_size==0";
+            "unsupported shape: need H%128==0, I%64==0, 1<=E<=64, 1<=K<=8, K<=E, E%ep_size==0, "
+            "1<=max_tokens<=8192";
         return HYMOE_ERR_INVALID_ARG;
     }
     if (cudaSetDevice(cfg->device) != cudaSuccess) {
@@ -529,9 +530,9 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     if (T > 0) {
         const int n_chunks = (T + kRouterTok - 1) / kRouterTok;
         c->phase_begin();
-        HY_CUDA(c, launch_router(dx, T, H, L.router, E, K, dbias, dlog, dprob, c->topk_w,
-                                 c->topk_idx, c->chunk_counts, st));
-        c->phase_end(HYMOE_PHASE_ROUTER);
+        HY_CUDA(c, launch_router(dx, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
+                                 c->topk_w, c->topk_idx, c->chunk_counts, st));
+        c->phase_end(HYMOE_PHASE_ROUTER, 2);
         const bool gemv = T <= kGemvMaxRows;
         PlanArgs pa{};
         pa.chunk_counts = c->chunk_counts;
