@@ -4,35 +4,44 @@
 // (src/rms_norm.cpp:55-63 gate_up, :81-89 down) with one persistent grouped GEMM per
 // projection over all experts (and the shared expert as one more group).
 //
-// Orientation ("swap AB"): the weight slab is the MMA's A operand (M = 128 weight rows)
-// and the group's token rows are B (N = 16..256 tokens, multiple of 16), so a group's last,
-// ragged token tile costs at most 15 padding columns instead of a padded 128-row M tile.
-//   D[128 weight rows, N tokens] (fp32, TMEM) += A[128, 64] (fp16, smem) * B[N, 64]^T (fp16)
-// per 64-wide K stage, as four K=16 tcgen05.mma.cta_group::1.kind::f16 instructions.
+// Orientation ("swap AB"): weight rows are the MMA's M dimension and a group's token rows
+// are N (16..256, multiple of 16), so a group's last, ragged token tile costs at most 15
+// padding columns instead of a padded 128-row M tile.
 //
-// Warp roles (448 threads, one CTA per SM, persistent over the work list):
-//   warp 0      TMA producer: 2-D tiled load of the B tile (fp16 token rows, 128B swizzle)
-//               and one 1-D bulk copy of the raw GGUF weight tile, both on full[s]
-//   warp 1      TMEM allocator + MMA issuer (one thread), commits to empty[s] / acc_full[b]
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (each warp its 32-lane quarter),
-//               transpose through shared memory, SwiGLU -> fp16 (gate_up) or fp32 (down)
-//   warps 6..13 dequantisers: GGUF Q4_0/Q8_0/F16 tile -> fp16 A tile in the canonical
-//               K-major 128B-swizzled layout, one (row, GGUF block) per thread
-// Pipelines: STAGES-deep ring (full/a_ready/empty mbarriers) for K stages; two TMEM
-// accumulators (2 x 256 columns) so the epilogue of one tile overlaps the next tile's MMAs.
-// Every mbarrier wait is bounded in time; on expiry the CTA records an error code and
-// unwinds (and still releases its tensor memory).
+// 2-SM pairs (tcgen05 cta_group::2, clusters of two CTAs on neighbouring SMs): a pair
+// tile is 256 weight rows x N tokens x 64 K per stage.  Each CTA dequantises its own
+// 128-row weight tile (A half) and TMA-loads its own N/2 token rows (B half); the leader
+// CTA issues
+//   D[256, N] (fp32, TMEM; each CTA holds its 128 rows) += A[256, 64] * B[N, 64]^T
+// as four K=16 tcgen05.mma.cta_group::2.kind::f16 instructions, and its commits arrive
+// on both CTAs' barriers.  Per SM this halves the token-operand traffic (L2 -> SMEM and
+// SMEM -> tensor core) of a 128 x N single-SM tile.
+//
+// Warp roles (448 threads per CTA, one CTA per SM, persistent over the work list):
+//   warp 0      producer: TMA 2-D load of this CTA's B half (128B swizzle) + one bulk copy
+//               of its raw GGUF weight tile, both completing on the local full[s]
+//   warp 1      TMEM allocation for the pair; in the leader, the MMA issuer
+//   warps 2..5  epilogue: tcgen05.ld of this CTA's accumulator rows, transpose through
+//               shared memory, SwiGLU -> fp16 (gate_up) or fp32 (down)
+//   warps 6..13 dequantisers: GGUF Q4_0/Q8_0/F16 tile -> fp16 A half in the canonical
+//               K-major 128B-swizzled layout, one (row, GGUF block) per thread; they then
+//               arrive on the leader's a_ready[s]
+// Barriers: full[s] (local), a_ready[s] (leader, 16 warp arrivals from both CTAs),
+// empty[s] / acc_full[b] (both CTAs, from the leader's multicast commits), acc_empty[b]
+// (leader, 8 epilogue warp arrivals).  Every wait is bounded in time; on expiry the CTA
+// records an error code, unwinds, lets in-flight copies land and releases tensor memory.
 #include "common.cuh"
 #include "kernels.h"
+
+#include <algorithm>
 
 namespace hymoe {
 
 namespace {
 
 constexpr int kThreads = 448;
-constexpr int kBRows = 256;                     // B tile rows (TMA box height)
-constexpr int kABytes = kTileRows * 128;        // 16 KB fp16 A stage
-constexpr int kBBytes = kBRows * 128;           // 32 KB fp16 B stage
+constexpr int kABytes = kTileRows * 128;        // 16 KB fp16 A half
+constexpr int kBBytes = kMaxBoxRows * 128;      // 16 KB fp16 B half (largest box)
 constexpr int kStageLd = 33;                    // epilogue staging row stride (floats)
 constexpr int kAccCols = 256;
 constexpr int kTmemCols = 512;
@@ -52,6 +61,17 @@ __device__ __forceinline__ bool named_bar_and(int id, int n, bool p) {
         : "r"(static_cast<uint32_t>(p)), "r"(id), "r"(n)
         : "memory");
     return r != 0;
+}
+
+// Pair tile width: the item's token count rounded up to the MMA's granularity (16).
+__device__ __forceinline__ int pair_n(int rows) {
+    const int n = (rows + 15) & ~15;
+    return n < 16 ? 16 : (n > 2 * kMaxBoxRows ? 2 * kMaxBoxRows : n);
+}
+
+// Smallest TMA box (rows) covering this CTA's half of the pair tile.
+__device__ __forceinline__ int box_index(int half) {
+    return half <= box_rows(0) ? 0 : half <= box_rows(1) ? 1 : 2;
 }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
@@ -131,7 +151,7 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 
 template <int WT, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
+    gemm_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs a) {
     constexpr int RAW = tile_bytes(WT);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -150,28 +170,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&aready[s], 8);
+            mbar_init(&aready[s], 16);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);
+            mbar_init(&acc_empty[b], 8);
         }
         mbar_init(mma_done, 1);
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_holder, kTmemCols);
-        tmem_relinquish();
+        tmem_alloc_2sm(tmem_holder, kTmemCols);
+        tmem_relinquish_2sm();
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     const int n_items = *a.n_items;
+    const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
     int* err = a.err;
 
     if (warp == 0) {
@@ -179,9 +203,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
-            for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+            for (int w = cid; ok && w < n_items; w += ncl) {
                 const int4 item = a.items[w];
-                const uint8_t* wt = a.wtiles[item.x] + static_cast<size_t>(item.y) * a.n_ks * RAW;
+                const int rb = 2 * item.y + static_cast<int>(rank);
+                const bool has_tile = rb < a.n_rb;
+                const int n = pair_n(item.w), half = n >> 1;
+                const int bi = box_index(half);
+                const uint32_t bbytes = static_cast<uint32_t>(box_rows(bi)) * 128u;
+                const uint8_t* wt = a.wtiles[item.x] + static_cast<size_t>(has_tile ? rb : 0) * a.n_ks * RAW;
                 for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
@@ -189,9 +218,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], kBBytes + RAW);
-                    tma_load_2d(sB + s * kBBytes, &tmap_b, &full[s], ks * kTileK, item.z);
-                    bulk_load(sRaw + s * RAW, wt + static_cast<size_t>(ks) * RAW, RAW, &full[s]);
+                    mbar_arrive_expect_tx(&full[s], bbytes + (has_tile ? RAW : 0));
+                    tma_load_2d(sB + s * kBBytes, &maps.b[bi], &full[s], ks * kTileK,
+                                item.z + static_cast<int>(rank) * half);
+                    if (has_tile)
+                        bulk_load(sRaw + s * RAW, wt + static_cast<size_t>(ks) * RAW, RAW, &full[s]);
                 }
             }
             // Let every copy this CTA issued land before shared memory goes away.
@@ -200,23 +231,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // ------------------------------------------------------------ MMA issuer (leader)
+        if (leader && lane == 0) {
             uint32_t it = 0, tc = 0;
             bool ok = true;
-            for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x, ++tc) {
+            for (int w = cid; ok && w < n_items; w += ncl, ++tc) {
                 const int4 item = a.items[w];
-                int n = ((item.w + 15) / 16) * 16;
-                n = n < 16 ? 16 : (n > kAccCols ? kAccCols : n);
-                const uint32_t idesc = idesc_f16_f32(kTileRows, n);
+                const uint32_t idesc = idesc_f16_f32(2 * kTileRows, pair_n(item.w));
                 const uint32_t ab = tc & 1, aph = (tc >> 1) & 1;
-                if (!mbar_wait(&acc_empty[ab], aph ^ 1, err, DEVERR_TIMEOUT_MMA)) break;
+                if (!mbar_wait_cluster(&acc_empty[ab], aph ^ 1, err, DEVERR_TIMEOUT_MMA)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + ab * kAccCols;
                 for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(&aready[s], ph, err, DEVERR_TIMEOUT_MMA)) {
+                    if (!mbar_wait_cluster(&aready[s], ph, err, DEVERR_TIMEOUT_MMA)) {
                         ok = false;
                         break;
                     }
@@ -225,16 +254,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t b_addr = smem_u32(sB + s * kBBytes);
 #pragma unroll
                     for (int kk = 0; kk < kTileK / 16; ++kk)
-                        mma_f16_ss(d_tmem, sw128_kmajor_desc(a_addr + kk * 32),
-                                   sw128_kmajor_desc(b_addr + kk * 32), idesc,
-                                   (ks | kk) != 0 ? 1u : 0u);
-                    mma_commit(&empty[s]);
+                        mma_f16_ss_2sm(d_tmem, sw128_kmajor_desc(a_addr + kk * 32),
+                                       sw128_kmajor_desc(b_addr + kk * 32), idesc,
+                                       (ks | kk) != 0 ? 1u : 0u);
+                    mma_commit_2sm_mc(&empty[s], 0x3);
                 }
                 if (!ok) break;
-                mma_commit(&acc_full[ab]);
+                mma_commit_2sm_mc(&acc_full[ab], 0x3);
             }
-            // All MMAs issued by this thread complete before tensor memory is released.
-            mma_commit(mma_done);
+            // All pair MMAs complete before either CTA releases tensor memory.
+            mma_commit_2sm(mma_done);
             mbar_drain(mma_done, 0);
         }
         __syncwarp();
@@ -243,10 +272,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;            // TMEM lane quarter this warp may access
         const int et = tid - 64;           // 0..127
         const int tok = et >> 2, seg = et & 3;
+        const uint32_t acc_empty_leader0 = mapa_shared(&acc_empty[0], 0);
+        const uint32_t acc_empty_leader1 = mapa_shared(&acc_empty[1], 0);
         uint32_t tc = 0;
-        for (int w = blockIdx.x; w < n_items; w += gridDim.x, ++tc) {
+        for (int w = cid; w < n_items; w += ncl, ++tc) {
             const int4 item = a.items[w];
-            const int rb = item.y, row0 = item.z, nrows = item.w;
+            const int rb = 2 * item.y + static_cast<int>(rank);
+            const bool has_tile = rb < a.n_rb;
+            const int row0 = item.z, nrows = item.w;
             const uint32_t ab = tc & 1, aph = (tc >> 1) & 1;
             const bool got = mbar_wait(&acc_full[ab], aph, err, DEVERR_TIMEOUT_EPILOGUE);
             if (!named_bar_and(1, 128, got)) break;
@@ -260,8 +293,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (ch == nchunks - 1) {
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[ab]);
+                    if (lane == 0) mbar_arrive_cluster(ab ? acc_empty_leader1 : acc_empty_leader0);
                 }
+                if (!has_tile) continue;  // warp-uniform; no staging barrier below either
                 float* srow = sStage + (q * 32 + lane) * kStageLd;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) srow[j] = __uint_as_float(v[j]);
@@ -307,7 +341,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int e = tid - 192;  // 0..255
         uint32_t it = 0;
         bool ok = true;
-        for (int w = blockIdx.x; ok && w < n_items; w += gridDim.x) {
+        for (int w = cid; ok && w < n_items; w += ncl) {
+            const int4 item = a.items[w];
+            const bool has_tile = 2 * item.y + static_cast<int>(rank) < a.n_rb;
             for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
                 const int s = it % STAGES;
                 const uint32_t ph = (it / STAGES) & 1;
@@ -315,19 +351,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                dequant_entry<WT>(sRaw + s * RAW, sA + s * kABytes, e);
+                if (has_tile) dequant_entry<WT>(sRaw + s * RAW, sA + s * kABytes, e);
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&aready[s]);
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(&aready[s], 0));
             }
         }
     }
 
     tc_fence_before();
     __syncthreads();
+    cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        tmem_dealloc_2sm(tmem, kTmemCols);
     }
 }
 
@@ -338,26 +375,49 @@ constexpr size_t smem_bytes() {
 }
 
 template <int WT, int STAGES>
-cudaError_t launch_typed(const CUtensorMap& tmap_b, const GemmArgs& a, int n_sms,
-                         cudaStream_t st) {
+cudaError_t launch_typed(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st) {
     constexpr size_t smem = smem_bytes<WT, STAGES>();
     static_assert(smem <= 232448, "shared memory budget");
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<WT, STAGES>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+    auto kern = gemm_tc_kernel<WT, STAGES>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    gemm_tc_kernel<WT, STAGES><<<n_sms, kThreads, smem, st>>>(tmap_b, a);
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // Persistent grid: as many pairs as can be resident at once.
+    static int max_clusters[16] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int& mc = max_clusters[WT & 15];
+    if (mc == 0) {
+        cfg.gridDim = dim3(2 * (n_sms / 2));
+        if (cudaOccupancyMaxActiveClusters(&mc, kern, &cfg) != cudaSuccess || mc <= 0) {
+            cudaGetLastError();
+            mc = n_sms / 2;
+        }
+    }
+    cfg.gridDim = dim3(2 * std::min(mc, n_sms / 2));
+    e = cudaLaunchKernelEx(&cfg, kern, maps, a);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_gemm_tc(const CUtensorMap& tmap_b, const GemmArgs& a, int n_sms,
-                           cudaStream_t st) {
+cudaError_t launch_gemm_tc(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st) {
     switch (a.wtype) {
-        case W_Q4_0: return launch_typed<W_Q4_0, 3>(tmap_b, a, n_sms, st);
-        case W_Q8_0: return launch_typed<W_Q8_0, 3>(tmap_b, a, n_sms, st);
-        case W_F16: return launch_typed<W_F16, 3>(tmap_b, a, n_sms, st);
+        case W_Q4_0: return launch_typed<W_Q4_0, 5>(maps, a, n_sms, st);
+        case W_Q8_0: return launch_typed<W_Q8_0, 5>(maps, a, n_sms, st);
+        case W_F16: return launch_typed<W_F16, 4>(maps, a, n_sms, st);
         default: return cudaErrorInvalidValue;
     }
 }

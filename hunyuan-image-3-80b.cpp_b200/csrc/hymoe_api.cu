@@ -103,7 +103,7 @@ struct hymoe_ctx {
     float* y = nullptr;
     uint8_t* tmp = nullptr;   // load / synthesis staging of one GGUF tensor
     size_t tmp_bytes = 0;
-    CUtensorMap tmap_xp{}, tmap_h{};
+    GemmMaps maps_xp{}, maps_h{};
 
     float* bias_dev = nullptr;
 
@@ -175,17 +175,26 @@ cudaError_t dalloc(T** p, size_t count) {
     return cudaMalloc(reinterpret_cast<void**>(p), sizeof(T) * (count ? count : 1));
 }
 
-hymoe_status make_tmap(hymoe_ctx* c, CUtensorMap* map, void* base, uint64_t K, uint64_t rows) {
+hymoe_status make_tmap(hymoe_ctx* c, CUtensorMap* map, void* base, uint64_t K, uint64_t rows,
+                       uint32_t box_rows_) {
     EncodeTiledFn enc = get_encode_fn();
     if (!enc) return c->fail(HYMOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[2] = {K, rows};
     cuuint64_t strides[1] = {K * 2};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), 256u};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), box_rows_};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return c->fail(HYMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", r);
+    return HYMOE_OK;
+}
+
+hymoe_status make_maps(hymoe_ctx* c, GemmMaps* m, void* base, uint64_t K, uint64_t rows) {
+    for (int i = 0; i < kNumBoxes; ++i) {
+        hymoe_status st = make_tmap(c, &m->b[i], base, K, rows, static_cast<uint32_t>(box_rows(i)));
+        if (st != HYMOE_OK) return st;
+    }
     return HYMOE_OK;
 }
 
@@ -346,8 +355,8 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     if (e != cudaSuccess) return bail(c->cuda_fail(e, "scratch allocation"));
     if (cudaMemset(c->err_word, 0, sizeof(int)) != cudaSuccess)
         return bail(c->fail(HYMOE_ERR_CUDA, "cudaMemset failed"));
-    hymoe_status st = make_tmap(c, &c->tmap_xp, c->xp, H, rows);
-    if (st == HYMOE_OK) st = make_tmap(c, &c->tmap_h, c->hbuf, I, rows);
+    hymoe_status st = make_maps(c, &c->maps_xp, c->xp, H, rows);
+    if (st == HYMOE_OK) st = make_maps(c, &c->maps_h, c->hbuf, I, rows);
     if (st != HYMOE_OK) return bail(st);
     if (cfg->ep_size > 1)
         return bail(c->fail(HYMOE_ERR_UNSUPPORTED, "expert parallelism not available"));
@@ -540,8 +549,10 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         pa.T = T;
         pa.E = E;
         pa.K = K;
-        pa.n_rb_gu = 2 * I / kTileRows;
-        pa.n_rb_dn = H / kTileRows;
+        // GEMV items cover one 128-row tile; tensor-core items a pair of tiles.
+        const int tiles_gu = 2 * I / kTileRows, tiles_dn = H / kTileRows;
+        pa.n_rb_gu = gemv ? tiles_gu : (tiles_gu + 1) / 2;
+        pa.n_rb_dn = gemv ? tiles_dn : (tiles_dn + 1) / 2;
         pa.tile_n = 256;
         pa.gemv = gemv ? 1 : 0;
         pa.goff = c->goff;
@@ -573,22 +584,24 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             ga.wtiles = L.d_gu_ptrs;
             ga.wtype = L.wtype;
             ga.n_ks = H / kTileK;
+            ga.n_rb = tiles_gu;
             ga.glu = 1;
             ga.out = c->hbuf;
             ga.out_ld = I;
             ga.err = c->err_word;
             c->phase_begin();
-            HY_CUDA(c, launch_gemm_tc(c->tmap_xp, ga, c->n_sms, st));
+            HY_CUDA(c, launch_gemm_tc(c->maps_xp, ga, c->n_sms, st));
             c->phase_end(HYMOE_PHASE_GATE_UP);
             ga.items = c->items_dn;
             ga.n_items = c->n_items + 1;
             ga.wtiles = L.d_dn_ptrs;
             ga.n_ks = I / kTileK;
+            ga.n_rb = tiles_dn;
             ga.glu = 0;
             ga.out = c->y;
             ga.out_ld = H;
             c->phase_begin();
-            HY_CUDA(c, launch_gemm_tc(c->tmap_h, ga, c->n_sms, st));
+            HY_CUDA(c, launch_gemm_tc(c->maps_h, ga, c->n_sms, st));
             c->phase_end(HYMOE_PHASE_DOWN);
         }
         c->phase_begin();

@@ -45,21 +45,26 @@ cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, co
                                   const int* chunk_base, const int* goff, int* slot_pos,
                                   __half* xp, cudaStream_t st);
 
-// ---- gemm_tc.cu (tcgen05 grouped GEMM)
+// ---- gemm_tc.cu (tcgen05 grouped GEMM, 2-SM pairs)
+constexpr int kNumBoxes = 3;
+constexpr int kMaxBoxRows = 128;
+__host__ __device__ constexpr int box_rows(int i) { return i == 0 ? 32 : i == 1 ? 64 : 128; }
+struct GemmMaps {
+    CUtensorMap b[kNumBoxes];  // token operand, fp16 [rows, K], box {64, box_rows(i)}, SW128
+};
 struct GemmArgs {
-    const int4* items;
+    const int4* items;             // {group, row-block pair, first row, rows}
     const int* n_items;
     const uint8_t* const* wtiles;  // [groups] tile base per group
     int wtype;
     int n_ks;                      // K / 64
+    int n_rb;                      // 128-row tiles per group matrix
     int glu;                       // 1: gate_up + SwiGLU epilogue -> fp16; 0: down -> fp32
     void* out;                     // [rows, out_ld]
     int out_ld;
     int* err;
 };
-// tmap_b: tensor map over the token operand (fp16 [rows, K], box {64, 256}, SW128).
-cudaError_t launch_gemm_tc(const CUtensorMap& tmap_b, const GemmArgs& a, int n_sms,
-                           cudaStream_t st);
+cudaError_t launch_gemm_tc(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st);
 
 // ---- gemv.cu (decode path, CUDA cores)
 constexpr int kGemvMaxRows = 8;

@@ -6,13 +6,15 @@
 //   top-K by probability, ties -> lower expert id   (:242-265, insertion with strict '<')
 //   w_k         = p_k / sum_{k'<K} p_k'              (:267-275)
 //
-// router_logits_kernel: every logit is one thread's sequential chain of separately rounded
-// multiplies and adds in h order - the operations the reference performs - so the logits
-// equal the reference's bit for bit.  A CTA covers 32 tokens x 8 experts (one chain per
-// thread); x and Wr are streamed through the read-only path with 16-byte loads (a row of x
-// is shared by the 8 expert threads of a token, a router row by the 32 token threads).
-// The chain's add latency bounds a call at roughly 4 x H cycles regardless of T.
-//
+// Logits: every logit is one thread's sequential chain of separately rounded multiplies
+// and adds in h order - the operations the reference performs - so the logits equal the
+// reference's bit for bit.  The add chain bounds a call at roughly 4 x H cycles; beyond
+// that the kernels are organised for operand reuse:
+//   router_logits_tiled_kernel (T > 8): CTA = 16 tokens x 32 experts, 128 threads with
+//     2 tokens x 2 experts (4 independent chains) each; x and Wr slabs of 128 columns
+//     stream through a 3-stage cp.async ring in shared memory.
+//   router_logits_decode_kernel (T <= 8): CTA = one expert; its router row and the T
+//     token rows are staged in shared memory once, then T threads run their chains.
 // router_topk_kernel: one warp per token (16 tokens = one dispatch chunk per CTA): softmax
 // with the sum taken in expert order, K rounds of warp-shuffle arg-max (ties to the lower
 // expert), renormalisation in rank order, and the chunk's per-expert token counts for the
@@ -26,44 +28,120 @@ namespace hymoe {
 
 namespace {
 
-constexpr int kLogitTok = 32;  // tokens per logits CTA
-constexpr int kLogitExp = 8;   // experts per logits CTA
 constexpr int kMaxE = 64;
+constexpr int kTT = 16;     // tokens per tiled CTA
+constexpr int kTE = 32;     // experts per tiled CTA
+constexpr int kKC = 128;    // columns per stage
+constexpr int kLd = kKC + 4;  // padded smem row (floats): 16-byte rows offset by 4 banks
+constexpr int kStages = 3;
+constexpr int kDecodeMaxT = 8;
 
-__global__ __launch_bounds__(256) void router_logits_kernel(const float* __restrict__ x, int T,
-                                                            int H, const float* __restrict__ Wr,
-                                                            int E, const float* __restrict__ bias,
-                                                            float* __restrict__ logits) {
-    const int t = blockIdx.x * kLogitTok + (threadIdx.x >> 3);
-    const int e = blockIdx.y * kLogitExp + (threadIdx.x & 7);
-    if (t >= T || e >= E) return;
-    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
-    const float4* wr = reinterpret_cast<const float4*>(Wr + static_cast<size_t>(e) * H);
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ float chain4(float acc, float4 a, float4 b) {
+    acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
+    acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
+    acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
+    return __fadd_rn(acc, __fmul_rn(a.w, b.w));
+}
+
+__global__ __launch_bounds__(128) void router_logits_tiled_kernel(
+    const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
+    const float* __restrict__ bias, float* __restrict__ logits) {
+    extern __shared__ float4 rsm4[];
+    float* sm = reinterpret_cast<float*>(rsm4);
+    float* Xs = sm;                          // [stages][kTT][kLd]
+    float* Ws = sm + kStages * kTT * kLd;    // [stages][kTE][kLd]
+    const int tid = threadIdx.x;
+    const int t0 = blockIdx.x * kTT, e0 = blockIdx.y * kTE;
+    const int tq = tid >> 4, eq = tid & 15;  // tokens 2tq, 2tq+1; experts eq, eq+16
+    const int nst = H / kKC;
+
+    auto load_stage = [&](int st, int ks) {
+        float* xs = Xs + st * kTT * kLd;
+        float* ws = Ws + st * kTE * kLd;
+        const int c0 = ks * kKC;
+        for (int i = tid; i < kTT * (kKC / 4); i += 128) {
+            const int r = i / (kKC / 4), c = (i % (kKC / 4)) * 4;
+            const int t = min(t0 + r, T - 1);
+            cp_async16(xs + r * kLd + c, x + static_cast<size_t>(t) * H + c0 + c);
+        }
+        for (int i = tid; i < kTE * (kKC / 4); i += 128) {
+            const int r = i / (kKC / 4), c = (i % (kKC / 4)) * 4;
+            const int e = min(e0 + r, E - 1);
+            cp_async16(ws + r * kLd + c, Wr + static_cast<size_t>(e) * H + c0 + c);
+        }
+    };
+
+    float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;  // [token][expert]
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) {
+        if (s < nst) load_stage(s, s);
+        cp_async_commit();
+    }
+    for (int ks = 0; ks < nst; ++ks) {
+        cp_async_wait<kStages - 2>();
+        __syncthreads();
+        if (ks + kStages - 1 < nst) load_stage((ks + kStages - 1) % kStages, ks + kStages - 1);
+        cp_async_commit();
+        const int st = ks % kStages;
+        const float* x0 = Xs + st * kTT * kLd + (2 * tq) * kLd;
+        const float* x1 = x0 + kLd;
+        const float* w0 = Ws + st * kTE * kLd + eq * kLd;
+        const float* w1 = w0 + 16 * kLd;
+#pragma unroll 8
+        for (int k = 0; k < kKC; k += 4) {
+            const float4 xa = *reinterpret_cast<const float4*>(x0 + k);
+            const float4 xb = *reinterpret_cast<const float4*>(x1 + k);
+            const float4 wa = *reinterpret_cast<const float4*>(w0 + k);
+            const float4 wb = *reinterpret_cast<const float4*>(w1 + k);
+            a00 = chain4(a00, xa, wa);
+            a01 = chain4(a01, xa, wb);
+            a10 = chain4(a10, xb, wa);
+            a11 = chain4(a11, xb, wb);
+        }
+    }
+    cp_async_wait<0>();
+    const int ta = t0 + 2 * tq, ea = e0 + eq;
+    const float b0 = (bias != nullptr && ea < E) ? bias[ea] : 0.f;
+    const float b1 = (bias != nullptr && ea + 16 < E) ? bias[ea + 16] : 0.f;
+    auto put = [&](int t, int e, float v, float b) {
+        if (t < T && e < E) logits[static_cast<size_t>(t) * E + e] = bias ? __fadd_rn(v, b) : v;
+    };
+    put(ta, ea, a00, b0);
+    put(ta, ea + 16, a01, b1);
+    put(ta + 1, ea, a10, b0);
+    put(ta + 1, ea + 16, a11, b1);
+}
+
+__global__ __launch_bounds__(128) void router_logits_decode_kernel(
+    const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
+    const float* __restrict__ bias, float* __restrict__ logits) {
+    extern __shared__ float4 rsm4[];
+    float* ws = reinterpret_cast<float*>(rsm4);  // [H]
+    float* xs = ws + H;                           // [T][H]
+    const int e = blockIdx.x;
+    for (int i = threadIdx.x * 4; i < H; i += 128 * 4)
+        cp_async16(ws + i, Wr + static_cast<size_t>(e) * H + i);
+    for (int i = threadIdx.x * 4; i < T * H; i += 128 * 4) cp_async16(xs + i, x + i);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    const int t = threadIdx.x;
+    if (t >= T) return;
+    const float* xr = xs + static_cast<size_t>(t) * H;
     float acc = 0.f;
-    const int n4 = H / 4;
-    int i = 0;
-    for (; i + 4 <= n4; i += 4) {
-        float4 xv[4], wv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            xv[u] = __ldg(xr + i + u);
-            wv[u] = __ldg(wr + i + u);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            acc = __fadd_rn(acc, __fmul_rn(xv[u].x, wv[u].x));
-            acc = __fadd_rn(acc, __fmul_rn(xv[u].y, wv[u].y));
-            acc = __fadd_rn(acc, __fmul_rn(xv[u].z, wv[u].z));
-            acc = __fadd_rn(acc, __fmul_rn(xv[u].w, wv[u].w));
-        }
-    }
-    for (; i < n4; ++i) {
-        const float4 xv = __ldg(xr + i), wv = __ldg(wr + i);
-        acc = __fadd_rn(acc, __fmul_rn(xv.x, wv.x));
-        acc = __fadd_rn(acc, __fmul_rn(xv.y, wv.y));
-        acc = __fadd_rn(acc, __fmul_rn(xv.z, wv.z));
-        acc = __fadd_rn(acc, __fmul_rn(xv.w, wv.w));
-    }
+#pragma unroll 8
+    for (int k = 0; k < H; k += 4)
+        acc = chain4(acc, *reinterpret_cast<const float4*>(xr + k), *reinterpret_cast<const float4*>(ws + k));
     if (bias != nullptr) acc = __fadd_rn(acc, bias[e]);
     logits[static_cast<size_t>(t) * E + e] = acc;
 }
@@ -149,9 +227,22 @@ __global__ __launch_bounds__(32 * kRouterTok) void router_topk_kernel(
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
                           int* topk_idx, int* chunk_counts, cudaStream_t st) {
-    dim3 g1((T + kLogitTok - 1) / kLogitTok, (E + kLogitExp - 1) / kLogitExp);
-    router_logits_kernel<<<g1, 256, 0, st>>>(x, T, H, Wr, E, bias, logits);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e;
+    if (T <= kDecodeMaxT) {
+        const size_t smem = sizeof(float) * static_cast<size_t>(H) * (1 + T);
+        e = cudaFuncSetAttribute(router_logits_decode_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        router_logits_decode_kernel<<<E, 128, smem, st>>>(x, T, H, Wr, E, bias, logits);
+    } else {
+        const size_t smem = sizeof(float) * kStages * (kTT + kTE) * kLd;
+        e = cudaFuncSetAttribute(router_logits_tiled_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        dim3 g((T + kTT - 1) / kTT, (E + kTE - 1) / kTE);
+        router_logits_tiled_kernel<<<g, 128, smem, st>>>(x, T, H, Wr, E, bias, logits);
+    }
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     router_topk_kernel<<<(T + kRouterTok - 1) / kRouterTok, 32 * kRouterTok, 0, st>>>(
         logits, T, E, K, probs, topk_w, topk_idx, chunk_counts);
