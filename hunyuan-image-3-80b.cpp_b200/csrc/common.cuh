@@ -241,9 +241,12 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
     return r;
 }
 
+// Arrive on a barrier of a (possibly remote) CTA of the cluster, given its shared::cluster
+// address.  Default (CTA-scope release) semantics, as CUTLASS's cluster barriers use: the
+// consumer of the data is the tensor core, ordered by fence.proxy.async on the writer and
+// tcgen05.fence::after_thread_sync on the issuer.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-                 : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {

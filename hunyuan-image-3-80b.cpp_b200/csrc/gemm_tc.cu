@@ -23,10 +23,11 @@
 //   warp 1      TMEM allocation for the pair; in the leader, the MMA issuer
 //   warps 2..5  epilogue: tcgen05.ld of this CTA's accumulator rows, transpose through
 //               shared memory, SwiGLU -> fp16 (gate_up) or fp32 (down)
-//   warps 6..13 dequantisers: GGUF Q4_0/Q8_0/F16 tile -> fp16 A half in the canonical
-//               K-major 128B-swizzled layout, one (row, GGUF block) per thread; they then
-//               arrive on the leader's a_ready[s]
-// Barriers: full[s] (local), a_ready[s] (leader, 16 warp arrivals from both CTAs),
+//   warps 6..13 dequantisers, two groups of four on alternate stages: GGUF Q4_0/Q8_0/F16
+//               tile -> fp16 A half in the canonical K-major 128B-swizzled layout, two
+//               (row, GGUF block) entries per thread; then arrive on the leader's a_ready[s]
+// Barriers: full[s] (local), a_ready[s] (leader, 8 warp arrivals: the 4 dequant warps of
+// the stage's group in each CTA),
 // empty[s] / acc_full[b] (both CTAs, from the leader's multicast commits), acc_empty[b]
 // (leader, 8 epilogue warp arrivals).  Every wait is bounded in time; on expiry the CTA
 // records an error code, unwinds, lets in-flight copies land and releases tensor memory.
@@ -34,6 +35,25 @@
 #include "kernels.h"
 
 #include <algorithm>
+
+// Optional pipeline trace (compiled only with -DHYMOE_TRACE): global-timer stamps of the
+// first kTraceIters stage iterations of cluster 0, read back by hymoe_trace_read.
+#ifdef HYMOE_TRACE
+constexpr int kTraceIters = 1024;
+__device__ unsigned long long g_trace[2][8][kTraceIters];
+#define HY_TRACE(ev, it)                                                   \
+    do {                                                                   \
+        if (blockIdx.x < 2 && (it) < static_cast<uint32_t>(kTraceIters))   \
+            g_trace[blockIdx.x][ev][it] = globaltimer_ns();                \
+    } while (0)
+extern "C" int hymoe_trace_read(void* host, size_t bytes) {
+    return static_cast<int>(cudaMemcpyFromSymbol(host, g_trace, bytes < sizeof(g_trace) ? bytes : sizeof(g_trace)));
+}
+#else
+#define HY_TRACE(ev, it) \
+    do {                 \
+    } while (0)
+#endif
 
 namespace hymoe {
 
@@ -175,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&aready[s], 16);
+            mbar_init(&aready[s], 8);  // 4 dequant warps of each CTA
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -218,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
+                    HY_TRACE(0, it);
                     mbar_arrive_expect_tx(&full[s], bbytes + (has_tile ? RAW : 0));
                     tma_load_2d(sB + s * kBBytes, &maps.b[bi], &full[s], ks * kTileK,
                                 item.z + static_cast<int>(rank) * half);
@@ -239,16 +260,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int4 item = a.items[w];
                 const uint32_t idesc = idesc_f16_f32(2 * kTileRows, pair_n(item.w));
                 const uint32_t ab = tc & 1, aph = (tc >> 1) & 1;
-                if (!mbar_wait_cluster(&acc_empty[ab], aph ^ 1, err, DEVERR_TIMEOUT_MMA)) break;
+                if (!mbar_wait(&acc_empty[ab], aph ^ 1, err, DEVERR_TIMEOUT_MMA)) break;
+                HY_TRACE(4, tc);
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + ab * kAccCols;
                 for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait_cluster(&aready[s], ph, err, DEVERR_TIMEOUT_MMA)) {
+                    if (!mbar_wait(&aready[s], ph, err, DEVERR_TIMEOUT_MMA)) {
                         ok = false;
                         break;
                     }
+                    HY_TRACE(3, it);
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + s * kABytes);
                     const uint32_t b_addr = smem_u32(sB + s * kBBytes);
@@ -282,6 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row0 = item.z, nrows = item.w;
             const uint32_t ab = tc & 1, aph = (tc >> 1) & 1;
             const bool got = mbar_wait(&acc_full[ab], aph, err, DEVERR_TIMEOUT_EPILOGUE);
+            if (et == 0) HY_TRACE(5, tc);
             if (!named_bar_and(1, 128, got)) break;
             tc_fence_after();
             const uint32_t d_tmem = tmem + ab * kAccCols + (static_cast<uint32_t>(q * 32) << 16);
@@ -338,22 +362,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ dequantisers
-        const int e = tid - 192;  // 0..255
+        // Two groups of four warps take alternate stages, so two stages are converted
+        // concurrently; each thread converts entries e and e + 128 of its stage.
+        const int dq = tid - 192;  // 0..255
+        const uint32_t grp = static_cast<uint32_t>(dq >> 7);
+        const int e = dq & 127;
         uint32_t it = 0;
         bool ok = true;
         for (int w = cid; ok && w < n_items; w += ncl) {
             const int4 item = a.items[w];
             const bool has_tile = 2 * item.y + static_cast<int>(rank) < a.n_rb;
             for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
+                if ((it & 1u) != grp) continue;
                 const int s = it % STAGES;
                 const uint32_t ph = (it / STAGES) & 1;
                 if (!mbar_wait(&full[s], ph, err, DEVERR_TIMEOUT_DEQUANT)) {
                     ok = false;
                     break;
                 }
-                if (has_tile) dequant_entry<WT>(sRaw + s * RAW, sA + s * kABytes, e);
+                if (e == 0) HY_TRACE(1, it);
+                if (has_tile) {
+                    dequant_entry<WT>(sRaw + s * RAW, sA + s * kABytes, e);
+                    dequant_entry<WT>(sRaw + s * RAW, sA + s * kABytes, e + 128);
+                }
                 fence_proxy_async_smem();
                 __syncwarp();
+                if (e == 0) HY_TRACE(2, it);
                 if (lane == 0) mbar_arrive_cluster(mapa_shared(&aready[s], 0));
             }
         }
