@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(&empty[s], ph ^ 1, err, DEVERR_TIMEOUT_PRODUCER)) {
+                    if (!mbar_wait_poll(&empty[s], ph ^ 1, err, DEVERR_TIMEOUT_PRODUCER)) {
                         ok = false;
                         break;
                     }
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(&aready[s], ph, err, DEVERR_TIMEOUT_MMA)) {
+                    if (!mbar_wait_poll(&aready[s], ph, err, DEVERR_TIMEOUT_MMA)) {
                         ok = false;
                         break;
                     }
