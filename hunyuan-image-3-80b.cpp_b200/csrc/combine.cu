@@ -11,33 +11,32 @@ namespace hymoe {
 
 namespace {
 
-__global__ __launch_bounds__(256) void combine_kernel(const float* __restrict__ y,
+__global__ __launch_bounds__(256) void combine_kernel(const float* __restrict__ y_shared,
+                                                      const float* __restrict__ y_routed,
                                                       const int* __restrict__ slot_pos,
                                                       const float* __restrict__ topk_w,
-                                                      const int* __restrict__ goff,
                                                       const float* resid, float* out, int T,
-                                                      int H, int E, int K) {
-    __shared__ int pos[9];
+                                                      int H, int K) {
+    __shared__ int pos[8];
     __shared__ float w[8];
     const int t = blockIdx.y;
     if (threadIdx.x < K) {
         pos[threadIdx.x] = slot_pos[t * K + threadIdx.x];
         w[threadIdx.x] = topk_w[t * K + threadIdx.x];
     }
-    if (threadIdx.x == 0) pos[8] = goff[E] + t;
     __syncthreads();
     const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (j >= H) return;
     float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < K; ++k) {
-        const float4 v = *reinterpret_cast<const float4*>(y + static_cast<size_t>(pos[k]) * H + j);
+        const float4 v = *reinterpret_cast<const float4*>(y_routed + static_cast<size_t>(pos[k]) * H + j);
         const float wk = w[k];
         r.x = __fadd_rn(r.x, __fmul_rn(wk, v.x));
         r.y = __fadd_rn(r.y, __fmul_rn(wk, v.y));
         r.z = __fadd_rn(r.z, __fmul_rn(wk, v.z));
         r.w = __fadd_rn(r.w, __fmul_rn(wk, v.w));
     }
-    const float4 s = *reinterpret_cast<const float4*>(y + static_cast<size_t>(pos[8]) * H + j);
+    const float4 s = *reinterpret_cast<const float4*>(y_shared + static_cast<size_t>(t) * H + j);
     float4 o = make_float4(__fadd_rn(s.x, r.x), __fadd_rn(s.y, r.y), __fadd_rn(s.z, r.z),
                            __fadd_rn(s.w, r.w));
     if (resid != nullptr) {
@@ -50,11 +49,11 @@ __global__ __launch_bounds__(256) void combine_kernel(const float* __restrict__ 
 
 }  // namespace
 
-cudaError_t launch_combine(const float* y, const int* slot_pos, const float* topk_w,
-                           const int* goff, const float* resid, float* out, int T, int H, int E,
+cudaError_t launch_combine(const float* y_shared, const float* y_routed, const int* slot_pos,
+                           const float* topk_w, const float* resid, float* out, int T, int H,
                            int K, cudaStream_t st) {
     dim3 grid((H / 4 + 255) / 256, T);
-    combine_kernel<<<grid, 256, 0, st>>>(y, slot_pos, topk_w, goff, resid, out, T, H, E, K);
+    combine_kernel<<<grid, 256, 0, st>>>(y_shared, y_routed, slot_pos, topk_w, resid, out, T, H, K);
     return cudaGetLastError();
 }
 

@@ -1,12 +1,19 @@
-// dispatch.cu — token permutation: per-expert prefix scan, GEMM work lists, and the
-// scatter/gather of token rows into expert-sorted order.
+// dispatch.cu — token permutation: per-expert prefix scan, GEMM segments and work lists,
+// and the scatter/gather of token rows into expert-sorted order.
 //
 // The reference has no explicit dispatch: its loop calls the FFN once per (token, rank)
 // pair (src/attention.cpp:285-299).  Here the T*K (token, rank) pairs are counting-sorted
-// by expert, stably by token, so every expert's tokens form one contiguous row range of
-// the fp16 activation matrix `xp` that the grouped GEMMs read.  Row ranges:
-//   group e < E : [goff[e], goff[e] + count_e)  routed expert e
-//   group E     : [T*K, T*K + T)                shared expert (every token, in order)
+// by global expert id, stably by token.  Expert e's pairs become rows
+// [goff[e], goff[e] + count_e) of the routed-row matrix; since expert-parallel ranks own
+// consecutive experts, that order is also destination-rank-major.
+//
+// GEMM input layout (one fp16 matrix per call):
+//   rows [0, T)        the shared expert's rows (every local token, in order)
+//   rows [T, T + R)    routed rows: on one GPU the sorted pairs themselves; with expert
+//                      parallelism the rows received from every rank (source-major,
+//                      then local expert)
+// A segment {weight group, first row, rows} names a run of rows that one expert's weights
+// multiply; work items tile segments into (row-block, up to tile_n rows) pieces.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -21,7 +28,7 @@ constexpr int kMaxChunksPerPart = 32;  // 16 parts x 32 chunks x 16 tokens = 819
 
 __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
     __shared__ int part_sum[64][17];
-    __shared__ int gcnt[66], goff_s[67], ioff_gu[67], ioff_dn[67], ntt_s[66];
+    __shared__ int gcnt_s[64], goff_s[65];
     const int tid = threadIdx.x;
     const int e = tid >> 4, part = tid & 15;
     const int cpp = (a.n_chunks + 15) / 16;
@@ -39,30 +46,20 @@ __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
     if (tid < 64) {
         int tot = 0;
         for (int p = 0; p < 16; ++p) tot += part_sum[tid][p];
-        gcnt[tid] = tid < a.E ? tot : 0;
+        gcnt_s[tid] = tid < a.E ? tot : 0;
     }
     __syncthreads();
     if (tid == 0) {
-        gcnt[a.E] = a.T;  // shared expert: every token
-        int off = 0, ngu = 0, ndn = 0;
-        for (int g = 0; g <= a.E; ++g) {
+        int off = 0;
+        for (int g = 0; g < a.E; ++g) {
             goff_s[g] = off;
-            off += gcnt[g];
-            const int ntt = a.gemv ? (gcnt[g] > 0) : (gcnt[g] + a.tile_n - 1) / a.tile_n;
-            ntt_s[g] = ntt;
-            ioff_gu[g] = ngu;
-            ioff_dn[g] = ndn;
-            ngu += ntt * a.n_rb_gu;
-            ndn += ntt * a.n_rb_dn;
+            off += gcnt_s[g];
         }
-        goff_s[a.E + 1] = off;
-        ioff_gu[a.E + 1] = ngu;
-        ioff_dn[a.E + 1] = ndn;
-        a.n_items[0] = ngu;
-        a.n_items[1] = ndn;
+        goff_s[a.E] = off;  // == T * K
     }
     __syncthreads();
-    for (int g = tid; g < a.E + 2; g += blockDim.x) a.goff[g] = goff_s[g];
+    for (int g = tid; g <= a.E; g += blockDim.x) a.goff[g] = goff_s[g];
+    for (int g = tid; g < a.E; g += blockDim.x) a.gcnt[g] = gcnt_s[g];
     if (e < a.E) {
         int base = goff_s[e];
         for (int p = 0; p < part; ++p) base += part_sum[e][p];
@@ -73,27 +70,62 @@ __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
             base += cnt[i];
         }
     }
-    // Work items, group-major then row block then token tile: consecutive items share a
-    // weight tile, so concurrently running CTAs hit it in L2.  Flat loop over all items;
-    // the group of an item is found by binary search over the item offsets.
+    // Single-GPU segments: shared expert first, then one segment per routed expert.
+    if (a.segs != nullptr) {
+        if (tid == 0) {
+            a.segs[0] = make_int4(a.E, 0, a.T, 0);
+            *a.n_segs = a.E + 1;
+        }
+        for (int g = tid; g < a.E; g += blockDim.x)
+            a.segs[1 + g] = make_int4(g, a.T + goff_s[g], gcnt_s[g], 0);
+    }
+}
+
+// Work items from segments: segment-major, then row block, then token tile, so
+// consecutive items share a weight tile and concurrently running CTAs hit it in L2.
+__global__ __launch_bounds__(1024) void items_kernel(ItemsArgs a) {
+    __shared__ int4 seg[kMaxSegs];
+    __shared__ int ntt_s[kMaxSegs], ioff_gu[kMaxSegs + 1], ioff_dn[kMaxSegs + 1];
+    const int tid = threadIdx.x;
+    const int ns = min(*a.n_segs, kMaxSegs);
+    for (int i = tid; i < ns; i += blockDim.x) {
+        const int4 sg = a.segs[i];
+        seg[i] = sg;
+        ntt_s[i] = sg.z <= 0 ? 0 : (a.gemv ? (sg.z + kGemvMaxRows - 1) / kGemvMaxRows
+                                          : (sg.z + a.tile_n - 1) / a.tile_n);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int ngu = 0, ndn = 0;
+        for (int i = 0; i < ns; ++i) {
+            ioff_gu[i] = ngu;
+            ioff_dn[i] = ndn;
+            ngu += ntt_s[i] * a.n_rb_gu;
+            ndn += ntt_s[i] * a.n_rb_dn;
+        }
+        ioff_gu[ns] = ngu;
+        ioff_dn[ns] = ndn;
+        a.n_items[0] = ngu;
+        a.n_items[1] = ndn;
+    }
+    __syncthreads();
+    const int tn = a.gemv ? kGemvMaxRows : a.tile_n;
     for (int which = 0; which < 2; ++which) {
         const int* ioff = which ? ioff_dn : ioff_gu;
-        const int nrb = which ? a.n_rb_dn : a.n_rb_gu;
         int4* items = which ? a.items_dn : a.items_gu;
-        const int total = ioff[a.E + 1];
+        const int total = ioff[ns];
         for (int i = tid; i < total; i += blockDim.x) {
-            int lo = 0, hi = a.E;  // find g with ioff[g] <= i < ioff[g + 1]
+            int lo = 0, hi = ns - 1;  // last segment with ioff <= i
             while (lo < hi) {
                 const int mid = (lo + hi + 1) >> 1;
                 if (ioff[mid] <= i) lo = mid;
                 else hi = mid - 1;
             }
-            const int g = lo, local = i - ioff[g];
-            const int ntt = ntt_s[g];
+            const int4 sg = seg[lo];
+            const int local = i - ioff[lo];
+            const int ntt = ntt_s[lo];
             const int rb = local / ntt, tt = local - rb * ntt;
-            const int tn = a.gemv ? gcnt[g] : a.tile_n;
-            items[i] = make_int4(g, rb, goff_s[g] + tt * tn, min(tn, gcnt[g] - tt * tn));
-            (void)nrb;
+            items[i] = make_int4(sg.x, rb, sg.y + tt * tn, min(tn, sg.z - tt * tn));
         }
     }
 }
@@ -104,10 +136,10 @@ __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
 // to fp16 once and written to its K routed rows and its shared-expert row.
 __global__ __launch_bounds__(256) void scatter_gather_kernel(
     const float* __restrict__ x, int T, int H, int E, int K, const int* __restrict__ topk_idx,
-    const int* __restrict__ chunk_base, const int* __restrict__ goff, int* __restrict__ slot_pos,
-    __half* __restrict__ xp) {
+    const int* __restrict__ chunk_base, int* __restrict__ slot_pos, __half* __restrict__ xp_routed,
+    __half* __restrict__ xp_shared) {
     __shared__ int sidx[kRouterTok][8];
-    __shared__ int spos[kRouterTok][9];
+    __shared__ int spos[kRouterTok][8];
     const int c = blockIdx.x, t0 = c * kRouterTok, tid = threadIdx.x;
     const int nt = min(kRouterTok, T - t0);
     if (tid < kRouterTok * 8) {
@@ -127,7 +159,6 @@ __global__ __launch_bounds__(256) void scatter_gather_kernel(
             slot_pos[(t0 + tt) * K + k] = pos;
         }
     }
-    if (tid < kRouterTok) spos[tid][8] = goff[E] + t0 + tid;
     __syncthreads();
     for (int tt = 0; tt < nt; ++tt) {
         const float* xr = x + static_cast<size_t>(t0 + tt) * H;
@@ -142,10 +173,27 @@ __global__ __launch_bounds__(256) void scatter_gather_kernel(
             v.z = *reinterpret_cast<const uint32_t*>(&h2);
             v.w = *reinterpret_cast<const uint32_t*>(&h3);
             for (int k = 0; k < K; ++k)
-                *reinterpret_cast<uint4*>(xp + static_cast<size_t>(spos[tt][k]) * H + j) = v;
-            *reinterpret_cast<uint4*>(xp + static_cast<size_t>(spos[tt][8]) * H + j) = v;
+                *reinterpret_cast<uint4*>(xp_routed + static_cast<size_t>(spos[tt][k]) * H + j) = v;
+            *reinterpret_cast<uint4*>(xp_shared + static_cast<size_t>(t0 + tt) * H + j) = v;
         }
     }
+}
+
+// Expert-parallel receive segments from the gathered count matrix C[N][E]: the shared
+// expert over the local rows first, then (source s, local expert le) runs in source-major
+// order starting at row T.  Single thread: at most E + 1 segments.
+__global__ void ep_segments_kernel(const int* __restrict__ C, int N, int rank, int el, int E,
+                                   int T, int4* __restrict__ segs, int* __restrict__ n_segs) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    segs[0] = make_int4(el, 0, T, 0);
+    int row = T, n = 1;
+    for (int s = 0; s < N; ++s)
+        for (int le = 0; le < el; ++le) {
+            const int cnt = C[s * E + rank * el + le];
+            segs[n++] = make_int4(le, row, cnt, 0);
+            row += cnt;
+        }
+    *n_segs = n;
 }
 
 }  // namespace
@@ -155,12 +203,23 @@ cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st) {
+    items_kernel<<<1, 1024, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
-                                  const int* chunk_base, const int* goff, int* slot_pos,
-                                  __half* xp, cudaStream_t st) {
+                                  const int* chunk_base, int* slot_pos, __half* xp_routed,
+                                  __half* xp_shared, cudaStream_t st) {
     const int blocks = (T + kRouterTok - 1) / kRouterTok;
-    scatter_gather_kernel<<<blocks, 256, 0, st>>>(x, T, H, E, K, topk_idx, chunk_base, goff,
-                                                  slot_pos, xp);
+    scatter_gather_kernel<<<blocks, 256, 0, st>>>(x, T, H, E, K, topk_idx, chunk_base, slot_pos,
+                                                  xp_routed, xp_shared);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_segments(const int* C, int N, int rank, int el, int E, int T, int4* segs,
+                               int* n_segs, cudaStream_t st) {
+    ep_segments_kernel<<<1, 32, 0, st>>>(C, N, rank, el, E, T, segs, n_segs);
     return cudaGetLastError();
 }
 

@@ -1,19 +1,29 @@
 // hymoe_api.cu — the C ABI (include/hymoe.h): context, device weight store, and the
-// per-call orchestration of the MoE block on one GPU.
+// per-call orchestration of the MoE block on one GPU or expert-parallel over several.
 //
 // Forward pipeline for one layer call (all on the context's stream):
 //   [H2D x, residual]        (HYMOE_HOST_PTRS only)
-//   router_kernel            logits / softmax / top-K / renorm + per-chunk expert counts
-//   plan_kernel              prefix scan -> group offsets, chunk bases, GEMM work lists
-//   scatter_gather_kernel    stable counting sort of (token, rank) pairs; fp16 rows -> xp
+//   router                   logits / softmax / top-K / renorm + per-chunk expert counts
+//   plan_kernel              per-expert counts, offsets and chunk bases of the pair sort
+//   scatter_gather_kernel    stable counting sort of (token, rank) pairs into fp16 rows;
+//                            shared-expert rows go to rows [0, T) of the GEMM input
+//   [expert parallel]        all-gather of per-expert counts, grouped ncclSend/ncclRecv
+//                            of routed rows to the ranks that own their experts
+//   items_kernel             GEMM work items from the row segments
 //   gate_up GEMM             tcgen05 grouped GEMM + SwiGLU epilogue -> h (fp16)
 //                            (grouped GEMV when n_tokens <= 8: decode regime)
-//   down GEMM                -> y (fp32), one row per (token, expert) pair + shared rows
+//   down GEMM                -> y (fp32)
+//   [expert parallel]        grouped ncclSend/ncclRecv of routed results back to sources
 //   combine_kernel           out = residual + shared + sum_k w_k y_k
 //   [D2H out, debug]         (HYMOE_HOST_PTRS only)
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cstdlib>
+#include <thread>
 
 #include <algorithm>
 #include <cstdarg>
@@ -106,6 +116,19 @@ struct hymoe_ctx {
     GemmMaps maps_xp{}, maps_h{};
 
     float* bias_dev = nullptr;
+    int4* segs = nullptr;
+    int* n_segs = nullptr;
+    int* gcnt = nullptr;
+
+    // expert parallelism
+    ncclComm_t comm = nullptr;
+    bool comm_broken = false;
+    __half* xp_send = nullptr;   // [T*K, H] routed rows in destination order
+    float* y_ret = nullptr;      // [T*K, H] routed results back from their ranks
+    int* C_dev = nullptr;        // [N][E] gathered per-expert counts
+    int* C_host = nullptr;       // pinned copy
+    cudaEvent_t ev_counts = nullptr;
+    double ep_timeout_s = 60.0;
 
     // per-phase profiling (hymoe_profile)
     bool prof = false;
@@ -161,6 +184,9 @@ struct hymoe_ctx {
                     "%s: %s", what, cudaGetErrorString(e));
     }
 };
+
+hymoe_status ep_poll(hymoe_ctx* c, const char* what);
+hymoe_status ep_wait_event(hymoe_ctx* c, cudaEvent_t ev, const char* what);
 
 #define HY_CUDA(ctx, call)                                          \
     do {                                                            \
@@ -255,6 +281,62 @@ hymoe_status load_matrix(hymoe_ctx* c, const hymoe_tensor* t, uint8_t* dst, int 
 
 }  // namespace
 
+namespace {
+
+double now_s() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+}  // namespace
+
+// Polls the non-blocking communicator until its pending operation is enqueued (or fails);
+// on the deadline the communicator is aborted and marked broken.
+hymoe_status ep_poll(hymoe_ctx* c, const char* what) {
+    const double t0 = now_s();
+    while (true) {
+        ncclResult_t st = ncclSuccess;
+        ncclResult_t r = ncclCommGetAsyncError(c->comm, &st);
+        if (r != ncclSuccess || (st != ncclSuccess && st != ncclInProgress)) {
+            c->comm_broken = true;
+            return c->fail(HYMOE_ERR_NCCL, "%s: %s", what,
+                           ncclGetErrorString(r != ncclSuccess ? r : st));
+        }
+        if (st == ncclSuccess) return HYMOE_OK;
+        if (now_s() - t0 > c->ep_timeout_s) {
+            c->comm_broken = true;
+            ncclCommAbort(c->comm);
+            c->comm = nullptr;
+            return c->fail(HYMOE_ERR_TIMEOUT, "%s: no progress within %.0f s", what, c->ep_timeout_s);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+// Waits for `ev` with a deadline while watching the communicator for asynchronous errors.
+hymoe_status ep_wait_event(hymoe_ctx* c, cudaEvent_t ev, const char* what) {
+    const double t0 = now_s();
+    while (true) {
+        const cudaError_t q = cudaEventQuery(ev);
+        if (q == cudaSuccess) return HYMOE_OK;
+        if (q != cudaErrorNotReady) return c->cuda_fail(q, what);
+        if (c->comm) {
+            ncclResult_t st = ncclSuccess;
+            ncclCommGetAsyncError(c->comm, &st);
+            if (st != ncclSuccess && st != ncclInProgress) {
+                c->comm_broken = true;
+                return c->fail(HYMOE_ERR_NCCL, "%s: %s", what, ncclGetErrorString(st));
+            }
+        }
+        if (now_s() - t0 > c->ep_timeout_s) {
+            c->comm_broken = true;
+            if (c->comm) ncclCommAbort(c->comm);
+            c->comm = nullptr;
+            return c->fail(HYMOE_ERR_TIMEOUT, "%s: no completion within %.0f s", what, c->ep_timeout_s);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
 // ============================================================================ C ABI
 
 extern "C" {
@@ -263,7 +345,9 @@ const char* hymoe_version(void) { return "hymoe 0.1 (sm_100a)"; }
 
 hymoe_status hymoe_nccl_unique_id(void* out128) {
     if (!out128) return HYMOE_ERR_INVALID_ARG;
-    return HYMOE_ERR_UNSUPPORTED;
+    static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id is 128 bytes");
+    return ncclGetUniqueId(static_cast<ncclUniqueId*>(out128)) == ncclSuccess ? HYMOE_OK
+                                                                              : HYMOE_ERR_NCCL;
 }
 
 const char* hymoe_last_error(const hymoe_ctx* ctx) {
@@ -322,11 +406,15 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     const size_t T = cfg->max_tokens;
     // Rows of the expert-sorted activation matrix: local pairs + shared rows, plus (for
     // expert parallelism) rows received from other ranks.
-    size_t rows = T * (K + 1);
+    const int N = cfg->ep_size, el = c->e_local;
+    // GEMM input rows: T shared rows, then routed rows (all local pairs on one GPU; with
+    // expert parallelism at most min(K, E/N) rows per token of each of the N ranks).
+    const size_t routed_cap = N == 1 ? T * K : static_cast<size_t>(N) * T * std::min<uint32_t>(K, el);
+    const size_t rows = T + routed_cap;
     c->rows_cap = rows;
     const size_t n_chunks = (T + kRouterTok - 1) / kRouterTok;
     const int n_rb = std::max<int>(2 * I / kTileRows, H / kTileRows);
-    c->max_items = n_rb * static_cast<int>(rows / 256 + c->groups + 2);
+    c->max_items = n_rb * static_cast<int>(rows / kGemvMaxRows + kMaxSegs + 1);
     cudaError_t e = cudaSuccess;
     auto A = [&](cudaError_t r) {
         if (e == cudaSuccess) e = r;
@@ -341,6 +429,9 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     A(dalloc(&c->chunk_counts, n_chunks * E));
     A(dalloc(&c->chunk_base, n_chunks * E));
     A(dalloc(&c->goff, E + 2));
+    A(dalloc(&c->gcnt, E));
+    A(dalloc(&c->segs, kMaxSegs));
+    A(dalloc(&c->n_segs, 1));
     A(dalloc(&c->bias_dev, E));
     A(dalloc(&c->slot_pos, T * K));
     A(dalloc(&c->n_items, 2));
@@ -350,6 +441,13 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     A(dalloc(&c->xp, rows * H));
     A(dalloc(&c->hbuf, rows * I));
     A(dalloc(&c->y, rows * H));
+    if (N > 1) {
+        A(dalloc(&c->xp_send, T * K * H));
+        A(dalloc(&c->y_ret, T * K * H));
+        A(dalloc(&c->C_dev, static_cast<size_t>(N) * E));
+        A(cudaMallocHost(reinterpret_cast<void**>(&c->C_host), sizeof(int) * N * E));
+        A(cudaEventCreateWithFlags(&c->ev_counts, cudaEventDisableTiming));
+    }
     c->tmp_bytes = static_cast<size_t>(2 * I) * H * 4;  // largest GGUF tensor (F32 gate_up)
     A(dalloc(&c->tmp, c->tmp_bytes));
     if (e != cudaSuccess) return bail(c->cuda_fail(e, "scratch allocation"));
@@ -358,8 +456,21 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     hymoe_status st = make_maps(c, &c->maps_xp, c->xp, H, rows);
     if (st == HYMOE_OK) st = make_maps(c, &c->maps_h, c->hbuf, I, rows);
     if (st != HYMOE_OK) return bail(st);
-    if (cfg->ep_size > 1)
-        return bail(c->fail(HYMOE_ERR_UNSUPPORTED, "expert parallelism not available"));
+    if (N > 1) {
+        if (!cfg->nccl_unique_id) return bail(c->fail(HYMOE_ERR_INVALID_ARG, "ep_size > 1 needs nccl_unique_id"));
+        if (const char* v = getenv("HYMOE_EP_TIMEOUT_S")) c->ep_timeout_s = atof(v);
+        // Non-blocking communicator: joining is polled against a deadline so that a rank
+        // that never arrives ends this call with an error instead of a hang.
+        ncclConfig_t ncfg = NCCL_CONFIG_INITIALIZER;
+        ncfg.blocking = 0;
+        ncclUniqueId id;
+        memcpy(&id, cfg->nccl_unique_id, sizeof(id));
+        ncclResult_t r = ncclCommInitRankConfig(&c->comm, N, id, cfg->ep_rank, &ncfg);
+        if (r != ncclSuccess && r != ncclInProgress)
+            return bail(c->fail(HYMOE_ERR_NCCL, "ncclCommInitRankConfig: %s", ncclGetErrorString(r)));
+        st = ep_poll(c, "joining the expert-parallel communicator");
+        if (st != HYMOE_OK) return bail(st);
+    }
     *out = c;
     return HYMOE_OK;
 }
@@ -389,6 +500,18 @@ void hymoe_destroy(hymoe_ctx* c) {
     cudaFree(c->hbuf);
     cudaFree(c->y);
     cudaFree(c->tmp);
+    if (c->comm) {
+        if (c->comm_broken) ncclCommAbort(c->comm);
+        else ncclCommDestroy(c->comm);
+    }
+    cudaFree(c->xp_send);
+    cudaFree(c->y_ret);
+    cudaFree(c->C_dev);
+    if (c->C_host) cudaFreeHost(c->C_host);
+    if (c->ev_counts) cudaEventDestroy(c->ev_counts);
+    cudaFree(c->gcnt);
+    cudaFree(c->segs);
+    cudaFree(c->n_segs);
     c->prof_clear();
     for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
@@ -404,6 +527,14 @@ hymoe_status hymoe_set_stream(hymoe_ctx* c, void* stream) {
 hymoe_status hymoe_synchronize(hymoe_ctx* c) {
     if (!c) return HYMOE_ERR_INVALID_ARG;
     HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    if (c->cfg.ep_size > 1 && c->comm) {
+        // Bounded: a peer that stopped taking part ends the wait with an error.
+        cudaEvent_t ev = c->take_event();
+        HY_CUDA(c, cudaEventRecord(ev, c->stream));
+        hymoe_status s2 = ep_wait_event(c, ev, "synchronize");
+        c->ev_pool.push_back(ev);
+        if (s2 != HYMOE_OK) return s2;
+    }
     HY_CUDA(c, cudaStreamSynchronize(c->stream));
     int word = 0;
     HY_CUDA(c, cudaMemcpy(&word, c->err_word, sizeof(int), cudaMemcpyDeviceToHost));
@@ -506,9 +637,13 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         return c->fail(HYMOE_ERR_INVALID_ARG, "n_tokens %u exceeds max_tokens %u", n_tokens,
                        c->cfg.max_tokens);
     if ((!x || !out) && n_tokens > 0) return c->fail(HYMOE_ERR_INVALID_ARG, "null x/out");
+    const bool ep = c->cfg.ep_size > 1;
+    if (ep && (c->comm_broken || !c->comm))
+        return c->fail(HYMOE_ERR_STATE, "expert-parallel communicator is unusable after an earlier failure");
     HY_CUDA(c, cudaSetDevice(c->cfg.device));
     const LayerStore& L = c->layers[layer];
     const int T = static_cast<int>(n_tokens), H = c->H, I = c->I, E = c->E, K = c->K;
+    const int N = c->cfg.ep_size, rank = c->cfg.ep_rank, el = c->e_local;
     const bool host = (flags & HYMOE_HOST_PTRS) != 0;
     cudaStream_t st = c->stream;
     const size_t xbytes = static_cast<size_t>(T) * H * sizeof(float);
@@ -535,77 +670,172 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         if (dlog) dlog = c->logits;
         if (dprob) dprob = c->probs;
     }
+    // A rank with no tokens still takes part in every collective of the exchange.
+    if (T == 0 && !ep) return host ? hymoe_synchronize(c) : HYMOE_OK;
 
+    bool gemv = T <= kGemvMaxRows;  // decode regime: every segment has at most 8 rows
+    const int tiles_gu = 2 * I / kTileRows, tiles_dn = H / kTileRows;
     if (T > 0) {
         const int n_chunks = (T + kRouterTok - 1) / kRouterTok;
         c->phase_begin();
         HY_CUDA(c, launch_router(dx, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
                                  c->topk_w, c->topk_idx, c->chunk_counts, st));
         c->phase_end(HYMOE_PHASE_ROUTER, 2);
-        const bool gemv = T <= kGemvMaxRows;
         PlanArgs pa{};
         pa.chunk_counts = c->chunk_counts;
         pa.n_chunks = n_chunks;
         pa.T = T;
         pa.E = E;
         pa.K = K;
-        // GEMV items cover one 128-row tile; tensor-core items a pair of tiles.
-        const int tiles_gu = 2 * I / kTileRows, tiles_dn = H / kTileRows;
-        pa.n_rb_gu = gemv ? tiles_gu : (tiles_gu + 1) / 2;
-        pa.n_rb_dn = gemv ? tiles_dn : (tiles_dn + 1) / 2;
-        pa.tile_n = 256;
-        pa.gemv = gemv ? 1 : 0;
         pa.goff = c->goff;
+        pa.gcnt = c->gcnt;
         pa.chunk_base = c->chunk_base;
-        pa.items_gu = c->items_gu;
-        pa.items_dn = c->items_dn;
-        pa.n_items = c->n_items;
+        pa.segs = ep ? nullptr : c->segs;
+        pa.n_segs = c->n_segs;
         c->phase_begin();
         HY_CUDA(c, launch_plan(pa, st));
         c->phase_end(HYMOE_PHASE_PLAN);
         c->phase_begin();
-        HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->goff,
-                                         c->slot_pos, c->xp, st));
+        HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
+                                         ep ? c->xp_send : c->xp + static_cast<size_t>(T) * H,
+                                         c->xp, st));
         c->phase_end(HYMOE_PHASE_DISPATCH);
-        if (gemv) {
-            const int active = std::min(E, T * K) + 1;
-            c->phase_begin();
-            HY_CUDA(c, launch_gemv(c->items_gu, c->n_items, pa.n_rb_gu * active, L.d_gu_ptrs,
-                                   L.wtype, H / kTileK, 1, c->xp, H, c->hbuf, I, st));
-            c->phase_end(HYMOE_PHASE_GATE_UP);
-            c->phase_begin();
-            HY_CUDA(c, launch_gemv(c->items_dn, c->n_items + 1, pa.n_rb_dn * active, L.d_dn_ptrs,
-                                   L.wtype, I / kTileK, 0, c->hbuf, I, c->y, H, st));
-            c->phase_end(HYMOE_PHASE_DOWN);
-        } else {
-            GemmArgs ga{};
-            ga.items = c->items_gu;
-            ga.n_items = c->n_items;
-            ga.wtiles = L.d_gu_ptrs;
-            ga.wtype = L.wtype;
-            ga.n_ks = H / kTileK;
-            ga.n_rb = tiles_gu;
-            ga.glu = 1;
-            ga.out = c->hbuf;
-            ga.out_ld = I;
-            ga.err = c->err_word;
-            c->phase_begin();
-            HY_CUDA(c, launch_gemm_tc(c->maps_xp, ga, c->n_sms, st));
-            c->phase_end(HYMOE_PHASE_GATE_UP);
-            ga.items = c->items_dn;
-            ga.n_items = c->n_items + 1;
-            ga.wtiles = L.d_dn_ptrs;
-            ga.n_ks = I / kTileK;
-            ga.n_rb = tiles_dn;
-            ga.glu = 0;
-            ga.out = c->y;
-            ga.out_ld = H;
-            c->phase_begin();
-            HY_CUDA(c, launch_gemm_tc(c->maps_h, ga, c->n_sms, st));
-            c->phase_end(HYMOE_PHASE_DOWN);
-        }
+    } else {
+        HY_CUDA(c, cudaMemsetAsync(c->gcnt, 0, sizeof(int) * E, st));
+    }
+
+    std::vector<size_t> send_cnt(N, 0), send_off(N, 0), recv_cnt(N, 0), recv_off(N, 0);
+    if (ep) {
+        // Count exchange: every rank learns how many rows each rank sends to each expert.
         c->phase_begin();
-        HY_CUDA(c, launch_combine(c->y, c->slot_pos, c->topk_w, c->goff, dres, dout, T, H, E, K, st));
+        ncclResult_t r = ncclAllGather(c->gcnt, c->C_dev, E, ncclInt32, c->comm, st);
+        if (r != ncclSuccess && r != ncclInProgress)
+            return c->fail(HYMOE_ERR_NCCL, "ncclAllGather(counts): %s", ncclGetErrorString(r));
+        hymoe_status s2 = ep_poll(c, "count exchange");
+        if (s2 != HYMOE_OK) return s2;
+        HY_CUDA(c, cudaMemcpyAsync(c->C_host, c->C_dev, sizeof(int) * N * E, cudaMemcpyDeviceToHost, st));
+        HY_CUDA(c, cudaEventRecord(c->ev_counts, st));
+        s2 = ep_wait_event(c, c->ev_counts, "count exchange");
+        if (s2 != HYMOE_OK) return s2;
+        size_t so = 0, ro = T, total_sent = 0;
+        for (int d = 0; d < N; ++d) {
+            size_t sc = 0, rc = 0;
+            for (int le = 0; le < el; ++le) {
+                sc += static_cast<size_t>(c->C_host[rank * E + d * el + le]);
+                rc += static_cast<size_t>(c->C_host[d * E + rank * el + le]);
+            }
+            send_cnt[d] = sc;
+            send_off[d] = so;
+            so += sc;
+            recv_cnt[d] = rc;
+            recv_off[d] = ro;
+            ro += rc;
+            total_sent += sc;
+        }
+        size_t max_rows = static_cast<size_t>(T);
+        for (int le = 0; le < el; ++le) {
+            size_t rows_le = 0;
+            for (int src = 0; src < N; ++src) rows_le += static_cast<size_t>(c->C_host[src * E + rank * el + le]);
+            max_rows = std::max(max_rows, rows_le);
+        }
+        gemv = max_rows <= static_cast<size_t>(kGemvMaxRows);
+        if (total_sent != static_cast<size_t>(T) * K)
+            return c->fail(HYMOE_ERR_STATE, "count exchange inconsistent: %zu rows for %d pairs", total_sent, T * K);
+        if (ro > c->rows_cap)
+            return c->fail(HYMOE_ERR_INVALID_ARG, "received %zu rows exceed capacity %zu (max_tokens differs across ranks?)",
+                           ro, c->rows_cap);
+        // Token rows to the ranks that own their experts (fp16, H per row).
+        ncclGroupStart();
+        for (int d = 0; d < N; ++d) {
+            if (send_cnt[d])
+                ncclSend(c->xp_send + send_off[d] * H, send_cnt[d] * H, ncclFloat16, d, c->comm, st);
+            if (recv_cnt[d])
+                ncclRecv(c->xp + recv_off[d] * H, recv_cnt[d] * H, ncclFloat16, d, c->comm, st);
+        }
+        r = ncclGroupEnd();
+        if (r != ncclSuccess && r != ncclInProgress)
+            return c->fail(HYMOE_ERR_NCCL, "token exchange: %s", ncclGetErrorString(r));
+        s2 = ep_poll(c, "token exchange");
+        if (s2 != HYMOE_OK) return s2;
+        HY_CUDA(c, launch_ep_segments(c->C_dev, N, rank, el, E, T, c->segs, c->n_segs, st));
+        c->phase_end(HYMOE_PHASE_EP_DISPATCH, 2);
+    }
+
+    ItemsArgs ia{};
+    ia.segs = c->segs;
+    ia.n_segs = c->n_segs;
+    ia.n_rb_gu = gemv ? tiles_gu : (tiles_gu + 1) / 2;  // GEMV: one tile; tensor core: tile pairs
+    ia.n_rb_dn = gemv ? tiles_dn : (tiles_dn + 1) / 2;
+    ia.tile_n = 256;
+    ia.gemv = gemv ? 1 : 0;
+    ia.items_gu = c->items_gu;
+    ia.items_dn = c->items_dn;
+    ia.n_items = c->n_items;
+    c->phase_begin();
+    HY_CUDA(c, launch_items(ia, st));
+    c->phase_end(HYMOE_PHASE_PLAN);
+    const size_t rows_in_use = ep ? recv_off[N - 1] + recv_cnt[N - 1] : static_cast<size_t>(T) * (K + 1);
+    if (gemv) {
+        const int max_it = static_cast<int>(std::min<size_t>(
+            c->max_items, static_cast<size_t>(tiles_gu) * ((rows_in_use + kGemvMaxRows - 1) / kGemvMaxRows + kMaxSegs)));
+        c->phase_begin();
+        HY_CUDA(c, launch_gemv(c->items_gu, c->n_items, max_it, L.d_gu_ptrs, L.wtype, H / kTileK, 1,
+                               c->xp, H, c->hbuf, I, st));
+        c->phase_end(HYMOE_PHASE_GATE_UP);
+        c->phase_begin();
+        HY_CUDA(c, launch_gemv(c->items_dn, c->n_items + 1, max_it, L.d_dn_ptrs, L.wtype, I / kTileK,
+                               0, c->hbuf, I, c->y, H, st));
+        c->phase_end(HYMOE_PHASE_DOWN);
+    } else {
+        GemmArgs ga{};
+        ga.items = c->items_gu;
+        ga.n_items = c->n_items;
+        ga.wtiles = L.d_gu_ptrs;
+        ga.wtype = L.wtype;
+        ga.n_ks = H / kTileK;
+        ga.n_rb = tiles_gu;
+        ga.glu = 1;
+        ga.out = c->hbuf;
+        ga.out_ld = I;
+        ga.err = c->err_word;
+        c->phase_begin();
+        HY_CUDA(c, launch_gemm_tc(c->maps_xp, ga, c->n_sms, st));
+        c->phase_end(HYMOE_PHASE_GATE_UP);
+        ga.items = c->items_dn;
+        ga.n_items = c->n_items + 1;
+        ga.wtiles = L.d_dn_ptrs;
+        ga.n_ks = I / kTileK;
+        ga.n_rb = tiles_dn;
+        ga.glu = 0;
+        ga.out = c->y;
+        ga.out_ld = H;
+        c->phase_begin();
+        HY_CUDA(c, launch_gemm_tc(c->maps_h, ga, c->n_sms, st));
+        c->phase_end(HYMOE_PHASE_DOWN);
+    }
+
+    const float* y_routed = c->y + static_cast<size_t>(T) * H;
+    if (ep) {
+        // Routed results back to the ranks their tokens came from (fp32, H per row).
+        c->phase_begin();
+        ncclGroupStart();
+        for (int d = 0; d < N; ++d) {
+            if (recv_cnt[d])
+                ncclSend(c->y + recv_off[d] * H, recv_cnt[d] * H, ncclFloat32, d, c->comm, st);
+            if (send_cnt[d])
+                ncclRecv(c->y_ret + send_off[d] * H, send_cnt[d] * H, ncclFloat32, d, c->comm, st);
+        }
+        ncclResult_t r = ncclGroupEnd();
+        if (r != ncclSuccess && r != ncclInProgress)
+            return c->fail(HYMOE_ERR_NCCL, "result exchange: %s", ncclGetErrorString(r));
+        hymoe_status s2 = ep_poll(c, "result exchange");
+        if (s2 != HYMOE_OK) return s2;
+        c->phase_end(HYMOE_PHASE_EP_COMBINE);
+        y_routed = c->y_ret;
+    }
+    if (T > 0) {
+        c->phase_begin();
+        HY_CUDA(c, launch_combine(c->y, y_routed, c->slot_pos, c->topk_w, dres, dout, T, H, K, st));
         c->phase_end(HYMOE_PHASE_COMBINE);
         if (dbg) {
             const cudaMemcpyKind kd = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;

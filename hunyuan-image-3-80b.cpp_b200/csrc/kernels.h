@@ -22,28 +22,41 @@ cudaError_t launch_synth_f32(float* dst, uint64_t n, uint64_t seed, uint64_t str
 
 // ---- router.cu
 constexpr int kRouterTok = 16;  // tokens per router CTA (= dispatch chunk)
+constexpr int kGemvMaxRows = 8; // token rows per GEMV work item
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
                           int* topk_idx, int* chunk_counts, cudaStream_t st);
 
 // ---- dispatch.cu
+constexpr int kMaxSegs = 80;  // >= E + 1 (E <= 64)
 struct PlanArgs {
     const int* chunk_counts;  // [n_chunks][E]
     int n_chunks, T, E, K;
-    int n_rb_gu, n_rb_dn;     // row blocks of gate_up / down matrices
-    int tile_n;               // token rows per GEMM work item (tensor-core path)
-    int gemv;                 // 1: one work item per (group, row block)
-    int* goff;                // [E + 2] group row offsets (group E = shared expert)
+    int* goff;                // [E + 1] routed-row offset of each expert (goff[E] = T*K)
+    int* gcnt;                // [E]     routed rows of each expert
     int* chunk_base;          // [n_chunks][E]
-    int4* items_gu;           // {group, row block, row start, rows}
-    int4* items_dn;
-    int* n_items;             // [2]: gate_up, down
+    int4* segs;               // single-GPU segments (NULL: expert-parallel mode)
+    int* n_segs;
 };
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
 
+struct ItemsArgs {
+    const int4* segs;         // {weight group, first row, rows, -}
+    const int* n_segs;
+    int n_rb_gu, n_rb_dn;     // row blocks per item for gate_up / down
+    int tile_n;               // token rows per tensor-core item
+    int gemv;                 // 1: items of at most kGemvMaxRows rows for the GEMV path
+    int4* items_gu;           // {group, row block, first row, rows}
+    int4* items_dn;
+    int* n_items;             // [2]: gate_up, down
+};
+cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st);
+
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
-                                  const int* chunk_base, const int* goff, int* slot_pos,
-                                  __half* xp, cudaStream_t st);
+                                  const int* chunk_base, int* slot_pos, __half* xp_routed,
+                                  __half* xp_shared, cudaStream_t st);
+cudaError_t launch_ep_segments(const int* C, int N, int rank, int el, int E, int T, int4* segs,
+                               int* n_segs, cudaStream_t st);
 
 // ---- gemm_tc.cu (tcgen05 grouped GEMM, 2-SM pairs)
 constexpr int kNumBoxes = 3;
@@ -67,14 +80,14 @@ struct GemmArgs {
 cudaError_t launch_gemm_tc(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st);
 
 // ---- gemv.cu (decode path, CUDA cores)
-constexpr int kGemvMaxRows = 8;
 cudaError_t launch_gemv(const int4* items, const int* n_items, int max_items,
                         const uint8_t* const* wtiles, int wtype, int n_ks, int glu,
                         const __half* act, int act_ld, void* out, int out_ld, cudaStream_t st);
 
 // ---- combine.cu
-cudaError_t launch_combine(const float* y, const int* slot_pos, const float* topk_w,
-                           const int* goff, const float* resid, float* out, int T, int H, int E,
+// out[t] = resid[t] + y_shared[t] + sum_k w[t,k] * y_routed[slot_pos[t,k]]
+cudaError_t launch_combine(const float* y_shared, const float* y_routed, const int* slot_pos,
+                           const float* topk_w, const float* resid, float* out, int T, int H,
                            int K, cudaStream_t st);
 
 }  // namespace hymoe

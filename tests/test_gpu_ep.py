@@ -1,0 +1,106 @@
+"""Expert-parallel GPU tests (2+ GPUs): one child process per GPU; rank r owns experts
+[r*E/N, (r+1)*E/N), receives the rows routed to them over NCCL and sends the results back.
+
+Every output row's arithmetic is independent of how rows are tiled, so the expert-parallel
+output must be bit-identical to the single-GPU forward of the same tokens; it is also
+checked against the oracle within the parity tolerance.  Skipped with fewer than 2 GPUs.
+"""
+import multiprocessing as mp
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from moe_cases import REL_L2_TOL, host_layer, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+H, I, E, K, SEED, WT = 512, 256, 64, 8, 41, O.Q4_0
+
+
+def _gpu_count() -> int:
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _layer(orc):
+    return host_layer(orc, SEED, 0, H, I, E, WT)
+
+
+def _ep_worker(rank, world, nccl_id, tokens, q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "oracle"), os.path.join(root, "hunyuan-image-3-80b.cpp_b200"),
+                    os.path.dirname(os.path.abspath(__file__))]
+    try:
+        import oracle as O2
+        import hymoe
+        orc = O2.Oracle()
+        lay = host_layer(orc, SEED, 0, H, I, E, WT)
+        el = E // world
+        mine = range(rank * el, (rank + 1) * el)
+        egu = [lay["egu"][e] if e in mine else None for e in range(E)]
+        edn = [lay["edn"][e] if e in mine else None for e in range(E)]
+        m = hymoe.MoE(H, I, E, K, 1, max(max(tokens), 16), device=rank, ep_rank=rank,
+                      ep_size=world, nccl_id=nccl_id)
+        m.load_layer(0, lay["router"], lay["sgu"], lay["sdn"], egu, edn, WT)
+        outs = []
+        for call, t in enumerate(tokens):
+            x = O2.synth_x(orc, SEED + 100 * call + rank, t, H)
+            bias = O2.zipf_bias(SEED + call, E)
+            outs.append(m.forward_host(0, x, bias=bias, debug=True))
+        m.close()
+        q.put((rank, "ok", outs))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, f"error: {e!r}", None))
+
+
+def _run_ep(world, tokens_per_rank):
+    import hymoe
+    nccl_id = hymoe.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, nccl_id, tokens_per_rank[r], q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        rank, status, outs = q.get(timeout=600)
+        assert status == "ok", f"rank {rank}: {status}"
+        res[rank] = outs
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return res
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("tokens", [[[200, 3], [150, 0]], [[64], [5]], [[300], [300]]])
+def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens):
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    world = 2
+    res = _run_ep(world, tokens)
+    import hymoe
+    lay = _layer(orc)
+    ncalls = len(tokens[0])
+    single = hymoe.MoE(H, I, E, K, 1, max(max(t) for t in tokens) + 16, device=0)
+    single.load_layer(0, lay["router"], lay["sgu"], lay["sdn"], lay["egu"], lay["edn"], WT)
+    for call in range(ncalls):
+        bias = O.zipf_bias(SEED + call, E)
+        for rank in range(world):
+            t = tokens[rank][call]
+            x = O.synth_x(orc, SEED + 100 * call + rank, t, H)
+            ep_out = res[rank][call]
+            ref = single.forward_host(0, x, bias=bias, debug=True)
+            assert np.array_equal(ep_out["idx"], ref["idx"])
+            assert np.array_equal(ep_out["out"], ref["out"]), f"rank {rank} call {call}"
+            if t:
+                o = orc.moe_forward(x, lay["router"], lay["sgu_f"], lay["sdn_f"], lay["egu_f"],
+                                    lay["edn_f"], K, I, bias=bias)
+                assert rel_l2(ep_out["out"], o["out"]) <= REL_L2_TOL
+    single.close()
