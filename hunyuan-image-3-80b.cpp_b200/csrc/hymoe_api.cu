@@ -741,9 +741,18 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         gemv = max_rows <= static_cast<size_t>(kGemvMaxRows);
         if (total_sent != static_cast<size_t>(T) * K)
             return c->fail(HYMOE_ERR_STATE, "count exchange inconsistent: %zu rows for %d pairs", total_sent, T * K);
-        if (ro > c->rows_cap)
-            return c->fail(HYMOE_ERR_INVALID_ARG, "received %zu rows exceed capacity %zu (max_tokens differs across ranks?)",
-                           ro, c->rows_cap);
+        // Every rank checks every rank's receive size (all hold the full count matrix), so
+        // either all ranks proceed to the exchange or all return this error.
+        for (int d = 0; d < N; ++d) {
+            size_t rd = 0, td = 0;
+            for (int src = 0; src < N; ++src)
+                for (int le = 0; le < el; ++le) rd += static_cast<size_t>(c->C_host[src * E + d * el + le]);
+            for (int e2 = 0; e2 < E; ++e2) td += static_cast<size_t>(c->C_host[d * E + e2]);
+            if (td / K + rd > c->rows_cap)
+                return c->fail(HYMOE_ERR_INVALID_ARG,
+                               "rank %d would receive %zu rows, above capacity %zu (max_tokens must be the "
+                               "same job-wide bound on every rank)", d, rd, c->rows_cap);
+        }
         // Token rows to the ranks that own their experts (fp16, H per row).
         ncclGroupStart();
         for (int d = 0; d < N; ++d) {

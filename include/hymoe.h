@@ -58,7 +58,8 @@ typedef struct {
     uint32_t num_experts;           /* E, 64 (num_experts, :21); 8..64                    */
     uint32_t moe_topk;              /* K, 8 (moe_topk, :22); 1..8                         */
     uint32_t num_layers;            /* layer slots this context holds                     */
-    uint32_t max_tokens;            /* largest n_tokens of one hymoe_forward (this rank), <= 8192 */
+    uint32_t max_tokens;            /* largest n_tokens of one hymoe_forward, <= 8192; with
+                                       expert parallelism the same job-wide bound on every rank */
     int32_t device;                 /* CUDA device ordinal                                */
     /* Expert parallelism: ep_size ranks each own num_experts/ep_size consecutive
      * experts.  ep_size == 1 runs everything locally.  For ep_size > 1,

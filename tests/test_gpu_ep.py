@@ -31,7 +31,7 @@ def _layer(orc):
     return host_layer(orc, SEED, 0, H, I, E, WT)
 
 
-def _ep_worker(rank, world, nccl_id, tokens, q):
+def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [os.path.join(root, "oracle"), os.path.join(root, "hunyuan-image-3-80b.cpp_b200"),
@@ -45,7 +45,7 @@ def _ep_worker(rank, world, nccl_id, tokens, q):
         mine = range(rank * el, (rank + 1) * el)
         egu = [lay["egu"][e] if e in mine else None for e in range(E)]
         edn = [lay["edn"][e] if e in mine else None for e in range(E)]
-        m = hymoe.MoE(H, I, E, K, 1, max(max(tokens), 16), device=rank, ep_rank=rank,
+        m = hymoe.MoE(H, I, E, K, 1, max_tokens, device=rank, ep_rank=rank,
                       ep_size=world, nccl_id=nccl_id)
         m.load_layer(0, lay["router"], lay["sgu"], lay["sdn"], egu, edn, WT)
         outs = []
@@ -64,7 +64,8 @@ def _run_ep(world, tokens_per_rank):
     nccl_id = hymoe.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_ep_worker, args=(r, world, nccl_id, tokens_per_rank[r], q))
+    max_tokens = max(16, max(max(t) for t in tokens_per_rank))  # job-wide bound
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, nccl_id, tokens_per_rank[r], max_tokens, q))
              for r in range(world)]
     for p in procs:
         p.start()
