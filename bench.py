@@ -18,8 +18,10 @@ generated on the device).  A step is one hymoe_forward over the 4096 tokens.
 
 --impl reference times the reference's CPU implementation with all host cores (token
 sharded over processes; the MoE is per-token independent) on the same workload.
-Under torchrun (N > 1) every rank runs an independent replica of the layer on its own
-4096 tokens (expert parallelism arrives with the EP runtime).
+Under torchrun (N > 1) the layer runs expert-parallel: rank r owns experts
+[r*64/N, (r+1)*64/N) (plus the router and the shared expert), processes its own 4096 tokens,
+and tokens/results move by NCCL all-to-all inside the timed step (weak scaling: per-GPU
+tokens fixed).  --bias zipf gives the skewed-load variant of the expert-parallel config.
 """
 from __future__ import annotations
 
@@ -103,7 +105,14 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     T = args.tokens
-    m = hymoe.MoE(H, I, E, K, 1, T, device=local_rank)
+    if world > 1:
+        # Expert parallelism: rank 0 makes the NCCL id, every rank owns E/world experts.
+        box = [hymoe.nccl_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(box, src=0)
+        m = hymoe.MoE(H, I, E, K, 1, T, device=local_rank, ep_rank=rank, ep_size=world,
+                      nccl_id=box[0])
+    else:
+        m = hymoe.MoE(H, I, E, K, 1, T, device=local_rank)
     m.synth_layer(0, hymoe.TYPE_Q4_0, args.seed, 0.02)
     # A dedicated stream: torch's default stream has handle 0, which the C ABI reads as
     # "the context's own stream".  Every torch op and event below runs on this stream.
@@ -112,7 +121,13 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     m.set_stream(stream.cuda_stream)
     g = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank)
     x = torch.randn(T, H, device=dev, generator=g, dtype=torch.float32)
-    bias = (torch.randn(E, device=dev, generator=g) * 0.5).contiguous()
+    if args.bias == "zipf":
+        sys.path.insert(0, ORACLE)
+        from oracle import zipf_bias  # the seeded Zipf(1.1) expert skew of the EP workload
+        bias = torch.from_numpy(zipf_bias(args.seed, E)).to(dev)
+    else:
+        gb = torch.Generator(device=dev).manual_seed(args.seed)
+        bias = (torch.randn(E, device=dev, generator=gb) * 0.5).contiguous()
     out = torch.empty_like(x)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
@@ -199,11 +214,11 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
         "data": "synthetic (seeded; random-init Q4_0 weights generated on device)",
-        "config": {"workload": "cfg3: one MoE block, Q4_0 experts, 4096 tokens/step/GPU, "
-                               "router bias ~N(0,0.5)",
+        "config": {"workload": f"cfg3/cfg4: one MoE block, Q4_0 experts, {T} tokens/step/GPU, "
+                               f"router bias {'Zipf(1.1) over a seeded expert permutation' if args.bias == 'zipf' else '~N(0,0.5)'}",
                    "model": "HunyuanImage-3.0 MoE block H=4096 I=3072 E=64+1 shared top-8",
                    "global_batch": T * world, "seq_len": T,
-                   "parallelism": "replicas" if world > 1 else "single",
+                   "parallelism": f"ep{world} (E/{world} experts per GPU, NCCL all-to-all)" if world > 1 else "single",
                    "l2": "flushed between steps (256 MiB write outside the timed events)"},
         "tflops_total": round(flop_total / (ms_per_step / 1e3) / 1e12, 1),
         "frac_of_peak_total": round(flop_total / (ms_per_step / 1e3) / 1e12 / pk["tf_sus"], 4),
@@ -218,7 +233,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                         "mean": float(counts.mean())},
     }
     m.close()
-    if args.decode and rank == 0:
+    if args.decode and world == 1:
         res["decode"] = run_decode(args, local_rank)
     return res
 
@@ -397,6 +412,7 @@ def main():
     ap.add_argument("--impl", default="hymoe", choices=["hymoe", "reference"])
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--bias", default="normal", choices=["normal", "zipf"])
     ap.add_argument("--no-cpu", dest="cpu", action="store_false")
     ap.add_argument("--no-decode", dest="decode", action="store_false")
     args = ap.parse_args()

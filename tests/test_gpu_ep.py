@@ -1,9 +1,10 @@
 """Expert-parallel GPU tests (2+ GPUs): one child process per GPU; rank r owns experts
 [r*E/N, (r+1)*E/N), receives the rows routed to them over NCCL and sends the results back.
 
-Every output row's arithmetic is independent of how rows are tiled, so the expert-parallel
-output must be bit-identical to the single-GPU forward of the same tokens; it is also
-checked against the oracle within the parity tolerance.  Skipped with fewer than 2 GPUs.
+Every output row's arithmetic is independent of how rows are tiled, so when both runs use
+the tensor-core path the expert-parallel output must be bit-identical to the single-GPU
+forward of the same tokens; it is also checked against the oracle within the parity
+tolerance.  Skipped with fewer than 2 GPUs.
 """
 import multiprocessing as mp
 import os
@@ -99,7 +100,13 @@ def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens):
             ep_out = res[rank][call]
             ref = single.forward_host(0, x, bias=bias, debug=True)
             assert np.array_equal(ep_out["idx"], ref["idx"])
-            assert np.array_equal(ep_out["out"], ref["out"]), f"rank {rank} call {call}"
+            # Same GEMM path on both sides (every call above the 8-token decode regime):
+            # identical bits.  Otherwise the decode GEMV and the tensor-core path differ in
+            # rounding, within the parity tolerance.
+            if all(tokens[r][call] > 8 for r in range(world)):
+                assert np.array_equal(ep_out["out"], ref["out"]), f"rank {rank} call {call}"
+            elif t:
+                assert rel_l2(ep_out["out"], ref["out"]) <= REL_L2_TOL
             if t:
                 o = orc.moe_forward(x, lay["router"], lay["sgu_f"], lay["sdn_f"], lay["egu_f"],
                                     lay["edn_f"], K, I, bias=bias)
