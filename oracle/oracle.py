@@ -53,7 +53,7 @@ def build(ref: bool | None = None) -> None:
     if ref is None:
         ref = os.path.isdir(os.path.join(refdir, "src"))
     if ref:
-        targets.append("ref")
+        targets += ["ref", "ref-gpu"]
     subprocess.run(["make", "-s", "-C", HERE, f"REF={refdir}", *targets], check=True)
 
 
