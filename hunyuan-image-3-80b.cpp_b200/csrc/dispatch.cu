@@ -21,6 +21,62 @@ namespace hymoe {
 
 namespace {
 
+// Work items from segments (executed by a whole 1024-thread CTA; `seg` in shared memory):
+// segment-major, then row block, then token tile, so consecutive items share a weight tile
+// and concurrently running CTAs hit it in L2.
+__device__ void build_items(const int4* seg, int ns, const ItemsArgs& a, int* ntt_s, int* ioff_gu,
+                            int* ioff_dn) {
+    const int tid = threadIdx.x;
+    for (int i = tid; i < ns; i += blockDim.x) {
+        const int cnt = seg[i].z;
+        ntt_s[i] = cnt <= 0 ? 0 : (a.gemv ? (cnt + kGemvMaxRows - 1) / kGemvMaxRows
+                                         : (cnt + a.tile_n - 1) / a.tile_n);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int ngu = 0, ndn = 0;
+        for (int i = 0; i < ns; ++i) {
+            ioff_gu[i] = ngu;
+            ioff_dn[i] = ndn;
+            ngu += ntt_s[i] * a.n_rb_gu;
+            ndn += ntt_s[i] * a.n_rb_dn;
+        }
+        ioff_gu[ns] = ngu;
+        ioff_dn[ns] = ndn;
+        a.n_items[0] = ngu;
+        a.n_items[1] = ndn;
+    }
+    __syncthreads();
+    const int tn = a.gemv ? kGemvMaxRows : a.tile_n;
+    for (int which = 0; which < 2; ++which) {
+        const int* ioff = which ? ioff_dn : ioff_gu;
+        int4* items = which ? a.items_dn : a.items_gu;
+        const int total = ioff[ns];
+        for (int i = tid; i < total; i += blockDim.x) {
+            int lo = 0, hi = ns - 1;  // last segment with ioff <= i
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (ioff[mid] <= i) lo = mid;
+                else hi = mid - 1;
+            }
+            const int4 sg = seg[lo];
+            const int local = i - ioff[lo];
+            const int ntt = ntt_s[lo];
+            const int rb = local / ntt, tt = local - rb * ntt;
+            items[i] = make_int4(sg.x, rb, sg.y + tt * tn, min(tn, sg.z - tt * tn));
+        }
+    }
+}
+
+__global__ __launch_bounds__(1024) void items_kernel(ItemsArgs a) {
+    __shared__ int4 seg[kMaxSegs];
+    __shared__ int ntt_s[kMaxSegs], ioff_gu[kMaxSegs + 1], ioff_dn[kMaxSegs + 1];
+    const int ns = min(*a.n_segs, kMaxSegs);
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) seg[i] = a.segs[i];
+    __syncthreads();
+    build_items(seg, ns, a, ntt_s, ioff_gu, ioff_dn);
+}
+
 // One CTA of 1024 threads.  (expert, part) = (tid / 16, tid % 16) owns a contiguous run of
 // at most kMaxChunksPerPart router chunks; its counts stay in registers between the column
 // sum and the base write-out.
@@ -70,63 +126,19 @@ __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
             base += cnt[i];
         }
     }
-    // Single-GPU segments: shared expert first, then one segment per routed expert.
+    // Single-GPU segments (shared expert first, then one segment per routed expert) and
+    // their work items, in this same launch.
     if (a.segs != nullptr) {
+        __shared__ int4 seg[kMaxSegs];
+        __shared__ int ntt_s[kMaxSegs], ioff_gu[kMaxSegs + 1], ioff_dn[kMaxSegs + 1];
         if (tid == 0) {
-            a.segs[0] = make_int4(a.E, 0, a.T, 0);
+            seg[0] = make_int4(a.E, 0, a.T, 0);
             *a.n_segs = a.E + 1;
         }
-        for (int g = tid; g < a.E; g += blockDim.x)
-            a.segs[1 + g] = make_int4(g, a.T + goff_s[g], gcnt_s[g], 0);
-    }
-}
-
-// Work items from segments: segment-major, then row block, then token tile, so
-// consecutive items share a weight tile and concurrently running CTAs hit it in L2.
-__global__ __launch_bounds__(1024) void items_kernel(ItemsArgs a) {
-    __shared__ int4 seg[kMaxSegs];
-    __shared__ int ntt_s[kMaxSegs], ioff_gu[kMaxSegs + 1], ioff_dn[kMaxSegs + 1];
-    const int tid = threadIdx.x;
-    const int ns = min(*a.n_segs, kMaxSegs);
-    for (int i = tid; i < ns; i += blockDim.x) {
-        const int4 sg = a.segs[i];
-        seg[i] = sg;
-        ntt_s[i] = sg.z <= 0 ? 0 : (a.gemv ? (sg.z + kGemvMaxRows - 1) / kGemvMaxRows
-                                          : (sg.z + a.tile_n - 1) / a.tile_n);
-    }
-    __syncthreads();
-    if (tid == 0) {
-        int ngu = 0, ndn = 0;
-        for (int i = 0; i < ns; ++i) {
-            ioff_gu[i] = ngu;
-            ioff_dn[i] = ndn;
-            ngu += ntt_s[i] * a.n_rb_gu;
-            ndn += ntt_s[i] * a.n_rb_dn;
-        }
-        ioff_gu[ns] = ngu;
-        ioff_dn[ns] = ndn;
-        a.n_items[0] = ngu;
-        a.n_items[1] = ndn;
-    }
-    __syncthreads();
-    const int tn = a.gemv ? kGemvMaxRows : a.tile_n;
-    for (int which = 0; which < 2; ++which) {
-        const int* ioff = which ? ioff_dn : ioff_gu;
-        int4* items = which ? a.items_dn : a.items_gu;
-        const int total = ioff[ns];
-        for (int i = tid; i < total; i += blockDim.x) {
-            int lo = 0, hi = ns - 1;  // last segment with ioff <= i
-            while (lo < hi) {
-                const int mid = (lo + hi + 1) >> 1;
-                if (ioff[mid] <= i) lo = mid;
-                else hi = mid - 1;
-            }
-            const int4 sg = seg[lo];
-            const int local = i - ioff[lo];
-            const int ntt = ntt_s[lo];
-            const int rb = local / ntt, tt = local - rb * ntt;
-            items[i] = make_int4(sg.x, rb, sg.y + tt * tn, min(tn, sg.z - tt * tn));
-        }
+        for (int g = tid; g < a.E; g += blockDim.x) seg[1 + g] = make_int4(g, a.T + goff_s[g], gcnt_s[g], 0);
+        __syncthreads();
+        for (int i = tid; i <= a.E; i += blockDim.x) a.segs[i] = seg[i];
+        build_items(seg, a.E + 1, a.items, ntt_s, ioff_gu, ioff_dn);
     }
 }
 

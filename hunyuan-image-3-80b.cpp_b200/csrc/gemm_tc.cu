@@ -161,13 +161,6 @@ __device__ __forceinline__ void dequant_entry<W_F16>(const uint8_t* raw, uint8_t
     for (int c = 0; c < 4; ++c) *reinterpret_cast<uint4*>(A + sw128_offset(r, 4 * b + c)) = src[c];
 }
 
-// Time-bounded wait that ignores the error word: used only to let copies already in
-// flight land before the CTA exits.
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-    const uint64_t t0 = globaltimer_ns();
-    while (!mbar_try_wait(bar, parity))
-        if (globaltimer_ns() - t0 > kWaitBudgetNs) return;
-}
 
 template <int WT, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)

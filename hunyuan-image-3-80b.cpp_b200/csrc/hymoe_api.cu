@@ -29,6 +29,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -89,6 +90,21 @@ namespace hymoe {
 void set_thread_error(const char* msg) { g_create_error = msg ? msg : ""; }
 }  // namespace hymoe
 
+struct GraphKey {
+    uint32_t layer, n_tokens;
+    const void* p[8];
+    GraphKey(uint32_t l, uint32_t n, const void* a, const void* b, const void* c, const void* d,
+             const void* e, const void* f, const void* g, const void* h)
+        : layer(l), n_tokens(n), p{a, b, c, d, e, f, g, h} {}
+    bool operator<(const GraphKey& o) const {
+        if (layer != o.layer) return layer < o.layer;
+        if (n_tokens != o.n_tokens) return n_tokens < o.n_tokens;
+        for (int i = 0; i < 8; ++i)
+            if (p[i] != o.p[i]) return p[i] < o.p[i];
+        return false;
+    }
+};
+
 struct hymoe_ctx {
     hymoe_config cfg{};
     std::string err;
@@ -129,6 +145,12 @@ struct hymoe_ctx {
     int* C_host = nullptr;       // pinned copy
     cudaEvent_t ev_counts = nullptr;
     double ep_timeout_s = 60.0;
+
+    std::map<GraphKey, cudaGraphExec_t> graphs;  // HYMOE_USE_GRAPH replays
+    void clear_graphs() {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        graphs.clear();
+    }
 
     // per-phase profiling (hymoe_profile)
     bool prof = false;
@@ -512,6 +534,7 @@ void hymoe_destroy(hymoe_ctx* c) {
     cudaFree(c->gcnt);
     cudaFree(c->segs);
     cudaFree(c->n_segs);
+    c->clear_graphs();
     c->prof_clear();
     for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
@@ -569,6 +592,7 @@ hymoe_status hymoe_load_layer(hymoe_ctx* c, uint32_t layer, const hymoe_tensor* 
                            "expert %d tensors: bad shape/size or type differs from the shared expert", ge);
     }
     const int wt = tile_type_for(gt);
+    c->clear_graphs();
     hymoe_status st = ensure_layer(c, layer, wt);
     if (st != HYMOE_OK) return st;
     LayerStore& L = c->layers[layer];
@@ -599,6 +623,7 @@ hymoe_status hymoe_synth_layer(hymoe_ctx* c, uint32_t layer, int32_t ggml_type, 
     HY_CUDA(c, cudaSetDevice(c->cfg.device));
     const int H = c->H, I = c->I, E = c->E;
     const int wt = tile_type_for(ggml_type);
+    c->clear_graphs();
     hymoe_status st = ensure_layer(c, layer, wt);
     if (st != HYMOE_OK) return st;
     LayerStore& L = c->layers[layer];
@@ -673,190 +698,228 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     // A rank with no tokens still takes part in every collective of the exchange.
     if (T == 0 && !ep) return host ? hymoe_synchronize(c) : HYMOE_OK;
 
-    bool gemv = T <= kGemvMaxRows;  // decode regime: every segment has at most 8 rows
-    const int tiles_gu = 2 * I / kTileRows, tiles_dn = H / kTileRows;
-    if (T > 0) {
-        const int n_chunks = (T + kRouterTok - 1) / kRouterTok;
-        c->phase_begin();
-        HY_CUDA(c, launch_router(dx, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
-                                 c->topk_w, c->topk_idx, c->chunk_counts, st));
-        c->phase_end(HYMOE_PHASE_ROUTER, 2);
-        PlanArgs pa{};
-        pa.chunk_counts = c->chunk_counts;
-        pa.n_chunks = n_chunks;
-        pa.T = T;
-        pa.E = E;
-        pa.K = K;
-        pa.goff = c->goff;
-        pa.gcnt = c->gcnt;
-        pa.chunk_base = c->chunk_base;
-        pa.segs = ep ? nullptr : c->segs;
-        pa.n_segs = c->n_segs;
-        c->phase_begin();
-        HY_CUDA(c, launch_plan(pa, st));
-        c->phase_end(HYMOE_PHASE_PLAN);
-        c->phase_begin();
-        HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
-                                         ep ? c->xp_send : c->xp + static_cast<size_t>(T) * H,
-                                         c->xp, st));
-        c->phase_end(HYMOE_PHASE_DISPATCH);
-    } else {
-        HY_CUDA(c, cudaMemsetAsync(c->gcnt, 0, sizeof(int) * E, st));
-    }
+    auto device_part = [&]() -> hymoe_status {
+        bool gemv = T <= kGemvMaxRows;  // decode regime: every segment has at most 8 rows
+        const int tiles_gu = 2 * I / kTileRows, tiles_dn = H / kTileRows;
+        auto items_args = [&](bool gv) {
+            ItemsArgs ia{};
+            ia.segs = c->segs;
+            ia.n_segs = c->n_segs;
+            ia.n_rb_gu = gv ? tiles_gu : (tiles_gu + 1) / 2;  // GEMV: one tile; tensor core: tile pairs
+            ia.n_rb_dn = gv ? tiles_dn : (tiles_dn + 1) / 2;
+            ia.tile_n = 256;
+            ia.gemv = gv ? 1 : 0;
+            ia.items_gu = c->items_gu;
+            ia.items_dn = c->items_dn;
+            ia.n_items = c->n_items;
+            return ia;
+        };
+        if (T > 0) {
+            const int n_chunks = (T + kRouterTok - 1) / kRouterTok;
+            c->phase_begin();
+            HY_CUDA(c, launch_router(dx, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
+                                     c->topk_w, c->topk_idx, c->chunk_counts, st));
+            c->phase_end(HYMOE_PHASE_ROUTER, 2);
+            PlanArgs pa{};
+            pa.chunk_counts = c->chunk_counts;
+            pa.n_chunks = n_chunks;
+            pa.T = T;
+            pa.E = E;
+            pa.K = K;
+            pa.goff = c->goff;
+            pa.gcnt = c->gcnt;
+            pa.chunk_base = c->chunk_base;
+            pa.segs = ep ? nullptr : c->segs;
+            pa.n_segs = c->n_segs;
+            pa.items = items_args(gemv);
+            c->phase_begin();
+            HY_CUDA(c, launch_plan(pa, st));
+            c->phase_end(HYMOE_PHASE_PLAN);
+            c->phase_begin();
+            HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
+                                             ep ? c->xp_send : c->xp + static_cast<size_t>(T) * H,
+                                             c->xp, st));
+            c->phase_end(HYMOE_PHASE_DISPATCH);
+        } else {
+            HY_CUDA(c, cudaMemsetAsync(c->gcnt, 0, sizeof(int) * E, st));
+        }
 
-    std::vector<size_t> send_cnt(N, 0), send_off(N, 0), recv_cnt(N, 0), recv_off(N, 0);
-    if (ep) {
-        // Count exchange: every rank learns how many rows each rank sends to each expert.
-        c->phase_begin();
-        ncclResult_t r = ncclAllGather(c->gcnt, c->C_dev, E, ncclInt32, c->comm, st);
-        if (r != ncclSuccess && r != ncclInProgress)
-            return c->fail(HYMOE_ERR_NCCL, "ncclAllGather(counts): %s", ncclGetErrorString(r));
-        hymoe_status s2 = ep_poll(c, "count exchange");
-        if (s2 != HYMOE_OK) return s2;
-        HY_CUDA(c, cudaMemcpyAsync(c->C_host, c->C_dev, sizeof(int) * N * E, cudaMemcpyDeviceToHost, st));
-        HY_CUDA(c, cudaEventRecord(c->ev_counts, st));
-        s2 = ep_wait_event(c, c->ev_counts, "count exchange");
-        if (s2 != HYMOE_OK) return s2;
-        size_t so = 0, ro = T, total_sent = 0;
-        for (int d = 0; d < N; ++d) {
-            size_t sc = 0, rc = 0;
-            for (int le = 0; le < el; ++le) {
-                sc += static_cast<size_t>(c->C_host[rank * E + d * el + le]);
-                rc += static_cast<size_t>(c->C_host[d * E + rank * el + le]);
+        std::vector<size_t> send_cnt(N, 0), send_off(N, 0), recv_cnt(N, 0), recv_off(N, 0);
+        if (ep) {
+            // Count exchange: every rank learns how many rows each rank sends to each expert.
+            c->phase_begin();
+            ncclResult_t r = ncclAllGather(c->gcnt, c->C_dev, E, ncclInt32, c->comm, st);
+            if (r != ncclSuccess && r != ncclInProgress)
+                return c->fail(HYMOE_ERR_NCCL, "ncclAllGather(counts): %s", ncclGetErrorString(r));
+            hymoe_status s2 = ep_poll(c, "count exchange");
+            if (s2 != HYMOE_OK) return s2;
+            HY_CUDA(c, cudaMemcpyAsync(c->C_host, c->C_dev, sizeof(int) * N * E, cudaMemcpyDeviceToHost, st));
+            HY_CUDA(c, cudaEventRecord(c->ev_counts, st));
+            s2 = ep_wait_event(c, c->ev_counts, "count exchange");
+            if (s2 != HYMOE_OK) return s2;
+            size_t so = 0, ro = T, total_sent = 0;
+            for (int d = 0; d < N; ++d) {
+                size_t sc = 0, rc = 0;
+                for (int le = 0; le < el; ++le) {
+                    sc += static_cast<size_t>(c->C_host[rank * E + d * el + le]);
+                    rc += static_cast<size_t>(c->C_host[d * E + rank * el + le]);
+                }
+                send_cnt[d] = sc;
+                send_off[d] = so;
+                so += sc;
+                recv_cnt[d] = rc;
+                recv_off[d] = ro;
+                ro += rc;
+                total_sent += sc;
             }
-            send_cnt[d] = sc;
-            send_off[d] = so;
-            so += sc;
-            recv_cnt[d] = rc;
-            recv_off[d] = ro;
-            ro += rc;
-            total_sent += sc;
+            size_t max_rows = static_cast<size_t>(T);
+            for (int le = 0; le < el; ++le) {
+                size_t rows_le = 0;
+                for (int src = 0; src < N; ++src) rows_le += static_cast<size_t>(c->C_host[src * E + rank * el + le]);
+                max_rows = std::max(max_rows, rows_le);
+            }
+            gemv = max_rows <= static_cast<size_t>(kGemvMaxRows);
+            if (total_sent != static_cast<size_t>(T) * K)
+                return c->fail(HYMOE_ERR_STATE, "count exchange inconsistent: %zu rows for %d pairs", total_sent, T * K);
+            // Every rank checks every rank's receive size (all hold the full count matrix), so
+            // either all ranks proceed to the exchange or all return this error.
+            for (int d = 0; d < N; ++d) {
+                size_t rd = 0, td = 0;
+                for (int src = 0; src < N; ++src)
+                    for (int le = 0; le < el; ++le) rd += static_cast<size_t>(c->C_host[src * E + d * el + le]);
+                for (int e2 = 0; e2 < E; ++e2) td += static_cast<size_t>(c->C_host[d * E + e2]);
+                if (td / K + rd > c->rows_cap)
+                    return c->fail(HYMOE_ERR_INVALID_ARG,
+                                   "rank %d would receive %zu rows, above capacity %zu (max_tokens must be the "
+                                   "same job-wide bound on every rank)", d, rd, c->rows_cap);
+            }
+            // Token rows to the ranks that own their experts (fp16, H per row).
+            ncclGroupStart();
+            for (int d = 0; d < N; ++d) {
+                if (send_cnt[d])
+                    ncclSend(c->xp_send + send_off[d] * H, send_cnt[d] * H, ncclFloat16, d, c->comm, st);
+                if (recv_cnt[d])
+                    ncclRecv(c->xp + recv_off[d] * H, recv_cnt[d] * H, ncclFloat16, d, c->comm, st);
+            }
+            r = ncclGroupEnd();
+            if (r != ncclSuccess && r != ncclInProgress)
+                return c->fail(HYMOE_ERR_NCCL, "token exchange: %s", ncclGetErrorString(r));
+            s2 = ep_poll(c, "token exchange");
+            if (s2 != HYMOE_OK) return s2;
+            HY_CUDA(c, launch_ep_segments(c->C_dev, N, rank, el, E, T, c->segs, c->n_segs, st));
+            c->phase_end(HYMOE_PHASE_EP_DISPATCH, 2);
         }
-        size_t max_rows = static_cast<size_t>(T);
-        for (int le = 0; le < el; ++le) {
-            size_t rows_le = 0;
-            for (int src = 0; src < N; ++src) rows_le += static_cast<size_t>(c->C_host[src * E + rank * el + le]);
-            max_rows = std::max(max_rows, rows_le);
-        }
-        gemv = max_rows <= static_cast<size_t>(kGemvMaxRows);
-        if (total_sent != static_cast<size_t>(T) * K)
-            return c->fail(HYMOE_ERR_STATE, "count exchange inconsistent: %zu rows for %d pairs", total_sent, T * K);
-        // Every rank checks every rank's receive size (all hold the full count matrix), so
-        // either all ranks proceed to the exchange or all return this error.
-        for (int d = 0; d < N; ++d) {
-            size_t rd = 0, td = 0;
-            for (int src = 0; src < N; ++src)
-                for (int le = 0; le < el; ++le) rd += static_cast<size_t>(c->C_host[src * E + d * el + le]);
-            for (int e2 = 0; e2 < E; ++e2) td += static_cast<size_t>(c->C_host[d * E + e2]);
-            if (td / K + rd > c->rows_cap)
-                return c->fail(HYMOE_ERR_INVALID_ARG,
-                               "rank %d would receive %zu rows, above capacity %zu (max_tokens must be the "
-                               "same job-wide bound on every rank)", d, rd, c->rows_cap);
-        }
-        // Token rows to the ranks that own their experts (fp16, H per row).
-        ncclGroupStart();
-        for (int d = 0; d < N; ++d) {
-            if (send_cnt[d])
-                ncclSend(c->xp_send + send_off[d] * H, send_cnt[d] * H, ncclFloat16, d, c->comm, st);
-            if (recv_cnt[d])
-                ncclRecv(c->xp + recv_off[d] * H, recv_cnt[d] * H, ncclFloat16, d, c->comm, st);
-        }
-        r = ncclGroupEnd();
-        if (r != ncclSuccess && r != ncclInProgress)
-            return c->fail(HYMOE_ERR_NCCL, "token exchange: %s", ncclGetErrorString(r));
-        s2 = ep_poll(c, "token exchange");
-        if (s2 != HYMOE_OK) return s2;
-        HY_CUDA(c, launch_ep_segments(c->C_dev, N, rank, el, E, T, c->segs, c->n_segs, st));
-        c->phase_end(HYMOE_PHASE_EP_DISPATCH, 2);
-    }
 
-    ItemsArgs ia{};
-    ia.segs = c->segs;
-    ia.n_segs = c->n_segs;
-    ia.n_rb_gu = gemv ? tiles_gu : (tiles_gu + 1) / 2;  // GEMV: one tile; tensor core: tile pairs
-    ia.n_rb_dn = gemv ? tiles_dn : (tiles_dn + 1) / 2;
-    ia.tile_n = 256;
-    ia.gemv = gemv ? 1 : 0;
-    ia.items_gu = c->items_gu;
-    ia.items_dn = c->items_dn;
-    ia.n_items = c->n_items;
-    c->phase_begin();
-    HY_CUDA(c, launch_items(ia, st));
-    c->phase_end(HYMOE_PHASE_PLAN);
-    const size_t rows_in_use = ep ? recv_off[N - 1] + recv_cnt[N - 1] : static_cast<size_t>(T) * (K + 1);
-    if (gemv) {
-        const int max_it = static_cast<int>(std::min<size_t>(
-            c->max_items, static_cast<size_t>(tiles_gu) * ((rows_in_use + kGemvMaxRows - 1) / kGemvMaxRows + kMaxSegs)));
-        c->phase_begin();
-        HY_CUDA(c, launch_gemv(c->items_gu, c->n_items, max_it, L.d_gu_ptrs, L.wtype, H / kTileK, 1,
-                               c->xp, H, c->hbuf, I, st));
-        c->phase_end(HYMOE_PHASE_GATE_UP);
-        c->phase_begin();
-        HY_CUDA(c, launch_gemv(c->items_dn, c->n_items + 1, max_it, L.d_dn_ptrs, L.wtype, I / kTileK,
-                               0, c->hbuf, I, c->y, H, st));
-        c->phase_end(HYMOE_PHASE_DOWN);
+        if (ep) {  // single GPU: the plan kernel built the work items already
+            c->phase_begin();
+            HY_CUDA(c, launch_items(items_args(gemv), st));
+            c->phase_end(HYMOE_PHASE_PLAN);
+        }
+        const size_t rows_in_use = ep ? recv_off[N - 1] + recv_cnt[N - 1] : static_cast<size_t>(T) * (K + 1);
+        if (gemv) {
+            const int max_it = static_cast<int>(std::min<size_t>(
+                c->max_items, static_cast<size_t>(tiles_gu) * ((rows_in_use + kGemvMaxRows - 1) / kGemvMaxRows + kMaxSegs)));
+            c->phase_begin();
+            HY_CUDA(c, launch_gemv(c->items_gu, c->n_items, max_it, L.d_gu_ptrs, L.wtype, H / kTileK, 1,
+                                   c->xp, H, c->hbuf, I, c->err_word, st));
+            c->phase_end(HYMOE_PHASE_GATE_UP);
+            c->phase_begin();
+            HY_CUDA(c, launch_gemv(c->items_dn, c->n_items + 1, max_it, L.d_dn_ptrs, L.wtype, I / kTileK,
+                                   0, c->hbuf, I, c->y, H, c->err_word, st));
+            c->phase_end(HYMOE_PHASE_DOWN);
+        } else {
+            GemmArgs ga{};
+            ga.items = c->items_gu;
+            ga.n_items = c->n_items;
+            ga.wtiles = L.d_gu_ptrs;
+            ga.wtype = L.wtype;
+            ga.n_ks = H / kTileK;
+            ga.n_rb = tiles_gu;
+            ga.glu = 1;
+            ga.out = c->hbuf;
+            ga.out_ld = I;
+            ga.err = c->err_word;
+            c->phase_begin();
+            HY_CUDA(c, launch_gemm_tc(c->maps_xp, ga, c->n_sms, st));
+            c->phase_end(HYMOE_PHASE_GATE_UP);
+            ga.items = c->items_dn;
+            ga.n_items = c->n_items + 1;
+            ga.wtiles = L.d_dn_ptrs;
+            ga.n_ks = I / kTileK;
+            ga.n_rb = tiles_dn;
+            ga.glu = 0;
+            ga.out = c->y;
+            ga.out_ld = H;
+            c->phase_begin();
+            HY_CUDA(c, launch_gemm_tc(c->maps_h, ga, c->n_sms, st));
+            c->phase_end(HYMOE_PHASE_DOWN);
+        }
+
+        const float* y_routed = c->y + static_cast<size_t>(T) * H;
+        if (ep) {
+            // Routed results back to the ranks their tokens came from (fp32, H per row).
+            c->phase_begin();
+            ncclGroupStart();
+            for (int d = 0; d < N; ++d) {
+                if (recv_cnt[d])
+                    ncclSend(c->y + recv_off[d] * H, recv_cnt[d] * H, ncclFloat32, d, c->comm, st);
+                if (send_cnt[d])
+                    ncclRecv(c->y_ret + send_off[d] * H, send_cnt[d] * H, ncclFloat32, d, c->comm, st);
+            }
+            ncclResult_t r = ncclGroupEnd();
+            if (r != ncclSuccess && r != ncclInProgress)
+                return c->fail(HYMOE_ERR_NCCL, "result exchange: %s", ncclGetErrorString(r));
+            hymoe_status s2 = ep_poll(c, "result exchange");
+            if (s2 != HYMOE_OK) return s2;
+            c->phase_end(HYMOE_PHASE_EP_COMBINE);
+            y_routed = c->y_ret;
+        }
+        if (T > 0) {
+            c->phase_begin();
+            HY_CUDA(c, launch_combine(c->y, y_routed, c->slot_pos, c->topk_w, dres, dout, T, H, K, st));
+            c->phase_end(HYMOE_PHASE_COMBINE);
+            if (dbg) {
+                const cudaMemcpyKind kd = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+                if (dbg->topk_weights)
+                    HY_CUDA(c, cudaMemcpyAsync(dbg->topk_weights, c->topk_w, sizeof(float) * T * K, kd, st));
+                if (dbg->topk_indices)
+                    HY_CUDA(c, cudaMemcpyAsync(dbg->topk_indices, c->topk_idx, sizeof(int) * T * K, kd, st));
+                if (host && dlog)
+                    HY_CUDA(c, cudaMemcpyAsync(dbg->router_logits, dlog, sizeof(float) * T * E, kd, st));
+                if (host && dprob)
+                    HY_CUDA(c, cudaMemcpyAsync(dbg->router_probs, dprob, sizeof(float) * T * E, kd, st));
+            }
+        }
+        return HYMOE_OK;
+    };
+
+    const bool graph = (flags & HYMOE_USE_GRAPH) && !ep && !host && !c->prof && T > 0;
+    if (!graph) {
+        hymoe_status s2 = device_part();
+        if (s2 != HYMOE_OK) return s2;
     } else {
-        GemmArgs ga{};
-        ga.items = c->items_gu;
-        ga.n_items = c->n_items;
-        ga.wtiles = L.d_gu_ptrs;
-        ga.wtype = L.wtype;
-        ga.n_ks = H / kTileK;
-        ga.n_rb = tiles_gu;
-        ga.glu = 1;
-        ga.out = c->hbuf;
-        ga.out_ld = I;
-        ga.err = c->err_word;
-        c->phase_begin();
-        HY_CUDA(c, launch_gemm_tc(c->maps_xp, ga, c->n_sms, st));
-        c->phase_end(HYMOE_PHASE_GATE_UP);
-        ga.items = c->items_dn;
-        ga.n_items = c->n_items + 1;
-        ga.wtiles = L.d_dn_ptrs;
-        ga.n_ks = I / kTileK;
-        ga.n_rb = tiles_dn;
-        ga.glu = 0;
-        ga.out = c->y;
-        ga.out_ld = H;
-        c->phase_begin();
-        HY_CUDA(c, launch_gemm_tc(c->maps_h, ga, c->n_sms, st));
-        c->phase_end(HYMOE_PHASE_DOWN);
-    }
-
-    const float* y_routed = c->y + static_cast<size_t>(T) * H;
-    if (ep) {
-        // Routed results back to the ranks their tokens came from (fp32, H per row).
-        c->phase_begin();
-        ncclGroupStart();
-        for (int d = 0; d < N; ++d) {
-            if (recv_cnt[d])
-                ncclSend(c->y + recv_off[d] * H, recv_cnt[d] * H, ncclFloat32, d, c->comm, st);
-            if (send_cnt[d])
-                ncclRecv(c->y_ret + send_off[d] * H, send_cnt[d] * H, ncclFloat32, d, c->comm, st);
+        // One captured graph per (layer, token count, buffers); replayed while they repeat.
+        const GraphKey key{layer, n_tokens, dx, dres, dout, dbias, dlog, dprob,
+                           dbg ? dbg->topk_weights : nullptr, dbg ? dbg->topk_indices : nullptr};
+        auto hit = c->graphs.find(key);
+        if (hit == c->graphs.end()) {
+            if (c->graphs.size() >= 64) c->clear_graphs();
+            HY_CUDA(c, cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            hymoe_status s2 = device_part();
+            cudaGraph_t g = nullptr;
+            const cudaError_t ec = cudaStreamEndCapture(st, &g);
+            if (s2 != HYMOE_OK) {
+                if (g) cudaGraphDestroy(g);
+                return s2;
+            }
+            if (ec != cudaSuccess) return c->cuda_fail(ec, "cudaStreamEndCapture");
+            cudaGraphExec_t ex = nullptr;
+            const cudaError_t ei = cudaGraphInstantiate(&ex, g, 0);
+            cudaGraphDestroy(g);
+            if (ei != cudaSuccess) return c->cuda_fail(ei, "cudaGraphInstantiate");
+            hit = c->graphs.emplace(key, ex).first;
         }
-        ncclResult_t r = ncclGroupEnd();
-        if (r != ncclSuccess && r != ncclInProgress)
-            return c->fail(HYMOE_ERR_NCCL, "result exchange: %s", ncclGetErrorString(r));
-        hymoe_status s2 = ep_poll(c, "result exchange");
-        if (s2 != HYMOE_OK) return s2;
-        c->phase_end(HYMOE_PHASE_EP_COMBINE);
-        y_routed = c->y_ret;
-    }
-    if (T > 0) {
-        c->phase_begin();
-        HY_CUDA(c, launch_combine(c->y, y_routed, c->slot_pos, c->topk_w, dres, dout, T, H, K, st));
-        c->phase_end(HYMOE_PHASE_COMBINE);
-        if (dbg) {
-            const cudaMemcpyKind kd = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
-            if (dbg->topk_weights)
-                HY_CUDA(c, cudaMemcpyAsync(dbg->topk_weights, c->topk_w, sizeof(float) * T * K, kd, st));
-            if (dbg->topk_indices)
-                HY_CUDA(c, cudaMemcpyAsync(dbg->topk_indices, c->topk_idx, sizeof(int) * T * K, kd, st));
-            if (host && dlog)
-                HY_CUDA(c, cudaMemcpyAsync(dbg->router_logits, dlog, sizeof(float) * T * E, kd, st));
-            if (host && dprob)
-                HY_CUDA(c, cudaMemcpyAsync(dbg->router_probs, dprob, sizeof(float) * T * E, kd, st));
-        }
+        HY_CUDA(c, cudaGraphLaunch(hit->second, st));
     }
     if (host) {
         if (T > 0) HY_CUDA(c, cudaMemcpyAsync(out, dout, xbytes, cudaMemcpyDeviceToHost, st));

@@ -29,17 +29,6 @@ cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, 
 
 // ---- dispatch.cu
 constexpr int kMaxSegs = 80;  // >= E + 1 (E <= 64)
-struct PlanArgs {
-    const int* chunk_counts;  // [n_chunks][E]
-    int n_chunks, T, E, K;
-    int* goff;                // [E + 1] routed-row offset of each expert (goff[E] = T*K)
-    int* gcnt;                // [E]     routed rows of each expert
-    int* chunk_base;          // [n_chunks][E]
-    int4* segs;               // single-GPU segments (NULL: expert-parallel mode)
-    int* n_segs;
-};
-cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
-
 struct ItemsArgs {
     const int4* segs;         // {weight group, first row, rows, -}
     const int* n_segs;
@@ -50,6 +39,18 @@ struct ItemsArgs {
     int4* items_dn;
     int* n_items;             // [2]: gate_up, down
 };
+struct PlanArgs {
+    const int* chunk_counts;  // [n_chunks][E]
+    int n_chunks, T, E, K;
+    int* goff;                // [E + 1] routed-row offset of each expert (goff[E] = T*K)
+    int* gcnt;                // [E]     routed rows of each expert
+    int* chunk_base;          // [n_chunks][E]
+    int4* segs;               // single-GPU segments + work items built in the same launch
+    int* n_segs;              // (segs == NULL: expert-parallel mode, items built later)
+    ItemsArgs items;
+};
+cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
+
 cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st);
 
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
@@ -82,7 +83,8 @@ cudaError_t launch_gemm_tc(const GemmMaps& maps, const GemmArgs& a, int n_sms, c
 // ---- gemv.cu (decode path, CUDA cores)
 cudaError_t launch_gemv(const int4* items, const int* n_items, int max_items,
                         const uint8_t* const* wtiles, int wtype, int n_ks, int glu,
-                        const __half* act, int act_ld, void* out, int out_ld, cudaStream_t st);
+                        const __half* act, int act_ld, void* out, int out_ld, int* err,
+                        cudaStream_t st);
 
 // ---- combine.cu
 // out[t] = resid[t] + y_shared[t] + sum_k w[t,k] * y_routed[slot_pos[t,k]]

@@ -16,6 +16,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "hymoe.h")
 
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0 = 0, 1, 2, 8
 HOST_PTRS = 1
+USE_GRAPH = 2
 
 STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OOM", 4: "UNSUPPORTED", 5: "NCCL",
           6: "TIMEOUT", 7: "STATE"}
@@ -197,8 +198,10 @@ class MoE:
         return res
 
     def forward_device(self, layer: int, x_ptr: int, out_ptr: int, T: int, resid_ptr=None,
-                       bias_ptr=None, dbg: Debug | None = None, host: bool = False) -> None:
-        """Raw pointers (device memory unless host=True); asynchronous on the set stream."""
+                       bias_ptr=None, dbg: Debug | None = None, host: bool = False,
+                       graph: bool = False) -> None:
+        """Raw pointers (device memory unless host=True); asynchronous on the set stream.
+        graph=True replays a captured CUDA graph for repeated (layer, T, pointers)."""
+        flags = (HOST_PTRS if host else 0) | (USE_GRAPH if graph else 0)
         self._check(self.L.hymoe_forward(self.h, layer, x_ptr, resid_ptr, out_ptr, T, bias_ptr,
-                                         C.byref(dbg) if dbg else None,
-                                         HOST_PTRS if host else 0))
+                                         C.byref(dbg) if dbg else None, flags))

@@ -46,7 +46,12 @@ enum {
 
 /* flags for hymoe_load_layer / hymoe_forward */
 enum {
-    HYMOE_HOST_PTRS = 1 /* pointers are host memory (copied H2D / D2H inside the call) */
+    HYMOE_HOST_PTRS = 1, /* pointers are host memory (copied H2D / D2H inside the call) */
+    HYMOE_USE_GRAPH = 2  /* hymoe_forward, one GPU, device pointers: capture the call's device
+                            work into a CUDA graph keyed by (layer, n_tokens, pointers) on first
+                            use and replay it on later calls with the same key (removes launch
+                            overhead in decode loops).  Graphs are dropped when a layer is
+                            (re)loaded; profiling disables replay. */
 };
 
 typedef struct hymoe_ctx hymoe_ctx;

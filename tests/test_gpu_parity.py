@@ -170,3 +170,28 @@ def test_errors_are_statuses(orc):
         m.forward_host(0, np.zeros((17, 256), np.float32))
     assert ei.value.status in (1, 7)
     m.close()
+
+
+@pytest.mark.parametrize("T", [3, 40])
+def test_graph_replay_matches_eager(orc, T):
+    """HYMOE_USE_GRAPH: the captured graph reads the buffers' current contents on every
+    replay, giving the same bits as the eager call."""
+    torch = pytest.importorskip("torch")
+    H, I, E, K, seed, wt = 512, 256, 64, 8, 17, O.Q8_0
+    lay = host_layer(orc, seed, 0, H, I, E, wt)
+    m = _ctx(H, I, E, K, T)
+    _load(m, lay, wt)
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        m.set_stream(st.cuda_stream)
+        xd = torch.empty(T, H, device="cuda")
+        od = torch.empty_like(xd)
+        for call in range(3):
+            x = O.synth_x(orc, seed + call, T, H)
+            xd.copy_(torch.from_numpy(x))
+            m.forward_device(0, xd.data_ptr(), od.data_ptr(), T, graph=True)
+            m.synchronize()
+            got = od.cpu().numpy()
+            eager = m.forward_host(0, x)["out"]
+            assert np.array_equal(got, eager), f"call {call}"
+    m.close()
