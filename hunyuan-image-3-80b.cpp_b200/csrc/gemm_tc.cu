@@ -142,8 +142,9 @@ __device__ __forceinline__ void dequant_entry<W_Q8_0>(const uint8_t* raw, uint8_
     uint32_t h[16];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const uint32_t p0 = __byte_perm(w[i], 0, 0x4140) ^ 0x64806480u;
-        const uint32_t p1 = __byte_perm(w[i], 0, 0x4342) ^ 0x64806480u;
+        // excess-128 bytes u = q + 128 -> halves 1024 + u (high byte 0x64 from the constant)
+        const uint32_t p0 = __byte_perm(w[i], 0x64u, 0x4140);
+        const uint32_t p1 = __byte_perm(w[i], 0x64u, 0x4342);
         h[2 * i] = h2_bits(__hmul2(__hsub2(bits_h2(p0), off), d2));
         h[2 * i + 1] = h2_bits(__hmul2(__hsub2(bits_h2(p1), off), d2));
     }

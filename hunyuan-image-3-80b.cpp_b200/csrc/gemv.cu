@@ -1,14 +1,25 @@
-// gemv.cu — grouped GEMV for decode-sized groups (work items of at most kGemvMaxRows token
-// rows), bound by HBM bandwidth.  Same work items and tile format as the tensor-core path.
+// gemv.cu — grouped weight-streaming kernel for decode-sized groups (work items of at most
+// kGemvMaxRows = 64 token rows), bound by HBM bandwidth.  Same work items and weight tile
+// format as the tensor-core path.
 //
-// CTA = 128 threads on one (group, 128-row block, <= 8 token rows) item.  Thread 0 streams
-// the item's weight tiles along K through a kRing-slot ring of 1-D bulk copies
-// (cp.async.bulk, mbarrier transaction counts), so every CTA keeps kRing tiles (Q8_0:
-// 8 x 8.7 KB) in flight - the depth HBM needs.  Each thread owns two (row, GGUF block)
-// entries of every tile: it dequantises them exactly in fp32 ((q - 8) or q via the 2^23
-// magic number), accumulates each block's dot product with the fp16 activations in fp32 and
-// scales it by the block's d once.  gate_up items end with the SwiGLU (silu of rows 0..63
-// times rows 64..127) and write fp16; down items write fp32.
+// CTA = 256 threads (8 warps) on one (group, 128-row block, <= 64 token rows) item.  Thread 0
+// streams the item's weight tiles along K through a ring of `slots` stages: each stage is one
+// 1-D bulk copy of two consecutive raw GGUF tiles plus, per tile, one 2-D TMA load of the
+// matching activation slice (64 halves x 8/16/32/64 token rows, 128-byte swizzle), all
+// completing on the stage's mbarrier.  Several stages per CTA and several CTAs per SM keep
+// enough bytes in flight for HBM; one CTA barrier per stage (two tiles) keeps the
+// bookkeeping per byte small.
+//
+// Math: mma.sync m16n8k16 (fp16 x fp16, fp32 accumulate), weights as A (warp w owns the
+// 16-row group w of the tile), token rows as B in n-tiles of 8.  The quants become exact
+// fp16 integers (q - 8 or q, via the 0x6400 magic-number trick); the block scale d is applied
+// to each block's fp32 partial sums for items of up to 16 rows, or folded into the fp16
+// weights (the tensor-core path's rounding) for larger items.  A k-permutation shared by A and B (each thread's MMA k positions
+// 2c, 2c+1, 2c+8, 2c+9, c = lane % 4, hold four CONSECUTIVE quants of a GGUF block) lets each
+// thread build its A fragments from wide shared-memory loads of raw quants; B columns are
+// token rows permuted so that the swizzled activation loads are free of bank conflicts too.
+// gate_up items end with the SwiGLU (silu of rows 0..63 times rows 64..127) and write fp16;
+// down items write fp32.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -16,221 +27,359 @@ namespace hymoe {
 
 namespace {
 
-constexpr int kGemvThreads = 128;
-constexpr int kRing = 8;
+constexpr int kGemvThreads = 256;
+constexpr int kStageTiles = 2;  // k-tiles per pipeline stage (one barrier round each)
+constexpr int kGL = kGemvMaxRows + 1;  // row pitch (floats) of the result staging G
 
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// Four consecutive excess-128 Q8_0 bytes (one 32-bit word) -> two half2 {q0,q1}, {q2,q3}.
+__device__ __forceinline__ void q8x4_to_h2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const __half2 off = __float2half2_rn(1152.0f);  // 1024 magic + 128 excess
+    lo = h2u(__hsub2(u2h(__byte_perm(w, 0x64u, 0x4140)), off));
+    hi = h2u(__hsub2(u2h(__byte_perm(w, 0x64u, 0x4342)), off));
+}
+
+// Nibbles of four consecutive Q4_0 bytes -> (q - 8) as half2: low nibbles (first half of the
+// block) and high nibbles (second half).
+__device__ __forceinline__ void q4x4_to_h2(uint32_t w, uint32_t (&low)[2], uint32_t (&high)[2]) {
+    const __half2 off = __float2half2_rn(1032.0f);  // 1024 magic + 8 offset
+    const uint32_t p0 = __byte_perm(w, 0, 0x4140), p1 = __byte_perm(w, 0, 0x4342);
+    low[0] = h2u(__hsub2(u2h((p0 & 0x000F000Fu) | 0x64006400u), off));
+    low[1] = h2u(__hsub2(u2h((p1 & 0x000F000Fu) | 0x64006400u), off));
+    high[0] = h2u(__hsub2(u2h(((p0 >> 4) & 0x000F000Fu) | 0x64006400u), off));
+    high[1] = h2u(__hsub2(u2h(((p1 >> 4) & 0x000F000Fu) | 0x64006400u), off));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Token row of the n-tile held by B column m (m = lane / 4 for the B fragment, 2c and 2c + 1
+// for the accumulator): a permutation chosen so that each shared-memory phase of the
+// activation loads touches distinct banks under the 128-byte swizzle.
 template <int WT>
-struct RawBlock;
+__device__ __forceinline__ int col_token(int m) {
+    if constexpr (WT == W_Q4_0) return ((m & 3) << 1) | (m >> 2);  // half-warps: rows 0,2,4,6 / 1,3,5,7
+    else return ((m & 1) << 2) | (m >> 1);                          // quarter-warps: rows n, n + 4
+}
 
-template <>
-struct RawBlock<W_Q4_0> {
-    uint4 q;
-    float d;
-    __device__ __forceinline__ void load(const uint8_t* tile, int e) {
-        d = __half2float(*reinterpret_cast<const __half*>(tile + 2 * e));
-        q = *reinterpret_cast<const uint4*>(tile + 512 + 16 * e);
-    }
-    __device__ __forceinline__ void values(float (&v)[32]) const {
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+// A fragments of one 16-row group (MMA rows g and g + 8 = tile rows r0 and r0 + 8) for both
+// GGUF blocks b and both k-steps s of each: a[b][s][0..3].  Element order inside a
+// 32-element block (the k-permutation; x uses the same one):
+//   Q8_0, F16: thread c holds elements 8c + 4s + {0..3}
+//   Q4_0:      thread c holds elements 16s + 4c + {0..3} (low nibbles s = 0, high s = 1)
+// PRE: the fragments are multiplied by the block scales in fp16 (the tensor-core path's
+// rounding of each weight); otherwise they hold the exact integers q (Q8_0) or q - 8 (Q4_0)
+// and d[b][row] returns the scales, applied to each block's fp32 partial sums.
+template <int WT, bool PRE>
+__device__ __forceinline__ void tile_frags(const uint8_t* tile, int r0, int c, uint32_t (&a)[2][2][4],
+                                           float (&d)[2][2]) {
+    if constexpr (WT == W_F16) {  // tile [128 rows][64 halves]
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-            v[i] = __int_as_float(0x4B000000 | (byte & 0xFu)) - 8388616.0f;
-            v[i + 16] = __int_as_float(0x4B000000 | (byte >> 4)) - 8388616.0f;
+        for (int b = 0; b < 2; ++b) {
+            const uint4 v0 = *reinterpret_cast<const uint4*>(tile + (r0 * 64 + 32 * b + 8 * c) * 2);
+            const uint4 v1 = *reinterpret_cast<const uint4*>(tile + ((r0 + 8) * 64 + 32 * b + 8 * c) * 2);
+            a[b][0][0] = v0.x; a[b][0][2] = v0.y; a[b][1][0] = v0.z; a[b][1][2] = v0.w;
+            a[b][0][1] = v1.x; a[b][0][3] = v1.y; a[b][1][1] = v1.z; a[b][1][3] = v1.w;
+            d[b][0] = d[b][1] = 1.0f;
         }
-    }
-};
-
-template <>
-struct RawBlock<W_Q8_0> {
-    uint4 q0, q1;
-    float d;
-    __device__ __forceinline__ void load(const uint8_t* tile, int e) {
-        d = __half2float(*reinterpret_cast<const __half*>(tile + 2 * e));
-        q0 = *reinterpret_cast<const uint4*>(tile + 512 + 32 * e);
-        q1 = *reinterpret_cast<const uint4*>(tile + 512 + 32 * e + 16);
-    }
-    __device__ __forceinline__ void values(float (&v)[32]) const {
-        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    } else {
+        // scales: entries 2r, 2r + 1 (blocks 0, 1 of row r) are one 32-bit word
+        const __half2 s0 = *reinterpret_cast<const __half2*>(tile + 4 * r0);
+        const __half2 s1 = *reinterpret_cast<const __half2*>(tile + 4 * (r0 + 8));
+        const uint8_t* q = tile + 512;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-            v[i] = __int_as_float(0x4B000000 | (byte ^ 0x80u)) - 8388736.0f;
-        }
-    }
-};
-
-template <>
-struct RawBlock<W_F16> {
-    uint4 h[4];
-    float d;
-    __device__ __forceinline__ void load(const uint8_t* tile, int e) {
-        const int r = e >> 1, b = e & 1;
-        const uint4* p = reinterpret_cast<const uint4*>(tile + r * 128 + b * 64);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) h[i] = p[i];
-        d = 1.0f;
-    }
-    __device__ __forceinline__ void values(float (&v)[32]) const {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const __half2* hp = reinterpret_cast<const __half2*>(&h[i]);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float2 f = __half22float2(hp[j]);
-                v[8 * i + 2 * j] = f.x;
-                v[8 * i + 2 * j + 1] = f.y;
+        for (int b = 0; b < 2; ++b) {
+            if constexpr (WT == W_Q8_0) {
+                const uint2 v0 = *reinterpret_cast<const uint2*>(q + 32 * (2 * r0 + b) + 8 * c);
+                const uint2 v1 = *reinterpret_cast<const uint2*>(q + 32 * (2 * (r0 + 8) + b) + 8 * c);
+                q8x4_to_h2(v0.x, a[b][0][0], a[b][0][2]);
+                q8x4_to_h2(v0.y, a[b][1][0], a[b][1][2]);
+                q8x4_to_h2(v1.x, a[b][0][1], a[b][0][3]);
+                q8x4_to_h2(v1.y, a[b][1][1], a[b][1][3]);
+            } else {  // Q4_0
+                uint32_t l0[2], h0[2], l1[2], h1[2];
+                q4x4_to_h2(*reinterpret_cast<const uint32_t*>(q + 16 * (2 * r0 + b) + 4 * c), l0, h0);
+                q4x4_to_h2(*reinterpret_cast<const uint32_t*>(q + 16 * (2 * (r0 + 8) + b) + 4 * c), l1, h1);
+                a[b][0][0] = l0[0]; a[b][0][2] = l0[1]; a[b][0][1] = l1[0]; a[b][0][3] = l1[1];
+                a[b][1][0] = h0[0]; a[b][1][2] = h0[1]; a[b][1][1] = h1[0]; a[b][1][3] = h1[1];
             }
         }
+        if constexpr (PRE) {
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                const __half2 d0 = b ? __high2half2(s0) : __low2half2(s0);  // row r0
+                const __half2 d1 = b ? __high2half2(s1) : __low2half2(s1);  // row r0 + 8
+#pragma unroll
+                for (int s = 0; s < 2; ++s) {
+                    a[b][s][0] = h2u(__hmul2(u2h(a[b][s][0]), d0));
+                    a[b][s][2] = h2u(__hmul2(u2h(a[b][s][2]), d0));
+                    a[b][s][1] = h2u(__hmul2(u2h(a[b][s][1]), d1));
+                    a[b][s][3] = h2u(__hmul2(u2h(a[b][s][3]), d1));
+                }
+            }
+        } else {
+            d[0][0] = __low2float(s0); d[1][0] = __high2float(s0);
+            d[0][1] = __low2float(s1); d[1][1] = __high2float(s1);
+        }
     }
+}
+
+// B fragments of one token row (128 bytes = 64 halves, 16-byte chunks swizzled by XOR with
+// row & 7) for both blocks and k-steps, in the element order of tile_frags.
+template <int WT>
+__device__ __forceinline__ void x_frags(const uint8_t* xrow, int sw, int c, uint32_t (&bx)[2][2][2]) {
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        if constexpr (WT == W_Q4_0) {
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {  // halves 32b + 16s + 4c .. +3
+                const int chunk = 4 * b + 2 * s + (c >> 1);
+                const uint2 v = *reinterpret_cast<const uint2*>(xrow + 16 * (chunk ^ sw) + 8 * (c & 1));
+                bx[b][s][0] = v.x;
+                bx[b][s][1] = v.y;
+            }
+        } else {  // halves 32b + 8c .. +7
+            const uint4 v = *reinterpret_cast<const uint4*>(xrow + 16 * ((4 * b + c) ^ sw));
+            bx[b][0][0] = v.x; bx[b][0][1] = v.y;
+            bx[b][1][0] = v.z; bx[b][1][1] = v.w;
+        }
+    }
+}
+
+__host__ __device__ __forceinline__ int box_index(int nrows) {
+    return nrows <= 8 ? 0 : nrows <= 16 ? 1 : nrows <= 32 ? 2 : 3;
+}
+
+struct GemvItem {
+    int rb, row0, nrows, n_ks, slots, xb_max, glu, out_ld;
+    const uint8_t* wt;  // first weight tile of the item's row block
+    const CUtensorMap* xmap;
+    void* out;
+    int* err;
 };
 
-template <int WT>
-__global__ __launch_bounds__(kGemvThreads) void gemv_kernel(const int4* __restrict__ items,
-                                                            const int* __restrict__ n_items,
-                                                            const uint8_t* const* __restrict__ wtiles,
-                                                            int n_ks, int glu,
-                                                            const __half* __restrict__ act, int act_ld,
-                                                            void* __restrict__ out, int out_ld,
-                                                            int* err) {
+// One work item with NT n-tiles of 8 token rows (NT * 8 = the activation box height).
+// Thread 0 alone polls the stage barriers (its acquire of the completed phase, followed by
+// the CTA barrier, orders every thread's reads after the copies); the same CTA barrier
+// tells thread 0 that the previous stage has been consumed, so it can be refilled.
+// Up to 16 token rows the block scales are applied to each block's fp32 partial sums
+// (exact weights); from 17 rows on they are folded into the fp16 weights once per tile,
+// which costs fewer instructions than per-token scaling there.
+template <int WT, int NT>
+__device__ __forceinline__ void run_item(const GemvItem& p, uint8_t* base, uint64_t* full) {
     constexpr int TB = tile_bytes(WT);
-    extern __shared__ __align__(128) uint8_t gsm[];
-    uint8_t* ring = gsm;                                            // kRing x TB
-    uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRing * TB);
-    float* G = reinterpret_cast<float*>(full + kRing);             // [128][kGemvMaxRows + 1]
-    if (static_cast<int>(blockIdx.x) >= *n_items) return;
-    const int4 it = items[blockIdx.x];
-    const int g = it.x, rb = it.y, row0 = it.z, nrows = min(it.w, kGemvMaxRows);
-    const int tid = threadIdx.x;
-    const uint8_t* wt = wtiles[g] + static_cast<size_t>(rb) * n_ks * TB;
+    const int xs_bytes = kStageTiles * p.xb_max;          // activation part of a stage
+    uint8_t* xring = base;                                 // slots x xs_bytes
+    uint8_t* wring = base + static_cast<size_t>(p.slots) * xs_bytes;  // slots x kStageTiles x TB
+    float* G = reinterpret_cast<float*>(base);  // [128][kGL], reuses the ring afterwards
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gq = lane >> 2, c = lane & 3;
+    const int r0 = 16 * warp + gq;
+    const int slots = p.slots, n_ks = p.n_ks;
+    const int n_st = (n_ks + kStageTiles - 1) / kStageTiles;
 
-    if (tid == 0) {
-        for (int s = 0; s < kRing; ++s) mbar_init(&full[s], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
+    // Stage j: k-tiles [kStageTiles j, kStageTiles j + cnt): one bulk copy of the (contiguous)
+    // weight tiles and one activation box per tile, all on the stage's barrier.
+    auto issue = [&](int stage, int j) {
+        const int t0 = kStageTiles * j, cnt = min(kStageTiles, n_ks - t0);
+        mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(cnt) * (TB + NT * 1024u));
+        bulk_load(wring + static_cast<size_t>(stage) * kStageTiles * TB, p.wt + static_cast<size_t>(t0) * TB,
+                  static_cast<uint32_t>(cnt) * TB, &full[stage]);
+        for (int i = 0; i < cnt; ++i)
+            tma_load_2d(xring + static_cast<size_t>(stage) * xs_bytes + i * p.xb_max, p.xmap, &full[stage],
+                        (t0 + i) * kTileK, p.row0);
+    };
+    int issued = min(slots, n_st);  // stages issued; meaningful in thread 0 only
     if (tid == 0)
-        for (int s = 0; s < kRing && s < n_ks; ++s) {
-            mbar_arrive_expect_tx(&full[s], TB);
-            bulk_load(ring + s * TB, wt + static_cast<size_t>(s) * TB, TB, &full[s]);
+        for (int j = 0; j < issued; ++j) issue(j, j);
+
+    float acc[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    const int tok_b = col_token<WT>(gq);  // token row (within an n-tile) of this lane's B column
+
+    int s = 0, fail_st = -1;
+    uint32_t phase = 0;
+    for (int j = 0; j < n_st; ++j) {
+        const bool got = tid != 0 || mbar_wait(&full[s], phase, p.err, DEVERR_TIMEOUT_DEQUANT);
+        if (!__syncthreads_and(got)) {  // uniform: every thread leaves the loop here
+            fail_st = j;
+            break;
         }
-
-    float acc[2][kGemvMaxRows];
+        // Every thread has finished stage j - 1: its slot takes stage j - 1 + slots.
+        if (tid == 0 && j > 0 && j - 1 + slots < n_st) {
+            issue(s == 0 ? slots - 1 : s - 1, j - 1 + slots);
+            issued = j + slots;
+        }
+        const int cnt = min(kStageTiles, n_ks - kStageTiles * j);
+        const uint8_t* wst = wring + static_cast<size_t>(s) * kStageTiles * TB;
+        const uint8_t* xst = xring + static_cast<size_t>(s) * xs_bytes;
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+        for (int i = 0; i < kStageTiles; ++i) {
+            if (i < cnt) {
+                constexpr bool kPre = NT >= 4;
+                uint32_t a[2][2][4];
+                float d[2][2];
+                tile_frags<WT, kPre>(wst + i * TB, r0, c, a, d);
+                const uint8_t* xt = xst + i * p.xb_max;
 #pragma unroll
-        for (int n = 0; n < kGemvMaxRows; ++n) acc[h][n] = 0.f;
-
-    // `ok` stays uniform across the CTA (__syncthreads_and), so every thread takes the same
-    // path; after a failed (timed-out) wait no further copies are issued and the copies
-    // still in flight, tiles [fail_ks, issued), are waited for (bounded) before returning.
-    bool ok = true;
-    int issued = min(kRing, n_ks), fail_ks = -1;
-    for (int ks = 0; ks < n_ks; ++ks) {
-        const int s = ks % kRing;
-        const bool got = ok && mbar_wait(&full[s], (ks / kRing) & 1, err, DEVERR_TIMEOUT_DEQUANT);
-        if (got) {
-            const uint8_t* tile = ring + s * TB;
+                for (int nt = 0; nt < NT; ++nt) {
+                    const int n = 8 * nt + tok_b;
+                    uint32_t bx[2][2][2];
+                    x_frags<WT>(xt + 128 * n, n & 7, c, bx);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int e = tid + h * kGemvThreads;  // entry (row e >> 1, block e & 1)
-                RawBlock<WT> blk;
-                blk.load(tile, e);
-                float v[32];
-                blk.values(v);
-                const int k0 = ks * kTileK + (e & 1) * 32;
-#pragma unroll
-                for (int n = 0; n < kGemvMaxRows; ++n) {
-                    if (n >= nrows) break;
-                    const uint4* xr = reinterpret_cast<const uint4*>(act + static_cast<size_t>(row0 + n) * act_ld + k0);
-                    float sum = 0.f;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const uint4 xv = __ldg(xr + c);
-                        const __half2* hp = reinterpret_cast<const __half2*>(&xv);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const float2 f = __half22float2(hp[j]);
-                            sum = fmaf(v[8 * c + 2 * j], f.x, sum);
-                            sum = fmaf(v[8 * c + 2 * j + 1], f.y, sum);
+                    for (int b = 0; b < 2; ++b) {
+                        if constexpr (kPre) {
+                            mma16816(acc[nt], a[b][0], bx[b][0][0], bx[b][0][1]);
+                            mma16816(acc[nt], a[b][1], bx[b][1][0], bx[b][1][1]);
+                        } else {
+                            float blk[4] = {0.f, 0.f, 0.f, 0.f};
+                            mma16816(blk, a[b][0], bx[b][0][0], bx[b][0][1]);
+                            mma16816(blk, a[b][1], bx[b][1][0], bx[b][1][1]);
+                            acc[nt][0] = fmaf(d[b][0], blk[0], acc[nt][0]);
+                            acc[nt][1] = fmaf(d[b][0], blk[1], acc[nt][1]);
+                            acc[nt][2] = fmaf(d[b][1], blk[2], acc[nt][2]);
+                            acc[nt][3] = fmaf(d[b][1], blk[3], acc[nt][3]);
                         }
                     }
-                    acc[h][n] = fmaf(blk.d, sum, acc[h][n]);
                 }
             }
         }
-        const bool was_ok = ok;
-        ok = __syncthreads_and(got) != 0;  // also: every thread is done with slot s
-        if (was_ok && !ok) fail_ks = ks;
-        if (ok && ks + kRing < n_ks) {
-            if (tid == 0) {
-                mbar_arrive_expect_tx(&full[s], TB);
-                bulk_load(ring + s * TB, wt + static_cast<size_t>(ks + kRing) * TB, TB, &full[s]);
-            }
-            issued = ks + kRing + 1;
+        if (++s == slots) {
+            s = 0;
+            phase ^= 1u;
         }
     }
-    if (!ok) {
+    if (fail_st >= 0) {
+        // Copies still in flight, stages [fail_st, issued), land before the exit.
         if (tid == 0)
-            for (int t = fail_ks; t < issued; ++t) mbar_drain(&full[t % kRing], (t / kRing) & 1);
+            for (int t = fail_st; t < issued; ++t) mbar_drain(&full[t % slots], (t / slots) & 1);
         __syncthreads();
         return;
     }
-    // Entries 2r and 2r+1 (blocks 0 and 1 of row r) sit in adjacent lanes for h = 0, 1.
+    __syncthreads();  // every thread is done with the ring: it becomes G
+    const int t0 = col_token<WT>(2 * c), t1 = col_token<WT>(2 * c + 1);
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int n = 0; n < kGemvMaxRows; ++n) acc[h][n] += __shfl_xor_sync(0xffffffffu, acc[h][n], 1);
-    if ((tid & 1) == 0)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int r = (tid + h * kGemvThreads) >> 1;
-#pragma unroll
-            for (int n = 0; n < kGemvMaxRows; ++n) G[r * (kGemvMaxRows + 1) + n] = acc[h][n];
-        }
+    for (int nt = 0; nt < NT; ++nt) {
+        G[r0 * kGL + 8 * nt + t0] = acc[nt][0];
+        G[r0 * kGL + 8 * nt + t1] = acc[nt][1];
+        G[(r0 + 8) * kGL + 8 * nt + t0] = acc[nt][2];
+        G[(r0 + 8) * kGL + 8 * nt + t1] = acc[nt][3];
+    }
     __syncthreads();
-    if (glu) {
-        __half* o = static_cast<__half*>(out);
+    const int nrows = p.nrows;
+    if (p.glu) {
+        __half* o = static_cast<__half*>(p.out);
         for (int i = tid; i < kGluHalf * nrows; i += kGemvThreads) {
             const int j = i % kGluHalf, n = i / kGluHalf;
-            o[static_cast<size_t>(row0 + n) * out_ld + rb * kGluHalf + j] =
-                __float2half_rn(silu_mul(G[j * (kGemvMaxRows + 1) + n],
-                                         G[(kGluHalf + j) * (kGemvMaxRows + 1) + n]));
+            o[static_cast<size_t>(p.row0 + n) * p.out_ld + p.rb * kGluHalf + j] =
+                __float2half_rn(silu_mul(G[j * kGL + n], G[(kGluHalf + j) * kGL + n]));
         }
     } else {
-        float* o = static_cast<float*>(out);
+        float* o = static_cast<float*>(p.out);
         for (int i = tid; i < kTileRows * nrows; i += kGemvThreads) {
             const int r = i % kTileRows, n = i / kTileRows;
-            o[static_cast<size_t>(row0 + n) * out_ld + rb * kTileRows + r] = G[r * (kGemvMaxRows + 1) + n];
+            o[static_cast<size_t>(p.row0 + n) * p.out_ld + p.rb * kTileRows + r] = G[r * kGL + n];
         }
     }
 }
 
 template <int WT>
-cudaError_t launch_t(const int4* items, const int* n_items, int max_items,
-                     const uint8_t* const* wtiles, int n_ks, int glu, const __half* act, int act_ld,
-                     void* out, int out_ld, int* err, cudaStream_t st) {
-    const size_t smem = static_cast<size_t>(kRing) * tile_bytes(WT) + kRing * 8 +
-                        sizeof(float) * kTileRows * (kGemvMaxRows + 1);
+__global__ __launch_bounds__(kGemvThreads, 3) void gemv_kernel(const __grid_constant__ GemvMaps maps,
+                                                            const int4* __restrict__ items,
+                                                            const int* __restrict__ n_items,
+                                                            const uint8_t* const* __restrict__ wtiles,
+                                                            int n_ks, int glu, int slots, int xb_max,
+                                                            void* __restrict__ out, int out_ld,
+                                                            int* err) {
+    constexpr int TB = tile_bytes(WT);
+    extern __shared__ uint8_t gsm_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + static_cast<size_t>(slots) * kStageTiles * (xb_max + TB));
+    if (static_cast<int>(blockIdx.x) >= *n_items) return;
+    const int4 it = items[blockIdx.x];
+    // The host sizes the activation box (xb_max / 128 rows) from the largest group.
+    if (it.w > (xb_max >> 7)) {
+        if (threadIdx.x == 0) atomicOr(err, DEVERR_BAD_ITEM);
+        return;
+    }
+    const int bi = box_index(it.w);
+    GemvItem p;
+    p.rb = it.y;
+    p.row0 = it.z;
+    p.nrows = it.w;
+    p.n_ks = n_ks;
+    p.slots = slots;
+    p.xb_max = xb_max;
+    p.glu = glu;
+    p.out_ld = out_ld;
+    p.wt = wtiles[it.x] + static_cast<size_t>(it.y) * n_ks * TB;
+    p.xmap = &maps.x[bi];
+    p.out = out;
+    p.err = err;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < slots; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    switch (bi) {
+        case 0: run_item<WT, 1>(p, base, full); break;
+        case 1: run_item<WT, 2>(p, base, full); break;
+        case 2: run_item<WT, 4>(p, base, full); break;
+        default: run_item<WT, 8>(p, base, full); break;
+    }
+}
+
+// Stages per CTA: as many as fit in ~72 KB (three CTAs per SM), at least 2 and at most 4;
+// the ring must also hold the result staging G.
+template <int WT>
+void gemv_smem(int max_box, int* slots, int* xb_max, size_t* smem) {
+    *xb_max = 1024 << max_box;
+    const size_t stage = static_cast<size_t>(kStageTiles) * (tile_bytes(WT) + *xb_max);
+    int s = static_cast<int>((72u * 1024u) / stage);
+    s = s < 2 ? 2 : s > 4 ? 4 : s;
+    const size_t g_bytes = sizeof(float) * kTileRows * kGL;
+    while (static_cast<size_t>(s) * stage < g_bytes) ++s;
+    *slots = s;
+    *smem = 1024 + static_cast<size_t>(s) * stage + 8u * s;
+}
+
+template <int WT>
+cudaError_t launch_t(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
+                     const uint8_t* const* wtiles, int n_ks, int glu, int max_rows, void* out,
+                     int out_ld, int* err, cudaStream_t st) {
+    int slots = 0, xb_max = 0;
+    size_t smem = 0;
+    gemv_smem<WT>(box_index(max_rows), &slots, &xb_max, &smem);
     cudaError_t e = cudaFuncSetAttribute(gemv_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    gemv_kernel<WT><<<max_items, kGemvThreads, smem, st>>>(items, n_items, wtiles, n_ks, glu, act,
-                                                           act_ld, out, out_ld, err);
+    gemv_kernel<WT><<<max_items, kGemvThreads, smem, st>>>(maps, items, n_items, wtiles, n_ks, glu, slots,
+                                                           xb_max, out, out_ld, err);
     return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_gemv(const int4* items, const int* n_items, int max_items,
-                        const uint8_t* const* wtiles, int wtype, int n_ks, int glu,
-                        const __half* act, int act_ld, void* out, int out_ld, int* err,
-                        cudaStream_t st) {
+cudaError_t launch_gemv(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
+                        const uint8_t* const* wtiles, int wtype, int n_ks, int glu, int max_rows,
+                        void* out, int out_ld, int* err, cudaStream_t st) {
     if (max_items <= 0) return cudaSuccess;
+    if (max_rows < 1 || max_rows > kGemvMaxRows) return cudaErrorInvalidValue;
     switch (wtype) {
-        case W_Q4_0: return launch_t<W_Q4_0>(items, n_items, max_items, wtiles, n_ks, glu, act, act_ld, out, out_ld, err, st);
-        case W_Q8_0: return launch_t<W_Q8_0>(items, n_items, max_items, wtiles, n_ks, glu, act, act_ld, out, out_ld, err, st);
-        default: return launch_t<W_F16>(items, n_items, max_items, wtiles, n_ks, glu, act, act_ld, out, out_ld, err, st);
+        case W_Q4_0: return launch_t<W_Q4_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, err, st);
+        case W_Q8_0: return launch_t<W_Q8_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, err, st);
+        default: return launch_t<W_F16>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, err, st);
     }
 }
 

@@ -130,6 +130,7 @@ struct hymoe_ctx {
     uint8_t* tmp = nullptr;   // load / synthesis staging of one GGUF tensor
     size_t tmp_bytes = 0;
     GemmMaps maps_xp{}, maps_h{};
+    GemvMaps gmaps_xp{}, gmaps_h{};
 
     float* bias_dev = nullptr;
     int4* segs = nullptr;
@@ -238,9 +239,13 @@ hymoe_status make_tmap(hymoe_ctx* c, CUtensorMap* map, void* base, uint64_t K, u
     return HYMOE_OK;
 }
 
-hymoe_status make_maps(hymoe_ctx* c, GemmMaps* m, void* base, uint64_t K, uint64_t rows) {
+hymoe_status make_maps(hymoe_ctx* c, GemmMaps* m, GemvMaps* gm, void* base, uint64_t K, uint64_t rows) {
     for (int i = 0; i < kNumBoxes; ++i) {
         hymoe_status st = make_tmap(c, &m->b[i], base, K, rows, static_cast<uint32_t>(box_rows(i)));
+        if (st != HYMOE_OK) return st;
+    }
+    for (int i = 0; i < kGemvBoxes; ++i) {
+        hymoe_status st = make_tmap(c, &gm->x[i], base, K, rows, static_cast<uint32_t>(gemv_box_rows(i)));
         if (st != HYMOE_OK) return st;
     }
     return HYMOE_OK;
@@ -475,8 +480,8 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     if (e != cudaSuccess) return bail(c->cuda_fail(e, "scratch allocation"));
     if (cudaMemset(c->err_word, 0, sizeof(int)) != cudaSuccess)
         return bail(c->fail(HYMOE_ERR_CUDA, "cudaMemset failed"));
-    hymoe_status st = make_maps(c, &c->maps_xp, c->xp, H, rows);
-    if (st == HYMOE_OK) st = make_maps(c, &c->maps_h, c->hbuf, I, rows);
+    hymoe_status st = make_maps(c, &c->maps_xp, &c->gmaps_xp, c->xp, H, rows);
+    if (st == HYMOE_OK) st = make_maps(c, &c->maps_h, &c->gmaps_h, c->hbuf, I, rows);
     if (st != HYMOE_OK) return bail(st);
     if (N > 1) {
         if (!cfg->nccl_unique_id) return bail(c->fail(HYMOE_ERR_INVALID_ARG, "ep_size > 1 needs nccl_unique_id"));
@@ -699,7 +704,10 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     if (T == 0 && !ep) return host ? hymoe_synchronize(c) : HYMOE_OK;
 
     auto device_part = [&]() -> hymoe_status {
-        bool gemv = T <= kGemvMaxRows;  // decode regime: every segment has at most 8 rows
+        // Decode regime: every group has at most kGemvMaxRows rows (on one GPU a group has
+        // at most T rows: the shared expert T, a routed expert at most one row per token).
+        bool gemv = T <= kGemvMaxRows;
+        size_t gemv_rows = static_cast<size_t>(T);
         const int tiles_gu = 2 * I / kTileRows, tiles_dn = H / kTileRows;
         auto items_args = [&](bool gv) {
             ItemsArgs ia{};
@@ -779,6 +787,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
                 max_rows = std::max(max_rows, rows_le);
             }
             gemv = max_rows <= static_cast<size_t>(kGemvMaxRows);
+            gemv_rows = max_rows;
             if (total_sent != static_cast<size_t>(T) * K)
                 return c->fail(HYMOE_ERR_STATE, "count exchange inconsistent: %zu rows for %d pairs", total_sent, T * K);
             // Every rank checks every rank's receive size (all hold the full count matrix), so
@@ -820,12 +829,13 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             const int max_it = static_cast<int>(std::min<size_t>(
                 c->max_items, static_cast<size_t>(tiles_gu) * ((rows_in_use + kGemvMaxRows - 1) / kGemvMaxRows + kMaxSegs)));
             c->phase_begin();
-            HY_CUDA(c, launch_gemv(c->items_gu, c->n_items, max_it, L.d_gu_ptrs, L.wtype, H / kTileK, 1,
-                                   c->xp, H, c->hbuf, I, c->err_word, st));
+            const int mr = static_cast<int>(std::max<size_t>(1, gemv_rows));
+            HY_CUDA(c, launch_gemv(c->gmaps_xp, c->items_gu, c->n_items, max_it, L.d_gu_ptrs, L.wtype, H / kTileK,
+                                   1, mr, c->hbuf, I, c->err_word, st));
             c->phase_end(HYMOE_PHASE_GATE_UP);
             c->phase_begin();
-            HY_CUDA(c, launch_gemv(c->items_dn, c->n_items + 1, max_it, L.d_dn_ptrs, L.wtype, I / kTileK,
-                                   0, c->hbuf, I, c->y, H, c->err_word, st));
+            HY_CUDA(c, launch_gemv(c->gmaps_h, c->items_dn, c->n_items + 1, max_it, L.d_dn_ptrs, L.wtype,
+                                   I / kTileK, 0, mr, c->y, H, c->err_word, st));
             c->phase_end(HYMOE_PHASE_DOWN);
         } else {
             GemmArgs ga{};

@@ -22,7 +22,7 @@ cudaError_t launch_synth_f32(float* dst, uint64_t n, uint64_t seed, uint64_t str
 
 // ---- router.cu
 constexpr int kRouterTok = 16;  // tokens per router CTA (= dispatch chunk)
-constexpr int kGemvMaxRows = 8; // token rows per GEMV work item
+constexpr int kGemvMaxRows = 64; // token rows per GEMV work item
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
                           int* topk_idx, int* chunk_counts, cudaStream_t st);
@@ -80,11 +80,16 @@ struct GemmArgs {
 };
 cudaError_t launch_gemm_tc(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st);
 
-// ---- gemv.cu (decode path, CUDA cores)
-cudaError_t launch_gemv(const int4* items, const int* n_items, int max_items,
-                        const uint8_t* const* wtiles, int wtype, int n_ks, int glu,
-                        const __half* act, int act_ld, void* out, int out_ld, int* err,
-                        cudaStream_t st);
+// ---- gemv.cu (decode path: weight streaming, mma.sync)
+constexpr int kGemvBoxes = 4;
+__host__ __device__ constexpr int gemv_box_rows(int i) { return 8 << i; }  // 8, 16, 32, 64
+struct GemvMaps {
+    CUtensorMap x[kGemvBoxes];  // activation operand, fp16 [rows, K], box {64, gemv_box_rows(i)}, SW128
+};
+// max_rows: the largest item (<= kGemvMaxRows); it sizes the activation stages.
+cudaError_t launch_gemv(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
+                        const uint8_t* const* wtiles, int wtype, int n_ks, int glu, int max_rows,
+                        void* out, int out_ld, int* err, cudaStream_t st);
 
 // ---- combine.cu
 // out[t] = resid[t] + y_shared[t] + sum_k w[t,k] * y_routed[slot_pos[t,k]]

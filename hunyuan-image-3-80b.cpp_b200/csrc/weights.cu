@@ -1,8 +1,10 @@
 // weights.cu — GGUF -> device tile re-tiling, and the on-device synthetic generator.
 //
-// Re-tiling keeps every GGUF block's bytes (fp16 d + quants) unchanged, so the device
-// holds exactly the GGUF Q4_0 / Q8_0 bytes (hunyuan_gguf_loader.cpp:172-177 sizes); F32
-// and F16 matrices become F16 tiles.
+// Re-tiling keeps every GGUF block's information unchanged, so the device holds exactly the
+// GGUF Q4_0 / Q8_0 bytes (hunyuan_gguf_loader.cpp:172-177 sizes): the fp16 d and the Q4_0
+// nibbles verbatim, the Q8_0 int8 quants stored excess-128 (q ^ 0x80 = q + 128 as an
+// unsigned byte), which lets the kernels turn a byte into the fp16 value 1024 + q + 128
+// with a single byte permute.  F32 and F16 matrices become F16 tiles.
 //
 // The generator restates the test oracle's published algorithm on the device:
 // Philox4x32-10 (Salmon et al., SC'11) per element, Irwin-Hall sum of its 8 16-bit
@@ -47,7 +49,8 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, int src_type,
         tile[2 * e] = sb[0];
         tile[2 * e + 1] = sb[1];
         uint8_t* q = tile + 512 + e * qn;
-        for (int j = 0; j < qn; ++j) q[j] = sb[2 + j];
+        const uint8_t flip = dst_type == W_Q8_0 ? 0x80 : 0x00;
+        for (int j = 0; j < qn; ++j) q[j] = sb[2 + j] ^ flip;
     } else {  // F16 tile row r, halves [32 b, 32 b + 32)
         __half* row = reinterpret_cast<__half*>(tile) + r * kTileK + 32 * b;
         if (src_type == W_F16) {

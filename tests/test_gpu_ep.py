@@ -100,10 +100,10 @@ def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens):
             ep_out = res[rank][call]
             ref = single.forward_host(0, x, bias=bias, debug=True)
             assert np.array_equal(ep_out["idx"], ref["idx"])
-            # Same GEMM path on both sides (every call above the 8-token decode regime):
-            # identical bits.  Otherwise the decode GEMV and the tensor-core path differ in
-            # rounding, within the parity tolerance.
-            if all(tokens[r][call] > 8 for r in range(world)):
+            # Same GEMM path on both sides (every call above the 64-row decode regime):
+            # identical bits.  Otherwise the decode kernel and the tensor-core path sum the
+            # same fp16 products in a different order, within the parity tolerance.
+            if all(tokens[r][call] > 64 for r in range(world)):
                 assert np.array_equal(ep_out["out"], ref["out"]), f"rank {rank} call {call}"
             elif t:
                 assert rel_l2(ep_out["out"], ref["out"]) <= REL_L2_TOL

@@ -74,10 +74,10 @@ def test_full_shape_vs_reference_golden_device_weights(orc, name):
 
 
 @pytest.mark.parametrize("wt", [O.Q4_0, O.Q8_0])
-@pytest.mark.parametrize("T", [1, 3, 8, 9, 16, 33, 64, 257, 600])
+@pytest.mark.parametrize("T", [1, 3, 8, 9, 16, 24, 33, 64, 65, 257, 600])
 def test_token_counts_vs_oracle(orc, wt, T):
-    """Decode (grouped GEMV, T <= 8) and tensor-core paths, single and multiple token
-    tiles per expert, ragged tails."""
+    """Decode (weight-streaming kernel, T <= 64: activation boxes of 8/16/32/64 rows) and
+    tensor-core paths (T > 64), single and multiple token tiles per expert, ragged tails."""
     H, I, E, K, seed = 512, 256, 64, 8, 21
     lay = host_layer(orc, seed, 0, H, I, E, wt)
     x = O.synth_x(orc, seed + T, T, H)
