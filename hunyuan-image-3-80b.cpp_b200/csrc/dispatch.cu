@@ -16,52 +16,47 @@
 // multiply; work items tile segments into (row-block, up to tile_n rows) pieces.
 #include "common.cuh"
 #include "kernels.h"
+#include "topk.cuh"
 
 namespace hymoe {
 
 namespace {
 
-// Work items from segments (executed by a whole 1024-thread CTA; `seg` in shared memory):
-// segment-major, then row block, then token tile, so consecutive items share a weight tile
-// and concurrently running CTAs hit it in L2.
-__device__ void build_items(const int4* seg, int ns, const ItemsArgs& a, int* ntt_s, int* ioff_gu,
-                            int* ioff_dn) {
+// Work items from segments (executed by a whole CTA; `seg` in shared memory, pre: shared
+// scratch of kMaxSegs + 1 ints): segment-major, then row block, then token tile, so
+// consecutive items share a weight tile and concurrently running CTAs hit it in L2.
+__device__ void build_items(const int4* seg, int ns, const ItemsArgs& a, int* pre) {
     const int tid = threadIdx.x;
+    const int tn = a.gemv ? kGemvMaxRows : a.tile_n;
     for (int i = tid; i < ns; i += blockDim.x) {
         const int cnt = seg[i].z;
-        ntt_s[i] = cnt <= 0 ? 0 : (a.gemv ? (cnt + kGemvMaxRows - 1) / kGemvMaxRows
-                                         : (cnt + a.tile_n - 1) / a.tile_n);
+        pre[i] = cnt <= 0 ? 0 : (cnt + tn - 1) / tn;  // token tiles of segment i
     }
     __syncthreads();
-    if (tid == 0) {
-        int ngu = 0, ndn = 0;
-        for (int i = 0; i < ns; ++i) {
-            ioff_gu[i] = ngu;
-            ioff_dn[i] = ndn;
-            ngu += ntt_s[i] * a.n_rb_gu;
-            ndn += ntt_s[i] * a.n_rb_dn;
+    if (tid < 32) {
+        const int tot = warp_exclusive_scan(pre, ns);  // pre[i] = tiles before segment i
+        if (tid == 0) {
+            pre[ns] = tot;
+            a.n_items[0] = tot * a.n_rb_gu;
+            a.n_items[1] = tot * a.n_rb_dn;
         }
-        ioff_gu[ns] = ngu;
-        ioff_dn[ns] = ndn;
-        a.n_items[0] = ngu;
-        a.n_items[1] = ndn;
     }
     __syncthreads();
-    const int tn = a.gemv ? kGemvMaxRows : a.tile_n;
     for (int which = 0; which < 2; ++which) {
-        const int* ioff = which ? ioff_dn : ioff_gu;
+        const int n_rb = which ? a.n_rb_dn : a.n_rb_gu;
         int4* items = which ? a.items_dn : a.items_gu;
-        const int total = ioff[ns];
+        const int total = pre[ns] * n_rb;
         for (int i = tid; i < total; i += blockDim.x) {
-            int lo = 0, hi = ns - 1;  // last segment with ioff <= i
+            const int key = i / n_rb;
+            int lo = 0, hi = ns - 1;  // last segment with pre <= key
             while (lo < hi) {
                 const int mid = (lo + hi + 1) >> 1;
-                if (ioff[mid] <= i) lo = mid;
+                if (pre[mid] <= key) lo = mid;
                 else hi = mid - 1;
             }
             const int4 sg = seg[lo];
-            const int local = i - ioff[lo];
-            const int ntt = ntt_s[lo];
+            const int local = i - pre[lo] * n_rb;
+            const int ntt = pre[lo + 1] - pre[lo];
             const int rb = local / ntt, tt = local - rb * ntt;
             items[i] = make_int4(sg.x, rb, sg.y + tt * tn, min(tn, sg.z - tt * tn));
         }
@@ -70,11 +65,27 @@ __device__ void build_items(const int4* seg, int ns, const ItemsArgs& a, int* nt
 
 __global__ __launch_bounds__(1024) void items_kernel(ItemsArgs a) {
     __shared__ int4 seg[kMaxSegs];
-    __shared__ int ntt_s[kMaxSegs], ioff_gu[kMaxSegs + 1], ioff_dn[kMaxSegs + 1];
+    __shared__ int pre[kMaxSegs + 1];
     const int ns = min(*a.n_segs, kMaxSegs);
     for (int i = threadIdx.x; i < ns; i += blockDim.x) seg[i] = a.segs[i];
     __syncthreads();
-    build_items(seg, ns, a, ntt_s, ioff_gu, ioff_dn);
+    build_items(seg, ns, a, pre);
+}
+
+// Single-GPU segments (shared expert first, then one segment per routed expert) and their
+// work items.  goff_s / gcnt_s: the routed-row offsets and counts in shared memory.
+__device__ void single_gpu_items(const PlanArgs& a, const int* goff_s, const int* gcnt_s) {
+    __shared__ int4 seg[kMaxSegs];
+    __shared__ int pre[kMaxSegs + 1];
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        seg[0] = make_int4(a.E, 0, a.T, 0);
+        *a.n_segs = a.E + 1;
+    }
+    for (int g = tid; g < a.E; g += blockDim.x) seg[1 + g] = make_int4(g, a.T + goff_s[g], gcnt_s[g], 0);
+    __syncthreads();
+    for (int i = tid; i <= a.E; i += blockDim.x) a.segs[i] = seg[i];
+    build_items(seg, a.E + 1, a.items, pre);
 }
 
 // One CTA of 1024 threads.  (expert, part) = (tid / 16, tid % 16) owns a contiguous run of
@@ -84,7 +95,7 @@ constexpr int kMaxChunksPerPart = 32;  // 16 parts x 32 chunks x 16 tokens = 819
 
 __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
     __shared__ int part_sum[64][17];
-    __shared__ int gcnt_s[64], goff_s[65];
+    __shared__ int gcnt_s[64], goff_s[kMaxSegs + 1];
     const int tid = threadIdx.x;
     const int e = tid >> 4, part = tid & 15;
     const int cpp = (a.n_chunks + 15) / 16;
@@ -103,15 +114,12 @@ __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
         int tot = 0;
         for (int p = 0; p < 16; ++p) tot += part_sum[tid][p];
         gcnt_s[tid] = tid < a.E ? tot : 0;
+        goff_s[tid] = gcnt_s[tid];
     }
     __syncthreads();
-    if (tid == 0) {
-        int off = 0;
-        for (int g = 0; g < a.E; ++g) {
-            goff_s[g] = off;
-            off += gcnt_s[g];
-        }
-        goff_s[a.E] = off;  // == T * K
+    if (tid < 32) {
+        const int tot = warp_exclusive_scan(goff_s, a.E);
+        if (tid == 0) goff_s[a.E] = tot;  // == T * K
     }
     __syncthreads();
     for (int g = tid; g <= a.E; g += blockDim.x) a.goff[g] = goff_s[g];
@@ -126,27 +134,47 @@ __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
             base += cnt[i];
         }
     }
-    // Single-GPU segments (shared expert first, then one segment per routed expert) and
-    // their work items, in this same launch.
-    if (a.segs != nullptr) {
-        __shared__ int4 seg[kMaxSegs];
-        __shared__ int ntt_s[kMaxSegs], ioff_gu[kMaxSegs + 1], ioff_dn[kMaxSegs + 1];
-        if (tid == 0) {
-            seg[0] = make_int4(a.E, 0, a.T, 0);
-            *a.n_segs = a.E + 1;
-        }
-        for (int g = tid; g < a.E; g += blockDim.x) seg[1 + g] = make_int4(g, a.T + goff_s[g], gcnt_s[g], 0);
-        __syncthreads();
-        for (int i = tid; i <= a.E; i += blockDim.x) a.segs[i] = seg[i];
-        build_items(seg, a.E + 1, a.items, ntt_s, ioff_gu, ioff_dn);
-    }
+    // Single-GPU segments and their work items, in this same launch.
+    if (a.segs != nullptr) single_gpu_items(a, goff_s, gcnt_s);
 }
 
-// One CTA per router chunk of 16 tokens.  Position of pair (t, k) with expert e:
+// Decode front end for T <= 16 (one router chunk): top-K of every token (warp t routes token
+// t) followed by the plan of that single chunk, in one launch.
+__global__ __launch_bounds__(1024) void topk_plan_kernel(const float* __restrict__ logits, int T, int K,
+                                                         float* __restrict__ probs_out,
+                                                         float* __restrict__ topk_w,
+                                                         int* __restrict__ topk_idx, PlanArgs a) {
+    __shared__ float pbuf[kRouterTok][kMaxE];
+    __shared__ int gcnt_s[kMaxE], goff_s[kMaxSegs + 1];
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (tid < kMaxE) gcnt_s[tid] = 0;
+    __syncthreads();
+    if (warp < T) topk_token(logits, warp, a.E, K, probs_out, topk_w, topk_idx, pbuf[warp], gcnt_s);
+    __syncthreads();
+    if (tid < 64) goff_s[tid] = tid < a.E ? gcnt_s[tid] : 0;
+    __syncthreads();
+    if (tid < 32) {
+        const int tot = warp_exclusive_scan(goff_s, a.E);
+        if (tid == 0) goff_s[a.E] = tot;
+    }
+    __syncthreads();
+    for (int g = tid; g <= a.E; g += blockDim.x) a.goff[g] = goff_s[g];
+    for (int g = tid; g < a.E; g += blockDim.x) {
+        a.gcnt[g] = gcnt_s[g];
+        a.chunk_base[g] = goff_s[g];  // the only chunk starts at each expert's offset
+    }
+    if (a.segs != nullptr) single_gpu_items(a, goff_s, gcnt_s);
+}
+
+// Grid (router chunk of 16 tokens, column slice of kScatterCols).  Position of pair (t, k)
+// with expert e:
 //   chunk_base[c][e] + #{earlier tokens of the chunk that also chose e}
-// which is the stable (token-ordered) counting sort.  Then each token row is converted
-// to fp16 once and written to its K routed rows and its shared-expert row.
-__global__ __launch_bounds__(256) void scatter_gather_kernel(
+// which is the stable (token-ordered) counting sort (every slice recomputes it; slice 0
+// publishes slot_pos).  Then each token row slice is converted to fp16 once and written to
+// its K routed rows and its shared-expert row.
+constexpr int kScatterCols = 256;
+
+__global__ __launch_bounds__(128) void scatter_gather_kernel(
     const float* __restrict__ x, int T, int H, int E, int K, const int* __restrict__ topk_idx,
     const int* __restrict__ chunk_base, int* __restrict__ slot_pos, __half* __restrict__ xp_routed,
     __half* __restrict__ xp_shared) {
@@ -154,12 +182,12 @@ __global__ __launch_bounds__(256) void scatter_gather_kernel(
     __shared__ int spos[kRouterTok][8];
     const int c = blockIdx.x, t0 = c * kRouterTok, tid = threadIdx.x;
     const int nt = min(kRouterTok, T - t0);
-    if (tid < kRouterTok * 8) {
-        const int tt = tid >> 3, k = tid & 7;
+    {
+        const int tt = tid >> 3, k = tid & 7;  // 128 threads = 16 tokens x 8 ranks
         sidx[tt][k] = (tt < nt && k < K) ? topk_idx[(t0 + tt) * K + k] : -1;
     }
     __syncthreads();
-    if (tid < kRouterTok * 8) {
+    {
         const int tt = tid >> 3, k = tid & 7;
         if (tt < nt && k < K) {
             const int e = sidx[tt][k];
@@ -168,26 +196,27 @@ __global__ __launch_bounds__(256) void scatter_gather_kernel(
                 for (int kk = 0; kk < K; ++kk) rank += sidx[p][kk] == e;
             const int pos = chunk_base[c * E + e] + rank;
             spos[tt][k] = pos;
-            slot_pos[(t0 + tt) * K + k] = pos;
+            if (blockIdx.y == 0) slot_pos[(t0 + tt) * K + k] = pos;
         }
     }
     __syncthreads();
-    for (int tt = 0; tt < nt; ++tt) {
+    // 128 threads x 8 columns = 4 token rows of the slice per pass
+    const int j = blockIdx.y * kScatterCols + (tid & 31) * 8;
+    if (j >= H) return;
+    for (int tt = tid >> 5; tt < nt; tt += 4) {
         const float* xr = x + static_cast<size_t>(t0 + tt) * H;
-        for (int j = tid * 8; j < H; j += 256 * 8) {
-            const float4 a = *reinterpret_cast<const float4*>(xr + j);
-            const float4 b = *reinterpret_cast<const float4*>(xr + j + 4);
-            const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
-            const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
-            uint4 v;
-            v.x = *reinterpret_cast<const uint32_t*>(&h0);
-            v.y = *reinterpret_cast<const uint32_t*>(&h1);
-            v.z = *reinterpret_cast<const uint32_t*>(&h2);
-            v.w = *reinterpret_cast<const uint32_t*>(&h3);
-            for (int k = 0; k < K; ++k)
-                *reinterpret_cast<uint4*>(xp_routed + static_cast<size_t>(spos[tt][k]) * H + j) = v;
-            *reinterpret_cast<uint4*>(xp_shared + static_cast<size_t>(t0 + tt) * H + j) = v;
-        }
+        const float4 a = *reinterpret_cast<const float4*>(xr + j);
+        const float4 b = *reinterpret_cast<const float4*>(xr + j + 4);
+        const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+        const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+        uint4 v;
+        v.x = *reinterpret_cast<const uint32_t*>(&h0);
+        v.y = *reinterpret_cast<const uint32_t*>(&h1);
+        v.z = *reinterpret_cast<const uint32_t*>(&h2);
+        v.w = *reinterpret_cast<const uint32_t*>(&h3);
+        for (int k = 0; k < K; ++k)
+            *reinterpret_cast<uint4*>(xp_routed + static_cast<size_t>(spos[tt][k]) * H + j) = v;
+        *reinterpret_cast<uint4*>(xp_shared + static_cast<size_t>(t0 + tt) * H + j) = v;
     }
 }
 
@@ -215,6 +244,13 @@ cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, float* topk_w,
+                             int* topk_idx, const PlanArgs& a, cudaStream_t st) {
+    if (T > kRouterTok || a.n_chunks != 1) return cudaErrorInvalidValue;
+    topk_plan_kernel<<<1, 1024, 0, st>>>(logits, T, K, probs, topk_w, topk_idx, a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st) {
     items_kernel<<<1, 1024, 0, st>>>(a);
     return cudaGetLastError();
@@ -223,8 +259,8 @@ cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st) {
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
                                   const int* chunk_base, int* slot_pos, __half* xp_routed,
                                   __half* xp_shared, cudaStream_t st) {
-    const int blocks = (T + kRouterTok - 1) / kRouterTok;
-    scatter_gather_kernel<<<blocks, 256, 0, st>>>(x, T, H, E, K, topk_idx, chunk_base, slot_pos,
+    dim3 grid((T + kRouterTok - 1) / kRouterTok, (H + kScatterCols - 1) / kScatterCols);
+    scatter_gather_kernel<<<grid, 128, 0, st>>>(x, T, H, E, K, topk_idx, chunk_base, slot_pos,
                                                   xp_routed, xp_shared);
     return cudaGetLastError();
 }

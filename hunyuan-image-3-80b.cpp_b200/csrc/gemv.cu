@@ -28,6 +28,7 @@ namespace hymoe {
 namespace {
 
 constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kStageTiles = 2;  // k-tiles per pipeline stage (one barrier round each)
 constexpr int kGL = kGemvMaxRows + 1;  // row pitch (floats) of the result staging G
 
@@ -340,6 +341,164 @@ __global__ __launch_bounds__(kGemvThreads, 3) void gemv_kernel(const __grid_cons
     }
 }
 
+// ---- persistent streaming variant for items of at most 8 token rows (Q4_0 / Q8_0).
+//
+// One CTA per SM; the CTA takes items blockIdx.x, blockIdx.x + gridDim.x, ...  Warp w owns
+// k-tiles w, w + 8, ... of every item and streams them, one bulk copy of the weight tile and
+// one 8-row activation box per tile, through a private ring of R slots: no barrier is shared
+// between warps inside an item, and the ring runs on into the next item.  Each warp
+// accumulates all 128 rows of the tile (8 row groups, exact block scales); at the item's end
+// the 8 warp partials meet in shared memory and are summed in warp order (deterministic), and
+// the item's output is written.
+constexpr int kRedLd = 9;  // token pitch (floats) of the partial buffer: conflict-free sums
+
+template <int WT, int R>
+__global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
+    const __grid_constant__ GemvMaps maps, const int4* __restrict__ items, const int* __restrict__ n_items,
+    const uint8_t* const* __restrict__ wtiles, int n_ks, int glu, void* __restrict__ out, int out_ld,
+    int* err) {
+    constexpr int TB = tile_bytes(WT);
+    extern __shared__ uint8_t gsm_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* xbox = base;                                           // [8 warps][R][1024] (1024-aligned)
+    uint8_t* wbuf = base + kGemvWarps * R * 1024;                  // [8 warps][R][TB]
+    float* red = reinterpret_cast<float*>(wbuf + kGemvWarps * R * TB);  // [8][128][kRedLd]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + kGemvWarps * kTileRows * kRedLd);  // [8][R]
+    __shared__ int abort_flag;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gq = lane >> 2, c = lane & 3;
+    const int n_it = *n_items, G = gridDim.x;
+    const int per_item = warp < n_ks ? (n_ks - warp + kGemvWarps - 1) / kGemvWarps : 0;
+    const int my_items = static_cast<int>(blockIdx.x) < n_it ? (n_it - blockIdx.x + G - 1) / G : 0;
+    const int total = my_items * per_item;  // this warp's tiles
+    uint64_t* wb = bars + warp * R;
+    uint8_t* wx = xbox + warp * R * 1024;
+    uint8_t* ww = wbuf + static_cast<size_t>(warp) * R * TB;
+    if (lane == 0)
+        for (int r = 0; r < R; ++r) mbar_init(&wb[r], 1);
+    if (tid == 0) abort_flag = 0;
+    fence_mbar_init();
+    __syncthreads();
+
+    auto issue = [&](int q) {  // lane 0: tile q of this warp's stream
+        const int i = q / per_item, m = q - i * per_item;
+        const int4 it = items[blockIdx.x + i * G];
+        const int k = warp + kGemvWarps * m, slot = q % R;
+        mbar_arrive_expect_tx(&wb[slot], TB + 1024u);
+        bulk_load(ww + slot * TB, wtiles[it.x] + (static_cast<size_t>(it.y) * n_ks + k) * TB, TB, &wb[slot]);
+        tma_load_2d(wx + slot * 1024, &maps.x[0], &wb[slot], k * kTileK, it.z);
+    };
+    int issued = 0, done = 0;  // lane 0's stream positions
+    if (lane == 0)
+        for (; issued < min(R, total); ++issued) issue(issued);
+
+    const int tok_b = col_token<WT>(gq);
+    const int t0 = col_token<WT>(2 * c), t1 = col_token<WT>(2 * c + 1);
+    for (int i = 0; i < my_items; ++i) {
+        const int4 it = items[blockIdx.x + i * G];
+        float acc[8][4];
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[g][j] = 0.f;
+        bool failed = false;
+        for (int m = 0; m < per_item; ++m) {
+            const int q = i * per_item + m, slot = q % R;
+            int got = 1;
+            if (lane == 0) got = mbar_wait(&wb[slot], (q / R) & 1, err, DEVERR_TIMEOUT_DEQUANT) ? 1 : 0;
+            __syncwarp();
+            if (!__shfl_sync(0xffffffffu, got, 0)) {
+                failed = true;
+                break;
+            }
+            const uint8_t* tile = ww + slot * TB;
+            uint32_t bx[2][2][2];
+            x_frags<WT>(wx + slot * 1024 + 128 * tok_b, tok_b & 7, c, bx);
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+                uint32_t a[2][2][4];
+                float d[2][2];
+                tile_frags<WT, false>(tile, 16 * g + gq, c, a, d);
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    float blk[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma16816(blk, a[b][0], bx[b][0][0], bx[b][0][1]);
+                    mma16816(blk, a[b][1], bx[b][1][0], bx[b][1][1]);
+                    acc[g][0] = fmaf(d[b][0], blk[0], acc[g][0]);
+                    acc[g][1] = fmaf(d[b][0], blk[1], acc[g][1]);
+                    acc[g][2] = fmaf(d[b][1], blk[2], acc[g][2]);
+                    acc[g][3] = fmaf(d[b][1], blk[3], acc[g][3]);
+                }
+            }
+            __syncwarp();  // every lane is done with the slot
+            if (lane == 0) {
+                done = q + 1;
+                if (issued < total) issue(issued++);
+            }
+        }
+        if (failed && lane == 0) abort_flag = 1;
+        // this warp's partial -> red[warp]
+        float* rw = red + warp * kTileRows * kRedLd;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const int r0 = 16 * g + gq;
+            rw[r0 * kRedLd + t0] = acc[g][0];
+            rw[r0 * kRedLd + t1] = acc[g][1];
+            rw[(r0 + 8) * kRedLd + t0] = acc[g][2];
+            rw[(r0 + 8) * kRedLd + t1] = acc[g][3];
+        }
+        __syncthreads();
+        if (abort_flag) break;
+        const int nrows = min(it.w, 8), row0 = it.z, rb = it.y;
+        auto sum = [&](int r, int n) {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < kGemvWarps; ++w) v += red[(w * kTileRows + r) * kRedLd + n];
+            return v;
+        };
+        if (glu) {
+            __half* o = static_cast<__half*>(out);
+            for (int e = tid; e < kGluHalf * nrows; e += kGemvThreads) {
+                const int j = e % kGluHalf, n = e / kGluHalf;
+                o[static_cast<size_t>(row0 + n) * out_ld + rb * kGluHalf + j] =
+                    __float2half_rn(silu_mul(sum(j, n), sum(kGluHalf + j, n)));
+            }
+        } else {
+            float* o = static_cast<float*>(out);
+            for (int e = tid; e < kTileRows * nrows; e += kGemvThreads) {
+                const int r = e % kTileRows, n = e / kTileRows;
+                o[static_cast<size_t>(row0 + n) * out_ld + rb * kTileRows + r] = sum(r, n);
+            }
+        }
+        __syncthreads();  // red is free again
+    }
+    if (abort_flag) {
+        // Copies this warp issued but did not consume land before the exit (bounded waits).
+        if (lane == 0)
+            for (int q = done; q < issued; ++q) mbar_drain(&wb[q % R], (q / R) & 1);
+        __syncwarp();
+    }
+}
+
+template <int WT, int R>
+size_t stream_smem() {
+    return 1024 + static_cast<size_t>(kGemvWarps) * R * (1024 + tile_bytes(WT)) +
+           sizeof(float) * kGemvWarps * kTileRows * kRedLd + 8u * kGemvWarps * R;
+}
+
+template <int WT, int R>
+cudaError_t launch_stream(const GemvMaps& maps, const int4* items, const int* n_items, int n_sms,
+                          const uint8_t* const* wtiles, int n_ks, int glu, void* out, int out_ld, int* err,
+                          cudaStream_t st) {
+    const size_t smem = stream_smem<WT, R>();
+    cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<WT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    gemv_stream_kernel<WT, R><<<n_sms, kGemvThreads, smem, st>>>(maps, items, n_items, wtiles, n_ks, glu, out,
+                                                                 out_ld, err);
+    return cudaGetLastError();
+}
+
 // Stages per CTA: as many as fit in ~72 KB (three CTAs per SM), at least 2 and at most 4;
 // the ring must also hold the result staging G.
 template <int WT>
@@ -373,9 +532,13 @@ cudaError_t launch_t(const GemvMaps& maps, const int4* items, const int* n_items
 
 cudaError_t launch_gemv(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
                         const uint8_t* const* wtiles, int wtype, int n_ks, int glu, int max_rows,
-                        void* out, int out_ld, int* err, cudaStream_t st) {
+                        void* out, int out_ld, int* err, int n_sms, cudaStream_t st) {
     if (max_items <= 0) return cudaSuccess;
     if (max_rows < 1 || max_rows > kGemvMaxRows) return cudaErrorInvalidValue;
+    if (max_rows <= 8 && wtype == W_Q8_0)
+        return launch_stream<W_Q8_0, 2>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, err, st);
+    if (max_rows <= 8 && wtype == W_Q4_0)
+        return launch_stream<W_Q4_0, 3>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, err, st);
     switch (wtype) {
         case W_Q4_0: return launch_t<W_Q4_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, err, st);
         case W_Q8_0: return launch_t<W_Q8_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, err, st);

@@ -724,10 +724,12 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         };
         if (T > 0) {
             const int n_chunks = (T + kRouterTok - 1) / kRouterTok;
+            // T <= 16 (one router chunk): the top-K runs inside the plan launch.
+            const bool fused = n_chunks == 1;
             c->phase_begin();
             HY_CUDA(c, launch_router(dx, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
-                                     c->topk_w, c->topk_idx, c->chunk_counts, st));
-            c->phase_end(HYMOE_PHASE_ROUTER, 2);
+                                     c->topk_w, c->topk_idx, c->chunk_counts, !fused, st));
+            c->phase_end(HYMOE_PHASE_ROUTER, fused ? 1 : 2);
             PlanArgs pa{};
             pa.chunk_counts = c->chunk_counts;
             pa.n_chunks = n_chunks;
@@ -741,7 +743,10 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             pa.n_segs = c->n_segs;
             pa.items = items_args(gemv);
             c->phase_begin();
-            HY_CUDA(c, launch_plan(pa, st));
+            if (fused)
+                HY_CUDA(c, launch_topk_plan(dlog ? dlog : c->logits, T, K, dprob, c->topk_w, c->topk_idx, pa, st));
+            else
+                HY_CUDA(c, launch_plan(pa, st));
             c->phase_end(HYMOE_PHASE_PLAN);
             c->phase_begin();
             HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
@@ -831,11 +836,11 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             c->phase_begin();
             const int mr = static_cast<int>(std::max<size_t>(1, gemv_rows));
             HY_CUDA(c, launch_gemv(c->gmaps_xp, c->items_gu, c->n_items, max_it, L.d_gu_ptrs, L.wtype, H / kTileK,
-                                   1, mr, c->hbuf, I, c->err_word, st));
+                                   1, mr, c->hbuf, I, c->err_word, c->n_sms, st));
             c->phase_end(HYMOE_PHASE_GATE_UP);
             c->phase_begin();
             HY_CUDA(c, launch_gemv(c->gmaps_h, c->items_dn, c->n_items + 1, max_it, L.d_dn_ptrs, L.wtype,
-                                   I / kTileK, 0, mr, c->y, H, c->err_word, st));
+                                   I / kTileK, 0, mr, c->y, H, c->err_word, c->n_sms, st));
             c->phase_end(HYMOE_PHASE_DOWN);
         } else {
             GemmArgs ga{};

@@ -23,9 +23,10 @@ cudaError_t launch_synth_f32(float* dst, uint64_t n, uint64_t seed, uint64_t str
 // ---- router.cu
 constexpr int kRouterTok = 16;  // tokens per router CTA (= dispatch chunk)
 constexpr int kGemvMaxRows = 64; // token rows per GEMV work item
+// Logits, then (topk = true) the top-K kernel with per-chunk expert counts.
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
-                          int* topk_idx, int* chunk_counts, cudaStream_t st);
+                          int* topk_idx, int* chunk_counts, bool topk, cudaStream_t st);
 
 // ---- dispatch.cu
 constexpr int kMaxSegs = 80;  // >= E + 1 (E <= 64)
@@ -50,6 +51,9 @@ struct PlanArgs {
     ItemsArgs items;
 };
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
+// T <= kRouterTok (one chunk): top-K of every token and the plan in one launch.
+cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, float* topk_w,
+                             int* topk_idx, const PlanArgs& a, cudaStream_t st);
 
 cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st);
 
@@ -86,10 +90,11 @@ __host__ __device__ constexpr int gemv_box_rows(int i) { return 8 << i; }  // 8,
 struct GemvMaps {
     CUtensorMap x[kGemvBoxes];  // activation operand, fp16 [rows, K], box {64, gemv_box_rows(i)}, SW128
 };
-// max_rows: the largest item (<= kGemvMaxRows); it sizes the activation stages.
+// max_rows: the largest item (<= kGemvMaxRows); it sizes the activation stages.  Items of at
+// most 8 rows (Q4_0 / Q8_0) run on the persistent streaming variant with n_sms CTAs.
 cudaError_t launch_gemv(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
                         const uint8_t* const* wtiles, int wtype, int n_ks, int glu, int max_rows,
-                        void* out, int out_ld, int* err, cudaStream_t st);
+                        void* out, int out_ld, int* err, int n_sms, cudaStream_t st);
 
 // ---- combine.cu
 // out[t] = resid[t] + y_shared[t] + sum_k w[t,k] * y_routed[slot_pos[t,k]]

@@ -10,9 +10,11 @@
 // and adds in h order - the operations the reference performs - so the logits equal the
 // reference's bit for bit.  The add chain bounds a call at roughly 4 x H cycles; beyond
 // that the kernels are organised for operand reuse:
-//   router_logits_tiled_kernel (T > 8): CTA = 16 tokens x 32 experts, 128 threads with
+//   router_logits_tiled_kernel (T > 64): CTA = 16 tokens x 32 experts, 128 threads with
 //     2 tokens x 2 experts (4 independent chains) each; x and Wr slabs of 128 columns
 //     stream through a 3-stage cp.async ring in shared memory.
+//   router_logits_small_kernel (8 < T <= 64): CTA = 8 tokens x 8 experts, one chain per
+//     thread, deeper ring: the latency-bound chains spread over many CTAs.
 //   router_logits_decode_kernel (T <= 8): CTA = one expert; its router row and the T
 //     token rows are staged in shared memory once, then T threads run their chains.
 // router_topk_kernel: one warp per token (16 tokens = one dispatch chunk per CTA): softmax
@@ -23,18 +25,19 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "topk.cuh"
 
 namespace hymoe {
 
 namespace {
 
-constexpr int kMaxE = 64;
 constexpr int kTT = 16;     // tokens per tiled CTA
 constexpr int kTE = 32;     // experts per tiled CTA
 constexpr int kKC = 128;    // columns per stage
 constexpr int kLd = kKC + 4;  // padded smem row (floats): 16-byte rows offset by 4 banks
 constexpr int kStages = 3;
 constexpr int kDecodeMaxT = 8;
+constexpr int kSmallMaxT = 64;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
@@ -122,6 +125,8 @@ __global__ __launch_bounds__(128) void router_logits_tiled_kernel(
     put(ta + 1, ea + 16, a11, b1);
 }
 
+// T <= 8: CTA = one expert; its router row and the T token rows are staged in shared memory
+// once, then T threads run their chains without further synchronisation.
 __global__ __launch_bounds__(128) void router_logits_decode_kernel(
     const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
     const float* __restrict__ bias, float* __restrict__ logits) {
@@ -146,78 +151,75 @@ __global__ __launch_bounds__(128) void router_logits_decode_kernel(
     logits[static_cast<size_t>(t) * E + e] = acc;
 }
 
+// 8 < T <= 64: CTA = 8 tokens x 8 experts, 64 threads with one chain each (the chains are
+// latency-bound, so they are spread over (T / 8) x (E / 8) CTAs).  x and Wr slabs of 256
+// columns stream through a 6-stage cp.async ring.
+constexpr int kSmallTT = 8, kSmallTE = 8;
+constexpr int kSmallKC = 256, kSmallLd = kSmallKC + 4, kSmallStages = 6;
+
+__global__ __launch_bounds__(64) void router_logits_small_kernel(
+    const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
+    const float* __restrict__ bias, float* __restrict__ logits) {
+    extern __shared__ float4 rsm4[];
+    float* sm = reinterpret_cast<float*>(rsm4);
+    float* Xs = sm;                                 // [stages][kSmallTT][kSmallLd]
+    float* Ws = sm + kSmallStages * kSmallTT * kSmallLd;      // [stages][kSmallTE][kSmallLd]
+    const int tid = threadIdx.x;
+    const int t0 = blockIdx.x * kSmallTT, e0 = blockIdx.y * kSmallTE;
+    const int nt = min(kSmallTT, T - t0), ne = min(kSmallTE, E - e0);
+    const int tt = tid / kSmallTE, ee = tid % kSmallTE;
+    const int nst = (H + kSmallKC - 1) / kSmallKC;  // H is a multiple of 128
+
+    auto load_stage = [&](int st, int ks) {
+        float* xs = Xs + st * kSmallTT * kSmallLd;
+        float* ws = Ws + st * kSmallTE * kSmallLd;
+        const int c0 = ks * kSmallKC, q = min(kSmallKC, H - c0) / 4;  // float4 per row
+        for (int i = tid; i < nt * q; i += 64) {
+            const int r = i / q, c = (i % q) * 4;
+            cp_async16(xs + r * kSmallLd + c, x + static_cast<size_t>(t0 + r) * H + c0 + c);
+        }
+        for (int i = tid; i < ne * q; i += 64) {
+            const int r = i / q, c = (i % q) * 4;
+            cp_async16(ws + r * kSmallLd + c, Wr + static_cast<size_t>(e0 + r) * H + c0 + c);
+        }
+    };
+
+    float acc = 0.f;
+#pragma unroll
+    for (int s = 0; s < kSmallStages - 1; ++s) {
+        if (s < nst) load_stage(s, s);
+        cp_async_commit();
+    }
+    for (int ks = 0; ks < nst; ++ks) {
+        cp_async_wait<kSmallStages - 2>();
+        __syncthreads();
+        if (ks + kSmallStages - 1 < nst) load_stage((ks + kSmallStages - 1) % kSmallStages, ks + kSmallStages - 1);
+        cp_async_commit();
+        const int st = ks % kSmallStages;
+        const float* xr = Xs + st * kSmallTT * kSmallLd + tt * kSmallLd;
+        const float* wr = Ws + st * kSmallTE * kSmallLd + ee * kSmallLd;
+        const int ncol = min(kSmallKC, H - ks * kSmallKC);
+#pragma unroll 8
+        for (int k = 0; k < ncol; k += 4)
+            acc = chain4(acc, *reinterpret_cast<const float4*>(xr + k), *reinterpret_cast<const float4*>(wr + k));
+    }
+    cp_async_wait<0>();
+    if (tt < nt && ee < ne) {
+        const int t = t0 + tt, e = e0 + ee;
+        logits[static_cast<size_t>(t) * E + e] = bias != nullptr ? __fadd_rn(acc, bias[e]) : acc;
+    }
+}
+
 __global__ __launch_bounds__(32 * kRouterTok) void router_topk_kernel(
     const float* __restrict__ logits, int T, int E, int K, float* __restrict__ probs_out,
     float* __restrict__ topk_w, int* __restrict__ topk_idx, int* __restrict__ chunk_counts) {
     __shared__ float pbuf[kRouterTok][kMaxE];
     __shared__ int cnt[kMaxE];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     if (threadIdx.x < kMaxE) cnt[threadIdx.x] = 0;
     __syncthreads();
     const int t = blockIdx.x * kRouterTok + warp;
-    if (t < T) {
-        const bool v0 = lane < E, v1 = lane + 32 < E;
-        const float l0 = v0 ? logits[static_cast<size_t>(t) * E + lane] : -INFINITY;
-        const float l1 = v1 ? logits[static_cast<size_t>(t) * E + lane + 32] : -INFINITY;
-        float m = fmaxf(l0, l1);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float p0 = v0 ? expf(__fsub_rn(l0, m)) : 0.f;
-        float p1 = v1 ? expf(__fsub_rn(l1, m)) : 0.f;
-        pbuf[warp][lane] = p0;
-        pbuf[warp][lane + 32] = p1;
-        __syncwarp();
-        float s = 0.f;
-        if (lane == 0)
-            for (int ee = 0; ee < E; ++ee) s = __fadd_rn(s, pbuf[warp][ee]);
-        s = __shfl_sync(0xffffffffu, s, 0);
-        p0 = __fdiv_rn(p0, s);
-        p1 = __fdiv_rn(p1, s);
-        if (probs_out != nullptr) {
-            if (v0) probs_out[static_cast<size_t>(t) * E + lane] = p0;
-            if (v1) probs_out[static_cast<size_t>(t) * E + lane + 32] = p1;
-        }
-        bool taken0 = !v0, taken1 = !v1;
-        float selp = 0.f;  // lane k keeps the k-th selection
-        int sele = 0;
-        for (int k = 0; k < K; ++k) {
-            float bv;
-            int bi;
-            if (!taken0 && (taken1 || p0 >= p1)) {
-                bv = p0;
-                bi = lane;
-            } else if (!taken1) {
-                bv = p1;
-                bi = lane + 32;
-            } else {
-                bv = -1.f;
-                bi = 1 << 30;
-            }
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
-            }
-            if (bi == lane) taken0 = true;
-            if (bi == lane + 32) taken1 = true;
-            if (lane == k) {
-                selp = bv;
-                sele = bi;
-            }
-        }
-        // renormalise in rank order: sum_{k<K} p_k sequentially
-        float sw = 0.f;
-        for (int k = 0; k < K; ++k) sw = __fadd_rn(sw, __shfl_sync(0xffffffffu, selp, k));
-        if (lane < K) {
-            topk_w[static_cast<size_t>(t) * K + lane] = __fdiv_rn(selp, sw);
-            topk_idx[static_cast<size_t>(t) * K + lane] = sele;
-            atomicAdd(&cnt[sele], 1);
-        }
-    }
+    if (t < T) topk_token(logits, t, E, K, probs_out, topk_w, topk_idx, pbuf[warp], cnt);
     __syncthreads();
     if (threadIdx.x < E) chunk_counts[static_cast<size_t>(blockIdx.x) * E + threadIdx.x] = cnt[threadIdx.x];
 }
@@ -226,7 +228,7 @@ __global__ __launch_bounds__(32 * kRouterTok) void router_topk_kernel(
 
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
-                          int* topk_idx, int* chunk_counts, cudaStream_t st) {
+                          int* topk_idx, int* chunk_counts, bool topk, cudaStream_t st) {
     cudaError_t e;
     if (T <= kDecodeMaxT) {
         const size_t smem = sizeof(float) * static_cast<size_t>(H) * (1 + T);
@@ -234,6 +236,13 @@ cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, 
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         router_logits_decode_kernel<<<E, 128, smem, st>>>(x, T, H, Wr, E, bias, logits);
+    } else if (T <= kSmallMaxT) {
+        const size_t smem = sizeof(float) * kSmallStages * (kSmallTT + kSmallTE) * kSmallLd;
+        e = cudaFuncSetAttribute(router_logits_small_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        dim3 g((T + kSmallTT - 1) / kSmallTT, (E + kSmallTE - 1) / kSmallTE);
+        router_logits_small_kernel<<<g, 64, smem, st>>>(x, T, H, Wr, E, bias, logits);
     } else {
         const size_t smem = sizeof(float) * kStages * (kTT + kTE) * kLd;
         e = cudaFuncSetAttribute(router_logits_tiled_kernel,
@@ -243,7 +252,7 @@ cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, 
         router_logits_tiled_kernel<<<g, 128, smem, st>>>(x, T, H, Wr, E, bias, logits);
     }
     e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || !topk) return e;
     router_topk_kernel<<<(T + kRouterTok - 1) / kRouterTok, 32 * kRouterTok, 0, st>>>(
         logits, T, E, K, probs, topk_w, topk_idx, chunk_counts);
     return cudaGetLastError();

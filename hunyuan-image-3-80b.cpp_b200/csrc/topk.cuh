@@ -1,0 +1,111 @@
+// topk.cuh — per-token routing step shared by the top-K kernel and the fused decode
+// top-K + plan kernel: softmax with the sum taken in expert order, K rounds of warp-shuffle
+// arg-max (ties to the lower expert), renormalisation in rank order (src/attention.cpp:224-275).
+// Only expf may differ from the host libm in the last place.
+#pragma once
+
+#include <math.h>
+
+#include "common.cuh"
+
+namespace hymoe {
+
+constexpr int kMaxE = 64;
+
+// One warp routes token t.  pbuf: this warp's kMaxE floats of shared memory.  cnt: shared
+// per-expert counters of the caller's chunk (incremented for the token's K experts).
+__device__ __forceinline__ void topk_token(const float* __restrict__ logits, int t, int E, int K,
+                                           float* __restrict__ probs_out, float* __restrict__ topk_w,
+                                           int* __restrict__ topk_idx, float* pbuf, int* cnt) {
+    const int lane = threadIdx.x & 31;
+    const bool v0 = lane < E, v1 = lane + 32 < E;
+    const float l0 = v0 ? logits[static_cast<size_t>(t) * E + lane] : -INFINITY;
+    const float l1 = v1 ? logits[static_cast<size_t>(t) * E + lane + 32] : -INFINITY;
+    float m = fmaxf(l0, l1);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float p0 = v0 ? expf(__fsub_rn(l0, m)) : 0.f;
+    float p1 = v1 ? expf(__fsub_rn(l1, m)) : 0.f;
+    pbuf[lane] = p0;
+    pbuf[lane + 32] = p1;
+    __syncwarp();
+    float s = 0.f;
+    if (lane == 0)
+        for (int ee = 0; ee < E; ++ee) s = __fadd_rn(s, pbuf[ee]);
+    s = __shfl_sync(0xffffffffu, s, 0);
+    p0 = __fdiv_rn(p0, s);
+    p1 = __fdiv_rn(p1, s);
+    if (probs_out != nullptr) {
+        if (v0) probs_out[static_cast<size_t>(t) * E + lane] = p0;
+        if (v1) probs_out[static_cast<size_t>(t) * E + lane + 32] = p1;
+    }
+    bool taken0 = !v0, taken1 = !v1;
+    float selp = 0.f;  // lane k keeps the k-th selection
+    int sele = 0;
+    for (int k = 0; k < K; ++k) {
+        float bv;
+        int bi;
+        if (!taken0 && (taken1 || p0 >= p1)) {
+            bv = p0;
+            bi = lane;
+        } else if (!taken1) {
+            bv = p1;
+            bi = lane + 32;
+        } else {
+            bv = -1.f;
+            bi = 1 << 30;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bi == lane) taken0 = true;
+        if (bi == lane + 32) taken1 = true;
+        if (lane == k) {
+            selp = bv;
+            sele = bi;
+        }
+    }
+    // renormalise in rank order: sum_{k<K} p_k sequentially
+    float sw = 0.f;
+    for (int k = 0; k < K; ++k) sw = __fadd_rn(sw, __shfl_sync(0xffffffffu, selp, k));
+    if (lane < K) {
+        topk_w[static_cast<size_t>(t) * K + lane] = __fdiv_rn(selp, sw);
+        topk_idx[static_cast<size_t>(t) * K + lane] = sele;
+        atomicAdd(&cnt[sele], 1);
+    }
+}
+
+// Exclusive prefix sum of n <= 96 ints held in shared memory (in place, total returned in
+// out_total), computed by the calling warp (all 32 lanes).
+__device__ __forceinline__ int warp_exclusive_scan(int* v, int n) {
+    const int lane = threadIdx.x & 31;
+    int a[3], loc = 0;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        const int idx = 3 * lane + i;
+        a[i] = idx < n ? v[idx] : 0;
+        loc += a[i];
+    }
+    int inc = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += u;
+    }
+    int run = inc - loc;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        const int idx = 3 * lane + i;
+        if (idx < n) v[idx] = run;
+        run += a[i];
+    }
+    return __shfl_sync(0xffffffffu, inc, 31);
+}
+
+}  // namespace hymoe

@@ -162,8 +162,8 @@ hymoe_status hymoe_forward(hymoe_ctx* ctx, uint32_t layer, const float* x,
  * brackets each phase with CUDA events on the context's stream.  No reference
  * counterpart (the reference has no timers). */
 enum {
-    HYMOE_PHASE_ROUTER = 0,   /* router GEMV + softmax + top-K               */
-    HYMOE_PHASE_PLAN = 1,     /* prefix scan + work lists                    */
+    HYMOE_PHASE_ROUTER = 0,   /* router GEMV (+ softmax + top-K when T > 16) */
+    HYMOE_PHASE_PLAN = 1,     /* prefix scan + work lists (+ top-K, T <= 16) */
     HYMOE_PHASE_DISPATCH = 2, /* scatter / gather of token rows              */
     HYMOE_PHASE_GATE_UP = 3,  /* grouped gate_up GEMM + SwiGLU               */
     HYMOE_PHASE_DOWN = 4,     /* grouped down GEMM                           */
