@@ -39,6 +39,7 @@ enum DevErr : int {
     DEVERR_TIMEOUT_MMA = 4,
     DEVERR_TIMEOUT_EPILOGUE = 8,
     DEVERR_BAD_ITEM = 16,
+    DEVERR_TIMEOUT_PEER = 32,  // a peer GPU's flag did not arrive in time
 };
 
 // ------------------------------------------------------------------ PTX wrappers

@@ -223,14 +223,14 @@ __global__ __launch_bounds__(128) void scatter_gather_kernel(
 // Expert-parallel receive segments from the gathered count matrix C[N][E]: the shared
 // expert over the local rows first, then (source s, local expert le) runs in source-major
 // order starting at row T.  Single thread: at most E + 1 segments.
-__global__ void ep_segments_kernel(const int* __restrict__ C, int N, int rank, int el, int E,
+__global__ void ep_segments_kernel(const int* __restrict__ C, int ld, int N, int rank, int el,
                                    int T, int4* __restrict__ segs, int* __restrict__ n_segs) {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     segs[0] = make_int4(el, 0, T, 0);
     int row = T, n = 1;
     for (int s = 0; s < N; ++s)
         for (int le = 0; le < el; ++le) {
-            const int cnt = C[s * E + rank * el + le];
+            const int cnt = C[s * ld + rank * el + le];
             segs[n++] = make_int4(le, row, cnt, 0);
             row += cnt;
         }
@@ -265,9 +265,10 @@ cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, co
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_segments(const int* C, int N, int rank, int el, int E, int T, int4* segs,
+cudaError_t launch_ep_segments(const int* C, int ld, int N, int rank, int el, int E, int T, int4* segs,
                                int* n_segs, cudaStream_t st) {
-    ep_segments_kernel<<<1, 32, 0, st>>>(C, N, rank, el, E, T, segs, n_segs);
+    (void)E;
+    ep_segments_kernel<<<1, 32, 0, st>>>(C, ld, N, rank, el, T, segs, n_segs);
     return cudaGetLastError();
 }
 

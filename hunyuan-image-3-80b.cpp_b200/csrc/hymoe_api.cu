@@ -147,6 +147,15 @@ struct hymoe_ctx {
     cudaEvent_t ev_counts = nullptr;
     double ep_timeout_s = 60.0;
 
+    // expert parallelism over NVLink peer memory (the default transport; HYMOE_EP_TRANSPORT=nccl
+    // selects the NCCL send/recv exchange instead)
+    bool p2p = false;
+    EpPeers peers{};
+    int* ep_meta = nullptr;             // this rank's flags + count matrix
+    unsigned int* done_ctas = nullptr;  // dispatch completion counter
+    uint32_t epoch = 0;                 // calls made; flags carry it
+    std::vector<void*> ipc_opened;
+
     std::map<GraphKey, cudaGraphExec_t> graphs;  // HYMOE_USE_GRAPH replays
     void clear_graphs() {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
@@ -381,6 +390,112 @@ const char* hymoe_last_error(const hymoe_ctx* ctx) {
     return ctx ? ctx->err.c_str() : g_create_error.c_str();
 }
 
+// Maps every rank's xp, y and metadata block into this process (CUDA IPC; the handles travel
+// through the communicator).  Every rank must own a distinct GPU and the same max_tokens.  The
+// ranks agree on the outcome: either all use peer memory or all keep the NCCL exchange.
+hymoe_status ep_p2p_setup(hymoe_ctx* c) {
+    const int N = c->cfg.ep_size, me = c->cfg.ep_rank;
+    const size_t meta_ints = kEpCountOff + static_cast<size_t>(kEpMaxRanks) * (c->E + 1);
+    HY_CUDA(c, dalloc(&c->ep_meta, meta_ints));
+    HY_CUDA(c, cudaMemset(c->ep_meta, 0, meta_ints * sizeof(int)));
+    HY_CUDA(c, dalloc(&c->done_ctas, 1));
+    HY_CUDA(c, cudaMemset(c->done_ctas, 0, sizeof(unsigned int)));
+    struct Rec {
+        unsigned char uuid[16];
+        uint32_t max_tokens, ok, pad[2];
+        cudaIpcMemHandle_t h[3];
+    };
+    static_assert(sizeof(Rec) <= 256, "record");
+    Rec mine{};
+    cudaDeviceProp prop{};
+    HY_CUDA(c, cudaGetDeviceProperties(&prop, c->cfg.device));
+    memcpy(mine.uuid, &prop.uuid, 16);
+    mine.max_tokens = c->cfg.max_tokens;
+    mine.ok = 1;
+    if (cudaIpcGetMemHandle(&mine.h[0], c->xp) != cudaSuccess ||
+        cudaIpcGetMemHandle(&mine.h[1], c->y) != cudaSuccess ||
+        cudaIpcGetMemHandle(&mine.h[2], c->ep_meta) != cudaSuccess) {
+        cudaGetLastError();
+        mine.ok = 0;
+    }
+    char* dbuf = nullptr;
+    HY_CUDA(c, dalloc(&dbuf, 256 * (N + 1)));
+    std::vector<Rec> recs(N);
+    auto gather = [&]() -> hymoe_status {
+        HY_CUDA(c, cudaMemcpy(dbuf, &mine, sizeof(Rec), cudaMemcpyHostToDevice));
+        ncclResult_t r = ncclAllGather(dbuf, dbuf + 256, 256, ncclChar, c->comm, c->stream);
+        if (r != ncclSuccess && r != ncclInProgress)
+            return c->fail(HYMOE_ERR_NCCL, "ncclAllGather(peer handles): %s", ncclGetErrorString(r));
+        hymoe_status s2 = ep_poll(c, "peer handle exchange");
+        if (s2 != HYMOE_OK) return s2;
+        cudaEvent_t ev = c->take_event();
+        HY_CUDA(c, cudaEventRecord(ev, c->stream));
+        s2 = ep_wait_event(c, ev, "peer handle exchange");
+        c->ev_pool.push_back(ev);
+        if (s2 != HYMOE_OK) return s2;
+        for (int s = 0; s < N; ++s)
+            HY_CUDA(c, cudaMemcpy(&recs[s], dbuf + 256 * (s + 1), sizeof(Rec), cudaMemcpyDeviceToHost));
+        return HYMOE_OK;
+    };
+    hymoe_status st = gather();
+    if (st != HYMOE_OK) {
+        cudaFree(dbuf);
+        return st;
+    }
+    for (int s = 0; s < N; ++s) {
+        if (recs[s].max_tokens != c->cfg.max_tokens) {
+            cudaFree(dbuf);
+            return c->fail(HYMOE_ERR_INVALID_ARG, "rank %d has max_tokens %u, rank %d has %u (must be one job-wide bound)",
+                           s, recs[s].max_tokens, me, c->cfg.max_tokens);
+        }
+        for (int u = 0; u < s; ++u)
+            if (memcmp(recs[s].uuid, recs[u].uuid, 16) == 0) {
+                cudaFree(dbuf);
+                return c->fail(HYMOE_ERR_UNSUPPORTED, "ranks %d and %d run on the same GPU; expert parallelism "
+                               "needs one GPU per rank", u, s);
+            }
+    }
+    bool all_ok = true;
+    for (int s = 0; s < N; ++s) all_ok = all_ok && recs[s].ok;
+    EpPeers P{};
+    P.xp[me] = c->xp;
+    P.y[me] = c->y;
+    P.meta[me] = c->ep_meta;
+    for (int s = 0; s < N && all_ok && mine.ok; ++s) {
+        if (s == me) continue;
+        void* ptr[3] = {nullptr, nullptr, nullptr};
+        for (int i = 0; i < 3; ++i) {
+            if (cudaIpcOpenMemHandle(&ptr[i], recs[s].h[i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                mine.ok = 0;
+                break;
+            }
+            c->ipc_opened.push_back(ptr[i]);
+        }
+        P.xp[s] = static_cast<__half*>(ptr[0]);
+        P.y[s] = static_cast<float*>(ptr[1]);
+        P.meta[s] = static_cast<int*>(ptr[2]);
+    }
+    // second round: every rank learns whether every rank mapped every peer
+    if (all_ok) {
+        st = gather();
+        if (st != HYMOE_OK) {
+            cudaFree(dbuf);
+            return st;
+        }
+        for (int s = 0; s < N; ++s) all_ok = all_ok && recs[s].ok;
+    }
+    cudaFree(dbuf);
+    if (!all_ok) {  // keep the NCCL exchange
+        for (void* p : c->ipc_opened) cudaIpcCloseMemHandle(p);
+        c->ipc_opened.clear();
+        return HYMOE_OK;
+    }
+    c->peers = P;
+    c->p2p = true;
+    return HYMOE_OK;
+}
+
 hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     g_create_error.clear();
     if (!cfg || !out) {
@@ -497,6 +612,11 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
             return bail(c->fail(HYMOE_ERR_NCCL, "ncclCommInitRankConfig: %s", ncclGetErrorString(r)));
         st = ep_poll(c, "joining the expert-parallel communicator");
         if (st != HYMOE_OK) return bail(st);
+        const char* tr = getenv("HYMOE_EP_TRANSPORT");
+        if (N <= kEpMaxRanks && !(tr && strcmp(tr, "nccl") == 0)) {
+            st = ep_p2p_setup(c);
+            if (st != HYMOE_OK) return bail(st);
+        }
     }
     *out = c;
     return HYMOE_OK;
@@ -505,6 +625,19 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
 void hymoe_destroy(hymoe_ctx* c) {
     if (!c) return;
     cudaSetDevice(c->cfg.device);
+    if (c->p2p && c->comm && !c->comm_broken) {
+        // Peers may still read this rank's y (their combine) or write its xp: a bounded barrier
+        // over the communicator orders the frees after every rank's last call.
+        const ncclResult_t r = ncclAllReduce(c->gcnt, c->gcnt, 1, ncclInt32, ncclSum, c->comm, c->stream);
+        if ((r == ncclSuccess || r == ncclInProgress) && ep_poll(c, "destroy barrier") == HYMOE_OK) {
+            cudaEvent_t ev = c->take_event();
+            cudaEventRecord(ev, c->stream);
+            if (ep_wait_event(c, ev, "destroy barrier") != HYMOE_OK) c->comm_broken = true;
+            c->ev_pool.push_back(ev);
+        } else {
+            c->comm_broken = true;
+        }
+    }
     if (c->own_stream) cudaStreamSynchronize(c->own_stream);
     for (auto& L : c->layers) free_layer(L);
     cudaFree(c->x_dev);
@@ -531,6 +664,9 @@ void hymoe_destroy(hymoe_ctx* c) {
         if (c->comm_broken) ncclCommAbort(c->comm);
         else ncclCommDestroy(c->comm);
     }
+    for (void* p : c->ipc_opened) cudaIpcCloseMemHandle(p);
+    cudaFree(c->ep_meta);
+    cudaFree(c->done_ctas);
     cudaFree(c->xp_send);
     cudaFree(c->y_ret);
     cudaFree(c->C_dev);
@@ -568,6 +704,7 @@ hymoe_status hymoe_synchronize(hymoe_ctx* c) {
     HY_CUDA(c, cudaMemcpy(&word, c->err_word, sizeof(int), cudaMemcpyDeviceToHost));
     if (word != 0) {
         cudaMemset(c->err_word, 0, sizeof(int));
+        if (word & DEVERR_TIMEOUT_PEER) c->comm_broken = true;
         return c->fail(HYMOE_ERR_TIMEOUT, "device-side bounded wait expired (code 0x%x)", word);
     }
     return HYMOE_OK;
@@ -703,6 +840,9 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     // A rank with no tokens still takes part in every collective of the exchange.
     if (T == 0 && !ep) return host ? hymoe_synchronize(c) : HYMOE_OK;
 
+    const bool p2p = ep && c->p2p;
+    const uint32_t epoch = p2p ? ++c->epoch : 0;
+    const uint64_t budget_ns = static_cast<uint64_t>(c->ep_timeout_s * 1e9);
     auto device_part = [&]() -> hymoe_status {
         // Decode regime: every group has at most kGemvMaxRows rows (on one GPU a group has
         // at most T rows: the shared expert T, a routed expert at most one row per token).
@@ -748,17 +888,35 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             else
                 HY_CUDA(c, launch_plan(pa, st));
             c->phase_end(HYMOE_PHASE_PLAN);
-            c->phase_begin();
-            HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
-                                             ep ? c->xp_send : c->xp + static_cast<size_t>(T) * H,
-                                             c->xp, st));
-            c->phase_end(HYMOE_PHASE_DISPATCH);
+            if (!p2p) {  // peer-memory dispatch writes the rows straight to their owners
+                c->phase_begin();
+                HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
+                                                 ep ? c->xp_send : c->xp + static_cast<size_t>(T) * H,
+                                                 c->xp, st));
+                c->phase_end(HYMOE_PHASE_DISPATCH);
+            }
         } else {
             HY_CUDA(c, cudaMemsetAsync(c->gcnt, 0, sizeof(int) * E, st));
         }
 
         std::vector<size_t> send_cnt(N, 0), send_off(N, 0), recv_cnt(N, 0), recv_off(N, 0);
-        if (ep) {
+        if (p2p) {
+            // Counts to every rank, rows straight into their owners' matrices, then wait until
+            // every rank's rows have landed here (bounded device-side waits).
+            c->phase_begin();
+            HY_CUDA(c, launch_ep_counts(c->peers, N, rank, E, T, c->gcnt, epoch, budget_ns, c->err_word, st));
+            if (T > 0)
+                HY_CUDA(c, launch_ep_scatter(c->peers, N, rank, E, el, T, H, K, dx, c->topk_idx, c->chunk_base,
+                                             c->goff, c->slot_pos, c->done_ctas, epoch, st));
+            else
+                HY_CUDA(c, launch_ep_raise(c->peers, N, rank, kEpFlagDeliver, epoch, st));
+            HY_CUDA(c, launch_ep_wait(c->peers, N, rank, kEpFlagDeliver, epoch, budget_ns, c->err_word, st));
+            HY_CUDA(c, launch_ep_segments(c->ep_meta + kEpCountOff, E + 1, N, rank, el, E, T, c->segs, c->n_segs,
+                                          st));
+            c->phase_end(HYMOE_PHASE_EP_DISPATCH, 4);
+            // Received counts stay on the device: size the decode kernel for full 64-row items.
+            gemv_rows = kGemvMaxRows;
+        } else if (ep) {
             // Count exchange: every rank learns how many rows each rank sends to each expert.
             c->phase_begin();
             ncclResult_t r = ncclAllGather(c->gcnt, c->C_dev, E, ncclInt32, c->comm, st);
@@ -820,7 +978,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
                 return c->fail(HYMOE_ERR_NCCL, "token exchange: %s", ncclGetErrorString(r));
             s2 = ep_poll(c, "token exchange");
             if (s2 != HYMOE_OK) return s2;
-            HY_CUDA(c, launch_ep_segments(c->C_dev, N, rank, el, E, T, c->segs, c->n_segs, st));
+            HY_CUDA(c, launch_ep_segments(c->C_dev, E, N, rank, el, E, T, c->segs, c->n_segs, st));
             c->phase_end(HYMOE_PHASE_EP_DISPATCH, 2);
         }
 
@@ -829,7 +987,8 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             HY_CUDA(c, launch_items(items_args(gemv), st));
             c->phase_end(HYMOE_PHASE_PLAN);
         }
-        const size_t rows_in_use = ep ? recv_off[N - 1] + recv_cnt[N - 1] : static_cast<size_t>(T) * (K + 1);
+        const size_t rows_in_use = p2p ? c->rows_cap
+                                   : ep ? recv_off[N - 1] + recv_cnt[N - 1] : static_cast<size_t>(T) * (K + 1);
         if (gemv) {
             const int max_it = static_cast<int>(std::min<size_t>(
                 c->max_items, static_cast<size_t>(tiles_gu) * ((rows_in_use + kGemvMaxRows - 1) / kGemvMaxRows + kMaxSegs)));
@@ -871,7 +1030,17 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         }
 
         const float* y_routed = c->y + static_cast<size_t>(T) * H;
-        if (ep) {
+        if (p2p) {
+            // Results ready here; the combine reads every routed result from its owner's y.
+            c->phase_begin();
+            HY_CUDA(c, launch_ep_raise(c->peers, N, rank, kEpFlagReady, epoch, st));
+            if (T > 0)
+                HY_CUDA(c, launch_ep_combine(c->peers, N, rank, el, c->topk_idx, c->slot_pos, c->topk_w, dres, dout,
+                                             T, H, K, epoch, budget_ns, c->err_word, st));
+            else  // no tokens to combine: still wait, so that the next call's writes follow every owner's GEMMs
+                HY_CUDA(c, launch_ep_wait(c->peers, N, rank, kEpFlagReady, epoch, budget_ns, c->err_word, st));
+            c->phase_end(HYMOE_PHASE_EP_COMBINE, 2);
+        } else if (ep) {
             // Routed results back to the ranks their tokens came from (fp32, H per row).
             c->phase_begin();
             ncclGroupStart();
@@ -890,9 +1059,11 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             y_routed = c->y_ret;
         }
         if (T > 0) {
-            c->phase_begin();
-            HY_CUDA(c, launch_combine(c->y, y_routed, c->slot_pos, c->topk_w, dres, dout, T, H, K, st));
-            c->phase_end(HYMOE_PHASE_COMBINE);
+            if (!p2p) {
+                c->phase_begin();
+                HY_CUDA(c, launch_combine(c->y, y_routed, c->slot_pos, c->topk_w, dres, dout, T, H, K, st));
+                c->phase_end(HYMOE_PHASE_COMBINE);
+            }
             if (dbg) {
                 const cudaMemcpyKind kd = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
                 if (dbg->topk_weights)

@@ -60,8 +60,32 @@ cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st);
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
                                   const int* chunk_base, int* slot_pos, __half* xp_routed,
                                   __half* xp_shared, cudaStream_t st);
-cudaError_t launch_ep_segments(const int* C, int N, int rank, int el, int E, int T, int4* segs,
+// C: [N][ld] per-expert counts of every source rank (ld >= E).
+cudaError_t launch_ep_segments(const int* C, int ld, int N, int rank, int el, int E, int T, int4* segs,
                                int* n_segs, cudaStream_t st);
+
+// ---- ep_p2p.cu (expert-parallel dispatch / combine over NVLink peer memory)
+constexpr int kEpMaxRanks = 8;
+// Metadata block of every rank (ints): flags [count | deliver | ready][kEpMaxRanks], then the
+// count matrix [kEpMaxRanks][E + 1] (E per-expert pair counts + the source's token count).
+constexpr int kEpFlagCount = 0, kEpFlagDeliver = kEpMaxRanks, kEpFlagReady = 2 * kEpMaxRanks;
+constexpr int kEpCountOff = 3 * kEpMaxRanks;
+struct EpPeers {  // every rank's buffers as mapped in this process (own entry: local)
+    __half* xp[kEpMaxRanks];
+    float* y[kEpMaxRanks];
+    int* meta[kEpMaxRanks];
+};
+cudaError_t launch_ep_counts(const EpPeers& p, int N, int me, int E, int T, const int* gcnt, uint32_t epoch,
+                             uint64_t budget_ns, int* err, cudaStream_t st);
+cudaError_t launch_ep_scatter(const EpPeers& p, int N, int me, int E, int el, int T, int H, int K, const float* x,
+                              const int* topk_idx, const int* chunk_base, const int* goff, int* slot_pos,
+                              unsigned int* done_ctas, uint32_t epoch, cudaStream_t st);
+cudaError_t launch_ep_wait(const EpPeers& p, int N, int me, int flag_off, uint32_t epoch, uint64_t budget_ns,
+                           int* err, cudaStream_t st);
+cudaError_t launch_ep_raise(const EpPeers& p, int N, int me, int flag_off, uint32_t epoch, cudaStream_t st);
+cudaError_t launch_ep_combine(const EpPeers& p, int N, int me, int el, const int* topk_idx, const int* slot_pos,
+                              const float* topk_w, const float* resid, float* out, int T, int H, int K,
+                              uint32_t epoch, uint64_t budget_ns, int* err, cudaStream_t st);
 
 // ---- gemm_tc.cu (tcgen05 grouped GEMM, 2-SM pairs)
 constexpr int kNumBoxes = 3;

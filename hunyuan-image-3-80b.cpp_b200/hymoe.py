@@ -20,6 +20,7 @@ USE_GRAPH = 2
 
 STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OOM", 4: "UNSUPPORTED", 5: "NCCL",
           6: "TIMEOUT", 7: "STATE"}
+STATUS_TIMEOUT = 6
 
 # Every function include/hymoe.h declares.
 EXPORTS = ["hymoe_version", "hymoe_nccl_unique_id", "hymoe_create", "hymoe_destroy",

@@ -1,5 +1,7 @@
 """Expert-parallel GPU tests (2+ GPUs): one child process per GPU; rank r owns experts
-[r*E/N, (r+1)*E/N), receives the rows routed to them over NCCL and sends the results back.
+[r*E/N, (r+1)*E/N) and receives the rows routed to them.  Both transports run: peer memory
+(rows written straight into the owners' matrices, results read from them by the combine)
+and the NCCL send/recv exchange (HYMOE_EP_TRANSPORT=nccl).
 
 Every output row's arithmetic is independent of how rows are tiled, so when both runs use
 the tensor-core path the expert-parallel output must be bit-identical to the single-GPU
@@ -32,8 +34,9 @@ def _layer(orc):
     return host_layer(orc, SEED, 0, H, I, E, WT)
 
 
-def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q):
+def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p"):
     import sys
+    os.environ["HYMOE_EP_TRANSPORT"] = transport
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [os.path.join(root, "oracle"), os.path.join(root, "hunyuan-image-3-80b.cpp_b200"),
                     os.path.dirname(os.path.abspath(__file__))]
@@ -60,13 +63,14 @@ def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q):
         q.put((rank, f"error: {e!r}", None))
 
 
-def _run_ep(world, tokens_per_rank):
+def _run_ep(world, tokens_per_rank, transport="p2p"):
     import hymoe
     nccl_id = hymoe.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     max_tokens = max(16, max(max(t) for t in tokens_per_rank))  # job-wide bound
-    procs = [ctx.Process(target=_ep_worker, args=(r, world, nccl_id, tokens_per_rank[r], max_tokens, q))
+    procs = [ctx.Process(target=_ep_worker,
+                         args=(r, world, nccl_id, tokens_per_rank[r], max_tokens, q, transport))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -82,11 +86,12 @@ def _run_ep(world, tokens_per_rank):
 
 
 @pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
 @pytest.mark.parametrize("tokens", [[[200, 3], [150, 0]], [[64], [5]], [[300], [300]]])
-def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens):
+def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens, transport):
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     world = 2
-    res = _run_ep(world, tokens)
+    res = _run_ep(world, tokens, transport)
     import hymoe
     lay = _layer(orc)
     ncalls = len(tokens[0])
@@ -112,3 +117,63 @@ def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens):
                                     lay["edn_f"], K, I, bias=bias)
                 assert rel_l2(ep_out["out"], o["out"]) <= REL_L2_TOL
     single.close()
+
+
+def _timeout_worker(rank, world, nccl_id, q, go):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [os.path.join(root, "oracle"), os.path.join(root, "hunyuan-image-3-80b.cpp_b200"),
+                    os.path.dirname(os.path.abspath(__file__))]
+    os.environ["HYMOE_EP_TRANSPORT"] = "p2p"
+    os.environ["HYMOE_EP_TIMEOUT_S"] = "2"
+    try:
+        import oracle as O2
+        import hymoe
+        orc = O2.Oracle()
+        lay = host_layer(orc, SEED, 0, H, I, E, WT)
+        el = E // world
+        mine = range(rank * el, (rank + 1) * el)
+        egu = [lay["egu"][e] if e in mine else None for e in range(E)]
+        edn = [lay["edn"][e] if e in mine else None for e in range(E)]
+        m = hymoe.MoE(H, I, E, K, 1, 32, device=rank, ep_rank=rank, ep_size=world, nccl_id=nccl_id)
+        m.load_layer(0, lay["router"], lay["sgu"], lay["sdn"], egu, edn, WT)
+        x = O2.synth_x(orc, SEED + rank, 20, H)
+        m.forward_host(0, x)  # every rank takes part
+        status = "ok"
+        if rank == 0:
+            # Rank 1 skips this call (no kernels of its own in flight): rank 0's bounded
+            # device-side waits for rank 1's flags must run out and report a timeout.
+            try:
+                m.forward_host(0, x)
+                status = "no error"
+            except hymoe.HymoeError as e:
+                status = "timeout" if e.status == hymoe.STATUS_TIMEOUT else f"status {e.status}"
+            try:  # the context refuses further expert-parallel calls
+                m.forward_host(0, x)
+                status += " / accepted"
+            except hymoe.HymoeError:
+                pass
+            go.set()
+        else:
+            go.wait(120)  # stay mapped until rank 0's failed call has returned
+        m.close()
+        q.put((rank, status))
+    except Exception as e:
+        q.put((rank, f"error: {e!r}"))
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
+def test_peer_transport_bounded_wait_reports_timeout():
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import hymoe
+    nccl_id = hymoe.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q, go = ctx.Queue(), ctx.Event()
+    procs = [ctx.Process(target=_timeout_worker, args=(r, 2, nccl_id, q, go)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+    assert res[0] == "timeout", res
+    assert res[1] == "ok", res
