@@ -84,6 +84,27 @@ EncodeTiledFn get_encode_fn() {
     return fn;
 }
 
+using AddressRangeFn = PFN_cuMemGetAddressRange_v3020;
+
+// Base of the allocation holding `p` (an IPC handle maps the whole allocation).
+bool allocation_base(const void* p, uintptr_t* base) {
+    static AddressRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<AddressRangeFn>(f);
+    });
+    if (!fn) return false;
+    CUdeviceptr b = 0;
+    size_t sz = 0;
+    if (fn(&b, &sz, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return false;
+    *base = static_cast<uintptr_t>(b);
+    return true;
+}
+
 }  // namespace
 
 namespace hymoe {
@@ -146,6 +167,8 @@ struct hymoe_ctx {
     int* C_host = nullptr;       // pinned copy
     cudaEvent_t ev_counts = nullptr;
     double ep_timeout_s = 60.0;
+    bool joining = false;  // communicator setup: connection establishment gets a longer budget
+    double host_wait_s() const { return joining ? std::max(ep_timeout_s, 120.0) : ep_timeout_s; }
 
     // expert parallelism over NVLink peer memory (the default transport; HYMOE_EP_TRANSPORT=nccl
     // selects the NCCL send/recv exchange instead)
@@ -338,11 +361,11 @@ hymoe_status ep_poll(hymoe_ctx* c, const char* what) {
                            ncclGetErrorString(r != ncclSuccess ? r : st));
         }
         if (st == ncclSuccess) return HYMOE_OK;
-        if (now_s() - t0 > c->ep_timeout_s) {
+        if (now_s() - t0 > c->host_wait_s()) {
             c->comm_broken = true;
             ncclCommAbort(c->comm);
             c->comm = nullptr;
-            return c->fail(HYMOE_ERR_TIMEOUT, "%s: no progress within %.0f s", what, c->ep_timeout_s);
+            return c->fail(HYMOE_ERR_TIMEOUT, "%s: no progress within %.0f s", what, c->host_wait_s());
         }
         std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
@@ -363,11 +386,11 @@ hymoe_status ep_wait_event(hymoe_ctx* c, cudaEvent_t ev, const char* what) {
                 return c->fail(HYMOE_ERR_NCCL, "%s: %s", what, ncclGetErrorString(st));
             }
         }
-        if (now_s() - t0 > c->ep_timeout_s) {
+        if (now_s() - t0 > c->host_wait_s()) {
             c->comm_broken = true;
             if (c->comm) ncclCommAbort(c->comm);
             c->comm = nullptr;
-            return c->fail(HYMOE_ERR_TIMEOUT, "%s: no completion within %.0f s", what, c->ep_timeout_s);
+            return c->fail(HYMOE_ERR_TIMEOUT, "%s: no completion within %.0f s", what, c->host_wait_s());
         }
         std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
@@ -403,6 +426,7 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
     struct Rec {
         unsigned char uuid[16];
         uint32_t max_tokens, ok, pad[2];
+        uint64_t off[3];  // offset of each buffer inside the allocation its handle maps
         cudaIpcMemHandle_t h[3];
     };
     static_assert(sizeof(Rec) <= 256, "record");
@@ -412,11 +436,15 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
     memcpy(mine.uuid, &prop.uuid, 16);
     mine.max_tokens = c->cfg.max_tokens;
     mine.ok = 1;
-    if (cudaIpcGetMemHandle(&mine.h[0], c->xp) != cudaSuccess ||
-        cudaIpcGetMemHandle(&mine.h[1], c->y) != cudaSuccess ||
-        cudaIpcGetMemHandle(&mine.h[2], c->ep_meta) != cudaSuccess) {
-        cudaGetLastError();
-        mine.ok = 0;
+    const void* bufs[3] = {c->xp, c->y, c->ep_meta};
+    for (int i = 0; i < 3; ++i) {
+        uintptr_t base = 0;
+        if (!allocation_base(bufs[i], &base) || cudaIpcGetMemHandle(&mine.h[i], reinterpret_cast<void*>(base)) != cudaSuccess) {
+            cudaGetLastError();
+            mine.ok = 0;
+            break;
+        }
+        mine.off[i] = reinterpret_cast<uintptr_t>(bufs[i]) - base;
     }
     char* dbuf = nullptr;
     HY_CUDA(c, dalloc(&dbuf, 256 * (N + 1)));
@@ -472,9 +500,10 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
             }
             c->ipc_opened.push_back(ptr[i]);
         }
-        P.xp[s] = static_cast<__half*>(ptr[0]);
-        P.y[s] = static_cast<float*>(ptr[1]);
-        P.meta[s] = static_cast<int*>(ptr[2]);
+        if (!mine.ok) break;
+        P.xp[s] = reinterpret_cast<__half*>(static_cast<char*>(ptr[0]) + recs[s].off[0]);
+        P.y[s] = reinterpret_cast<float*>(static_cast<char*>(ptr[1]) + recs[s].off[1]);
+        P.meta[s] = reinterpret_cast<int*>(static_cast<char*>(ptr[2]) + recs[s].off[2]);
     }
     // second round: every rank learns whether every rank mapped every peer
     if (all_ok) {
@@ -601,6 +630,7 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     if (N > 1) {
         if (!cfg->nccl_unique_id) return bail(c->fail(HYMOE_ERR_INVALID_ARG, "ep_size > 1 needs nccl_unique_id"));
         if (const char* v = getenv("HYMOE_EP_TIMEOUT_S")) c->ep_timeout_s = atof(v);
+        c->joining = true;
         // Non-blocking communicator: joining is polled against a deadline so that a rank
         // that never arrives ends this call with an error instead of a hang.
         ncclConfig_t ncfg = NCCL_CONFIG_INITIALIZER;
@@ -617,6 +647,7 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
             st = ep_p2p_setup(c);
             if (st != HYMOE_OK) return bail(st);
         }
+        c->joining = false;
     }
     *out = c;
     return HYMOE_OK;
