@@ -64,35 +64,49 @@ def ncu_traffic():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """SM clock and clock-event reasons sampled through NVML every 2 ms during the timed region
+    (a background thread; the device is found by its CUDA UUID, else its PCI bus id)."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap"}
 
     def __init__(self, dev: int):
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        import threading
+        self.samples, self.mask, self.max_mhz, self.err = [], 0, None, None
+        self.stop_ev = threading.Event()
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-i", str(dev), "-lms", "200"], stdout=self.f,
-                                      stderr=subprocess.DEVNULL)
-        except OSError:
-            self.p = None
+            import pynvml as N
+            import torch
+            N.nvmlInit()
+            props = torch.cuda.get_device_properties(dev)
+            h = None
+            try:
+                h = N.nvmlDeviceGetHandleByUUID("GPU-" + str(props.uuid))
+            except Exception:
+                bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+                h = N.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+            get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                N.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def loop():
+                while not self.stop_ev.is_set():
+                    self.samples.append(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM))
+                    self.mask |= int(get_reasons(h))
+                    self.stop_ev.wait(0.002)
+            self.t = threading.Thread(target=loop, daemon=True)
+            self.t.start()
+        except Exception as e:  # no NVML: report it instead of a number
+            self.t, self.err = None, f"nvml unavailable: {e!r}"[:120]
 
     def stop(self) -> dict:
-        if self.p is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.p.terminate()
-        self.p.wait()
-        self.f.seek(0)
-        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.strip()]
-        os.unlink(self.f.name)
-        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4)
-                          if "Active" in r[5 + i] and "Not" not in r[5 + i]})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+        if self.t is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err], "samples": 0}
+        self.stop_ev.set()
+        self.t.join()
+        reasons = sorted(v for k, v in self.REASONS.items() if self.mask & k)
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples)}
 
 
 # --------------------------------------------------------------------------- GPU arm
@@ -113,7 +127,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                       nccl_id=box[0])
     else:
         m = hymoe.MoE(H, I, E, K, 1, T, device=local_rank)
-    m.synth_layer(0, hymoe.TYPE_Q4_0, args.seed, 0.02)
+    m.synth_layer(0, hymoe.TYPE_Q8_0 if args.wtype == "q8_0" else hymoe.TYPE_Q4_0, args.seed, 0.02)
     # A dedicated stream: torch's default stream has handle 0, which the C ABI reads as
     # "the context's own stream".  Every torch op and event below runs on this stream.
     stream = torch.cuda.Stream(device=dev)
@@ -143,8 +157,14 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     dbg = hymoe.Debug(None, None, None, dbg_idx.data_ptr())
     m.forward_device(0, x.data_ptr(), out.data_ptr(), T, bias_ptr=bias.data_ptr(), dbg=dbg)
     torch.cuda.synchronize()
-    counts = torch.bincount(dbg_idx.flatten().long(), minlength=E).cpu().numpy()
-    rows = T * K + T
+    counts_t = torch.bincount(dbg_idx.flatten().long(), minlength=E)
+    counts = counts_t.cpu().numpy()
+    if world > 1:  # rows this rank's GEMMs process: its T shared rows + the pairs it receives
+        torch.distributed.all_reduce(counts_t)
+        el = E // world
+        rows = T + int(counts_t[rank * el:(rank + 1) * el].sum())
+    else:
+        rows = T * K + T
     flop_gu = rows * FLOP_PER_PAIR_GU
     flop_dn = rows * FLOP_PER_PAIR_DN
     flop_total = flop_gu + flop_dn + T * FLOP_ROUTER_PER_TOKEN
@@ -213,12 +233,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
-        "data": "synthetic (seeded; random-init Q4_0 weights generated on device)",
-        "config": {"workload": f"cfg3/cfg4: one MoE block, Q4_0 experts, {T} tokens/step/GPU, "
+        "data": f"synthetic (seeded; random-init {args.wtype.upper()} weights generated on device)",
+        "config": {"workload": f"cfg3/cfg4: one MoE block, {args.wtype.upper()} experts, {T} tokens/step/GPU, "
                                f"router bias {'Zipf(1.1) over a seeded expert permutation' if args.bias == 'zipf' else '~N(0,0.5)'}",
                    "model": "HunyuanImage-3.0 MoE block H=4096 I=3072 E=64+1 shared top-8",
                    "global_batch": T * world, "seq_len": T,
-                   "parallelism": f"ep{world} (E/{world} experts per GPU, NCCL all-to-all)" if world > 1 else "single",
+                   "parallelism": f"ep{world} (E/{world} experts per GPU; token rows and results over NVLink peer memory)" if world > 1 else "single",
                    "l2": "flushed between steps (256 MiB write outside the timed events)"},
         "tflops_total": round(flop_total / (ms_per_step / 1e3) / 1e12, 1),
         "frac_of_peak_total": round(flop_total / (ms_per_step / 1e3) / 1e12 / pk["tf_sus"], 4),
@@ -421,6 +441,9 @@ def main():
     ap.add_argument("--bias", default="normal", choices=["normal", "zipf"])
     ap.add_argument("--no-cpu", dest="cpu", action="store_false")
     ap.add_argument("--no-decode", dest="decode", action="store_false")
+    # weights of the main (timed) workload: cfg3/cfg4 use Q4_0; q8_0 with --tokens 1..64 runs the
+    # decode workload through the same path (used for kernel captures)
+    ap.add_argument("--wtype", default="q4_0", choices=["q4_0", "q8_0"])
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))

@@ -351,6 +351,7 @@ __global__ __launch_bounds__(kGemvThreads, 3) void gemv_kernel(const __grid_cons
 // the 8 warp partials meet in shared memory and are summed in warp order (deterministic), and
 // the item's output is written.
 constexpr int kRedLd = 9;  // token pitch (floats) of the partial buffer: conflict-free sums
+constexpr int kStreamItems = 64;
 
 template <int WT, int R>
 __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
@@ -365,6 +366,10 @@ __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
     float* red = reinterpret_cast<float*>(wbuf + kGemvWarps * R * TB);  // [8][128][kRedLd]
     uint64_t* bars = reinterpret_cast<uint64_t*>(red + kGemvWarps * kTileRows * kRedLd);  // [8][R]
     __shared__ int abort_flag;
+    // This CTA's items and their weight row blocks, staged once (the issue path must not wait
+    // on global loads); more than kStreamItems items fall back to global reads.
+    __shared__ int4 s_item[kStreamItems];
+    __shared__ const uint8_t* s_wt[kStreamItems];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int gq = lane >> 2, c = lane & 3;
     const int n_it = *n_items, G = gridDim.x;
@@ -377,15 +382,24 @@ __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
     if (lane == 0)
         for (int r = 0; r < R; ++r) mbar_init(&wb[r], 1);
     if (tid == 0) abort_flag = 0;
+    for (int i = tid; i < min(my_items, kStreamItems); i += kGemvThreads) {
+        const int4 it = items[blockIdx.x + i * G];
+        s_item[i] = it;
+        s_wt[i] = wtiles[it.x] + static_cast<size_t>(it.y) * n_ks * TB;
+    }
     fence_mbar_init();
     __syncthreads();
+    auto item_at = [&](int i) {
+        return i < kStreamItems ? s_item[i] : items[blockIdx.x + i * G];
+    };
 
     auto issue = [&](int q) {  // lane 0: tile q of this warp's stream
         const int i = q / per_item, m = q - i * per_item;
-        const int4 it = items[blockIdx.x + i * G];
+        const int4 it = item_at(i);
+        const uint8_t* wt = i < kStreamItems ? s_wt[i] : wtiles[it.x] + static_cast<size_t>(it.y) * n_ks * TB;
         const int k = warp + kGemvWarps * m, slot = q % R;
         mbar_arrive_expect_tx(&wb[slot], TB + 1024u);
-        bulk_load(ww + slot * TB, wtiles[it.x] + (static_cast<size_t>(it.y) * n_ks + k) * TB, TB, &wb[slot]);
+        bulk_load(ww + slot * TB, wt + static_cast<size_t>(k) * TB, TB, &wb[slot]);
         tma_load_2d(wx + slot * 1024, &maps.x[0], &wb[slot], k * kTileK, it.z);
     };
     int issued = 0, done = 0;  // lane 0's stream positions
@@ -395,7 +409,7 @@ __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
     const int tok_b = col_token<WT>(gq);
     const int t0 = col_token<WT>(2 * c), t1 = col_token<WT>(2 * c + 1);
     for (int i = 0; i < my_items; ++i) {
-        const int4 it = items[blockIdx.x + i * G];
+        const int4 it = item_at(i);
         float acc[8][4];
 #pragma unroll
         for (int g = 0; g < 8; ++g)
