@@ -126,10 +126,14 @@ struct GraphKey {
     }
 };
 
+constexpr int kChunkMinTokens = 2048;  // host-pointer calls of at least this size are pipelined
+
 struct hymoe_ctx {
     hymoe_config cfg{};
     std::string err;
     cudaStream_t own_stream = nullptr;
+    cudaStream_t copy_stream = nullptr;  // host-pointer calls: chunk uploads beside the compute
+    cudaStream_t down_stream = nullptr;  // ... and chunk downloads
     cudaStream_t stream = nullptr;
     int n_sms = 148;
     int H = 0, I = 0, E = 0, K = 0;
@@ -570,7 +574,9 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
         hymoe_destroy(c);
         return st;
     };
-    if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess)
+    if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->down_stream, cudaStreamNonBlocking) != cudaSuccess)
         return bail(c->fail(HYMOE_ERR_CUDA, "cudaStreamCreate failed"));
     c->stream = c->own_stream;
 
@@ -670,6 +676,8 @@ void hymoe_destroy(hymoe_ctx* c) {
         }
     }
     if (c->own_stream) cudaStreamSynchronize(c->own_stream);
+    if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    if (c->down_stream) cudaStreamSynchronize(c->down_stream);
     for (auto& L : c->layers) free_layer(L);
     cudaFree(c->x_dev);
     cudaFree(c->resid_dev);
@@ -710,6 +718,8 @@ void hymoe_destroy(hymoe_ctx* c) {
     c->prof_clear();
     for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+    if (c->down_stream) cudaStreamDestroy(c->down_stream);
     delete c;
 }
 
@@ -845,6 +855,63 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     const bool host = (flags & HYMOE_HOST_PTRS) != 0;
     cudaStream_t st = c->stream;
     const size_t xbytes = static_cast<size_t>(T) * H * sizeof(float);
+
+    // Host buffers, one GPU, no debug outputs, at least 2048 tokens: the call runs in token
+    // chunks so that the copies overlap the compute — every upload is queued at once on one
+    // copy stream, each chunk computes when its upload has landed, and its download (second
+    // copy stream) starts when it is done.  Every token's result is independent of the
+    // others', so the output is the same as one call's.
+    if (host && !ep && !dbg && T >= kChunkMinTokens && !(flags & HYMOE_USE_GRAPH)) {
+        // ~2048-token chunks: smaller ones lose more GEMM efficiency than the overlap gains
+        const int n_ch = std::min(4, T / kChunkMinTokens);
+        const int per = (T + n_ch - 1) / n_ch;
+        cudaStream_t up = c->copy_stream, down = c->down_stream;
+        const float* dbias = nullptr;
+        if (router_bias) {
+            HY_CUDA(c, cudaMemcpyAsync(c->bias_dev, router_bias, sizeof(float) * E, cudaMemcpyHostToDevice, st));
+            dbias = c->bias_dev;
+        }
+        // both copy streams follow earlier work on the compute stream (they rewrite x_dev / out_dev)
+        std::vector<cudaEvent_t> evs;
+        auto ev = [&]() {
+            evs.push_back(c->take_event());
+            return evs.back();
+        };
+        cudaEvent_t ev0 = ev();
+        HY_CUDA(c, cudaEventRecord(ev0, st));
+        HY_CUDA(c, cudaStreamWaitEvent(up, ev0, 0));
+        HY_CUDA(c, cudaStreamWaitEvent(down, ev0, 0));
+        std::vector<cudaEvent_t> in(n_ch, nullptr);
+        for (int ch = 0; ch < n_ch; ++ch) {
+            const int t0 = ch * per, n = std::min(per, T - t0);
+            if (n <= 0) break;
+            const size_t off = static_cast<size_t>(t0) * H, bytes = static_cast<size_t>(n) * H * sizeof(float);
+            HY_CUDA(c, cudaMemcpyAsync(c->x_dev + off, x + off, bytes, cudaMemcpyHostToDevice, up));
+            if (residual)
+                HY_CUDA(c, cudaMemcpyAsync(c->resid_dev + off, residual + off, bytes, cudaMemcpyHostToDevice, up));
+            in[ch] = ev();
+            HY_CUDA(c, cudaEventRecord(in[ch], up));
+        }
+        hymoe_status result = HYMOE_OK;
+        for (int ch = 0; ch < n_ch && result == HYMOE_OK; ++ch) {
+            const int t0 = ch * per, n = std::min(per, T - t0);
+            if (n <= 0) break;
+            const size_t off = static_cast<size_t>(t0) * H, bytes = static_cast<size_t>(n) * H * sizeof(float);
+            HY_CUDA(c, cudaStreamWaitEvent(st, in[ch], 0));
+            result = hymoe_forward(c, layer, c->x_dev + off, residual ? c->resid_dev + off : nullptr, c->out_dev + off,
+                                   static_cast<uint32_t>(n), dbias, nullptr, flags & ~HYMOE_HOST_PTRS);
+            cudaEvent_t done = ev();
+            HY_CUDA(c, cudaEventRecord(done, st));
+            HY_CUDA(c, cudaStreamWaitEvent(down, done, 0));
+            HY_CUDA(c, cudaMemcpyAsync(out + off, c->out_dev + off, bytes, cudaMemcpyDeviceToHost, down));
+        }
+        cudaEvent_t fin = ev();
+        HY_CUDA(c, cudaEventRecord(fin, down));
+        HY_CUDA(c, cudaStreamWaitEvent(st, fin, 0));  // synchronising the stream covers the copies
+        hymoe_status sync = hymoe_synchronize(c);
+        for (cudaEvent_t e : evs) c->ev_pool.push_back(e);
+        return result != HYMOE_OK ? result : sync;
+    }
 
     const float* dx = x;
     const float* dres = residual;

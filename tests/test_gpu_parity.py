@@ -195,3 +195,28 @@ def test_graph_replay_matches_eager(orc, T):
             eager = m.forward_host(0, x)["out"]
             assert np.array_equal(got, eager), f"call {call}"
     m.close()
+
+
+def test_host_pointer_call_in_chunks_is_bit_identical(orc):
+    """Host-pointer calls of >= 2048 tokens run as pipelined token chunks (copies on a second
+    stream beside the compute); the output must equal one device-pointer call bit for bit."""
+    torch = pytest.importorskip("torch")
+    H, I, E, K, T, seed, wt = 256, 128, 16, 8, 6149, 17, O.Q4_0  # 3 chunks, the last one shorter
+    lay = host_layer(orc, seed, 0, H, I, E, wt)
+    x = O.synth_x(orc, seed, T, H)
+    resid = O.synth_x(orc, seed + 1, T, H)
+    bias = O.synth_bias(orc, seed, E)
+    m = _ctx(H, I, E, K, T)
+    _load(m, lay, wt)
+    host = m.forward_host(0, x, resid=resid, bias=bias)["out"]
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        xd, rd = torch.from_numpy(x).cuda(), torch.from_numpy(resid).cuda()
+        bd, od = torch.from_numpy(bias).cuda(), torch.empty(T, H, device="cuda")
+        m.set_stream(st.cuda_stream)
+        m.forward_device(0, xd.data_ptr(), od.data_ptr(), T, resid_ptr=rd.data_ptr(), bias_ptr=bd.data_ptr())
+    m.synchronize()
+    assert np.array_equal(host, od.cpu().numpy())
+    o = _oracle(orc, lay, x, K, I, bias=bias, resid=resid)
+    assert rel_l2(host, o["out"]) <= REL_L2_TOL
+    m.close()
