@@ -314,6 +314,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (lane == 0) mbar_arrive_cluster(ab ? acc_empty_leader1 : acc_empty_leader0);
                 }
                 if (!has_tile) continue;  // warp-uniform; no staging barrier below either
+                if (!a.glu) {
+                    // down projection: lane = output column, so for every token the warp's 32
+                    // lanes store 32 consecutive floats (128 B) straight from the registers
+                    float* o = static_cast<float*>(a.out) + static_cast<size_t>(row0 + ch * 32) * a.out_ld +
+                               rb * kTileRows + q * 32 + lane;
+                    const int nj = min(32, nrows - ch * 32);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < nj) o[static_cast<size_t>(j) * a.out_ld] = __uint_as_float(v[j]);
+                    continue;
+                }
                 float* srow = sStage + (q * 32 + lane) * kStageLd;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) srow[j] = __uint_as_float(v[j]);
@@ -321,35 +332,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int c = ch * 32 + tok;
                 if (c < nrows) {
                     const size_t row = static_cast<size_t>(row0 + c);
-                    if (a.glu) {
-                        uint32_t hv[8];
+                    uint32_t hv[8];
 #pragma unroll
-                        for (int jj = 0; jj < 8; ++jj) {
-                            const int j = seg * 16 + 2 * jj;
-                            const float h0 = silu_mul(sStage[j * kStageLd + tok],
-                                                      sStage[(kGluHalf + j) * kStageLd + tok]);
-                            const float h1 = silu_mul(sStage[(j + 1) * kStageLd + tok],
-                                                      sStage[(kGluHalf + j + 1) * kStageLd + tok]);
-                            hv[jj] = h2_bits(__floats2half2_rn(h0, h1));
-                        }
-                        uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) +
-                                                            row * a.out_ld + rb * kGluHalf +
-                                                            seg * 16);
-                        o[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-                        o[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
-                    } else {
-                        float4* o = reinterpret_cast<float4*>(static_cast<float*>(a.out) +
-                                                              row * a.out_ld + rb * kTileRows +
-                                                              seg * 32);
-#pragma unroll
-                        for (int jj = 0; jj < 8; ++jj) {
-                            const int n0 = seg * 32 + 4 * jj;
-                            o[jj] = make_float4(sStage[n0 * kStageLd + tok],
-                                                sStage[(n0 + 1) * kStageLd + tok],
-                                                sStage[(n0 + 2) * kStageLd + tok],
-                                                sStage[(n0 + 3) * kStageLd + tok]);
-                        }
+                    for (int jj = 0; jj < 8; ++jj) {
+                        const int j = seg * 16 + 2 * jj;
+                        const float h0 = silu_mul(sStage[j * kStageLd + tok],
+                                                  sStage[(kGluHalf + j) * kStageLd + tok]);
+                        const float h1 = silu_mul(sStage[(j + 1) * kStageLd + tok],
+                                                  sStage[(kGluHalf + j + 1) * kStageLd + tok]);
+                        hv[jj] = h2_bits(__floats2half2_rn(h0, h1));
                     }
+                    uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + row * a.out_ld +
+                                                        rb * kGluHalf + seg * 16);
+                    o[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                    o[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
                 }
                 named_bar_sync(1, 128);
             }
