@@ -78,14 +78,16 @@ __device__ void single_gpu_items(const PlanArgs& a, const int* goff_s, const int
     __shared__ int4 seg[kMaxSegs];
     __shared__ int pre[kMaxSegs + 1];
     const int tid = threadIdx.x;
+    const int s0 = a.shared_apart ? 0 : 1;  // the shared segment, unless it runs apart
+    const int ns = a.E + s0;
     if (tid == 0) {
-        seg[0] = make_int4(a.E, 0, a.T, 0);
-        *a.n_segs = a.E + 1;
+        if (s0) seg[0] = make_int4(a.E, 0, a.T, 0);
+        *a.n_segs = ns;
     }
-    for (int g = tid; g < a.E; g += blockDim.x) seg[1 + g] = make_int4(g, a.T + goff_s[g], gcnt_s[g], 0);
+    for (int g = tid; g < a.E; g += blockDim.x) seg[s0 + g] = make_int4(g, a.T + goff_s[g], gcnt_s[g], 0);
     __syncthreads();
-    for (int i = tid; i <= a.E; i += blockDim.x) a.segs[i] = seg[i];
-    build_items(seg, a.E + 1, a.items, pre);
+    for (int i = tid; i < ns; i += blockDim.x) a.segs[i] = seg[i];
+    build_items(seg, ns, a.items, pre);
 }
 
 // One CTA of 1024 threads.  (expert, part) = (tid / 16, tid % 16) owns a contiguous run of
@@ -216,7 +218,29 @@ __global__ __launch_bounds__(128) void scatter_gather_kernel(
         v.w = *reinterpret_cast<const uint32_t*>(&h3);
         for (int k = 0; k < K; ++k)
             *reinterpret_cast<uint4*>(xp_routed + static_cast<size_t>(spos[tt][k]) * H + j) = v;
-        *reinterpret_cast<uint4*>(xp_shared + static_cast<size_t>(t0 + tt) * H + j) = v;
+        if (xp_shared != nullptr) *reinterpret_cast<uint4*>(xp_shared + static_cast<size_t>(t0 + tt) * H + j) = v;
+    }
+}
+
+// One CTA: the shared expert's fp16 rows and its work items (decode sizes, T <= 8).
+__global__ __launch_bounds__(256) void shared_prep_kernel(const float* __restrict__ x, int T, int H,
+                                                          __half* __restrict__ xp, int group, int n_rb_gu,
+                                                          int n_rb_dn, int4* items_gu, int4* items_dn,
+                                                          int* n_items) {
+    const int tid = threadIdx.x;
+    for (int i = tid; i < n_rb_gu; i += blockDim.x) items_gu[i] = make_int4(group, i, 0, T);
+    for (int i = tid; i < n_rb_dn; i += blockDim.x) items_dn[i] = make_int4(group, i, 0, T);
+    if (tid == 0) {
+        n_items[0] = n_rb_gu;
+        n_items[1] = n_rb_dn;
+    }
+    for (int i = tid * 4; i < T * H; i += blockDim.x * 4) {
+        const float4 a = *reinterpret_cast<const float4*>(x + i);
+        const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+        uint2 v;
+        v.x = *reinterpret_cast<const uint32_t*>(&h0);
+        v.y = *reinterpret_cast<const uint32_t*>(&h1);
+        *reinterpret_cast<uint2*>(xp + i) = v;
     }
 }
 
@@ -262,6 +286,12 @@ cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, co
     dim3 grid((T + kRouterTok - 1) / kRouterTok, (H + kScatterCols - 1) / kScatterCols);
     scatter_gather_kernel<<<grid, 128, 0, st>>>(x, T, H, E, K, topk_idx, chunk_base, slot_pos,
                                                   xp_routed, xp_shared);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_shared_prep(const float* x, int T, int H, __half* xp, int group, int n_rb_gu,
+                               int n_rb_dn, int4* items_gu, int4* items_dn, int* n_items, cudaStream_t st) {
+    shared_prep_kernel<<<1, 256, 0, st>>>(x, T, H, xp, group, n_rb_gu, n_rb_dn, items_gu, items_dn, n_items);
     return cudaGetLastError();
 }
 

@@ -134,6 +134,10 @@ struct hymoe_ctx {
     cudaStream_t own_stream = nullptr;
     cudaStream_t copy_stream = nullptr;  // host-pointer calls: chunk uploads beside the compute
     cudaStream_t down_stream = nullptr;  // ... and chunk downloads
+    cudaStream_t side_stream = nullptr;  // decode calls: the shared expert beside the router
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    int4 *items_sh_gu = nullptr, *items_sh_dn = nullptr;
+    int* n_items_sh = nullptr;
     cudaStream_t stream = nullptr;
     int n_sms = 148;
     int H = 0, I = 0, E = 0, K = 0;
@@ -576,7 +580,10 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     };
     if (cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
         cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&c->down_stream, cudaStreamNonBlocking) != cudaSuccess)
+        cudaStreamCreateWithFlags(&c->down_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->side_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming) != cudaSuccess)
         return bail(c->fail(HYMOE_ERR_CUDA, "cudaStreamCreate failed"));
     c->stream = c->own_stream;
 
@@ -615,6 +622,9 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     A(dalloc(&c->err_word, 1));
     A(dalloc(&c->items_gu, c->max_items));
     A(dalloc(&c->items_dn, c->max_items));
+    A(dalloc(&c->items_sh_gu, n_rb));
+    A(dalloc(&c->items_sh_dn, n_rb));
+    A(dalloc(&c->n_items_sh, 2));
     A(dalloc(&c->xp, rows * H));
     A(dalloc(&c->hbuf, rows * I));
     A(dalloc(&c->y, rows * H));
@@ -678,6 +688,7 @@ void hymoe_destroy(hymoe_ctx* c) {
     if (c->own_stream) cudaStreamSynchronize(c->own_stream);
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
     if (c->down_stream) cudaStreamSynchronize(c->down_stream);
+    if (c->side_stream) cudaStreamSynchronize(c->side_stream);
     for (auto& L : c->layers) free_layer(L);
     cudaFree(c->x_dev);
     cudaFree(c->resid_dev);
@@ -720,6 +731,12 @@ void hymoe_destroy(hymoe_ctx* c) {
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     if (c->down_stream) cudaStreamDestroy(c->down_stream);
+    if (c->side_stream) cudaStreamDestroy(c->side_stream);
+    if (c->ev_fork) cudaEventDestroy(c->ev_fork);
+    if (c->ev_join) cudaEventDestroy(c->ev_join);
+    cudaFree(c->items_sh_gu);
+    cudaFree(c->items_sh_dn);
+    cudaFree(c->n_items_sh);
     delete c;
 }
 
@@ -960,6 +977,24 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             ia.n_items = c->n_items;
             return ia;
         };
+        // Decode sizes on one GPU: the shared expert needs no routing, so it streams its weights
+        // on a forked stream while the router, the plan and the dispatch run (on <= 48 CTAs,
+        // leaving SMs to them); the combine joins both streams.  From 4 tokens on the router's
+        // chains last long enough to hide it (measured: T=8 0.357 -> 0.351 ms; at T=1 the fork
+        // outlasted the front end and delayed the routed launch, 0.105 -> 0.119 ms).
+        const bool shared_apart = !ep && gemv && T >= 4 && T <= 8 && (L.wtype == W_Q4_0 || L.wtype == W_Q8_0);
+        if (shared_apart) {
+            cudaStream_t side = c->side_stream;
+            HY_CUDA(c, cudaEventRecord(c->ev_fork, st));
+            HY_CUDA(c, cudaStreamWaitEvent(side, c->ev_fork, 0));
+            HY_CUDA(c, launch_shared_prep(dx, T, H, c->xp, el, tiles_gu, tiles_dn, c->items_sh_gu, c->items_sh_dn,
+                                          c->n_items_sh, side));
+            HY_CUDA(c, launch_gemv(c->gmaps_xp, c->items_sh_gu, c->n_items_sh, tiles_gu, L.d_gu_ptrs, L.wtype,
+                                   H / kTileK, 1, T, c->hbuf, I, c->err_word, std::min(c->n_sms, tiles_gu), side));
+            HY_CUDA(c, launch_gemv(c->gmaps_h, c->items_sh_dn, c->n_items_sh + 1, tiles_dn, L.d_dn_ptrs, L.wtype,
+                                   I / kTileK, 0, T, c->y, H, c->err_word, std::min(c->n_sms, tiles_dn), side));
+            HY_CUDA(c, cudaEventRecord(c->ev_join, side));
+        }
         if (T > 0) {
             const int n_chunks = (T + kRouterTok - 1) / kRouterTok;
             // T <= 16 (one router chunk): the top-K runs inside the plan launch.
@@ -979,6 +1014,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             pa.chunk_base = c->chunk_base;
             pa.segs = ep ? nullptr : c->segs;
             pa.n_segs = c->n_segs;
+            pa.shared_apart = shared_apart ? 1 : 0;
             pa.items = items_args(gemv);
             c->phase_begin();
             if (fused)
@@ -990,7 +1026,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
                 c->phase_begin();
                 HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
                                                  ep ? c->xp_send : c->xp + static_cast<size_t>(T) * H,
-                                                 c->xp, st));
+                                                 shared_apart ? nullptr : c->xp, st));
                 c->phase_end(HYMOE_PHASE_DISPATCH);
             }
         } else {
@@ -1156,6 +1192,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             c->phase_end(HYMOE_PHASE_EP_COMBINE);
             y_routed = c->y_ret;
         }
+        if (shared_apart) HY_CUDA(c, cudaStreamWaitEvent(st, c->ev_join, 0));  // the shared expert's rows of y
         if (T > 0) {
             if (!p2p) {
                 c->phase_begin();

@@ -48,6 +48,7 @@ struct PlanArgs {
     int* chunk_base;          // [n_chunks][E]
     int4* segs;               // single-GPU segments + work items built in the same launch
     int* n_segs;              // (segs == NULL: expert-parallel mode, items built later)
+    int shared_apart;         // 1: the shared expert runs as its own launch (no segment here)
     ItemsArgs items;
 };
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
@@ -57,9 +58,14 @@ cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, fl
 
 cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st);
 
+// xp_shared == nullptr: the shared expert's rows are written elsewhere (launch_shared_prep).
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
                                   const int* chunk_base, int* slot_pos, __half* xp_routed,
                                   __half* xp_shared, cudaStream_t st);
+// The shared expert as its own launch: its fp16 rows xp[0, T) and its work items (one per
+// 128-row block, all T rows) for gate_up and down; n_items[2].
+cudaError_t launch_shared_prep(const float* x, int T, int H, __half* xp, int group, int n_rb_gu,
+                               int n_rb_dn, int4* items_gu, int4* items_dn, int* n_items, cudaStream_t st);
 // C: [N][ld] per-expert counts of every source rank (ld >= E).
 cudaError_t launch_ep_segments(const int* C, int ld, int N, int rank, int el, int E, int T, int4* segs,
                                int* n_segs, cudaStream_t st);

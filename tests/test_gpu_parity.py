@@ -172,7 +172,7 @@ def test_errors_are_statuses(orc):
     m.close()
 
 
-@pytest.mark.parametrize("T", [3, 40])
+@pytest.mark.parametrize("T", [3, 6, 40])
 def test_graph_replay_matches_eager(orc, T):
     """HYMOE_USE_GRAPH: the captured graph reads the buffers' current contents on every
     replay, giving the same bits as the eager call."""
