@@ -4,6 +4,8 @@
 //   moe    = shared + routed                         (src/attention.cpp:306-309)
 //   out    = residual + moe                          (src/decoder_layer.cpp:42)
 // Each element is a chain of separately rounded IEEE multiplies and adds in that order.
+// Routed expert results arrive as fp16 (the down projection stores them rounded once); the
+// shared expert's result and everything after are fp32.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -11,55 +13,71 @@ namespace hymoe {
 
 namespace {
 
-// Grid (H / 512, T), 128 threads x 4 columns.  All K routed rows are loaded before the
+// Eight consecutive fp16 values (16 bytes) as floats.
+__device__ __forceinline__ void load_half8(const __half* p, float (&f)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        f[2 * i] = v.x;
+        f[2 * i + 1] = v.y;
+    }
+}
+
+// Grid (H / 1024, T), 128 threads x 8 columns.  All K routed rows are loaded before the
 // arithmetic starts (K <= 8), so the loads overlap instead of following the FP chain.
 __global__ __launch_bounds__(128) void combine_kernel(const float* __restrict__ y_shared,
-                                                      const float* __restrict__ y_routed,
+                                                      const __half* __restrict__ y_routed,
                                                       const int* __restrict__ slot_pos,
                                                       const float* __restrict__ topk_w,
                                                       const float* resid, float* out, int T,
                                                       int H, int K) {
     const int t = blockIdx.y;
-    const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (j >= H) return;
-    float4 v[8];
+    float v[8][8];
     float w[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         if (k < K) {
             const int pos = __ldg(slot_pos + t * K + k);
             w[k] = __ldg(topk_w + t * K + k);
-            v[k] = *reinterpret_cast<const float4*>(y_routed + static_cast<size_t>(pos) * H + j);
+            load_half8(y_routed + static_cast<size_t>(pos) * H + j, v[k]);
         }
     }
-    const float4 s = *reinterpret_cast<const float4*>(y_shared + static_cast<size_t>(t) * H + j);
-    float4 h = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (resid != nullptr) h = *reinterpret_cast<const float4*>(resid + static_cast<size_t>(t) * H + j);
-    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* sr = y_shared + static_cast<size_t>(t) * H + j;
+    const float4 s0 = *reinterpret_cast<const float4*>(sr), s1 = *reinterpret_cast<const float4*>(sr + 4);
+    const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float h[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (resid != nullptr) {
+        const float* hr = resid + static_cast<size_t>(t) * H + j;
+        const float4 h0 = *reinterpret_cast<const float4*>(hr), h1 = *reinterpret_cast<const float4*>(hr + 4);
+        h[0] = h0.x; h[1] = h0.y; h[2] = h0.z; h[3] = h0.w;
+        h[4] = h1.x; h[5] = h1.y; h[6] = h1.z; h[7] = h1.w;
+    }
+    float o[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        if (k < K) {
-            r.x = __fadd_rn(r.x, __fmul_rn(w[k], v[k].x));
-            r.y = __fadd_rn(r.y, __fmul_rn(w[k], v[k].y));
-            r.z = __fadd_rn(r.z, __fmul_rn(w[k], v[k].z));
-            r.w = __fadd_rn(r.w, __fmul_rn(w[k], v[k].w));
-        }
+    for (int i = 0; i < 8; ++i) {
+        float r = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (k < K) r = __fadd_rn(r, __fmul_rn(w[k], v[k][i]));
+        o[i] = __fadd_rn(s[i], r);
+        if (resid != nullptr) o[i] = __fadd_rn(h[i], o[i]);
     }
-    float4 o = make_float4(__fadd_rn(s.x, r.x), __fadd_rn(s.y, r.y), __fadd_rn(s.z, r.z),
-                           __fadd_rn(s.w, r.w));
-    if (resid != nullptr)
-        o = make_float4(__fadd_rn(h.x, o.x), __fadd_rn(h.y, o.y), __fadd_rn(h.z, o.z),
-                        __fadd_rn(h.w, o.w));
-    *reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H + j) = o;
+    float* orow = out + static_cast<size_t>(t) * H + j;
+    *reinterpret_cast<float4*>(orow) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4*>(orow + 4) = make_float4(o[4], o[5], o[6], o[7]);
 }
 
 }  // namespace
 
-cudaError_t launch_combine(const float* y_shared, const float* y_routed, const int* slot_pos,
+cudaError_t launch_combine(const float* y_shared, const __half* y_routed, const int* slot_pos,
                            const float* topk_w, const float* resid, float* out, int T, int H,
                            int K, cudaStream_t st) {
     if (K > 8) return cudaErrorInvalidValue;
-    dim3 grid((H / 4 + 127) / 128, T);
+    dim3 grid((H / 8 + 127) / 128, T);
     combine_kernel<<<grid, 128, 0, st>>>(y_shared, y_routed, slot_pos, topk_w, resid, out, T, H, K);
     return cudaGetLastError();
 }

@@ -1,7 +1,7 @@
 // ep_p2p.cu — expert-parallel dispatch and combine over NVLink peer memory.
 //
-// Every rank maps the other ranks' activation matrix (xp, fp16), result matrix (y, fp32)
-// and metadata block (count matrix + flags) into its address space (CUDA IPC).  One call:
+// Every rank maps the other ranks' activation matrix (xp, fp16), routed-result matrix (yr,
+// fp16) and metadata block (count matrix + flags) into its address space (CUDA IPC).  One call:
 //
 //   ep_counts_kernel    my per-expert pair counts and my token count -> C[me] of every rank;
 //                       count flag; wait for every rank's count flag (bounded)
@@ -12,7 +12,7 @@
 //   (local GEMMs over rows [0, T + received))
 //   ep_raise_kernel     raise this rank's "results ready" flag on every rank
 //   ep_combine_kernel   wait for every owner's ready flag (bounded), then the weighted sum
-//                       reads each routed result directly from its owner's y (P2P loads)
+//                       reads each routed result directly from its owner's yr (P2P loads)
 //
 // Receive layout (same as the NCCL path): rows [0, T) the shared expert's local tokens, then
 // the rows of source rank 0, 1, ..., each in (local expert, source token) order.  A source
@@ -22,7 +22,7 @@
 // Flags carry the call's epoch (strictly increasing, the same on every rank) and are compared
 // with >=, so they never need resetting.  Ordering between calls needs no extra flags: a rank
 // starts writing a peer's xp (next call) only after its own combine finished reading every
-// owner's y, which waited for every owner's ready flag, raised after that owner's GEMMs.
+// owner's yr, which waited for every owner's ready flag, raised after that owner's GEMMs.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -159,12 +159,14 @@ __global__ void ep_raise_kernel(EpPeers peers, int N, int me, int flag_off, uint
         st_release_sys(reinterpret_cast<uint32_t*>(peers.meta[threadIdx.x]) + flag_off + me, epoch);
 }
 
-// out[t] = resid[t] + (y_shared[t] + sum_k w[t,k] * y_owner(k)[slot_pos[t,k]]), the owners'
-// rows read over NVLink; the same operation order as combine_kernel.  Grid (H / 512, T).
+// out[t] = resid[t] + (y_shared[t] + sum_k w[t,k] * yr_owner(k)[slot_pos[t,k]]), the owners'
+// fp16 rows read over NVLink (16 bytes per load); the same operation order as combine_kernel.
+// Grid (H / 1024, T), 128 threads x 8 columns.
 __global__ __launch_bounds__(128) void ep_combine_kernel(EpPeers peers, int N, int me, int el,
                                                          const int* __restrict__ topk_idx,
                                                          const int* __restrict__ slot_pos,
                                                          const float* __restrict__ topk_w,
+                                                         const float* __restrict__ y_shared,
                                                          const float* resid, float* out, int H, int K,
                                                          uint32_t epoch, uint64_t budget_ns, int* err) {
     __shared__ int ok;
@@ -174,9 +176,9 @@ __global__ __launch_bounds__(128) void ep_combine_kernel(EpPeers peers, int N, i
     __syncthreads();
     if (!ok) return;
     const int t = blockIdx.y;
-    const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (j >= H) return;
-    float4 v[8];
+    uint4 u[8];
     float w[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -184,28 +186,37 @@ __global__ __launch_bounds__(128) void ep_combine_kernel(EpPeers peers, int N, i
             const int d = __ldg(topk_idx + t * K + k) / el;
             const int row = __ldg(slot_pos + t * K + k);
             w[k] = __ldg(topk_w + t * K + k);
-            v[k] = *reinterpret_cast<const float4*>(peers.y[d] + static_cast<size_t>(row) * H + j);
+            u[k] = *reinterpret_cast<const uint4*>(peers.yr[d] + static_cast<size_t>(row) * H + j);
         }
     }
-    const float4 s = *reinterpret_cast<const float4*>(peers.y[me] + static_cast<size_t>(t) * H + j);
-    float4 h = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (resid != nullptr) h = *reinterpret_cast<const float4*>(resid + static_cast<size_t>(t) * H + j);
-    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* sr = y_shared + static_cast<size_t>(t) * H + j;
+    const float4 s0 = *reinterpret_cast<const float4*>(sr), s1 = *reinterpret_cast<const float4*>(sr + 4);
+    const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float h[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (resid != nullptr) {
+        const float* hr = resid + static_cast<size_t>(t) * H + j;
+        const float4 h0 = *reinterpret_cast<const float4*>(hr), h1 = *reinterpret_cast<const float4*>(hr + 4);
+        h[0] = h0.x; h[1] = h0.y; h[2] = h0.z; h[3] = h0.w;
+        h[4] = h1.x; h[5] = h1.y; h[6] = h1.z; h[7] = h1.w;
+    }
+    float o[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        if (k < K) {
-            r.x = __fadd_rn(r.x, __fmul_rn(w[k], v[k].x));
-            r.y = __fadd_rn(r.y, __fmul_rn(w[k], v[k].y));
-            r.z = __fadd_rn(r.z, __fmul_rn(w[k], v[k].z));
-            r.w = __fadd_rn(r.w, __fmul_rn(w[k], v[k].w));
+    for (int i = 0; i < 8; ++i) {
+        float r = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if (k < K) {
+                const uint32_t wd = i < 2 ? u[k].x : i < 4 ? u[k].y : i < 6 ? u[k].z : u[k].w;
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wd));
+                r = __fadd_rn(r, __fmul_rn(w[k], (i & 1) ? f.y : f.x));
+            }
         }
+        o[i] = __fadd_rn(s[i], r);
+        if (resid != nullptr) o[i] = __fadd_rn(h[i], o[i]);
     }
-    float4 o = make_float4(__fadd_rn(s.x, r.x), __fadd_rn(s.y, r.y), __fadd_rn(s.z, r.z),
-                           __fadd_rn(s.w, r.w));
-    if (resid != nullptr)
-        o = make_float4(__fadd_rn(h.x, o.x), __fadd_rn(h.y, o.y), __fadd_rn(h.z, o.z),
-                        __fadd_rn(h.w, o.w));
-    *reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H + j) = o;
+    float* orow = out + static_cast<size_t>(t) * H + j;
+    *reinterpret_cast<float4*>(orow) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4*>(orow + 4) = make_float4(o[4], o[5], o[6], o[7]);
 }
 
 }  // namespace
@@ -239,12 +250,12 @@ cudaError_t launch_ep_raise(const EpPeers& p, int N, int me, int flag_off, uint3
 }
 
 cudaError_t launch_ep_combine(const EpPeers& p, int N, int me, int el, const int* topk_idx, const int* slot_pos,
-                              const float* topk_w, const float* resid, float* out, int T, int H, int K,
-                              uint32_t epoch, uint64_t budget_ns, int* err, cudaStream_t st) {
+                              const float* topk_w, const float* y_shared, const float* resid, float* out, int T,
+                              int H, int K, uint32_t epoch, uint64_t budget_ns, int* err, cudaStream_t st) {
     if (K > 8) return cudaErrorInvalidValue;
-    dim3 grid((H / 4 + 127) / 128, T);
-    ep_combine_kernel<<<grid, 128, 0, st>>>(p, N, me, el, topk_idx, slot_pos, topk_w, resid, out, H, K, epoch,
-                                            budget_ns, err);
+    dim3 grid((H / 8 + 127) / 128, T);
+    ep_combine_kernel<<<grid, 128, 0, st>>>(p, N, me, el, topk_idx, slot_pos, topk_w, y_shared, resid, out, H, K,
+                                            epoch, budget_ns, err);
     return cudaGetLastError();
 }
 

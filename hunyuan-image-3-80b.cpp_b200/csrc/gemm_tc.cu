@@ -316,13 +316,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!has_tile) continue;  // warp-uniform; no staging barrier below either
                 if (!a.glu) {
                     // down projection: lane = output column, so for every token the warp's 32
-                    // lanes store 32 consecutive floats (128 B) straight from the registers
-                    float* o = static_cast<float*>(a.out) + static_cast<size_t>(row0 + ch * 32) * a.out_ld +
-                               rb * kTileRows + q * 32 + lane;
+                    // lanes store 32 consecutive values straight from the registers — fp32 for
+                    // the shared expert's rows, fp16 for routed results
+                    const size_t base = static_cast<size_t>(row0 + ch * 32) * a.out_ld + rb * kTileRows + q * 32 + lane;
                     const int nj = min(32, nrows - ch * 32);
+                    if (row0 < a.shared_rows) {
+                        float* o = static_cast<float*>(a.out) + base;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (j < nj) o[static_cast<size_t>(j) * a.out_ld] = __uint_as_float(v[j]);
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nj) o[static_cast<size_t>(j) * a.out_ld] = __uint_as_float(v[j]);
+                    } else {
+                        __half* o = a.out_r + base;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nj) o[static_cast<size_t>(j) * a.out_ld] = __float2half_rn(__uint_as_float(v[j]));
+                    }
                     continue;
                 }
                 float* srow = sStage + (q * 32 + lane) * kStageLd;

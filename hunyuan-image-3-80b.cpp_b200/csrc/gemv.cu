@@ -164,6 +164,8 @@ struct GemvItem {
     const uint8_t* wt;  // first weight tile of the item's row block
     const CUtensorMap* xmap;
     void* out;
+    __half* out_r;    // down projection: routed rows (>= shared_rows), fp16
+    int shared_rows;
     int* err;
 };
 
@@ -286,11 +288,16 @@ __device__ __forceinline__ void run_item(const GemvItem& p, uint8_t* base, uint6
             o[static_cast<size_t>(p.row0 + n) * p.out_ld + p.rb * kGluHalf + j] =
                 __float2half_rn(silu_mul(G[j * kGL + n], G[(kGluHalf + j) * kGL + n]));
         }
-    } else {
+    } else if (p.row0 < p.shared_rows) {
         float* o = static_cast<float*>(p.out);
         for (int i = tid; i < kTileRows * nrows; i += kGemvThreads) {
             const int r = i % kTileRows, n = i / kTileRows;
             o[static_cast<size_t>(p.row0 + n) * p.out_ld + p.rb * kTileRows + r] = G[r * kGL + n];
+        }
+    } else {
+        for (int i = tid; i < kTileRows * nrows; i += kGemvThreads) {
+            const int r = i % kTileRows, n = i / kTileRows;
+            p.out_r[static_cast<size_t>(p.row0 + n) * p.out_ld + p.rb * kTileRows + r] = __float2half_rn(G[r * kGL + n]);
         }
     }
 }
@@ -302,6 +309,7 @@ __global__ __launch_bounds__(kGemvThreads, 3) void gemv_kernel(const __grid_cons
                                                             const uint8_t* const* __restrict__ wtiles,
                                                             int n_ks, int glu, int slots, int xb_max,
                                                             void* __restrict__ out, int out_ld,
+                                                            __half* __restrict__ out_r, int shared_rows,
                                                             int* err) {
     constexpr int TB = tile_bytes(WT);
     extern __shared__ uint8_t gsm_raw[];
@@ -327,6 +335,8 @@ __global__ __launch_bounds__(kGemvThreads, 3) void gemv_kernel(const __grid_cons
     p.wt = wtiles[it.x] + static_cast<size_t>(it.y) * n_ks * TB;
     p.xmap = &maps.x[bi];
     p.out = out;
+    p.out_r = out_r;
+    p.shared_rows = shared_rows;
     p.err = err;
     if (threadIdx.x == 0) {
         for (int s = 0; s < slots; ++s) mbar_init(&full[s], 1);
@@ -357,7 +367,7 @@ template <int WT, int R>
 __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
     const __grid_constant__ GemvMaps maps, const int4* __restrict__ items, const int* __restrict__ n_items,
     const uint8_t* const* __restrict__ wtiles, int n_ks, int glu, void* __restrict__ out, int out_ld,
-    int* err) {
+    __half* __restrict__ out_r, int shared_rows, int* err) {
     constexpr int TB = tile_bytes(WT);
     extern __shared__ uint8_t gsm_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
@@ -477,11 +487,16 @@ __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
                 o[static_cast<size_t>(row0 + n) * out_ld + rb * kGluHalf + j] =
                     __float2half_rn(silu_mul(sum(j, n), sum(kGluHalf + j, n)));
             }
-        } else {
+        } else if (row0 < shared_rows) {
             float* o = static_cast<float*>(out);
             for (int e = tid; e < kTileRows * nrows; e += kGemvThreads) {
                 const int r = e % kTileRows, n = e / kTileRows;
                 o[static_cast<size_t>(row0 + n) * out_ld + rb * kTileRows + r] = sum(r, n);
+            }
+        } else {
+            for (int e = tid; e < kTileRows * nrows; e += kGemvThreads) {
+                const int r = e % kTileRows, n = e / kTileRows;
+                out_r[static_cast<size_t>(row0 + n) * out_ld + rb * kTileRows + r] = __float2half_rn(sum(r, n));
             }
         }
         __syncthreads();  // red is free again
@@ -502,14 +517,14 @@ size_t stream_smem() {
 
 template <int WT, int R>
 cudaError_t launch_stream(const GemvMaps& maps, const int4* items, const int* n_items, int n_sms,
-                          const uint8_t* const* wtiles, int n_ks, int glu, void* out, int out_ld, int* err,
-                          cudaStream_t st) {
+                          const uint8_t* const* wtiles, int n_ks, int glu, void* out, int out_ld, __half* out_r,
+                          int shared_rows, int* err, cudaStream_t st) {
     const size_t smem = stream_smem<WT, R>();
     cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<WT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     gemv_stream_kernel<WT, R><<<n_sms, kGemvThreads, smem, st>>>(maps, items, n_items, wtiles, n_ks, glu, out,
-                                                                 out_ld, err);
+                                                                 out_ld, out_r, shared_rows, err);
     return cudaGetLastError();
 }
 
@@ -530,7 +545,7 @@ void gemv_smem(int max_box, int* slots, int* xb_max, size_t* smem) {
 template <int WT>
 cudaError_t launch_t(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
                      const uint8_t* const* wtiles, int n_ks, int glu, int max_rows, void* out,
-                     int out_ld, int* err, cudaStream_t st) {
+                     int out_ld, __half* out_r, int shared_rows, int* err, cudaStream_t st) {
     int slots = 0, xb_max = 0;
     size_t smem = 0;
     gemv_smem<WT>(box_index(max_rows), &slots, &xb_max, &smem);
@@ -538,7 +553,7 @@ cudaError_t launch_t(const GemvMaps& maps, const int4* items, const int* n_items
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     gemv_kernel<WT><<<max_items, kGemvThreads, smem, st>>>(maps, items, n_items, wtiles, n_ks, glu, slots,
-                                                           xb_max, out, out_ld, err);
+                                                           xb_max, out, out_ld, out_r, shared_rows, err);
     return cudaGetLastError();
 }
 
@@ -546,17 +561,18 @@ cudaError_t launch_t(const GemvMaps& maps, const int4* items, const int* n_items
 
 cudaError_t launch_gemv(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
                         const uint8_t* const* wtiles, int wtype, int n_ks, int glu, int max_rows,
-                        void* out, int out_ld, int* err, int n_sms, cudaStream_t st) {
+                        void* out, int out_ld, __half* out_r, int shared_rows, int* err, int n_sms,
+                        cudaStream_t st) {
     if (max_items <= 0) return cudaSuccess;
     if (max_rows < 1 || max_rows > kGemvMaxRows) return cudaErrorInvalidValue;
     if (max_rows <= 8 && wtype == W_Q8_0)
-        return launch_stream<W_Q8_0, 2>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, err, st);
+        return launch_stream<W_Q8_0, 2>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, out_r, shared_rows, err, st);
     if (max_rows <= 8 && wtype == W_Q4_0)
-        return launch_stream<W_Q4_0, 3>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, err, st);
+        return launch_stream<W_Q4_0, 3>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, out_r, shared_rows, err, st);
     switch (wtype) {
-        case W_Q4_0: return launch_t<W_Q4_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, err, st);
-        case W_Q8_0: return launch_t<W_Q8_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, err, st);
-        default: return launch_t<W_F16>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, err, st);
+        case W_Q4_0: return launch_t<W_Q4_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st);
+        case W_Q8_0: return launch_t<W_Q8_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st);
+        default: return launch_t<W_F16>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st);
     }
 }
 

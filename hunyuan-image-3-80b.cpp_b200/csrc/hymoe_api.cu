@@ -155,7 +155,8 @@ struct hymoe_ctx {
     int *slot_pos = nullptr, *n_items = nullptr, *err_word = nullptr;
     int4 *items_gu = nullptr, *items_dn = nullptr;
     __half *xp = nullptr, *hbuf = nullptr;
-    float* y = nullptr;
+    float* y = nullptr;        // shared expert's results [T, H] fp32
+    __half* yr = nullptr;      // routed results, fp16, same row numbers as xp
     uint8_t* tmp = nullptr;   // load / synthesis staging of one GGUF tensor
     size_t tmp_bytes = 0;
     GemmMaps maps_xp{}, maps_h{};
@@ -170,7 +171,7 @@ struct hymoe_ctx {
     ncclComm_t comm = nullptr;
     bool comm_broken = false;
     __half* xp_send = nullptr;   // [T*K, H] routed rows in destination order
-    float* y_ret = nullptr;      // [T*K, H] routed results back from their ranks
+    __half* y_ret = nullptr;     // [T*K, H] routed results back from their ranks (fp16)
     int* C_dev = nullptr;        // [N][E] gathered per-expert counts
     int* C_host = nullptr;       // pinned copy
     cudaEvent_t ev_counts = nullptr;
@@ -444,7 +445,7 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
     memcpy(mine.uuid, &prop.uuid, 16);
     mine.max_tokens = c->cfg.max_tokens;
     mine.ok = 1;
-    const void* bufs[3] = {c->xp, c->y, c->ep_meta};
+    const void* bufs[3] = {c->xp, c->yr, c->ep_meta};
     for (int i = 0; i < 3; ++i) {
         uintptr_t base = 0;
         if (!allocation_base(bufs[i], &base) || cudaIpcGetMemHandle(&mine.h[i], reinterpret_cast<void*>(base)) != cudaSuccess) {
@@ -495,7 +496,7 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
     for (int s = 0; s < N; ++s) all_ok = all_ok && recs[s].ok;
     EpPeers P{};
     P.xp[me] = c->xp;
-    P.y[me] = c->y;
+    P.yr[me] = c->yr;
     P.meta[me] = c->ep_meta;
     for (int s = 0; s < N && all_ok && mine.ok; ++s) {
         if (s == me) continue;
@@ -510,7 +511,7 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
         }
         if (!mine.ok) break;
         P.xp[s] = reinterpret_cast<__half*>(static_cast<char*>(ptr[0]) + recs[s].off[0]);
-        P.y[s] = reinterpret_cast<float*>(static_cast<char*>(ptr[1]) + recs[s].off[1]);
+        P.yr[s] = reinterpret_cast<__half*>(static_cast<char*>(ptr[1]) + recs[s].off[1]);
         P.meta[s] = reinterpret_cast<int*>(static_cast<char*>(ptr[2]) + recs[s].off[2]);
     }
     // second round: every rank learns whether every rank mapped every peer
@@ -627,7 +628,8 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     A(dalloc(&c->n_items_sh, 2));
     A(dalloc(&c->xp, rows * H));
     A(dalloc(&c->hbuf, rows * I));
-    A(dalloc(&c->y, rows * H));
+    A(dalloc(&c->y, T * H));
+    A(dalloc(&c->yr, rows * H));
     if (N > 1) {
         A(dalloc(&c->xp_send, T * K * H));
         A(dalloc(&c->y_ret, T * K * H));
@@ -709,6 +711,7 @@ void hymoe_destroy(hymoe_ctx* c) {
     cudaFree(c->xp);
     cudaFree(c->hbuf);
     cudaFree(c->y);
+    cudaFree(c->yr);
     cudaFree(c->tmp);
     if (c->comm) {
         if (c->comm_broken) ncclCommAbort(c->comm);
@@ -990,9 +993,9 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             HY_CUDA(c, launch_shared_prep(dx, T, H, c->xp, el, tiles_gu, tiles_dn, c->items_sh_gu, c->items_sh_dn,
                                           c->n_items_sh, side));
             HY_CUDA(c, launch_gemv(c->gmaps_xp, c->items_sh_gu, c->n_items_sh, tiles_gu, L.d_gu_ptrs, L.wtype,
-                                   H / kTileK, 1, T, c->hbuf, I, c->err_word, std::min(c->n_sms, tiles_gu), side));
+                                   H / kTileK, 1, T, c->hbuf, I, nullptr, 0, c->err_word, std::min(c->n_sms, tiles_gu), side));
             HY_CUDA(c, launch_gemv(c->gmaps_h, c->items_sh_dn, c->n_items_sh + 1, tiles_dn, L.d_dn_ptrs, L.wtype,
-                                   I / kTileK, 0, T, c->y, H, c->err_word, std::min(c->n_sms, tiles_dn), side));
+                                   I / kTileK, 0, T, c->y, H, c->yr, T, c->err_word, std::min(c->n_sms, tiles_dn), side));
             HY_CUDA(c, cudaEventRecord(c->ev_join, side));
         }
         if (T > 0) {
@@ -1129,11 +1132,11 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             c->phase_begin();
             const int mr = static_cast<int>(std::max<size_t>(1, gemv_rows));
             HY_CUDA(c, launch_gemv(c->gmaps_xp, c->items_gu, c->n_items, max_it, L.d_gu_ptrs, L.wtype, H / kTileK,
-                                   1, mr, c->hbuf, I, c->err_word, c->n_sms, st));
+                                   1, mr, c->hbuf, I, nullptr, 0, c->err_word, c->n_sms, st));
             c->phase_end(HYMOE_PHASE_GATE_UP);
             c->phase_begin();
             HY_CUDA(c, launch_gemv(c->gmaps_h, c->items_dn, c->n_items + 1, max_it, L.d_dn_ptrs, L.wtype,
-                                   I / kTileK, 0, mr, c->y, H, c->err_word, c->n_sms, st));
+                                   I / kTileK, 0, mr, c->y, H, c->yr, T, c->err_word, c->n_sms, st));
             c->phase_end(HYMOE_PHASE_DOWN);
         } else {
             GemmArgs ga{};
@@ -1157,20 +1160,22 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             ga.n_rb = tiles_dn;
             ga.glu = 0;
             ga.out = c->y;
+            ga.out_r = c->yr;
+            ga.shared_rows = T;
             ga.out_ld = H;
             c->phase_begin();
             HY_CUDA(c, launch_gemm_tc(c->maps_h, ga, c->n_sms, st));
             c->phase_end(HYMOE_PHASE_DOWN);
         }
 
-        const float* y_routed = c->y + static_cast<size_t>(T) * H;
+        const __half* y_routed = c->yr + static_cast<size_t>(T) * H;
         if (p2p) {
             // Results ready here; the combine reads every routed result from its owner's y.
             c->phase_begin();
             HY_CUDA(c, launch_ep_raise(c->peers, N, rank, kEpFlagReady, epoch, st));
             if (T > 0)
-                HY_CUDA(c, launch_ep_combine(c->peers, N, rank, el, c->topk_idx, c->slot_pos, c->topk_w, dres, dout,
-                                             T, H, K, epoch, budget_ns, c->err_word, st));
+                HY_CUDA(c, launch_ep_combine(c->peers, N, rank, el, c->topk_idx, c->slot_pos, c->topk_w, c->y, dres,
+                                             dout, T, H, K, epoch, budget_ns, c->err_word, st));
             else  // no tokens to combine: still wait, so that the next call's writes follow every owner's GEMMs
                 HY_CUDA(c, launch_ep_wait(c->peers, N, rank, kEpFlagReady, epoch, budget_ns, c->err_word, st));
             c->phase_end(HYMOE_PHASE_EP_COMBINE, 2);
@@ -1180,9 +1185,9 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             ncclGroupStart();
             for (int d = 0; d < N; ++d) {
                 if (recv_cnt[d])
-                    ncclSend(c->y + recv_off[d] * H, recv_cnt[d] * H, ncclFloat32, d, c->comm, st);
+                    ncclSend(c->yr + recv_off[d] * H, recv_cnt[d] * H, ncclFloat16, d, c->comm, st);
                 if (send_cnt[d])
-                    ncclRecv(c->y_ret + send_off[d] * H, send_cnt[d] * H, ncclFloat32, d, c->comm, st);
+                    ncclRecv(c->y_ret + send_off[d] * H, send_cnt[d] * H, ncclFloat16, d, c->comm, st);
             }
             ncclResult_t r = ncclGroupEnd();
             if (r != ncclSuccess && r != ncclInProgress)

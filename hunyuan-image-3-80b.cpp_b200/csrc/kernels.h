@@ -77,8 +77,8 @@ constexpr int kEpMaxRanks = 8;
 constexpr int kEpFlagCount = 0, kEpFlagDeliver = kEpMaxRanks, kEpFlagReady = 2 * kEpMaxRanks;
 constexpr int kEpCountOff = 3 * kEpMaxRanks;
 struct EpPeers {  // every rank's buffers as mapped in this process (own entry: local)
-    __half* xp[kEpMaxRanks];
-    float* y[kEpMaxRanks];
+    __half* xp[kEpMaxRanks];   // activation matrices
+    __half* yr[kEpMaxRanks];   // routed-result matrices (fp16, same rows as xp)
     int* meta[kEpMaxRanks];
 };
 cudaError_t launch_ep_counts(const EpPeers& p, int N, int me, int E, int T, const int* gcnt, uint32_t epoch,
@@ -90,8 +90,8 @@ cudaError_t launch_ep_wait(const EpPeers& p, int N, int me, int flag_off, uint32
                            int* err, cudaStream_t st);
 cudaError_t launch_ep_raise(const EpPeers& p, int N, int me, int flag_off, uint32_t epoch, cudaStream_t st);
 cudaError_t launch_ep_combine(const EpPeers& p, int N, int me, int el, const int* topk_idx, const int* slot_pos,
-                              const float* topk_w, const float* resid, float* out, int T, int H, int K,
-                              uint32_t epoch, uint64_t budget_ns, int* err, cudaStream_t st);
+                              const float* topk_w, const float* y_shared, const float* resid, float* out, int T,
+                              int H, int K, uint32_t epoch, uint64_t budget_ns, int* err, cudaStream_t st);
 
 // ---- gemm_tc.cu (tcgen05 grouped GEMM, 2-SM pairs)
 constexpr int kNumBoxes = 3;
@@ -107,8 +107,10 @@ struct GemmArgs {
     int wtype;
     int n_ks;                      // K / 64
     int n_rb;                      // 128-row tiles per group matrix
-    int glu;                       // 1: gate_up + SwiGLU epilogue -> fp16; 0: down -> fp32
-    void* out;                     // [rows, out_ld]
+    int glu;                       // 1: gate_up + SwiGLU epilogue -> fp16; 0: down projection
+    void* out;                     // gate_up: fp16 [rows, out_ld]; down: fp32 rows [0, shared_rows)
+    __half* out_r;                 // down: fp16 rows [shared_rows, ...) (routed results)
+    int shared_rows;
     int out_ld;
     int* err;
 };
@@ -122,13 +124,16 @@ struct GemvMaps {
 };
 // max_rows: the largest item (<= kGemvMaxRows); it sizes the activation stages.  Items of at
 // most 8 rows (Q4_0 / Q8_0) run on the persistent streaming variant with n_sms CTAs.
+// glu = 0 (down projection): rows below shared_rows go to `out` (fp32), the others to
+// `out_r` (fp16, routed results); glu = 1: `out` fp16.
 cudaError_t launch_gemv(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
                         const uint8_t* const* wtiles, int wtype, int n_ks, int glu, int max_rows,
-                        void* out, int out_ld, int* err, int n_sms, cudaStream_t st);
+                        void* out, int out_ld, __half* out_r, int shared_rows, int* err, int n_sms,
+                        cudaStream_t st);
 
 // ---- combine.cu
-// out[t] = resid[t] + y_shared[t] + sum_k w[t,k] * y_routed[slot_pos[t,k]]
-cudaError_t launch_combine(const float* y_shared, const float* y_routed, const int* slot_pos,
+// out[t] = resid[t] + y_shared[t] + sum_k w[t,k] * y_routed[slot_pos[t,k]] (routed rows fp16)
+cudaError_t launch_combine(const float* y_shared, const __half* y_routed, const int* slot_pos,
                            const float* topk_w, const float* resid, float* out, int T, int H,
                            int K, cudaStream_t st);
 
