@@ -13,21 +13,9 @@ namespace hymoe {
 
 namespace {
 
-// Eight consecutive fp16 values (16 bytes) as floats.
-__device__ __forceinline__ void load_half8(const __half* p, float (&f)[8]) {
-    const uint4 u = *reinterpret_cast<const uint4*>(p);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        f[2 * i] = v.x;
-        f[2 * i + 1] = v.y;
-    }
-}
-
 // Grid (H / 1024, T), 128 threads x 8 columns.  All K routed rows are loaded before the
 // arithmetic starts (K <= 8), so the loads overlap instead of following the FP chain.
-__global__ __launch_bounds__(128) void combine_kernel(const float* __restrict__ y_shared,
+__global__ __launch_bounds__(128, 10) void combine_kernel(const float* __restrict__ y_shared,
                                                       const __half* __restrict__ y_routed,
                                                       const int* __restrict__ slot_pos,
                                                       const float* __restrict__ topk_w,
@@ -36,14 +24,14 @@ __global__ __launch_bounds__(128) void combine_kernel(const float* __restrict__ 
     const int t = blockIdx.y;
     const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (j >= H) return;
-    float v[8][8];
+    uint4 u[8];  // raw fp16 rows (converted inside the sum: fewer live registers)
     float w[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         if (k < K) {
             const int pos = __ldg(slot_pos + t * K + k);
             w[k] = __ldg(topk_w + t * K + k);
-            load_half8(y_routed + static_cast<size_t>(pos) * H + j, v[k]);
+            u[k] = *reinterpret_cast<const uint4*>(y_routed + static_cast<size_t>(pos) * H + j);
         }
     }
     const float* sr = y_shared + static_cast<size_t>(t) * H + j;
@@ -61,8 +49,13 @@ __global__ __launch_bounds__(128) void combine_kernel(const float* __restrict__ 
     for (int i = 0; i < 8; ++i) {
         float r = 0.f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-            if (k < K) r = __fadd_rn(r, __fmul_rn(w[k], v[k][i]));
+        for (int k = 0; k < 8; ++k) {
+            if (k < K) {
+                const uint32_t wd = i < 2 ? u[k].x : i < 4 ? u[k].y : i < 6 ? u[k].z : u[k].w;
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wd));
+                r = __fadd_rn(r, __fmul_rn(w[k], (i & 1) ? f.y : f.x));
+            }
+        }
         o[i] = __fadd_rn(s[i], r);
         if (resid != nullptr) o[i] = __fadd_rn(h[i], o[i]);
     }
