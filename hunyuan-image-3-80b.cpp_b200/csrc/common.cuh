@@ -25,6 +25,11 @@ namespace hymoe {
 constexpr int kTileRows = 128;  // weight rows per tile
 constexpr int kTileK = 64;      // K elements per tile (two GGUF blocks)
 constexpr int kGluHalf = 64;    // gate (or up) rows per gate_up tile
+// Row order inside a gate_up tile: four groups of 32 rows, each 16 gate rows followed by the
+// matching 16 up rows, so one TMEM lane quarter (one warp) holds both SwiGLU halves of its 16
+// output columns.  Output column j (0..63) of the tile:
+__host__ __device__ constexpr int glu_gate_row(int j) { return 32 * (j >> 4) + (j & 15); }
+__host__ __device__ constexpr int glu_up_row(int j) { return 32 * (j >> 4) + 16 + (j & 15); }
 
 enum WType : int { W_F32 = 0, W_F16 = 1, W_Q4_0 = 2, W_Q8_0 = 8 };
 

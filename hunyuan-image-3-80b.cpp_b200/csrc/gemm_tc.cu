@@ -21,8 +21,11 @@
 //   warp 0      producer: TMA 2-D load of this CTA's B half (128B swizzle) + one bulk copy
 //               of its raw GGUF weight tile, both completing on the local full[s]
 //   warp 1      TMEM allocation for the pair; in the leader, the MMA issuer
-//   warps 2..5  epilogue: tcgen05.ld of this CTA's accumulator rows, transpose through
-//               shared memory, SwiGLU -> fp16 (gate_up) or fp32 (down)
+//   warps 2..5  epilogue: tcgen05.ld of this CTA's accumulator rows straight to registers
+//               (lane = output row of the tile): gate_up pairs each gate row with its up row
+//               in the same warp (tile row order of glu_gate_row / glu_up_row) by one
+//               shuffle per token pair, SwiGLU -> fp16; down stores fp32 (shared expert) or
+//               fp16 (routed) rows; one coalesced segment per token, no shared memory
 //   warps 6..13 dequantisers, two groups of four on alternate stages: GGUF Q4_0/Q8_0/F16
 //               tile -> fp16 A half in the canonical K-major 128B-swizzled layout, two
 //               (row, GGUF block) entries per thread; then arrive on the leader's a_ready[s]
@@ -62,13 +65,8 @@ namespace {
 constexpr int kThreads = 448;
 constexpr int kABytes = kTileRows * 128;        // 16 KB fp16 A half
 constexpr int kBBytes = kMaxBoxRows * 128;      // 16 KB fp16 B half (largest box)
-constexpr int kStageLd = 33;                    // epilogue staging row stride (floats)
 constexpr int kAccCols = 256;
 constexpr int kTmemCols = 512;
-
-__device__ __forceinline__ void named_bar_sync(int id, int n) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 
 __device__ __forceinline__ bool named_bar_and(int id, int n, bool p) {
     uint32_t r;
@@ -173,8 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sA = smem;
     uint8_t* sB = sA + STAGES * kABytes;
     uint8_t* sRaw = sB + STAGES * kBBytes;
-    float* sStage = reinterpret_cast<float*>(sRaw + STAGES * RAW);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + kTileRows * kStageLd);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + STAGES * RAW);
     uint64_t* full = bars;
     uint64_t* aready = full + STAGES;
     uint64_t* empty = aready + STAGES;
@@ -288,7 +285,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3;            // TMEM lane quarter this warp may access
         const int et = tid - 64;           // 0..127
-        const int tok = et >> 2, seg = et & 3;
         const uint32_t acc_empty_leader0 = mapa_shared(&acc_empty[0], 0);
         const uint32_t acc_empty_leader1 = mapa_shared(&acc_empty[1], 0);
         uint32_t tc = 0;
@@ -333,29 +329,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     continue;
                 }
-                float* srow = sStage + (q * 32 + lane) * kStageLd;
+                // gate_up: lanes 0-15 hold gate rows (output column 16q + lane), lanes 16-31 the
+                // matching up rows.  Lanes < 16 finish tokens 0-15 of the chunk, lanes >= 16
+                // tokens 16-31; one shuffle per token pair swaps the missing halves.
+                const bool gate_lane = lane < 16;
+                __half* o = static_cast<__half*>(a.out) + static_cast<size_t>(row0 + ch * 32) * a.out_ld +
+                            rb * kGluHalf + 16 * q + (lane & 15);
+                const int nj = min(32, nrows - ch * 32);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) srow[j] = __uint_as_float(v[j]);
-                named_bar_sync(1, 128);
-                const int c = ch * 32 + tok;
-                if (c < nrows) {
-                    const size_t row = static_cast<size_t>(row0 + c);
-                    uint32_t hv[8];
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) {
-                        const int j = seg * 16 + 2 * jj;
-                        const float h0 = silu_mul(sStage[j * kStageLd + tok],
-                                                  sStage[(kGluHalf + j) * kStageLd + tok]);
-                        const float h1 = silu_mul(sStage[(j + 1) * kStageLd + tok],
-                                                  sStage[(kGluHalf + j + 1) * kStageLd + tok]);
-                        hv[jj] = h2_bits(__floats2half2_rn(h0, h1));
-                    }
-                    uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + row * a.out_ld +
-                                                        rb * kGluHalf + seg * 16);
-                    o[0] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-                    o[1] = make_uint4(hv[4], hv[5], hv[6], hv[7]);
+                for (int k = 0; k < 16; ++k) {
+                    const float send = __uint_as_float(gate_lane ? v[16 + k] : v[k]);
+                    const float recv = __shfl_xor_sync(0xffffffffu, send, 16);
+                    const float gt = gate_lane ? __uint_as_float(v[k]) : recv;
+                    const float up = gate_lane ? recv : __uint_as_float(v[16 + k]);
+                    const int t = gate_lane ? k : 16 + k;
+                    if (t < nj) o[static_cast<size_t>(t) * a.out_ld] = __float2half_rn(silu_mul(gt, up));
                 }
-                named_bar_sync(1, 128);
             }
         }
     } else {
@@ -402,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int WT, int STAGES>
 constexpr size_t smem_bytes() {
-    return 1024 + STAGES * (kABytes + kBBytes + tile_bytes(WT)) + kTileRows * kStageLd * 4 +
+    return 1024 + STAGES * (kABytes + kBBytes + tile_bytes(WT)) +
            (3 * STAGES + 5) * 8 + 16;
 }
 
@@ -447,7 +436,7 @@ cudaError_t launch_typed(const GemmMaps& maps, const GemmArgs& a, int n_sms, cud
 
 cudaError_t launch_gemm_tc(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st) {
     switch (a.wtype) {
-        case W_Q4_0: return launch_typed<W_Q4_0, 5>(maps, a, n_sms, st);
+        case W_Q4_0: return launch_typed<W_Q4_0, 6>(maps, a, n_sms, st);
         case W_Q8_0: return launch_typed<W_Q8_0, 5>(maps, a, n_sms, st);
         case W_F16: return launch_typed<W_F16, 4>(maps, a, n_sms, st);
         default: return cudaErrorInvalidValue;

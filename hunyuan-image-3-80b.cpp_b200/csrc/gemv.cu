@@ -18,7 +18,7 @@
 // 2c, 2c+1, 2c+8, 2c+9, c = lane % 4, hold four CONSECUTIVE quants of a GGUF block) lets each
 // thread build its A fragments from wide shared-memory loads of raw quants; B columns are
 // token rows permuted so that the swizzled activation loads are free of bank conflicts too.
-// gate_up items end with the SwiGLU (silu of rows 0..63 times rows 64..127) and write fp16;
+// gate_up items end with the SwiGLU (silu of each gate row times its up row) and write fp16;
 // down items write fp32.
 #include "common.cuh"
 #include "kernels.h"
@@ -286,7 +286,7 @@ __device__ __forceinline__ void run_item(const GemvItem& p, uint8_t* base, uint6
         for (int i = tid; i < kGluHalf * nrows; i += kGemvThreads) {
             const int j = i % kGluHalf, n = i / kGluHalf;
             o[static_cast<size_t>(p.row0 + n) * p.out_ld + p.rb * kGluHalf + j] =
-                __float2half_rn(silu_mul(G[j * kGL + n], G[(kGluHalf + j) * kGL + n]));
+                __float2half_rn(silu_mul(G[glu_gate_row(j) * kGL + n], G[glu_up_row(j) * kGL + n]));
         }
     } else if (p.row0 < p.shared_rows) {
         float* o = static_cast<float*>(p.out);
@@ -485,7 +485,7 @@ __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
             for (int e = tid; e < kGluHalf * nrows; e += kGemvThreads) {
                 const int j = e % kGluHalf, n = e / kGluHalf;
                 o[static_cast<size_t>(row0 + n) * out_ld + rb * kGluHalf + j] =
-                    __float2half_rn(silu_mul(sum(j, n), sum(kGluHalf + j, n)));
+                    __float2half_rn(silu_mul(sum(glu_gate_row(j), n), sum(glu_up_row(j), n)));
             }
         } else if (row0 < shared_rows) {
             float* o = static_cast<float*>(out);

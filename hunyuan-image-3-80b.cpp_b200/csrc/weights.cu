@@ -36,8 +36,10 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, int src_type,
     const int r = e >> 1, b = e & 1;
     const int rb = rb_ks / n_ks, ks = rb_ks % n_ks;
     int srow;
-    if (glu_I > 0)
-        srow = r < kGluHalf ? kGluHalf * rb + r : glu_I + kGluHalf * rb + (r - kGluHalf);
+    if (glu_I > 0) {  // gate_up tile: groups of 16 gate rows and their 16 up rows
+        const int j = 16 * (r >> 5) + (r & 15);
+        srow = (r & 16) ? glu_I + kGluHalf * rb + j : kGluHalf * rb + j;
+    }
     else
         srow = kTileRows * rb + r;
     const int bsz = gguf_block_bytes(src_type);

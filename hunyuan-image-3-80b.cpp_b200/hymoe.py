@@ -11,7 +11,8 @@ import os
 import subprocess
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libhymoe.so")
+# HYMOE_LIB: load another build of the library (e.g. to compare two builds on one machine)
+LIB_PATH = os.environ.get("HYMOE_LIB") or os.path.join(HERE, "libhymoe.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "hymoe.h")
 
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0 = 0, 1, 2, 8
