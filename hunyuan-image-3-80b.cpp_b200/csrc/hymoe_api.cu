@@ -1,19 +1,24 @@
 // hymoe_api.cu — the C ABI (include/hymoe.h): context, device weight store, and the
 // per-call orchestration of the MoE block on one GPU or expert-parallel over several.
 //
-// Forward pipeline for one layer call (all on the context's stream):
-//   [H2D x, residual]        (HYMOE_HOST_PTRS only)
-//   router                   logits / softmax / top-K / renorm + per-chunk expert counts
-//   plan_kernel              per-expert counts, offsets and chunk bases of the pair sort
+// Forward pipeline for one layer call (on the context's stream):
+//   [H2D x, residual]        (HYMOE_HOST_PTRS; >= 2048 tokens: pipelined token chunks with
+//                            the copies on two copy streams)
+//   router                   logits (+ softmax / top-K / renorm + per-chunk expert counts)
+//   plan_kernel              per-expert counts, offsets and chunk bases of the pair sort and
+//                            the work items (topk_plan_kernel: top-K + plan, <= 16 tokens)
 //   scatter_gather_kernel    stable counting sort of (token, rank) pairs into fp16 rows;
 //                            shared-expert rows go to rows [0, T) of the GEMM input
-//   [expert parallel]        all-gather of per-expert counts, grouped ncclSend/ncclRecv
-//                            of routed rows to the ranks that own their experts
-//   items_kernel             GEMM work items from the row segments
-//   gate_up GEMM             tcgen05 grouped GEMM + SwiGLU epilogue -> h (fp16)
-//                            (grouped GEMV when n_tokens <= 8: decode regime)
-//   down GEMM                -> y (fp32)
-//   [expert parallel]        grouped ncclSend/ncclRecv of routed results back to sources
+//   [expert parallel]        peer memory: counts to every rank, rows stored straight into
+//                            the owners' matrices (ep_p2p.cu); or NCCL: all-gather of counts
+//                            and grouped ncclSend/ncclRecv of the routed rows
+//   items_kernel             GEMM work items from the row segments (expert parallel)
+//   gate_up GEMM             tcgen05 grouped GEMM + SwiGLU epilogue -> h (fp16); decode
+//                            sizes (groups <= 64 rows): weight-streaming kernels, the shared
+//                            expert on a forked stream for 4-8 tokens
+//   down GEMM                -> y (shared expert, fp32) and yr (routed, fp16)
+//   [expert parallel]        peer memory: ready flags, the combine reads owners' yr; or
+//                            NCCL: routed results back to their sources
 //   combine_kernel           out = residual + shared + sum_k w_k y_k
 //   [D2H out, debug]         (HYMOE_HOST_PTRS only)
 #include <cuda.h>
@@ -1180,7 +1185,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
                 HY_CUDA(c, launch_ep_wait(c->peers, N, rank, kEpFlagReady, epoch, budget_ns, c->err_word, st));
             c->phase_end(HYMOE_PHASE_EP_COMBINE, 2);
         } else if (ep) {
-            // Routed results back to the ranks their tokens came from (fp32, H per row).
+            // Routed results back to the ranks their tokens came from (fp16, H per row).
             c->phase_begin();
             ncclGroupStart();
             for (int d = 0; d < N; ++d) {

@@ -68,7 +68,12 @@ typedef struct {
     int32_t device;                 /* CUDA device ordinal                                */
     /* Expert parallelism: ep_size ranks each own num_experts/ep_size consecutive
      * experts.  ep_size == 1 runs everything locally.  For ep_size > 1,
-     * nccl_unique_id points at the 128-byte id from hymoe_nccl_unique_id() on rank 0. */
+     * nccl_unique_id points at the 128-byte id from hymoe_nccl_unique_id() on rank 0;
+     * every rank runs in its own process on its own GPU of one node.  Token rows and
+     * results move over NVLink peer memory (ep_size <= 8; the ranks map each other's
+     * buffers in hymoe_create), or by NCCL send/recv when the environment sets
+     * HYMOE_EP_TRANSPORT=nccl.  A peer that stops taking part ends the call with
+     * HYMOE_ERR_TIMEOUT after HYMOE_EP_TIMEOUT_S seconds (default 60). */
     int32_t ep_rank;
     int32_t ep_size;
     const void* nccl_unique_id;
