@@ -171,10 +171,12 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
+    # The sampler starts before the barrier: NVML initialisation takes a different time on
+    # each rank, and a rank that enters the timed loop late makes its peers' first step wait.
+    clocks = Clocks(local_rank)
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    clocks = Clocks(local_rank)
     m.profile(True)
     for s in range(args.steps):
         flush.zero_()
@@ -202,6 +204,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     oh = torch.empty_like(xh).pin_memory()
     for _ in range(2):
         m.forward_device(0, xh.data_ptr(), oh.data_ptr(), T, bias_ptr=bh.data_ptr(), host=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
     e2e_ms = 0.0
     for s in range(args.steps):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -229,6 +234,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                 "algorithmic_flop_per_launch": flop_gu}
     phases = {k: round(v[0] / args.steps, 4) for k, v in prof.items() if v[1]}
     launches = sum(v[1] for v in prof.values())
+    per_rank = None
+    if world > 1:  # every rank's rows and phases: the slowest rank sets the step time
+        per_rank = [None] * world
+        torch.distributed.all_gather_object(per_rank, {"rank": rank, "rows": rows, "phases": phases})
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
@@ -252,6 +261,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         "expert_load": {"max": int(counts.max()), "min": int(counts.min()),
                         "mean": float(counts.mean())},
     }
+    if per_rank is not None:
+        res["ep_ranks"] = per_rank
     m.close()
     if args.decode and world == 1:
         res["decode"] = run_decode(args, local_rank)
