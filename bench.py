@@ -18,10 +18,12 @@ generated on the device).  A step is one hymoe_forward over the 4096 tokens.
 
 --impl reference times the reference's CPU implementation with all host cores (token
 sharded over processes; the MoE is per-token independent) on the same workload.
-Under torchrun (N > 1) the layer runs expert-parallel: rank r owns experts
-[r*64/N, (r+1)*64/N) (plus the router and the shared expert), processes its own 4096 tokens,
-and tokens/results move by NCCL all-to-all inside the timed step (weak scaling: per-GPU
-tokens fixed).  --bias zipf gives the skewed-load variant of the expert-parallel config.
+Under torchrun (N > 1) the layer runs expert-parallel: rank r owns 64/N experts (plus the
+router and the shared expert) — by default those of its slots in a placement that balances
+the experts' routed rows on a calibration batch (--placement contiguous: experts
+[r*64/N, (r+1)*64/N)) — processes its own 4096 tokens, and token rows and results move over
+NVLink peer memory inside the timed step (weak scaling: per-GPU tokens fixed).  --bias zipf
+gives the skewed-load variant of the expert-parallel config.
 """
 from __future__ import annotations
 
@@ -148,6 +150,24 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     def step():
         m.forward_device(0, x.data_ptr(), out.data_ptr(), T, bias_ptr=bias.data_ptr())
 
+    place = None
+    if world > 1 and args.placement == "balanced":
+        # Expert placement from a calibration batch (its own seed, not the timed tokens): the
+        # routed rows of every expert over all ranks, balanced greedily over the ranks; then
+        # every rank loads the experts of its slots.
+        gc = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 500)
+        xc = torch.randn(T, H, device=dev, generator=gc, dtype=torch.float32)
+        cal_idx = torch.empty(T, K, dtype=torch.int32, device=dev)
+        m.forward_device(0, xc.data_ptr(), out.data_ptr(), T, bias_ptr=bias.data_ptr(),
+                         dbg=hymoe.Debug(None, None, None, cal_idx.data_ptr()))
+        torch.cuda.synchronize()
+        cal = torch.bincount(cal_idx.flatten().long(), minlength=E)
+        torch.distributed.all_reduce(cal)
+        place = hymoe.balance_placement(cal.cpu().tolist(), world)
+        m.set_placement(0, place)
+        m.synth_layer(0, hymoe.TYPE_Q8_0 if args.wtype == "q8_0" else hymoe.TYPE_Q4_0, args.seed, 0.02)
+        del xc, cal_idx
+
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -162,7 +182,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     if world > 1:  # rows this rank's GEMMs process: its T shared rows + the pairs it receives
         torch.distributed.all_reduce(counts_t)
         el = E // world
-        rows = T + int(counts_t[rank * el:(rank + 1) * el].sum())
+        slot_of = place if place is not None else list(range(E))
+        mine = [e for e in range(E) if slot_of[e] // el == rank]
+        rows = T + int(counts_t[mine].sum())
     else:
         rows = T * K + T
     flop_gu = rows * FLOP_PER_PAIR_GU
@@ -248,6 +270,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                    "model": "HunyuanImage-3.0 MoE block H=4096 I=3072 E=64+1 shared top-8",
                    "global_batch": T * world, "seq_len": T,
                    "parallelism": f"ep{world} (E/{world} experts per GPU; token rows and results over NVLink peer memory)" if world > 1 else "single",
+                   "placement": ("greedy balance of each expert's routed rows on a calibration batch (own seed)"
+                                 if place is not None else "contiguous (rank r owns experts [r*E/N, (r+1)*E/N))") if world > 1 else None,
                    "l2": "flushed between steps (256 MiB write outside the timed events)"},
         "tflops_total": round(flop_total / (ms_per_step / 1e3) / 1e12, 1),
         "frac_of_peak_total": round(flop_total / (ms_per_step / 1e3) / 1e12 / pk["tf_sus"], 4),
@@ -455,6 +479,8 @@ def main():
     # weights of the main (timed) workload: cfg3/cfg4 use Q4_0; q8_0 with --tokens 1..64 runs the
     # decode workload through the same path (used for kernel captures)
     ap.add_argument("--wtype", default="q4_0", choices=["q4_0", "q8_0"])
+    ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="expert placement across ranks (N > 1)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))

@@ -151,7 +151,7 @@ __global__ __launch_bounds__(1024) void topk_plan_kernel(const float* __restrict
     const int tid = threadIdx.x, warp = tid >> 5;
     if (tid < kMaxE) gcnt_s[tid] = 0;
     __syncthreads();
-    if (warp < T) topk_token(logits, warp, a.E, K, probs_out, topk_w, topk_idx, pbuf[warp], gcnt_s);
+    if (warp < T) topk_token(logits, warp, a.E, K, probs_out, topk_w, topk_idx, pbuf[warp], gcnt_s, a.slot_of);
     __syncthreads();
     if (tid < 64) goff_s[tid] = tid < a.E ? gcnt_s[tid] : 0;
     __syncthreads();
@@ -261,6 +261,11 @@ __global__ void ep_segments_kernel(const int* __restrict__ C, int ld, int N, int
     *n_segs = n;
 }
 
+__global__ void unmap_slots_kernel(int* __restrict__ idx, const int* __restrict__ expert_of_slot, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) idx[i] = __ldg(expert_of_slot + idx[i]);
+}
+
 }  // namespace
 
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st) {
@@ -277,6 +282,12 @@ cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, fl
 
 cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st) {
     items_kernel<<<1, 1024, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_unmap_slots(int* idx, const int* expert_of_slot, int n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    unmap_slots_kernel<<<(n + 255) / 256, 256, 0, st>>>(idx, expert_of_slot, n);
     return cudaGetLastError();
 }
 

@@ -150,6 +150,15 @@ struct hymoe_ctx {
     int e_local = 0, e_first = 0;
     size_t gu_group_bytes = 0, dn_group_bytes = 0;
     std::vector<LayerStore> layers;
+    // Expert placement per layer: empty = identity (slot s holds expert s).  Otherwise
+    // expert_of_slot[l][s] is the expert in slot s, and place_dev[l] holds [E] slot_of then
+    // [E] expert_of_slot on the device.  Slot s lives on rank s / e_local as local expert
+    // s % e_local.
+    std::vector<std::vector<int>> expert_of_slot;
+    std::vector<int*> place_dev;
+    int expert_at(uint32_t layer, int slot) const {
+        return expert_of_slot[layer].empty() ? slot : expert_of_slot[layer][slot];
+    }
 
     // scratch (sized for max_tokens at create; expert-parallel receive side included)
     size_t rows_cap = 0;
@@ -577,6 +586,8 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     c->e_first = cfg->ep_rank * c->e_local;
     c->groups = c->e_local + 1;
     c->layers.resize(cfg->num_layers);
+    c->expert_of_slot.resize(cfg->num_layers);
+    c->place_dev.assign(cfg->num_layers, nullptr);
     cudaDeviceGetAttribute(&c->n_sms, cudaDevAttrMultiProcessorCount, cfg->device);
 
     auto bail = [&](hymoe_status st) {
@@ -697,6 +708,7 @@ void hymoe_destroy(hymoe_ctx* c) {
     if (c->down_stream) cudaStreamSynchronize(c->down_stream);
     if (c->side_stream) cudaStreamSynchronize(c->side_stream);
     for (auto& L : c->layers) free_layer(L);
+    for (int* p : c->place_dev) cudaFree(p);
     cudaFree(c->x_dev);
     cudaFree(c->resid_dev);
     cudaFree(c->out_dev);
@@ -794,7 +806,7 @@ hymoe_status hymoe_load_layer(hymoe_ctx* c, uint32_t layer, const hymoe_tensor* 
     if (!tensor_ok(shared_gate_up, 2 * I, H, gt) || !tensor_ok(shared_down, H, I, gt))
         return c->fail(HYMOE_ERR_INVALID_ARG, "shared expert tensors: bad shape/type/size");
     for (int le = 0; le < c->e_local; ++le) {
-        const int ge = c->e_first + le;
+        const int ge = c->expert_at(layer, c->e_first + le);
         if (!tensor_ok(&experts_gate_up[ge], 2 * I, H, gt) || !tensor_ok(&experts_down[ge], H, I, gt))
             return c->fail(HYMOE_ERR_INVALID_ARG,
                            "expert %d tensors: bad shape/size or type differs from the shared expert", ge);
@@ -810,8 +822,9 @@ hymoe_status hymoe_load_layer(hymoe_ctx* c, uint32_t layer, const hymoe_tensor* 
                                host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice, c->stream));
     for (int g = 0; g < c->groups; ++g) {
         const bool shared = g == c->e_local;
-        const hymoe_tensor* tg = shared ? shared_gate_up : &experts_gate_up[c->e_first + g];
-        const hymoe_tensor* td = shared ? shared_down : &experts_down[c->e_first + g];
+        const int ge = shared ? 0 : c->expert_at(layer, c->e_first + g);
+        const hymoe_tensor* tg = shared ? shared_gate_up : &experts_gate_up[ge];
+        const hymoe_tensor* td = shared ? shared_down : &experts_down[ge];
         st = load_matrix(c, tg, L.gu + c->gu_group_bytes * g, wt, 2 * I, H, I, host);
         if (st == HYMOE_OK) st = load_matrix(c, td, L.dn + c->dn_group_bytes * g, wt, H, I, 0, host);
         if (st != HYMOE_OK) return st;
@@ -845,7 +858,7 @@ hymoe_status hymoe_synth_layer(hymoe_ctx* c, uint32_t layer, int32_t ggml_type, 
     HY_CUDA(c, launch_synth_f32(L.router, static_cast<uint64_t>(E) * H, seed, sid(1, 0), scale, c->stream));
     for (int g = 0; g < c->groups; ++g) {
         const bool shared = g == c->e_local;
-        const int idx = shared ? 0xFFFF : c->e_first + g;
+        const int idx = shared ? 0xFFFF : c->expert_at(layer, c->e_first + g);
         HY_CUDA(c, launch_synth_gguf(c->tmp, ggml_type, static_cast<uint64_t>(2 * I) * H, seed,
                                      sid(2, idx), scale, c->stream));
         HY_CUDA(c, launch_repack(c->tmp, ggml_type, L.gu + c->gu_group_bytes * g, wt, 2 * I, H, I,
@@ -857,6 +870,66 @@ hymoe_status hymoe_synth_layer(hymoe_ctx* c, uint32_t layer, int32_t ggml_type, 
     }
     HY_CUDA(c, cudaStreamSynchronize(c->stream));
     L.loaded = true;
+    return HYMOE_OK;
+}
+
+hymoe_status hymoe_set_placement(hymoe_ctx* c, uint32_t layer, const int32_t* slot_of_expert) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
+    const int E = c->E;
+    std::vector<int> expert_of(E, -1);
+    bool identity = true;
+    if (slot_of_expert) {
+        for (int e = 0; e < E; ++e) {
+            const int s = slot_of_expert[e];
+            if (s < 0 || s >= E || expert_of[s] >= 0)
+                return c->fail(HYMOE_ERR_INVALID_ARG, "placement is not a permutation of 0..%d (expert %d -> %d)",
+                                E - 1, e, s);
+            expert_of[s] = e;
+            identity = identity && s == e;
+        }
+    }
+    HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    HY_CUDA(c, cudaStreamSynchronize(c->stream));  // no call of this layer still reads the old map
+    c->clear_graphs();
+    c->layers[layer].loaded = false;  // the experts of this rank's slots change: load again
+    if (identity) {
+        cudaFree(c->place_dev[layer]);
+        c->place_dev[layer] = nullptr;
+        c->expert_of_slot[layer].clear();
+        return HYMOE_OK;
+    }
+    if (!c->place_dev[layer]) HY_CUDA(c, dalloc(&c->place_dev[layer], 2 * static_cast<size_t>(E)));
+    std::vector<int> both(slot_of_expert, slot_of_expert + E);
+    both.insert(both.end(), expert_of.begin(), expert_of.end());
+    HY_CUDA(c, cudaMemcpy(c->place_dev[layer], both.data(), sizeof(int) * 2 * E, cudaMemcpyHostToDevice));
+    c->expert_of_slot[layer] = expert_of;
+    return HYMOE_OK;
+}
+
+// Greedy longest-processing-time placement with exactly E/ep_size experts per rank: experts in
+// decreasing load (ties: lower expert first) each go to the least-loaded rank that still has a
+// free slot (ties: lower rank), taking that rank's next slot.
+hymoe_status hymoe_balance_placement(uint32_t n_experts, uint32_t ep_size, const double* load,
+                                     int32_t* slot_of_expert) {
+    if (!load || !slot_of_expert || n_experts == 0 || ep_size == 0 || n_experts % ep_size != 0)
+        return HYMOE_ERR_INVALID_ARG;
+    const int E = static_cast<int>(n_experts), N = static_cast<int>(ep_size), el = E / N;
+    std::vector<int> order(E);
+    for (int e = 0; e < E; ++e) {
+        if (!(load[e] >= 0.0)) return HYMOE_ERR_INVALID_ARG;  // negative or NaN
+        order[e] = e;
+    }
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return load[a] > load[b]; });
+    std::vector<double> sum(N, 0.0);
+    std::vector<int> used(N, 0);
+    for (int e : order) {
+        int best = -1;
+        for (int r = 0; r < N; ++r)
+            if (used[r] < el && (best < 0 || sum[r] < sum[best])) best = r;
+        slot_of_expert[e] = best * el + used[best]++;
+        sum[best] += load[e];
+    }
     return HYMOE_OK;
 }
 
@@ -875,6 +948,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         return c->fail(HYMOE_ERR_STATE, "expert-parallel communicator is unusable after an earlier failure");
     HY_CUDA(c, cudaSetDevice(c->cfg.device));
     const LayerStore& L = c->layers[layer];
+    const int* slot_of = c->place_dev[layer];  // nullptr: identity placement
     const int T = static_cast<int>(n_tokens), H = c->H, I = c->I, E = c->E, K = c->K;
     const int N = c->cfg.ep_size, rank = c->cfg.ep_rank, el = c->e_local;
     const bool host = (flags & HYMOE_HOST_PTRS) != 0;
@@ -1009,7 +1083,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             const bool fused = n_chunks == 1;
             c->phase_begin();
             HY_CUDA(c, launch_router(dx, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
-                                     c->topk_w, c->topk_idx, c->chunk_counts, !fused, st));
+                                     c->topk_w, c->topk_idx, c->chunk_counts, slot_of, !fused, st));
             c->phase_end(HYMOE_PHASE_ROUTER, fused ? 1 : 2);
             PlanArgs pa{};
             pa.chunk_counts = c->chunk_counts;
@@ -1023,6 +1097,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             pa.segs = ep ? nullptr : c->segs;
             pa.n_segs = c->n_segs;
             pa.shared_apart = shared_apart ? 1 : 0;
+            pa.slot_of = slot_of;
             pa.items = items_args(gemv);
             c->phase_begin();
             if (fused)
@@ -1213,8 +1288,11 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
                 const cudaMemcpyKind kd = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
                 if (dbg->topk_weights)
                     HY_CUDA(c, cudaMemcpyAsync(dbg->topk_weights, c->topk_w, sizeof(float) * T * K, kd, st));
-                if (dbg->topk_indices)
+                if (dbg->topk_indices) {
+                    if (slot_of)  // slots back to expert ids (topk_idx is not read again in this call)
+                        HY_CUDA(c, launch_unmap_slots(c->topk_idx, slot_of + E, static_cast<int>(T * K), st));
                     HY_CUDA(c, cudaMemcpyAsync(dbg->topk_indices, c->topk_idx, sizeof(int) * T * K, kd, st));
+                }
                 if (host && dlog)
                     HY_CUDA(c, cudaMemcpyAsync(dbg->router_logits, dlog, sizeof(float) * T * E, kd, st));
                 if (host && dprob)

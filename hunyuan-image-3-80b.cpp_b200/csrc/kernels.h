@@ -23,10 +23,12 @@ cudaError_t launch_synth_f32(float* dst, uint64_t n, uint64_t seed, uint64_t str
 // ---- router.cu
 constexpr int kRouterTok = 16;  // tokens per router CTA (= dispatch chunk)
 constexpr int kGemvMaxRows = 64; // token rows per GEMV work item
-// Logits, then (topk = true) the top-K kernel with per-chunk expert counts.
+// Logits, then (topk = true) the top-K kernel with per-chunk slot counts (slot_of: expert ->
+// placement slot, nullptr for slot = expert; topk_idx holds slots).
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
-                          int* topk_idx, int* chunk_counts, bool topk, cudaStream_t st);
+                          int* topk_idx, int* chunk_counts, const int* slot_of, bool topk,
+                          cudaStream_t st);
 
 // ---- dispatch.cu
 constexpr int kMaxSegs = 80;  // >= E + 1 (E <= 64)
@@ -49,6 +51,7 @@ struct PlanArgs {
     int4* segs;               // single-GPU segments + work items built in the same launch
     int* n_segs;              // (segs == NULL: expert-parallel mode, items built later)
     int shared_apart;         // 1: the shared expert runs as its own launch (no segment here)
+    const int* slot_of;       // fused top-K: expert -> placement slot (nullptr: identity)
     ItemsArgs items;
 };
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
@@ -57,6 +60,8 @@ cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, fl
                              int* topk_idx, const PlanArgs& a, cudaStream_t st);
 
 cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st);
+// idx[i] = expert_of_slot[idx[i]] for i < n (top-K slots back to expert ids for the caller).
+cudaError_t launch_unmap_slots(int* idx, const int* expert_of_slot, int n, cudaStream_t st);
 
 // xp_shared == nullptr: the shared expert's rows are written elsewhere (launch_shared_prep).
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,

@@ -13,10 +13,14 @@ namespace hymoe {
 constexpr int kMaxE = 64;
 
 // One warp routes token t.  pbuf: this warp's kMaxE floats of shared memory.  cnt: shared
-// per-expert counters of the caller's chunk (incremented for the token's K experts).
+// per-slot counters of the caller's chunk (incremented for the token's K selections).
+// slot_of: expert -> placement slot (nullptr: slot = expert).  Selection, ties and weights are
+// decided on expert ids; topk_idx and cnt receive the selected experts' slots, so every later
+// step (sort, dispatch, GEMM groups, combine) works in slot order.
 __device__ __forceinline__ void topk_token(const float* __restrict__ logits, int t, int E, int K,
                                            float* __restrict__ probs_out, float* __restrict__ topk_w,
-                                           int* __restrict__ topk_idx, float* pbuf, int* cnt) {
+                                           int* __restrict__ topk_idx, float* pbuf, int* cnt,
+                                           const int* __restrict__ slot_of) {
     const int lane = threadIdx.x & 31;
     const bool v0 = lane < E, v1 = lane + 32 < E;
     const float l0 = v0 ? logits[static_cast<size_t>(t) * E + lane] : -INFINITY;
@@ -76,8 +80,9 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ logits, int
     for (int k = 0; k < K; ++k) sw = __fadd_rn(sw, __shfl_sync(0xffffffffu, selp, k));
     if (lane < K) {
         topk_w[static_cast<size_t>(t) * K + lane] = __fdiv_rn(selp, sw);
-        topk_idx[static_cast<size_t>(t) * K + lane] = sele;
-        atomicAdd(&cnt[sele], 1);
+        const int slot = slot_of != nullptr ? __ldg(slot_of + sele) : sele;
+        topk_idx[static_cast<size_t>(t) * K + lane] = slot;
+        atomicAdd(&cnt[slot], 1);
     }
 }
 

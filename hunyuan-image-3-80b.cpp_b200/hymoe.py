@@ -27,7 +27,7 @@ STATUS_TIMEOUT = 6
 EXPORTS = ["hymoe_version", "hymoe_nccl_unique_id", "hymoe_create", "hymoe_destroy",
            "hymoe_last_error", "hymoe_set_stream", "hymoe_synchronize", "hymoe_load_layer",
            "hymoe_synth_layer", "hymoe_forward", "hymoe_profile", "hymoe_profile_read",
-           "hymoe_ffn_noalloc"]
+           "hymoe_ffn_noalloc", "hymoe_set_placement", "hymoe_balance_placement"]
 
 PHASES = ["router", "plan", "dispatch", "gate_up", "down", "combine", "ep_dispatch",
           "ep_combine"]
@@ -87,6 +87,8 @@ def lib() -> C.CDLL:
         L.hymoe_profile.argtypes = [vp, C.c_int]
         L.hymoe_ffn_noalloc.argtypes = [C.POINTER(Tensor), C.POINTER(Tensor), vp, vp, u32, vp]
         L.hymoe_profile_read.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(C.c_int32), C.c_int]
+        L.hymoe_set_placement.argtypes = [vp, u32, C.POINTER(C.c_int32)]
+        L.hymoe_balance_placement.argtypes = [u32, u32, C.POINTER(C.c_double), C.POINTER(C.c_int32)]
         for f in EXPORTS:
             if f not in ("hymoe_version", "hymoe_destroy", "hymoe_last_error"):
                 getattr(L, f).restype = C.c_int
@@ -100,6 +102,18 @@ def nccl_unique_id() -> bytes:
     if st != 0:
         raise HymoeError(st, "hymoe_nccl_unique_id failed")
     return buf.raw
+
+
+def balance_placement(load, ep_size: int) -> list:
+    """slot_of_expert (a list of E ints) balancing per-expert `load` over ep_size ranks
+    (hymoe_balance_placement: greedy, heaviest expert first)."""
+    E = len(load)
+    buf = (C.c_double * E)(*[float(v) for v in load])
+    out = (C.c_int32 * E)()
+    st = lib().hymoe_balance_placement(E, ep_size, buf, out)
+    if st != 0:
+        raise HymoeError(st, f"hymoe_balance_placement: invalid arguments (E={E}, ep_size={ep_size})")
+    return list(out)
 
 
 def gguf_nbytes(t: int, n: int) -> int:
@@ -173,6 +187,17 @@ class MoE:
         ed = (Tensor * E)(*[_tensor(a, wtype, H, I) for a in experts_dn])
         self._check(self.L.hymoe_load_layer(self.h, layer, C.byref(r), C.byref(sg), C.byref(sd),
                                             eg, ed, HOST_PTRS))
+
+    def set_placement(self, layer: int, slot_of_expert) -> None:
+        """Expert placement (a permutation of 0..E-1, or None for identity); load the layer
+        again afterwards."""
+        if slot_of_expert is None:
+            self._check(self.L.hymoe_set_placement(self.h, layer, None))
+            return
+        if len(slot_of_expert) != self.E:
+            raise ValueError(f"placement needs {self.E} entries, got {len(slot_of_expert)}")
+        arr = (C.c_int32 * self.E)(*[int(v) for v in slot_of_expert])
+        self._check(self.L.hymoe_set_placement(self.h, layer, arr))
 
     def synth_layer(self, layer: int, wtype: int, seed: int, std: float = 0.02) -> None:
         self._check(self.L.hymoe_synth_layer(self.h, layer, wtype, seed, std))

@@ -143,12 +143,33 @@ hymoe_status hymoe_load_layer(hymoe_ctx* ctx, uint32_t layer, const hymoe_tensor
                               const hymoe_tensor* experts_down, int flags);
 
 /* Fills a layer with synthetic weights generated on the device: every tensor ~N(0,std)
- * by the library's Philox4x32-10 / Irwin-Hall generator (stream layout documented in
- * DESIGN.md), quantised to `ggml_type` with the GGUF rule.  The router stays F32.
- * Bit-identical to the CPU generator of the test oracle.  No reference counterpart:
- * it exists so benchmarks can build 40+ GB of weights without a host round trip. */
+ * by the library's Philox4x32-10 / Irwin-Hall generator (one stream per tensor: layer in
+ * the high 32 bits, kind 1 router / 2 gate_up / 3 down in bits 16-31, expert index or
+ * 0xFFFF for the shared expert in the low 16), quantised to `ggml_type` with the GGUF
+ * rule.  The router stays F32.  Bit-identical to the CPU generator of the test oracle.
+ * Experts are those of this rank's placement slots.  No reference counterpart: it exists
+ * so benchmarks can build 40+ GB of weights without a host round trip. */
 hymoe_status hymoe_synth_layer(hymoe_ctx* ctx, uint32_t layer, int32_t ggml_type,
                                uint64_t seed, float stddev);
+
+/* Expert placement of one layer for expert parallelism.  slot_of_expert[e] (a
+ * permutation of 0..E-1; NULL = identity, the default) puts expert e in slot s, held by
+ * rank s / (E/ep_size) as its local expert s % (E/ep_size).  Every rank must set the same
+ * placement.  The layer's weights are marked unloaded: call hymoe_load_layer (or
+ * hymoe_synth_layer) afterwards, which then loads the experts of this rank's slots.
+ * Routing, outputs and the debug indices (expert ids) do not depend on the placement; it
+ * only decides which rank computes which expert, so a placement that evens out the
+ * ranks' expected rows shortens the slowest rank's GEMMs.  No reference counterpart (the
+ * reference runs on one CPU). */
+hymoe_status hymoe_set_placement(hymoe_ctx* ctx, uint32_t layer, const int32_t* slot_of_expert);
+
+/* Host helper (no context, no device): a placement for hymoe_set_placement that balances
+ * per-expert loads `load[n_experts]` (e.g. routed rows observed on a calibration batch)
+ * over ep_size ranks of n_experts/ep_size experts each — greedy, heaviest expert first
+ * (ties: lower expert), to the least-loaded rank with a free slot (ties: lower rank).
+ * HYMOE_ERR_INVALID_ARG unless n_experts % ep_size == 0 and every load is >= 0. */
+hymoe_status hymoe_balance_placement(uint32_t n_experts, uint32_t ep_size, const double* load,
+                                     int32_t* slot_of_expert);
 
 /* The MoE block of one decoder layer for n_tokens tokens:
  *   out[t] = residual[t] + shared(x[t]) + sum_k w[t,k] * expert_{idx[t,k]}(x[t])

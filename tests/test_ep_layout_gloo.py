@@ -6,7 +6,9 @@ tests/ep_layout.py, and check it end to end:
   receives are exactly [T_d, T_d + received) — no gaps, no overlaps, within capacity;
 - each received row falls in the segment (source, local expert) of its pair;
 - routing results back by the same rows reproduces every source's own pairs (the combine's
-  inputs), whatever the token counts (including a rank with no tokens).
+  inputs), whatever the token counts (including a rank with no tokens);
+- with an expert placement (top-K slots instead of expert ids; the owner computes the expert
+  its slot holds), every source still gets back the results of its own experts.
 
 Failure detection: a rank that stops taking part makes the others' next collective end with
 an error within a short process-group timeout (no hang).
@@ -30,7 +32,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, tokens, q):
+def _worker(rank, world, port, tokens, q, place=False):
     import torch
     import torch.distributed as dist
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
@@ -39,7 +41,11 @@ def _worker(rank, world, port, tokens, q):
         el = E // world
         T = tokens[rank]
         rng = np.random.default_rng(100 + rank)
-        topk = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]) if T else np.zeros((0, K), np.int64)
+        experts = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]) if T else np.zeros((0, K), np.int64)
+        # placement: the same seeded permutation on every rank (identity without one)
+        slot_of = np.random.default_rng(5).permutation(E) if place else np.arange(E)
+        expert_of = np.argsort(slot_of)
+        topk = slot_of[experts]  # what the top-K step hands on: slots
         counts = torch.from_numpy(np.bincount(topk.ravel(), minlength=E).astype(np.int64))
         allc = [torch.zeros(E, dtype=torch.int64) for _ in range(world)]
         dist.all_gather(allc, counts)  # the count exchange
@@ -75,12 +81,13 @@ def _worker(rank, world, port, tokens, q):
                 assert len(hit) == 1 and hit[0][3] == s and hit[0][0] == e - rank * el
         # results back: owner returns row r's "result" (the pair's id) to its source; each
         # source must see exactly its own pairs in (t, k) order
-        result = {int(r): int(tid) * 100 + int(e) for s, rr, ee, tt in recv for r, e, tid in zip(rr, ee, tt)}
+        # the owner runs the expert its slot holds
+        result = {int(r): int(tid) * 100 + int(expert_of[e]) for s, rr, ee, tt in recv for r, e, tid in zip(rr, ee, tt)}
         res_all = [None] * world
         dist.all_gather_object(res_all, result)
         if T:
             back = np.array([res_all[o][int(r)] for o, r in zip(owner.ravel(), row.ravel())]).reshape(T, K)
-            expect = (np.arange(T)[:, None] + 10000 * rank) * 100 + topk
+            expect = (np.arange(T)[:, None] + 10000 * rank) * 100 + experts
             assert np.array_equal(back, expect)
         q.put((rank, "ok"))
     except Exception as e:  # report instead of hanging the parent
@@ -89,11 +96,11 @@ def _worker(rank, world, port, tokens, q):
         dist.destroy_process_group()
 
 
-def _run(world, tokens):
+def _run(world, tokens, place=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, tokens, q)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, tokens, q, place)) for r in range(world)]
     for p in ps:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(world))
@@ -105,6 +112,12 @@ def _run(world, tokens):
 @pytest.mark.parametrize("world,tokens", [(2, [37, 20]), (2, [16, 0]), (4, [9, 0, 33, 4])])
 def test_ep_row_layout_over_gloo(world, tokens):
     res = _run(world, tokens)
+    assert all(v == "ok" for v in res.values()), res
+
+
+@pytest.mark.parametrize("world,tokens", [(2, [29, 11]), (4, [7, 25, 0, 16])])
+def test_ep_row_layout_with_expert_placement_over_gloo(world, tokens):
+    res = _run(world, tokens, place=True)
     assert all(v == "ok" for v in res.values()), res
 
 

@@ -34,7 +34,13 @@ def _layer(orc):
     return host_layer(orc, SEED, 0, H, I, E, WT)
 
 
-def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p"):
+def _placement(world):
+    """Balanced placement for the Zipf bias of call 0 (expected load ~ exp(bias))."""
+    import hymoe
+    return hymoe.balance_placement(list(np.exp(O.zipf_bias(SEED, E))), world)
+
+
+def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p", place=None):
     import sys
     os.environ["HYMOE_EP_TRANSPORT"] = transport
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -46,11 +52,14 @@ def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p"):
         orc = O2.Oracle()
         lay = host_layer(orc, SEED, 0, H, I, E, WT)
         el = E // world
-        mine = range(rank * el, (rank + 1) * el)
+        slot_of = place if place is not None else list(range(E))
+        mine = {e for e in range(E) if slot_of[e] // el == rank}
         egu = [lay["egu"][e] if e in mine else None for e in range(E)]
         edn = [lay["edn"][e] if e in mine else None for e in range(E)]
         m = hymoe.MoE(H, I, E, K, 1, max_tokens, device=rank, ep_rank=rank,
                       ep_size=world, nccl_id=nccl_id)
+        if place is not None:
+            m.set_placement(0, place)
         m.load_layer(0, lay["router"], lay["sgu"], lay["sdn"], egu, edn, WT)
         outs = []
         for call, t in enumerate(tokens):
@@ -63,14 +72,14 @@ def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p"):
         q.put((rank, f"error: {e!r}", None))
 
 
-def _run_ep(world, tokens_per_rank, transport="p2p"):
+def _run_ep(world, tokens_per_rank, transport="p2p", place=None):
     import hymoe
     nccl_id = hymoe.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     max_tokens = max(16, max(max(t) for t in tokens_per_rank))  # job-wide bound
     procs = [ctx.Process(target=_ep_worker,
-                         args=(r, world, nccl_id, tokens_per_rank[r], max_tokens, q, transport))
+                         args=(r, world, nccl_id, tokens_per_rank[r], max_tokens, q, transport, place))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -87,11 +96,17 @@ def _run_ep(world, tokens_per_rank, transport="p2p"):
 
 @pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("transport", ["p2p", "nccl"])
-@pytest.mark.parametrize("tokens", [[[200, 3], [150, 0]], [[64], [5]], [[300], [300]]])
-def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens, transport):
+@pytest.mark.parametrize("tokens,placed", [([[200, 3], [150, 0]], False), ([[64], [5]], False),
+                                           ([[300], [300]], False), ([[200, 3], [150, 0]], True),
+                                           ([[300], [300]], True)])
+def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens, placed, transport):
+    """placed: experts on ranks by hymoe_balance_placement (not the contiguous split)."""
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     world = 2
-    res = _run_ep(world, tokens, transport)
+    place = _placement(world) if placed else None
+    if placed:
+        assert place != list(range(E))
+    res = _run_ep(world, tokens, transport, place)
     import hymoe
     lay = _layer(orc)
     ncalls = len(tokens[0])

@@ -220,3 +220,34 @@ def test_host_pointer_call_in_chunks_is_bit_identical(orc):
     o = _oracle(orc, lay, x, K, I, bias=bias, resid=resid)
     assert rel_l2(host, o["out"]) <= REL_L2_TOL
     m.close()
+
+
+def test_expert_placement_keeps_outputs_and_expert_ids(orc):
+    """hymoe_set_placement: the same layer loaded under a permuted placement gives the same
+    bits (outputs, weights) and the same expert ids in the debug indices, on every path
+    (fused top-K + plan at T <= 16, the decode kernels, the tensor-core GEMM); a placement
+    marks the layer unloaded; a non-permutation is refused."""
+    H, I, E, K, seed, wt = 512, 256, 64, 8, 23, O.Q4_0
+    lay = host_layer(orc, seed, 0, H, I, E, wt)
+    m = _ctx(H, I, E, K, 300)
+    _load(m, lay, wt)
+    bias = O.zipf_bias(seed, E)
+    xs = {T: O.synth_x(orc, seed + T, T, H) for T in (5, 40, 300)}
+    ref = {T: m.forward_host(0, x, bias=bias, debug=True) for T, x in xs.items()}
+    perm = list(np.random.default_rng(9).permutation(E))
+    m.set_placement(0, perm)
+    with pytest.raises(hymoe.HymoeError) as ei:
+        m.forward_host(0, xs[5])
+    assert ei.value.status == 7  # load again after a placement
+    _load(m, lay, wt)
+    for T, x in xs.items():
+        got = m.forward_host(0, x, bias=bias, debug=True)
+        assert np.array_equal(got["idx"], ref[T]["idx"]), T
+        assert np.array_equal(got["w"], ref[T]["w"]), T
+        assert np.array_equal(got["out"], ref[T]["out"]), T
+    with pytest.raises(hymoe.HymoeError):
+        m.set_placement(0, [0] * E)
+    m.set_placement(0, None)
+    _load(m, lay, wt)
+    assert np.array_equal(m.forward_host(0, xs[40], bias=bias)["out"], ref[40]["out"])
+    m.close()
