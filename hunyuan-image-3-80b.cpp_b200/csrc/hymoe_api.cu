@@ -873,6 +873,86 @@ hymoe_status hymoe_synth_layer(hymoe_ctx* c, uint32_t layer, int32_t ggml_type, 
     return HYMOE_OK;
 }
 
+// GGUF block decode of a router stored quantised (the reference's converter labels every
+// tensor of a layer with one type, scripts/convert_to_gguf.py:196-200): standard blocks,
+// F16 exact, Q8_0 q*d, Q4_0 (q-8)*d with element j in the low nibble of byte j and j+16 in
+// the high nibble; products in f32.
+static float half_to_float(uint16_t h) {
+    const uint32_t sign = static_cast<uint32_t>(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1Fu, mant = h & 0x3FFu, bits;
+    if (exp == 0x1F) {
+        bits = sign | 0x7F800000u | (mant << 13);
+    } else if (exp != 0) {
+        bits = sign | ((exp + 112u) << 23) | (mant << 13);
+    } else if (mant == 0) {
+        bits = sign;
+    } else {  // subnormal: normalise
+        int e = -1;
+        do {
+            mant <<= 1;
+            ++e;
+        } while (!(mant & 0x400u));
+        bits = sign | ((112u - static_cast<uint32_t>(e)) << 23) | ((mant & 0x3FFu) << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+static bool dequant_router(const hymoe_tensor* t, std::vector<float>* out) {
+    const size_t n = static_cast<size_t>(t->ne[0]) * static_cast<size_t>(t->ne[1]);
+    out->resize(n);
+    const uint8_t* p = static_cast<const uint8_t*>(t->data);
+    switch (t->ggml_type) {
+        case HYMOE_TYPE_F16:
+            for (size_t i = 0; i < n; ++i) {
+                uint16_t h;
+                std::memcpy(&h, p + 2 * i, 2);
+                (*out)[i] = half_to_float(h);
+            }
+            return true;
+        case HYMOE_TYPE_Q8_0:
+        case HYMOE_TYPE_Q4_0: {
+            const bool q8 = t->ggml_type == HYMOE_TYPE_Q8_0;
+            const size_t bs = q8 ? 34 : 18;
+            for (size_t b = 0; b < n / 32; ++b) {
+                const uint8_t* blk = p + b * bs;
+                uint16_t h;
+                std::memcpy(&h, blk, 2);
+                const float d = half_to_float(h);
+                for (int j = 0; j < 32; ++j) {
+                    const int q = q8 ? static_cast<int>(static_cast<int8_t>(blk[2 + j]))
+                                     : static_cast<int>(j < 16 ? (blk[2 + j] & 0xF) : (blk[2 + j - 16] >> 4)) - 8;
+                    (*out)[b * 32 + j] = static_cast<float>(q) * d;
+                }
+            }
+            return true;
+        }
+        default:
+            return false;
+    }
+}
+
+hymoe_status hymoe_load_layer_gguf(hymoe_ctx* c, uint32_t layer, const hymoe_gguf* file, uint32_t layer_idx) {
+    if (!c || !file) return HYMOE_ERR_INVALID_ARG;
+    const int E = c->E;
+    std::vector<hymoe_tensor> egu(E), edn(E);
+    hymoe_tensor router{}, sgu{}, sdn{};
+    const hymoe_status st = hymoe_gguf_moe_tensors(file, layer_idx, E, &router, &sgu, &sdn, egu.data(), edn.data());
+    if (st != HYMOE_OK) return c->fail(st, "GGUF layer %u: %s", layer_idx, hymoe_gguf_last_error());
+    std::vector<float> rf;
+    if (router.ggml_type != HYMOE_TYPE_F32) {
+        if (router.ne[0] != c->H || router.ne[1] != E || router.nbytes != gguf_nbytes(router.ggml_type, static_cast<int64_t>(E) * c->H) ||
+            !dequant_router(&router, &rf))
+            return c->fail(HYMOE_ERR_INVALID_ARG, "GGUF layer %u: router [%lld, %lld] of type %d", layer_idx,
+                           static_cast<long long>(router.ne[1]), static_cast<long long>(router.ne[0]), router.ggml_type);
+        router.data = rf.data();
+        router.ggml_type = HYMOE_TYPE_F32;
+        router.nbytes = rf.size() * sizeof(float);
+    }
+    return hymoe_load_layer(c, layer, &router, &sgu, &sdn, egu.data(), edn.data(), HYMOE_HOST_PTRS);
+}
+
 hymoe_status hymoe_set_placement(hymoe_ctx* c, uint32_t layer, const int32_t* slot_of_expert) {
     if (!c) return HYMOE_ERR_INVALID_ARG;
     if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);

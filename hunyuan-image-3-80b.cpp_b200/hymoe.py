@@ -27,7 +27,9 @@ STATUS_TIMEOUT = 6
 EXPORTS = ["hymoe_version", "hymoe_nccl_unique_id", "hymoe_create", "hymoe_destroy",
            "hymoe_last_error", "hymoe_set_stream", "hymoe_synchronize", "hymoe_load_layer",
            "hymoe_synth_layer", "hymoe_forward", "hymoe_profile", "hymoe_profile_read",
-           "hymoe_ffn_noalloc", "hymoe_set_placement", "hymoe_balance_placement"]
+           "hymoe_ffn_noalloc", "hymoe_set_placement", "hymoe_balance_placement",
+           "hymoe_gguf_open", "hymoe_gguf_close", "hymoe_gguf_last_error", "hymoe_gguf_tensor",
+           "hymoe_gguf_get_u32", "hymoe_gguf_moe_tensors", "hymoe_load_layer_gguf"]
 
 PHASES = ["router", "plan", "dispatch", "gate_up", "down", "combine", "ep_dispatch",
           "ep_combine"]
@@ -89,8 +91,19 @@ def lib() -> C.CDLL:
         L.hymoe_profile_read.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(C.c_int32), C.c_int]
         L.hymoe_set_placement.argtypes = [vp, u32, C.POINTER(C.c_int32)]
         L.hymoe_balance_placement.argtypes = [u32, u32, C.POINTER(C.c_double), C.POINTER(C.c_int32)]
+        L.hymoe_gguf_open.argtypes = [C.c_char_p, C.POINTER(vp)]
+        L.hymoe_gguf_close.argtypes = [vp]
+        L.hymoe_gguf_close.restype = None
+        L.hymoe_gguf_last_error.argtypes = []
+        L.hymoe_gguf_last_error.restype = C.c_char_p
+        L.hymoe_gguf_tensor.argtypes = [vp, C.c_char_p, C.POINTER(Tensor)]
+        L.hymoe_gguf_get_u32.argtypes = [vp, C.c_char_p, C.POINTER(u32)]
+        L.hymoe_gguf_moe_tensors.argtypes = [vp, u32, u32, C.POINTER(Tensor), C.POINTER(Tensor),
+                                             C.POINTER(Tensor), C.POINTER(Tensor), C.POINTER(Tensor)]
+        L.hymoe_load_layer_gguf.argtypes = [vp, u32, vp, u32]
         for f in EXPORTS:
-            if f not in ("hymoe_version", "hymoe_destroy", "hymoe_last_error"):
+            if f not in ("hymoe_version", "hymoe_destroy", "hymoe_last_error", "hymoe_gguf_close",
+                         "hymoe_gguf_last_error"):
                 getattr(L, f).restype = C.c_int
         _LIB = L
     return _LIB
@@ -114,6 +127,64 @@ def balance_placement(load, ep_size: int) -> list:
     if st != 0:
         raise HymoeError(st, f"hymoe_balance_placement: invalid arguments (E={E}, ep_size={ep_size})")
     return list(out)
+
+
+class GGUF:
+    """A GGUF weight file opened by the library (hymoe_gguf_*): parsed, mapped read-only."""
+
+    def __init__(self, path: str):
+        self.L = lib()
+        h = C.c_void_p()
+        st = self.L.hymoe_gguf_open(os.fsencode(path), C.byref(h))
+        if st != 0:
+            raise HymoeError(st, self.L.hymoe_gguf_last_error().decode(errors="replace"))
+        self.h = h
+
+    def _check(self, st: int) -> None:
+        if st != 0:
+            raise HymoeError(st, self.L.hymoe_gguf_last_error().decode(errors="replace"))
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.L.hymoe_gguf_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @staticmethod
+    def _view(t: Tensor) -> dict:
+        import numpy as np
+        raw = np.ctypeslib.as_array(C.cast(t.data, C.POINTER(C.c_uint8)), shape=(t.nbytes,)).copy()
+        return {"type": t.ggml_type, "ne": (t.ne[0], t.ne[1]), "nbytes": t.nbytes, "bytes": raw}
+
+    def tensor(self, name: str) -> dict:
+        """{type, ne (GGUF order), nbytes, bytes (a copy of the raw blocks)}."""
+        t = Tensor()
+        self._check(self.L.hymoe_gguf_tensor(self.h, name.encode(), C.byref(t)))
+        return self._view(t)
+
+    def get_u32(self, key: str) -> int:
+        v = C.c_uint32()
+        self._check(self.L.hymoe_gguf_get_u32(self.h, key.encode(), C.byref(v)))
+        return v.value
+
+    def moe_tensors(self, layer_idx: int, n_experts: int) -> dict:
+        r, sg, sd = Tensor(), Tensor(), Tensor()
+        eg, ed = (Tensor * n_experts)(), (Tensor * n_experts)()
+        self._check(self.L.hymoe_gguf_moe_tensors(self.h, layer_idx, n_experts, C.byref(r), C.byref(sg),
+                                                  C.byref(sd), eg, ed))
+        return {"router": self._view(r), "sgu": self._view(sg), "sdn": self._view(sd),
+                "egu": [self._view(t) for t in eg], "edn": [self._view(t) for t in ed]}
 
 
 def gguf_nbytes(t: int, n: int) -> int:
@@ -198,6 +269,10 @@ class MoE:
             raise ValueError(f"placement needs {self.E} entries, got {len(slot_of_expert)}")
         arr = (C.c_int32 * self.E)(*[int(v) for v in slot_of_expert])
         self._check(self.L.hymoe_set_placement(self.h, layer, arr))
+
+    def load_layer_gguf(self, layer: int, file: GGUF, layer_idx: int) -> None:
+        """Loads decoder layer `layer_idx` of an open GGUF file into layer slot `layer`."""
+        self._check(self.L.hymoe_load_layer_gguf(self.h, layer, file.h, layer_idx))
 
     def synth_layer(self, layer: int, wtype: int, seed: int, std: float = 0.02) -> None:
         self._check(self.L.hymoe_synth_layer(self.h, layer, wtype, seed, std))

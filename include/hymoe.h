@@ -67,7 +67,8 @@ typedef struct {
                                        expert parallelism the same job-wide bound on every rank */
     int32_t device;                 /* CUDA device ordinal                                */
     /* Expert parallelism: ep_size ranks each own num_experts/ep_size consecutive
-     * experts.  ep_size == 1 runs everything locally.  For ep_size > 1,
+     * placement slots (consecutive experts unless hymoe_set_placement permutes them).
+     * ep_size == 1 runs everything locally.  For ep_size > 1,
      * nccl_unique_id points at the 128-byte id from hymoe_nccl_unique_id() on rank 0;
      * every rank runs in its own process on its own GPU of one node.  Token rows and
      * results move over NVLink peer memory (ep_size <= 8; the ranks map each other's
@@ -228,6 +229,49 @@ hymoe_status hymoe_profile_read(hymoe_ctx* ctx, float* total_ms, int32_t* launch
  * that overlap on the GPU (unordered streams) race and give wrong results. */
 hymoe_status hymoe_ffn_noalloc(const hymoe_tensor* gate_up, const hymoe_tensor* down,
                                const float* x, float* y, uint32_t n_tokens, void* stream);
+
+/* ---- GGUF weight files (replaces HunyuanGGUFLoader, src/hunyuan_gguf_loader.h:20-71, for
+ * the MoE tensors).  A file (GGUF version 2 or 3) is parsed by the library and mapped
+ * read-only; tensors are views of their raw GGUF blocks in the mapping, valid until
+ * hymoe_gguf_close.  Every count, length and extent in the file is checked against its
+ * size: a malformed file gives HYMOE_ERR_INVALID_ARG (HYMOE_ERR_UNSUPPORTED for another
+ * version), never a read outside the mapping.  Host-only: no context, no device. */
+typedef struct hymoe_gguf hymoe_gguf;
+
+/* Opens and parses `path` (HunyuanGGUFLoader::open_layer, src/hunyuan_gguf_loader.cpp:125). */
+hymoe_status hymoe_gguf_open(const char* path, hymoe_gguf** out);
+void hymoe_gguf_close(hymoe_gguf* file);
+/* Message of this thread's last failing hymoe_gguf_* call. */
+const char* hymoe_gguf_last_error(void);
+
+/* Tensor `name` as a host view: data in the mapping, ggml_type, ne[0] innermost (GGUF
+ * order: columns), ne[1] rows, nbytes of its blocks.  F32/F16/Q4_0/Q8_0 tensors of 1 or 2
+ * dimensions; other types or ranks give HYMOE_ERR_UNSUPPORTED
+ * (HunyuanGGUFLoader::load_tensor, src/hunyuan_gguf_loader.cpp:150-161, without the
+ * dequantisation). */
+hymoe_status hymoe_gguf_tensor(const hymoe_gguf* file, const char* name, hymoe_tensor* out);
+
+/* A u32 metadata value, e.g. "hunyuan.num_experts" (HunyuanGGUFLoader::get_metadata_u32,
+ * src/hunyuan_gguf_loader.cpp:286-291). */
+hymoe_status hymoe_gguf_get_u32(const hymoe_gguf* file, const char* key, uint32_t* out);
+
+/* The MoE tensors of decoder layer `layer_idx` under the reference converter's names
+ * (scripts/convert_to_gguf.py:70-137; read at src/hunyuan_gguf_loader.cpp:260-277):
+ * blk.N.ffn_gate (router), blk.N.ffn_shared_gate_up / _down, and
+ * blk.N.ffn_expert_E_gate_up / _down for E < n_experts (arrays of n_experts). */
+hymoe_status hymoe_gguf_moe_tensors(const hymoe_gguf* file, uint32_t layer_idx, uint32_t n_experts,
+                                    hymoe_tensor* router, hymoe_tensor* shared_gate_up,
+                                    hymoe_tensor* shared_down, hymoe_tensor* experts_gate_up,
+                                    hymoe_tensor* experts_down);
+
+/* hymoe_gguf_moe_tensors for the context's E experts, then hymoe_load_layer from the
+ * mapping (HYMOE_HOST_PTRS) into layer slot `layer` (HunyuanGGUFLoader::load_layer_weights,
+ * src/hunyuan_gguf_loader.cpp:229-281, for the MoE part).  Expert blocks are read as
+ * standard GGUF Q4_0/Q8_0 (not the reference loader's Q4_0 decode,
+ * src/hunyuan_gguf_loader.cpp:41-72).  A router stored as F16/Q8_0/Q4_0 (the reference's
+ * converter gives every tensor of a layer one type) is decoded to F32 on the host first. */
+hymoe_status hymoe_load_layer_gguf(hymoe_ctx* ctx, uint32_t layer, const hymoe_gguf* file,
+                                   uint32_t layer_idx);
 
 #ifdef __cplusplus
 }

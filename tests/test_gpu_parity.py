@@ -251,3 +251,35 @@ def test_expert_placement_keeps_outputs_and_expert_ids(orc):
     _load(m, lay, wt)
     assert np.array_equal(m.forward_host(0, xs[40], bias=bias)["out"], ref[40]["out"])
     m.close()
+
+
+@pytest.mark.parametrize("router_type", [O.F32, O.Q8_0])
+def test_load_layer_from_gguf_file_matches_load_layer(orc, tmp_path, router_type):
+    """hymoe_load_layer_gguf: a layer written under the reference converter's names gives
+    the same bits as hymoe_load_layer of the same blocks.  A router stored as Q8_0 is decoded
+    on the host with the standard rule (gguf-py's dequantize)."""
+    gguf = pytest.importorskip("gguf")
+    from gguf_layer import write_moe_layer
+    H, I, E, K, seed, wt = 512, 256, 64, 8, 29, O.Q4_0
+    lay = host_layer(orc, seed, 0, H, I, E, wt)
+    path = str(tmp_path / "layer7.gguf")
+    write_moe_layer(path, 7, H, I, lay["router"], lay["sgu"], lay["sdn"], lay["egu"], lay["edn"], wt,
+                    router_type=router_type)
+    router = lay["router"]
+    if router_type != O.F32:
+        qt = gguf.GGMLQuantizationType(router_type)
+        router = gguf.quants.dequantize(gguf.quants.quantize(router, qt), qt).astype(np.float32)
+    x = O.synth_x(orc, seed, 200, H)
+    ref = hymoe.MoE(H, I, E, K, 1, 200)
+    ref.load_layer(0, router, lay["sgu"], lay["sdn"], lay["egu"], lay["edn"], wt)
+    want = ref.forward_host(0, x, debug=True)
+    ref.close()
+    m = hymoe.MoE(H, I, E, K, 2, 200)
+    with hymoe.GGUF(path) as f:
+        m.load_layer_gguf(1, f, 7)
+        with pytest.raises(hymoe.HymoeError):
+            m.load_layer_gguf(0, f, 6)  # no such layer in the file
+    got = m.forward_host(1, x, debug=True)
+    assert np.array_equal(got["logits"], want["logits"])
+    assert np.array_equal(got["out"], want["out"])
+    m.close()
