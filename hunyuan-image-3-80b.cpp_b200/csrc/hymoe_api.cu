@@ -156,6 +156,11 @@ struct hymoe_ctx {
     // s % e_local.
     std::vector<std::vector<int>> expert_of_slot;
     std::vector<int*> place_dev;
+    // Post-attention RMSNorm per layer (hymoe_set_norm): [H] weights on the device (nullptr:
+    // none) and eps; x_norm holds the normalised rows of a HYMOE_PRE_NORM call.
+    std::vector<float*> norm_w;
+    std::vector<float> norm_eps;
+    float* x_norm = nullptr;
     int expert_at(uint32_t layer, int slot) const {
         return expert_of_slot[layer].empty() ? slot : expert_of_slot[layer][slot];
     }
@@ -588,6 +593,8 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     c->layers.resize(cfg->num_layers);
     c->expert_of_slot.resize(cfg->num_layers);
     c->place_dev.assign(cfg->num_layers, nullptr);
+    c->norm_w.assign(cfg->num_layers, nullptr);
+    c->norm_eps.assign(cfg->num_layers, 0.f);
     cudaDeviceGetAttribute(&c->n_sms, cudaDevAttrMultiProcessorCount, cfg->device);
 
     auto bail = [&](hymoe_status st) {
@@ -709,6 +716,8 @@ void hymoe_destroy(hymoe_ctx* c) {
     if (c->side_stream) cudaStreamSynchronize(c->side_stream);
     for (auto& L : c->layers) free_layer(L);
     for (int* p : c->place_dev) cudaFree(p);
+    for (float* p : c->norm_w) cudaFree(p);
+    cudaFree(c->x_norm);
     cudaFree(c->x_dev);
     cudaFree(c->resid_dev);
     cudaFree(c->out_dev);
@@ -953,6 +962,27 @@ hymoe_status hymoe_load_layer_gguf(hymoe_ctx* c, uint32_t layer, const hymoe_ggu
     return hymoe_load_layer(c, layer, &router, &sgu, &sdn, egu.data(), edn.data(), HYMOE_HOST_PTRS);
 }
 
+hymoe_status hymoe_set_norm(hymoe_ctx* c, uint32_t layer, const float* weight, float eps, int flags) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
+    if (!(eps >= 0.f) || eps == INFINITY) return c->fail(HYMOE_ERR_INVALID_ARG, "eps %g", static_cast<double>(eps));
+    HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    HY_CUDA(c, cudaStreamSynchronize(c->stream));  // no call still reads the old weights
+    c->clear_graphs();                             // eps is baked into captured launches
+    if (!weight) {
+        cudaFree(c->norm_w[layer]);
+        c->norm_w[layer] = nullptr;
+        return HYMOE_OK;
+    }
+    if (!c->x_norm) HY_CUDA(c, dalloc(&c->x_norm, static_cast<size_t>(c->cfg.max_tokens) * c->H));
+    if (!c->norm_w[layer]) HY_CUDA(c, dalloc(&c->norm_w[layer], static_cast<size_t>(c->H)));
+    const bool host = (flags & HYMOE_HOST_PTRS) != 0;
+    HY_CUDA(c, cudaMemcpy(c->norm_w[layer], weight, sizeof(float) * c->H,
+                          host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice));
+    c->norm_eps[layer] = eps;
+    return HYMOE_OK;
+}
+
 hymoe_status hymoe_set_placement(hymoe_ctx* c, uint32_t layer, const int32_t* slot_of_expert) {
     if (!c) return HYMOE_ERR_INVALID_ARG;
     if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
@@ -1023,6 +1053,9 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         return c->fail(HYMOE_ERR_INVALID_ARG, "n_tokens %u exceeds max_tokens %u", n_tokens,
                        c->cfg.max_tokens);
     if ((!x || !out) && n_tokens > 0) return c->fail(HYMOE_ERR_INVALID_ARG, "null x/out");
+    const bool pre_norm = (flags & HYMOE_PRE_NORM) != 0;
+    if (pre_norm && !c->norm_w[layer])
+        return c->fail(HYMOE_ERR_STATE, "layer %u has no RMSNorm weights (hymoe_set_norm)", layer);
     const bool ep = c->cfg.ep_size > 1;
     if (ep && (c->comm_broken || !c->comm))
         return c->fail(HYMOE_ERR_STATE, "expert-parallel communicator is unusable after an earlier failure");
@@ -1066,7 +1099,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             if (n <= 0) break;
             const size_t off = static_cast<size_t>(t0) * H, bytes = static_cast<size_t>(n) * H * sizeof(float);
             HY_CUDA(c, cudaMemcpyAsync(c->x_dev + off, x + off, bytes, cudaMemcpyHostToDevice, up));
-            if (residual)
+            if (residual && residual != x)
                 HY_CUDA(c, cudaMemcpyAsync(c->resid_dev + off, residual + off, bytes, cudaMemcpyHostToDevice, up));
             in[ch] = ev();
             HY_CUDA(c, cudaEventRecord(in[ch], up));
@@ -1077,7 +1110,8 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             if (n <= 0) break;
             const size_t off = static_cast<size_t>(t0) * H, bytes = static_cast<size_t>(n) * H * sizeof(float);
             HY_CUDA(c, cudaStreamWaitEvent(st, in[ch], 0));
-            result = hymoe_forward(c, layer, c->x_dev + off, residual ? c->resid_dev + off : nullptr, c->out_dev + off,
+            const float* r = !residual ? nullptr : residual == x ? c->x_dev + off : c->resid_dev + off;
+            result = hymoe_forward(c, layer, c->x_dev + off, r, c->out_dev + off,
                                    static_cast<uint32_t>(n), dbias, nullptr, flags & ~HYMOE_HOST_PTRS);
             cudaEvent_t done = ev();
             HY_CUDA(c, cudaEventRecord(done, st));
@@ -1101,7 +1135,9 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     if (host) {
         if (T > 0) HY_CUDA(c, cudaMemcpyAsync(c->x_dev, x, xbytes, cudaMemcpyHostToDevice, st));
         dx = c->x_dev;
-        if (residual && T > 0) {
+        if (residual && residual == x) {
+            dres = c->x_dev;  // decoder_layer form out = h + moe(...): one upload
+        } else if (residual && T > 0) {
             HY_CUDA(c, cudaMemcpyAsync(c->resid_dev, residual, xbytes, cudaMemcpyHostToDevice, st));
             dres = c->resid_dev;
         }
@@ -1121,6 +1157,15 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     const uint32_t epoch = p2p ? ++c->epoch : 0;
     const uint64_t budget_ns = static_cast<uint64_t>(c->ep_timeout_s * 1e9);
     auto device_part = [&]() -> hymoe_status {
+        // HYMOE_PRE_NORM: the layer's RMSNorm first; everything below reads the normalised rows
+        // (the residual stays the caller's).  Timed with the router phase.
+        const float* dxn = dx;
+        if (pre_norm && T > 0) {
+            c->phase_begin();
+            HY_CUDA(c, launch_rmsnorm(dx, c->norm_w[layer], c->norm_eps[layer], T, H, c->x_norm, st));
+            c->phase_end(HYMOE_PHASE_ROUTER);
+            dxn = c->x_norm;
+        }
         // Decode regime: every group has at most kGemvMaxRows rows (on one GPU a group has
         // at most T rows: the shared expert T, a routed expert at most one row per token).
         bool gemv = T <= kGemvMaxRows;
@@ -1149,7 +1194,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             cudaStream_t side = c->side_stream;
             HY_CUDA(c, cudaEventRecord(c->ev_fork, st));
             HY_CUDA(c, cudaStreamWaitEvent(side, c->ev_fork, 0));
-            HY_CUDA(c, launch_shared_prep(dx, T, H, c->xp, el, tiles_gu, tiles_dn, c->items_sh_gu, c->items_sh_dn,
+            HY_CUDA(c, launch_shared_prep(dxn, T, H, c->xp, el, tiles_gu, tiles_dn, c->items_sh_gu, c->items_sh_dn,
                                           c->n_items_sh, side));
             HY_CUDA(c, launch_gemv(c->gmaps_xp, c->items_sh_gu, c->n_items_sh, tiles_gu, L.d_gu_ptrs, L.wtype,
                                    H / kTileK, 1, T, c->hbuf, I, nullptr, 0, c->err_word, std::min(c->n_sms, tiles_gu), side));
@@ -1162,7 +1207,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             // T <= 16 (one router chunk): the top-K runs inside the plan launch.
             const bool fused = n_chunks == 1;
             c->phase_begin();
-            HY_CUDA(c, launch_router(dx, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
+            HY_CUDA(c, launch_router(dxn, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
                                      c->topk_w, c->topk_idx, c->chunk_counts, slot_of, !fused, st));
             c->phase_end(HYMOE_PHASE_ROUTER, fused ? 1 : 2);
             PlanArgs pa{};
@@ -1187,7 +1232,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             c->phase_end(HYMOE_PHASE_PLAN);
             if (!p2p) {  // peer-memory dispatch writes the rows straight to their owners
                 c->phase_begin();
-                HY_CUDA(c, launch_scatter_gather(dx, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
+                HY_CUDA(c, launch_scatter_gather(dxn, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
                                                  ep ? c->xp_send : c->xp + static_cast<size_t>(T) * H,
                                                  shared_apart ? nullptr : c->xp, st));
                 c->phase_end(HYMOE_PHASE_DISPATCH);
@@ -1203,7 +1248,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             c->phase_begin();
             HY_CUDA(c, launch_ep_counts(c->peers, N, rank, E, T, c->gcnt, epoch, budget_ns, c->err_word, st));
             if (T > 0)
-                HY_CUDA(c, launch_ep_scatter(c->peers, N, rank, E, el, T, H, K, dx, c->topk_idx, c->chunk_base,
+                HY_CUDA(c, launch_ep_scatter(c->peers, N, rank, E, el, T, H, K, dxn, c->topk_idx, c->chunk_base,
                                              c->goff, c->slot_pos, c->done_ctas, epoch, st));
             else
                 HY_CUDA(c, launch_ep_raise(c->peers, N, rank, kEpFlagDeliver, epoch, st));
@@ -1388,7 +1433,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         if (s2 != HYMOE_OK) return s2;
     } else {
         // One captured graph per (layer, token count, buffers); replayed while they repeat.
-        const GraphKey key{layer, n_tokens, dx, dres, dout, dbias, dlog, dprob,
+        const GraphKey key{layer | (pre_norm ? 0x80000000u : 0u), n_tokens, dx, dres, dout, dbias, dlog, dprob,
                            dbg ? dbg->topk_weights : nullptr, dbg ? dbg->topk_indices : nullptr};
         auto hit = c->graphs.find(key);
         if (hit == c->graphs.end()) {

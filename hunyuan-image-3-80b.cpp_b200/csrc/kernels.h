@@ -142,4 +142,9 @@ cudaError_t launch_combine(const float* y_shared, const __half* y_routed, const 
                            const float* topk_w, const float* resid, float* out, int T, int H,
                            int K, cudaStream_t st);
 
+// ---- norm.cu
+// out = rms_norm_f32(x, w, eps) over T rows of H (H % 128 == 0), the reference's rounding.
+cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int T, int H, float* out,
+                           cudaStream_t st);
+
 }  // namespace hymoe

@@ -18,6 +18,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "hymoe.h")
 TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q8_0 = 0, 1, 2, 8
 HOST_PTRS = 1
 USE_GRAPH = 2
+PRE_NORM = 4
 
 STATUS = {0: "OK", 1: "INVALID_ARG", 2: "CUDA", 3: "OOM", 4: "UNSUPPORTED", 5: "NCCL",
           6: "TIMEOUT", 7: "STATE"}
@@ -29,7 +30,8 @@ EXPORTS = ["hymoe_version", "hymoe_nccl_unique_id", "hymoe_create", "hymoe_destr
            "hymoe_synth_layer", "hymoe_forward", "hymoe_profile", "hymoe_profile_read",
            "hymoe_ffn_noalloc", "hymoe_set_placement", "hymoe_balance_placement",
            "hymoe_gguf_open", "hymoe_gguf_close", "hymoe_gguf_last_error", "hymoe_gguf_tensor",
-           "hymoe_gguf_get_u32", "hymoe_gguf_moe_tensors", "hymoe_load_layer_gguf"]
+           "hymoe_gguf_get_u32", "hymoe_gguf_moe_tensors", "hymoe_load_layer_gguf",
+           "hymoe_set_norm"]
 
 PHASES = ["router", "plan", "dispatch", "gate_up", "down", "combine", "ep_dispatch",
           "ep_combine"]
@@ -101,6 +103,7 @@ def lib() -> C.CDLL:
         L.hymoe_gguf_moe_tensors.argtypes = [vp, u32, u32, C.POINTER(Tensor), C.POINTER(Tensor),
                                              C.POINTER(Tensor), C.POINTER(Tensor), C.POINTER(Tensor)]
         L.hymoe_load_layer_gguf.argtypes = [vp, u32, vp, u32]
+        L.hymoe_set_norm.argtypes = [vp, u32, vp, C.c_float, C.c_int]
         for f in EXPORTS:
             if f not in ("hymoe_version", "hymoe_destroy", "hymoe_last_error", "hymoe_gguf_close",
                          "hymoe_gguf_last_error"):
@@ -270,6 +273,17 @@ class MoE:
         arr = (C.c_int32 * self.E)(*[int(v) for v in slot_of_expert])
         self._check(self.L.hymoe_set_placement(self.h, layer, arr))
 
+    def set_norm(self, layer: int, weight, eps: float) -> None:
+        """Post-attention RMSNorm weights [H] (host numpy float32; None removes them)."""
+        import numpy as np
+        if weight is None:
+            self._check(self.L.hymoe_set_norm(self.h, layer, None, eps, HOST_PTRS))
+            return
+        w = np.ascontiguousarray(weight, dtype=np.float32)
+        if w.shape != (self.H,):
+            raise ValueError(f"norm weight must be [{self.H}], got {w.shape}")
+        self._check(self.L.hymoe_set_norm(self.h, layer, w.ctypes.data, eps, HOST_PTRS))
+
     def load_layer_gguf(self, layer: int, file: GGUF, layer_idx: int) -> None:
         """Loads decoder layer `layer_idx` of an open GGUF file into layer slot `layer`."""
         self._check(self.L.hymoe_load_layer_gguf(self.h, layer, file.h, layer_idx))
@@ -277,8 +291,10 @@ class MoE:
     def synth_layer(self, layer: int, wtype: int, seed: int, std: float = 0.02) -> None:
         self._check(self.L.hymoe_synth_layer(self.h, layer, wtype, seed, std))
 
-    def forward_host(self, layer: int, x, resid=None, bias=None, debug: bool = False) -> dict:
-        """x (and resid) float32 [T, H] numpy; returns numpy outputs."""
+    def forward_host(self, layer: int, x, resid=None, bias=None, debug: bool = False,
+                     pre_norm: bool = False) -> dict:
+        """x (and resid) float32 [T, H] numpy; returns numpy outputs.  pre_norm: x is the
+        un-normalised hidden state (HYMOE_PRE_NORM); resid="x" passes x itself as residual."""
         import numpy as np
         x = np.ascontiguousarray(x, dtype=np.float32)
         T = x.shape[0]
@@ -291,19 +307,21 @@ class MoE:
                        w=np.empty((T, self.K), np.float32), idx=np.empty((T, self.K), np.int32))
             dbg = Debug(res["logits"].ctypes.data, res["probs"].ctypes.data,
                         res["w"].ctypes.data, res["idx"].ctypes.data)
-        r = None if resid is None else np.ascontiguousarray(resid, dtype=np.float32)
+        r = None if resid is None else x if isinstance(resid, str) and resid == "x" else \
+            np.ascontiguousarray(resid, dtype=np.float32)
         b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
         self._check(self.L.hymoe_forward(self.h, layer, x.ctypes.data,
                                          None if r is None else r.ctypes.data, out.ctypes.data, T,
                                          None if b is None else b.ctypes.data,
-                                         C.byref(dbg) if dbg else None, HOST_PTRS))
+                                         C.byref(dbg) if dbg else None,
+                                         HOST_PTRS | (PRE_NORM if pre_norm else 0)))
         return res
 
     def forward_device(self, layer: int, x_ptr: int, out_ptr: int, T: int, resid_ptr=None,
                        bias_ptr=None, dbg: Debug | None = None, host: bool = False,
-                       graph: bool = False) -> None:
+                       graph: bool = False, pre_norm: bool = False) -> None:
         """Raw pointers (device memory unless host=True); asynchronous on the set stream.
         graph=True replays a captured CUDA graph for repeated (layer, T, pointers)."""
-        flags = (HOST_PTRS if host else 0) | (USE_GRAPH if graph else 0)
+        flags = (HOST_PTRS if host else 0) | (USE_GRAPH if graph else 0) | (PRE_NORM if pre_norm else 0)
         self._check(self.L.hymoe_forward(self.h, layer, x_ptr, resid_ptr, out_ptr, T, bias_ptr,
                                          C.byref(dbg) if dbg else None, flags))

@@ -47,11 +47,18 @@ enum {
 /* flags for hymoe_load_layer / hymoe_forward */
 enum {
     HYMOE_HOST_PTRS = 1, /* pointers are host memory (copied H2D / D2H inside the call) */
-    HYMOE_USE_GRAPH = 2  /* hymoe_forward, one GPU, device pointers: capture the call's device
+    HYMOE_USE_GRAPH = 2, /* hymoe_forward, one GPU, device pointers: capture the call's device
                             work into a CUDA graph keyed by (layer, n_tokens, pointers) on first
                             use and replay it on later calls with the same key (removes launch
                             overhead in decode loops).  Graphs are dropped when a layer is
                             (re)loaded; profiling disables replay. */
+    HYMOE_PRE_NORM = 4   /* hymoe_forward: x is the un-normalised hidden state h; the call first
+                            applies the layer's post-attention RMSNorm (hymoe_set_norm) with the
+                            reference's rounding, rms_norm_f32 (src/rms_norm.cpp:9-33) as
+                            src/decoder_layer.cpp:34 applies it, and runs the MoE block on the
+                            result.  With residual == x the call is decoder_layer's
+                            out = h + moe(rms_norm(h)) (src/decoder_layer.cpp:34-42); with
+                            HYMOE_HOST_PTRS, residual == x uploads x once. */
 };
 
 typedef struct hymoe_ctx hymoe_ctx;
@@ -152,6 +159,12 @@ hymoe_status hymoe_load_layer(hymoe_ctx* ctx, uint32_t layer, const hymoe_tensor
  * so benchmarks can build 40+ GB of weights without a host round trip. */
 hymoe_status hymoe_synth_layer(hymoe_ctx* ctx, uint32_t layer, int32_t ggml_type,
                                uint64_t seed, float stddev);
+
+/* Post-attention RMSNorm weights of one layer for HYMOE_PRE_NORM calls: weight [H] F32
+ * (GGUF blk.N.ffn_norm.weight; host memory with HYMOE_HOST_PTRS, else device), eps
+ * (HunyuanConfig::rms_norm_eps, GGUF hunyuan.rms_norm_eps).  Copied; weight == NULL removes
+ * them.  The first call also allocates a [max_tokens, H] F32 buffer for the normalised rows. */
+hymoe_status hymoe_set_norm(hymoe_ctx* ctx, uint32_t layer, const float* weight, float eps, int flags);
 
 /* Expert placement of one layer for expert parallelism.  slot_of_expert[e] (a
  * permutation of 0..E-1; NULL = identity, the default) puts expert e in slot s, held by

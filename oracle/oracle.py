@@ -185,6 +185,7 @@ class RefMoE:
         L.hyref_moe_forward.argtypes = [_fp, C.c_void_p, u32, u32, u32, u32, _fp, _fp, _fp,
                                         _i32p]
         L.hyref_swiglu_ffn.argtypes = [_fp, _fp, _fp, _fp, u32, u32, u32]
+        L.hyref_rms_norm.argtypes = [_fp, _fp, _fp, u32, u32, C.c_float]
 
     @staticmethod
     def available() -> bool:
@@ -210,6 +211,14 @@ class RefMoE:
         self.L.hyref_moe_forward(_ptr(x, _fp), handle, T, H, I, K, _ptr(out, _fp),
                                  _ptr(probs, _fp), _ptr(tw, _fp), _ptr(ti, _i32p))
         return dict(out=out, probs=probs, w=tw, idx=ti)
+
+    def rms_norm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        """The reference's rms_norm_f32 (src/rms_norm.cpp:9-33)."""
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        out = np.empty_like(x)
+        self.L.hyref_rms_norm(_ptr(x, _fp), _ptr(w, _fp), _ptr(out, _fp), x.shape[0], x.shape[1], eps)
+        return out
 
 
 def synth_layer_f32(orc: Oracle, seed: int, layer: int, H: int, I: int, E: int, wtype: int,

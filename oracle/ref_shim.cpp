@@ -9,6 +9,7 @@
 // It builds the reference's MoEWeights / HunyuanConfig from plain pointers and calls
 //   moe_forward_cpu   (src/attention.cpp:191-313, decl src/hunyuan_model.h:147-156)
 //   swiglu_ffn_f32    (src/rms_norm.cpp:39-91)
+//   rms_norm_f32      (src/rms_norm.cpp:9-33)
 // unchanged.
 #include "hunyuan_model.h"
 
@@ -67,6 +68,11 @@ void hyref_moe_forward(const float* x, const void* weights, uint32_t T, uint32_t
 void hyref_swiglu_ffn(const float* x, const float* gate_up, const float* down, float* out,
                       uint32_t n, uint32_t H, uint32_t I) {
     swiglu_ffn_f32(x, gate_up, down, out, n, H, I);
+}
+
+void hyref_rms_norm(const float* x, const float* weight, float* out, uint32_t T, uint32_t H,
+                    float eps) {
+    rms_norm_f32(x, weight, out, T, H, eps);
 }
 
 }  // extern "C"

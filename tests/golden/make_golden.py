@@ -60,6 +60,22 @@ def run_case(orc: O.Oracle, ref: O.RefMoE, name, H, I, E, K, T, wt, seed):
     print(f"{name}: reference {dt:.2f}s -> {os.path.getsize(path)} bytes")
 
 
+def run_rms_norm(orc: O.Oracle, ref: O.RefMoE) -> None:
+    """rms_norm_f32 (src/rms_norm.cpp:9-33) on rows of very different scales, with the inputs
+    stored (they are small)."""
+    rng = np.random.default_rng(7)
+    cases = {}
+    for name, T, H, eps in (("h512", 9, 512, 1e-5), ("h4096", 3, 4096, 1e-6)):
+        x = O.synth_x(orc, 31 + H, T, H)
+        x *= np.float32(10.0) ** rng.integers(-6, 5, size=(T, 1)).astype(np.float32)
+        w = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        cases[name] = (x, w, eps, ref.rms_norm(x, w, eps))
+    path = os.path.join(HERE, "rms_norm.npz")
+    np.savez_compressed(path, **{f"{n}_{k}": v for n, (x, w, eps, out) in cases.items()
+                                 for k, v in (("x", x), ("w", w), ("eps", np.float32(eps)), ("out", out))})
+    print(f"rms_norm: {os.path.getsize(path)} bytes")
+
+
 def main():
     orc = O.Oracle()
     ref = O.RefMoE()
@@ -67,6 +83,8 @@ def main():
     for c in CASES:
         if not only or c[0] in only:
             run_case(orc, ref, *c)
+    if not only or "rms_norm" in only:
+        run_rms_norm(orc, ref)
 
 
 if __name__ == "__main__":

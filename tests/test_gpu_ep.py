@@ -40,7 +40,10 @@ def _placement(world):
     return hymoe.balance_placement(list(np.exp(O.zipf_bias(SEED, E))), world)
 
 
-def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p", place=None):
+NORM_W = (1.0 + 0.05 * np.cos(np.arange(H))).astype(np.float32)
+
+
+def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p", place=None, pre_norm=False):
     import sys
     os.environ["HYMOE_EP_TRANSPORT"] = transport
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -61,25 +64,29 @@ def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p", pla
         if place is not None:
             m.set_placement(0, place)
         m.load_layer(0, lay["router"], lay["sgu"], lay["sdn"], egu, edn, WT)
+        if pre_norm:
+            m.set_norm(0, NORM_W, 1e-5)
         outs = []
         for call, t in enumerate(tokens):
             x = O2.synth_x(orc, SEED + 100 * call + rank, t, H)
             bias = O2.zipf_bias(SEED + call, E)
-            outs.append(m.forward_host(0, x, bias=bias, debug=True))
+            outs.append(m.forward_host(0, x, bias=bias, debug=True, resid="x" if pre_norm else None,
+                                       pre_norm=pre_norm))
         m.close()
         q.put((rank, "ok", outs))
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, f"error: {e!r}", None))
 
 
-def _run_ep(world, tokens_per_rank, transport="p2p", place=None):
+def _run_ep(world, tokens_per_rank, transport="p2p", place=None, pre_norm=False):
     import hymoe
     nccl_id = hymoe.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     max_tokens = max(16, max(max(t) for t in tokens_per_rank))  # job-wide bound
     procs = [ctx.Process(target=_ep_worker,
-                         args=(r, world, nccl_id, tokens_per_rank[r], max_tokens, q, transport, place))
+                         args=(r, world, nccl_id, tokens_per_rank[r], max_tokens, q, transport, place,
+                               pre_norm))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -131,6 +138,28 @@ def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens, placed, tran
                 o = orc.moe_forward(x, lay["router"], lay["sgu_f"], lay["sdn_f"], lay["egu_f"],
                                     lay["edn_f"], K, I, bias=bias)
                 assert rel_l2(ep_out["out"], o["out"]) <= REL_L2_TOL
+    single.close()
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
+def test_expert_parallel_pre_norm_matches_single_gpu(orc, transport):
+    """HYMOE_PRE_NORM on every rank: the dispatched rows are the normalised ones, the residual
+    the raw ones; bit-identical to the single-GPU call (all calls on the tensor-core path)."""
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    tokens = [[200], [130]]
+    res = _run_ep(2, tokens, transport, pre_norm=True)
+    import hymoe
+    lay = _layer(orc)
+    single = hymoe.MoE(H, I, E, K, 1, 216, device=0)
+    single.load_layer(0, lay["router"], lay["sgu"], lay["sdn"], lay["egu"], lay["edn"], WT)
+    single.set_norm(0, NORM_W, 1e-5)
+    bias = O.zipf_bias(SEED, E)
+    for rank in range(2):
+        x = O.synth_x(orc, SEED + rank, tokens[rank][0], H)
+        ref = single.forward_host(0, x, bias=bias, debug=True, resid="x", pre_norm=True)
+        assert np.array_equal(res[rank][0]["idx"], ref["idx"])
+        assert np.array_equal(res[rank][0]["out"], ref["out"]), f"rank {rank}"
     single.close()
 
 

@@ -283,3 +283,66 @@ def test_load_layer_from_gguf_file_matches_load_layer(orc, tmp_path, router_type
     assert np.array_equal(got["logits"], want["logits"])
     assert np.array_equal(got["out"], want["out"])
     m.close()
+
+
+@pytest.mark.parametrize("T", [1, 5, 40, 300])
+def test_pre_norm_is_the_reference_rms_norm_then_the_block(orc, T):
+    """HYMOE_PRE_NORM with residual = x is decoder_layer's out = h + moe(rms_norm(h))
+    (src/decoder_layer.cpp:34-42).  The device RMSNorm keeps the reference's rounding, so the
+    call gives the same bits (logits, routing, output) as the block run on the oracle's
+    rms_norm (itself pinned bit-exactly to the reference's rms_norm_f32 on the CPU)."""
+    H, I, E, K, seed, wt = 512, 256, 64, 8, 31, O.Q4_0
+    lay = host_layer(orc, seed, 0, H, I, E, wt)
+    m = _ctx(H, I, E, K, T)
+    _load(m, lay, wt)
+    rng = np.random.default_rng(T)
+    h = (O.synth_x(orc, seed + T, T, H) * 10.0 ** rng.integers(-3, 3, size=(T, 1))).astype(np.float32)
+    w = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    eps = 1e-5
+    with pytest.raises(hymoe.HymoeError) as ei:
+        m.forward_host(0, h, pre_norm=True)
+    assert ei.value.status == 7  # no RMSNorm weights yet
+    m.set_norm(0, w, eps)
+    xn = orc.rms_norm(h, w, eps)
+    want = m.forward_host(0, xn, resid=h, debug=True)
+    got = m.forward_host(0, h, resid="x", debug=True, pre_norm=True)
+    for k in ("logits", "idx", "w", "out"):
+        assert np.array_equal(got[k], want[k]), k
+    o = _oracle(orc, lay, xn, K, I, resid=h)
+    assert rel_l2(got["out"], o["out"]) <= REL_L2_TOL
+    m.close()
+
+
+def test_pre_norm_chunked_host_call_and_graph_replay(orc):
+    """The pipelined host-pointer call (>= 2048 tokens, x uploaded once as its own residual)
+    and a replayed CUDA graph give the same bits as the eager device call."""
+    torch = pytest.importorskip("torch")
+    H, I, E, K, seed, wt = 512, 256, 64, 8, 37, O.Q8_0
+    T = 4200
+    lay = host_layer(orc, seed, 0, H, I, E, wt)
+    m = _ctx(H, I, E, K, T)
+    _load(m, lay, wt)
+    rng = np.random.default_rng(3)
+    w = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    m.set_norm(0, w, 1e-6)
+    h = O.synth_x(orc, seed, T, H)
+    host = m.forward_host(0, h, resid="x", pre_norm=True)["out"]
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        m.set_stream(st.cuda_stream)
+        xd = torch.from_numpy(h).cuda()
+        od = torch.empty_like(xd)
+        m.forward_device(0, xd.data_ptr(), od.data_ptr(), T, resid_ptr=xd.data_ptr(), pre_norm=True)
+        m.synchronize()
+        assert np.array_equal(od.cpu().numpy(), host)
+        t = 6
+        xs = torch.empty(t, H, device="cuda")
+        os_ = torch.empty_like(xs)
+        for call in range(3):
+            xs.copy_(torch.from_numpy(O.synth_x(orc, seed + call, t, H)))
+            m.forward_device(0, xs.data_ptr(), os_.data_ptr(), t, resid_ptr=xs.data_ptr(), graph=True,
+                             pre_norm=True)
+            m.synchronize()
+            eager = m.forward_host(0, xs.cpu().numpy(), resid="x", pre_norm=True)["out"]
+            assert np.array_equal(os_.cpu().numpy(), eager), f"call {call}"
+    m.close()

@@ -1,6 +1,8 @@
 """CPU tests of the oracle (the checker): generator known answers, binary16 and GGUF
 block formats against numpy / gguf-py, and the MoE restatement against the golden
 fixtures produced by the reference's own moe_forward_cpu."""
+import os
+
 import numpy as np
 import pytest
 
@@ -117,3 +119,22 @@ def test_restatement_matches_compiled_reference(orc, seed):
     o = orc.moe_forward(x, rw, sgu, sdn, egu, edn, K, I)
     for k in ("out", "idx", "w", "probs"):
         assert np.array_equal(r[k], o[k]), k
+
+
+def test_rms_norm_restatement_matches_reference_golden(orc):
+    """oracle_rms_norm against the reference's rms_norm_f32 (src/rms_norm.cpp:9-33) outputs
+    stored in tests/golden/rms_norm.npz: bit-identical, rows spanning 1e-6 .. 1e4 in scale."""
+    d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "rms_norm.npz"))
+    for n in ("h512", "h4096"):
+        got = orc.rms_norm(d[f"{n}_x"], d[f"{n}_w"], float(d[f"{n}_eps"]))
+        assert np.array_equal(got, d[f"{n}_out"]), n
+
+
+@pytest.mark.skipif(not O.RefMoE.available(), reason="reference checker not built here")
+def test_rms_norm_restatement_matches_compiled_reference(orc):
+    ref = O.RefMoE()
+    rng = np.random.default_rng(5)
+    for T, H, eps in ((1, 128, 1e-5), (17, 384, 1e-6), (4, 4096, 0.0)):
+        x = (rng.standard_normal((T, H)) * 10.0 ** rng.integers(-5, 5, size=(T, 1))).astype(np.float32)
+        w = rng.standard_normal(H).astype(np.float32)
+        assert np.array_equal(orc.rms_norm(x, w, eps), ref.rms_norm(x, w, eps))
