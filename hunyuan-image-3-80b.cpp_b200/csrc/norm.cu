@@ -4,12 +4,13 @@
 // (every product rounded, then added: no fused multiply-add), rms = 1 / sqrt(sum / H + eps)
 // with IEEE-rounded division and square root, and out = (x * rms) * w[j] rounded left to right.
 //
-// The chain is inherently serial per token (H dependent adds), so tokens run in parallel:
-// a CTA owns 32 tokens, one chain per lane of warp 0, fed from shared memory.  All 256 threads
-// stage 32 x 128-column chunks with coalesced 16-byte loads, the next chunk's loads in flight
-// (registers) while warp 0 sums the current one; rows are padded to 132 floats so the 32
-// chain lanes' 16-byte reads hit distinct banks.  The normalised rows are then written by all
-// threads (x re-read through L2).  HBM bound: 8 bytes per element (x read, out written).
+// The chain is inherently serial per token (H dependent adds), so tokens run in parallel: a CTA
+// owns 16 tokens, one chain per lane of its first half-warp, fed from shared memory.  All 256
+// threads copy 16 x 128-column chunks into a 4-stage ring with 16-byte cp.async (three chunks in
+// flight while the current one is summed); rows are padded to 132 floats so the chain lanes'
+// 16-byte reads hit distinct banks.  The normalised rows are then written by all threads, four
+// independent 16-byte loads in flight per thread (x re-read, mostly from L2).  HBM bound: 8 bytes
+// per element (x read once from HBM, out written).
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -18,49 +19,47 @@
 namespace hymoe {
 namespace {
 
-constexpr int kNormTok = 32;            // tokens per CTA
+constexpr int kNormTok = 16;            // tokens per CTA
 constexpr int kNormCols = 128;          // columns per staged chunk
 constexpr int kNormLd = kNormCols + 4;  // padded row stride (floats)
+constexpr int kNormStages = 4;
 constexpr int kNormThreads = 256;
-constexpr int kNormLoads = kNormTok * kNormCols / 4 / kNormThreads;  // float4 per thread per chunk
+constexpr int kNormCopies = kNormTok * kNormCols / 4 / kNormThreads;  // 16-byte copies per thread per chunk
+constexpr int kNormUnroll = 4;
 
 __global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const float* __restrict__ x,
                                                                const float* __restrict__ w, float eps,
                                                                int T, int H, float* __restrict__ out) {
-    __shared__ __align__(16) float tile[2][kNormTok * kNormLd];
+    __shared__ __align__(16) float tile[kNormStages][kNormTok * kNormLd];
     __shared__ float rms_s[kNormTok];
     const int t0 = blockIdx.x * kNormTok;
     const int tid = threadIdx.x;
-    float4 r[kNormLoads];
-    auto load = [&](int c0) {
-#pragma unroll
-        for (int i = 0; i < kNormLoads; ++i) {
-            const int idx = tid + i * kNormThreads;
-            const int row = idx / (kNormCols / 4), q = idx % (kNormCols / 4);
-            const int t = t0 + row;
-            r[i] = t < T ? __ldg(reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H + c0) + q)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    };
-    auto store = [&](int buf) {
-#pragma unroll
-        for (int i = 0; i < kNormLoads; ++i) {
-            const int idx = tid + i * kNormThreads;
-            const int row = idx / (kNormCols / 4), q = idx % (kNormCols / 4);
-            *reinterpret_cast<float4*>(&tile[buf][row * kNormLd + 4 * q]) = r[i];
-        }
-    };
-    float ss = 0.f;
     const int n_chunks = H / kNormCols;
-    load(0);
+    auto issue = [&](int c) {
+        float* dst = tile[c % kNormStages];
+#pragma unroll
+        for (int i = 0; i < kNormCopies; ++i) {
+            const int idx = tid + i * kNormThreads;
+            const int row = idx / (kNormCols / 4), q = idx % (kNormCols / 4);
+            const int t = min(t0 + row, T - 1);  // rows past T copy a valid row; never written out
+            cp_async16(dst + row * kNormLd + 4 * q, x + static_cast<size_t>(t) * H + c * kNormCols + 4 * q);
+        }
+    };
+#pragma unroll
+    for (int c = 0; c < kNormStages - 1; ++c) {
+        if (c < n_chunks) issue(c);
+        cp_async_commit();
+    }
+    float ss = 0.f;
     for (int c = 0; c < n_chunks; ++c) {
-        // buffer c&1 was last read by warp 0 in chunk c-2, which it finished before the
-        // barrier of chunk c-1
-        store(c & 1);
+        cp_async_wait<kNormStages - 2>();  // this thread's copies of chunk c have landed
+        // every thread's copies of chunk c have landed, and the chain lanes are done with chunk
+        // c-1, whose stage the next issue reuses
         __syncthreads();
-        if (c + 1 < n_chunks) load((c + 1) * kNormCols);
+        if (c + kNormStages - 1 < n_chunks) issue(c + kNormStages - 1);
+        cp_async_commit();  // possibly empty: keeps the group count per iteration fixed
         if (tid < kNormTok) {
-            const float* row = &tile[c & 1][tid * kNormLd];
+            const float* row = &tile[c % kNormStages][tid * kNormLd];
 #pragma unroll 8
             for (int j = 0; j < kNormCols; j += 4) {
                 const float4 v = *reinterpret_cast<const float4*>(row + j);
@@ -71,23 +70,38 @@ __global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const float* __re
             }
         }
     }
+    cp_async_wait<0>();
     if (tid < kNormTok)
         rms_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(H)), eps)));
     __syncthreads();
     const int n4 = H / 4;
-    for (int i = tid; i < kNormTok * n4; i += kNormThreads) {
-        const int row = i / n4, q = i - row * n4;
-        const int t = t0 + row;
-        if (t >= T) break;  // rows grow with i
-        const float4 v = __ldg(reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H) + q);
-        const float4 g = __ldg(reinterpret_cast<const float4*>(w) + q);
-        const float s = rms_s[row];
-        float4 o;
-        o.x = __fmul_rn(__fmul_rn(v.x, s), g.x);
-        o.y = __fmul_rn(__fmul_rn(v.y, s), g.y);
-        o.z = __fmul_rn(__fmul_rn(v.z, s), g.z);
-        o.w = __fmul_rn(__fmul_rn(v.w, s), g.w);
-        reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H)[q] = o;
+    const int rows = min(kNormTok, T - t0);
+    const int total = rows * n4;
+    for (int base = tid; base < total; base += kNormUnroll * kNormThreads) {
+        float4 v[kNormUnroll], g[kNormUnroll];
+#pragma unroll
+        for (int u = 0; u < kNormUnroll; ++u) {
+            const int i = base + u * kNormThreads;
+            if (i < total) {
+                const int row = i / n4, q = i - row * n4;
+                v[u] = __ldg(reinterpret_cast<const float4*>(x + static_cast<size_t>(t0 + row) * H) + q);
+                g[u] = __ldg(reinterpret_cast<const float4*>(w) + q);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kNormUnroll; ++u) {
+            const int i = base + u * kNormThreads;
+            if (i < total) {
+                const int row = i / n4, q = i - row * n4;
+                const float s = rms_s[row];
+                float4 o;
+                o.x = __fmul_rn(__fmul_rn(v[u].x, s), g[u].x);
+                o.y = __fmul_rn(__fmul_rn(v[u].y, s), g[u].y);
+                o.z = __fmul_rn(__fmul_rn(v[u].z, s), g[u].z);
+                o.w = __fmul_rn(__fmul_rn(v[u].w, s), g[u].w);
+                reinterpret_cast<float4*>(out + static_cast<size_t>(t0 + row) * H)[q] = o;
+            }
+        }
     }
 }
 

@@ -39,16 +39,6 @@ constexpr int kStages = 3;
 constexpr int kDecodeMaxT = 8;
 constexpr int kSmallMaxT = 64;
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Two IEEE single-precision products, each rounded to nearest, in one packed instruction
 // (sm_100 f32x2): the same results as two __fmul_rn.
 __device__ __forceinline__ float2 mul2_rn(float ax, float ay, float bx, float by) {
