@@ -287,6 +287,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     }
     if per_rank is not None:
         res["ep_ranks"] = per_rank
+    if args.cpu and world == 1:
+        # the reference on a token sample of the same seeded layer; the GPU runs the same tokens
+        gf = (lambda xs: m.forward_host(0, xs, debug=True)) if args.wtype == "q4_0" else None
+        res["cpu_baseline"], res["parity"] = cpu_baseline_single(args.seed, gpu_forward=gf)
     m.close()
     if args.decode and world == 1:
         res["decode"] = run_decode(args, local_rank)
@@ -368,28 +372,61 @@ def _cpu_inputs(n_tokens: int, seed: int):
     return O, orc, x, w
 
 
-def cpu_baseline_single(seed: int, n_tokens: int = 12) -> dict:
-    """The reference's own moe_forward_cpu, one core (as written), on a token sample."""
+def parity_stats(gpu: dict, ref_out, ref_idx, k: int, tol: float = 1e-3, gap: float = 1e-4) -> dict:
+    """Bench-line parity of a GPU call against the reference on the same tokens: output
+    relative L2 (tolerance 1e-3) and top-K agreement, tokens whose K-th/(K+1)-th logit gap is
+    at most 1e-4 excluded as near ties (the GPU's pre-softmax logits equal the reference's)."""
+    import numpy as np
+    out = np.asarray(gpu["out"], np.float64)
+    ref = np.asarray(ref_out, np.float64)
+    rel = float(np.linalg.norm(out - ref) / max(np.linalg.norm(ref), 1e-30))
+    same = ties = bad = 0
+    for t in range(ref.shape[0]):
+        if np.array_equal(gpu["idx"][t], ref_idx[t]):
+            same += 1
+            continue
+        srt = np.sort(gpu["logits"][t])[::-1]
+        if srt[k - 1] - srt[k] <= gap:
+            ties += 1
+        else:
+            bad += 1
+    n = ref.shape[0]
+    return {"tokens": n, "rel_l2": rel, "rel_l2_tol": tol, "topk_match": same / n,
+            "near_ties_excluded": ties, "topk_mismatches": bad, "ok": bad == 0 and rel <= tol}
+
+
+def cpu_baseline_single(seed: int, n_tokens: int = 12, gpu_forward=None):
+    """The reference's own moe_forward_cpu, one core (as written), on a token sample; with
+    gpu_forward (tokens -> forward_host result with debug outputs) also the parity of the GPU
+    on the same tokens.  Returns (cpu_baseline, parity or None)."""
     O, orc, x, w = _cpu_inputs(n_tokens, seed)
     if O.RefMoE.available():
         ref = O.RefMoE()
         h = ref.weights(H, I, *w)
         t0 = time.perf_counter()
-        ref.moe_forward(x, h, E, H, I, K)
+        r = ref.moe_forward(x, h, E, H, I, K)
         dt = time.perf_counter() - t0
         ref.free(h)
         kind = "reference"
     else:
         one = O.Oracle(nthreads=1)
         t0 = time.perf_counter()
-        one.moe_forward(x, *w, K, I)
+        r = one.moe_forward(x, *w, K, I)
         dt = time.perf_counter() - t0
         kind = "port"
-    return {"value": round(n_tokens / dt, 3), "unit": "tokens/s", "cores": 1, "kind": kind,
+    base = {"value": round(n_tokens / dt, 3), "unit": "tokens/s", "cores": 1, "kind": kind,
             "sample": f"{n_tokens} tokens of the cfg3 workload through moe_forward_cpu "
                       f"(src/attention.cpp:191-313), F32-dequantised Q4_0 weights, no router bias "
                       f"(the reference has none; same per-token cost), "
                       f"{dt:.2f} s; host has {os.cpu_count()} cores"}
+    parity = None
+    if gpu_forward is not None:
+        try:
+            parity = parity_stats(gpu_forward(x), r["out"], r["idx"], K)
+            parity["against"] = kind
+        except Exception as e:  # reported, never fatal to the bench line
+            parity = {"error": repr(e)[:200]}
+    return base, parity
 
 
 def run_reference(args, rank: int, world: int) -> dict | None:
@@ -502,8 +539,6 @@ def main():
                                              device_id=torch.device("cuda", local_rank))
     res = run_gpu(args, rank, world, local_rank)
     if rank == 0:
-        if args.cpu and world == 1:
-            res["cpu_baseline"] = cpu_baseline_single(args.seed)
         print(json.dumps(res), flush=True)
     if world > 1:
         import torch
