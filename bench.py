@@ -297,6 +297,111 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     return res
 
 
+STACK_LAYERS, STACK_SEQ = 32, 4160
+STACK_METRIC = "MoE-stack tokens/s (32 Q4_0 MoE blocks, 4160-token sequence, layer by layer)"
+
+
+def run_stack(args, rank: int, world: int, local_rank: int) -> dict:
+    """cfg5: 32 MoE blocks (Q4_0, random-init per layer from one seed) applied layer by layer to
+    one 4160-token sequence, x <- x + MoE_l(RMSNorm(x)) with unit RMSNorm weights (the
+    post-attention half of src/decoder_layer.cpp:34-42; eps 1e-5), in place
+    (HYMOE_PRE_NORM, residual = out = x).  The sequence is split over the ranks, each of which
+    holds E/N experts of every layer.  A step is the whole stack; `value` = sequence tokens per
+    second (device time, max over ranks); `e2e` adds the upload of x and the download of the
+    result through the host API."""
+    import numpy as np
+    import torch
+    import hymoe
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    L = STACK_LAYERS
+    per = (STACK_SEQ + world - 1) // world
+    T = max(0, min(per, STACK_SEQ - rank * per))  # this rank's slice of the sequence
+    if world > 1:
+        box = [hymoe.nccl_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(box, src=0)
+        m = hymoe.MoE(H, I, E, K, L, per, device=local_rank, ep_rank=rank, ep_size=world, nccl_id=box[0])
+    else:
+        m = hymoe.MoE(H, I, E, K, L, per, device=local_rank)
+    ones = np.ones(H, np.float32)
+    for l in range(L):
+        m.synth_layer(l, hymoe.TYPE_Q4_0, args.seed, 0.02)
+        m.set_norm(l, ones, 1e-5)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    m.set_stream(stream.cuda_stream)
+    g = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank)
+    x0 = torch.randn(max(T, 1), H, device=dev, generator=g, dtype=torch.float32)[:T]
+    x = torch.empty_like(x0)
+
+    def stack(ptr):
+        for l in range(L):
+            m.forward_device(l, ptr, ptr, T, resid_ptr=ptr, pre_norm=True)
+
+    for _ in range(args.warmup):
+        x.copy_(x0)
+        stack(x.data_ptr())
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    clocks = Clocks(local_rank)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    m.profile(True)
+    for s in range(args.steps):
+        x.copy_(x0)  # every step starts from the same sequence (outside the timed events)
+        ev[s][0].record(stream)
+        stack(x.data_ptr())
+        ev[s][1].record(stream)
+    torch.cuda.synchronize()
+    m.profile(False)
+    prof = m.profile_read()
+    clk = clocks.stop()
+    dev_ms = sum(a.elapsed_time(b) for a, b in ev)
+    e2e_ms = 0.0
+    xh = x0.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    for s in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        x.copy_(xh, non_blocking=True)
+        stack(x.data_ptr())
+        oh.copy_(x, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        e2e_ms += a.elapsed_time(b)
+    if world > 1:
+        tt = torch.tensor([dev_ms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        dev_ms, e2e_ms = (float(v) for v in tt.tolist())
+    m.close()
+    ms = dev_ms / args.steps
+    return {
+        "metric": STACK_METRIC, "value": round(STACK_SEQ * args.steps / (dev_ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded; random-init Q4_0 weights of 32 layers generated on device)",
+        "config": {"workload": f"cfg5: {L} MoE blocks layer by layer on a {STACK_SEQ}-token sequence "
+                               f"({T} tokens on rank 0), x <- x + MoE(RMSNorm(x)), unit norm weights, no router bias",
+                   "model": "HunyuanImage-3.0 MoE block H=4096 I=3072 E=64+1 shared top-8, 32 layers",
+                   "global_batch": STACK_SEQ, "seq_len": STACK_SEQ,
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "l2": "weights of 32 layers (44 GB at N=1) far exceed L2"},
+        "phases_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in prof.items() if v[1]},
+        "e2e": {"value": round(STACK_SEQ * args.steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": xh.numel() * 4, "d2h_bytes_per_step": oh.numel() * 4,
+                "ms_per_step": round(e2e_ms / args.steps, 4)},
+        "gpu_launches": sum(v[1] for v in prof.values()),
+        "clocks": clk,
+    }
+
+
 def run_decode(args, local_rank: int) -> dict:
     """cfg2: Q8_0 weights, T = 1/8/64 tokens per step, HBM-bound grouped GEMV/GEMM."""
     import torch
@@ -518,6 +623,8 @@ def main():
     ap.add_argument("--wtype", default="q4_0", choices=["q4_0", "q8_0"])
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="expert placement across ranks (N > 1)")
+    ap.add_argument("--stack", action="store_true",
+                    help="cfg5 instead: 32 MoE blocks layer by layer on a 4160-token sequence")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -537,7 +644,7 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
-    res = run_gpu(args, rank, world, local_rank)
+    res = run_stack(args, rank, world, local_rank) if args.stack else run_gpu(args, rank, world, local_rank)
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:

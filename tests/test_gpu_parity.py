@@ -346,3 +346,38 @@ def test_pre_norm_chunked_host_call_and_graph_replay(orc):
             eager = m.forward_host(0, xs.cpu().numpy(), resid="x", pre_norm=True)["out"]
             assert np.array_equal(os_.cpu().numpy(), eager), f"call {call}"
     m.close()
+
+
+def test_layer_stack_in_place_matches_the_oracle(orc):
+    """The cfg5 recurrence x <- x + MoE_l(RMSNorm_l(x)) over 4 layers, in place on the device
+    (x, residual and out one buffer, HYMOE_PRE_NORM): every layer gives the bits of the same
+    call with separate buffers, and the stack stays within the parity tolerance of the
+    oracle's recurrence."""
+    torch = pytest.importorskip("torch")
+    H, I, E, K, T, L, wt, seed = 512, 256, 64, 8, 40, 4, O.Q4_0, 51
+    lays = [host_layer(orc, seed, l, H, I, E, wt) for l in range(L)]
+    rng = np.random.default_rng(seed)
+    ws = [(1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32) for _ in range(L)]
+    m = _ctx(H, I, E, K, T, layers=L)
+    for l in range(L):
+        _load(m, lays[l], wt, layer=l)
+        m.set_norm(l, ws[l], 1e-5)
+    x0 = O.synth_x(orc, seed, T, H)
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        m.set_stream(st.cuda_stream)
+        xd = torch.from_numpy(x0).cuda()
+        for l in range(L):
+            sep_in = xd.clone()
+            sep_out = torch.empty_like(xd)
+            m.forward_device(l, sep_in.data_ptr(), sep_out.data_ptr(), T, resid_ptr=sep_in.data_ptr(),
+                             pre_norm=True)
+            m.forward_device(l, xd.data_ptr(), xd.data_ptr(), T, resid_ptr=xd.data_ptr(), pre_norm=True)
+            m.synchronize()
+            assert torch.equal(xd, sep_out), f"layer {l}"
+        got = xd.cpu().numpy()
+    m.close()
+    x = x0.copy()
+    for l in range(L):
+        x = _oracle(orc, lays[l], orc.rms_norm(x, ws[l], 1e-5), K, I, resid=x)["out"]
+    assert rel_l2(got, x) <= REL_L2_TOL
