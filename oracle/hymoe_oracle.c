@@ -500,3 +500,115 @@ int oracle_moe_forward(const float* x, const float* resid, uint32_t T, uint32_t 
     free(ti);
     return rc;
 }
+
+
+/* ------------------------------------------------------------------ FULL-mode routing */
+
+/* softmax_f32 of src/hunyuan_moe_full.cpp:41-50: running max (strict >), expf of the
+ * differences summed in order, each divided by the sum. */
+static void full_softmax(float* x, uint32_t n) {
+    float mx = x[0];
+    for (uint32_t i = 1; i < n; ++i)
+        if (x[i] > mx) mx = x[i];
+    float sum = 0.0f;
+    for (uint32_t i = 0; i < n; ++i) {
+        x[i] = expf(x[i] - mx);
+        sum += x[i];
+    }
+    for (uint32_t i = 0; i < n; ++i) x[i] /= sum;
+}
+
+/* The k largest of x[0..n) in decreasing order, equal values in increasing index order
+ * (what the insertion of src/hunyuan_moe_full.cpp:56-82 keeps); slots past n are (0, 0). */
+static void full_topk(const float* x, uint32_t n, uint32_t k, float* vals, int32_t* ids) {
+    uint8_t taken[256] = {0};
+    for (uint32_t r = 0; r < k; ++r) {
+        int32_t b = -1;
+        for (uint32_t i = 0; i < n && i < 256; ++i)
+            if (!taken[i] && (b < 0 || x[i] > x[b])) b = (int32_t)i;
+        if (b < 0) {
+            vals[r] = 0.0f;
+            ids[r] = 0;
+            continue;
+        }
+        taken[b] = 1;
+        vals[r] = x[b];
+        ids[r] = b;
+    }
+}
+
+void oracle_topkgating_full(const float* logits, uint32_t T, uint32_t E, uint32_t K,
+                            int group_limited, uint32_t n_group, uint32_t topk_group,
+                            int drop_tokens, float capacity_factor, uint32_t min_capacity,
+                            int norm_topk_prob, float routed_scaling_factor, float* probs,
+                            int32_t* idx, float* w, uint8_t* keep, int32_t* exp_counts,
+                            uint32_t* capacity) {
+    *capacity = 0;
+    if (E == 0 || E > 256 || n_group > 256 || K == 0) return; /* the fixed tables below */
+    const uint32_t nk = K > topk_group ? K : topk_group;    /* entries full_topk writes */
+    float* gates = (float*)malloc(sizeof(float) * (size_t)T * E);
+    float* tv = (float*)malloc(sizeof(float) * nk);
+    int32_t* ti = (int32_t*)malloc(sizeof(int32_t) * nk);
+    for (uint32_t t = 0; t < T; ++t) {
+        float* g = gates + (size_t)t * E;
+        memcpy(g, logits + (size_t)t * E, sizeof(float) * E);
+        full_softmax(g, E);
+        memcpy(probs + (size_t)t * E, g, sizeof(float) * E);
+        if (group_limited && n_group > 0 && topk_group > 0) {
+            const uint32_t gs = E / n_group;
+            float score[256];
+            for (uint32_t q = 0; q < n_group; ++q) {
+                float m = 0.0f;
+                for (uint32_t e = 0; e < gs; ++e)
+                    if (g[q * gs + e] > m) m = g[q * gs + e];
+                score[q] = m;
+            }
+            full_topk(score, n_group, topk_group, tv, ti);
+            for (uint32_t q = 0; q < n_group; ++q) {
+                int sel = 0;
+                for (uint32_t r = 0; r < topk_group; ++r) sel |= ti[r] == (int32_t)q;
+                if (!sel)
+                    for (uint32_t e = 0; e < gs; ++e) g[q * gs + e] = 0.0f;
+            }
+        }
+        full_topk(g, E, K, tv, idx + (size_t)t * K);
+    }
+    for (uint32_t e = 0; e < E; ++e) exp_counts[e] = 0;
+    for (uint32_t i = 0; i < T * K; ++i) exp_counts[idx[i]]++;
+    uint32_t cap;
+    if (drop_tokens) {
+        const uint32_t f = (uint32_t)(capacity_factor * (float)K * (float)T / (float)E);
+        cap = f > K ? f : K;
+    } else {
+        cap = 0;
+        for (uint32_t e = 0; e < E; ++e)
+            if ((uint32_t)exp_counts[e] > cap) cap = (uint32_t)exp_counts[e];
+    }
+    if (cap < min_capacity) cap = min_capacity;
+    *capacity = cap;
+    for (uint32_t t = 0; t < T; ++t) {
+        const float* g = gates + (size_t)t * E;
+        const int32_t* id = idx + (size_t)t * K;
+        if (norm_topk_prob && K > 1) {
+            float s = 0.0f;
+            for (uint32_t k = 0; k < K; ++k) s += g[id[k]];
+            if (s < 1e-8f) s = 1e-8f;
+            for (uint32_t k = 0; k < K; ++k) w[(size_t)t * K + k] = g[id[k]] / s;
+        } else {
+            for (uint32_t k = 0; k < K; ++k) w[(size_t)t * K + k] = g[id[k]] * routed_scaling_factor;
+        }
+    }
+    /* priorities in k-major order */
+    int32_t* seen = (int32_t*)calloc(E, sizeof(int32_t));
+    for (uint32_t k = 0; k < K; ++k)
+        for (uint32_t t = 0; t < T; ++t) {
+            const int32_t e = idx[(size_t)t * K + k];
+            keep[(size_t)t * K + k] = (uint32_t)seen[e] < cap;
+            seen[e]++;
+        }
+    free(seen);
+    free(gates);
+    free(tv);
+    free(ti);
+}
+

@@ -86,6 +86,26 @@ int oracle_moe_forward(const float* x, const float* resid, uint32_t T, uint32_t 
                        float* out, float* dbg_logits, float* dbg_probs, float* dbg_w,
                        int32_t* dbg_idx, int nthreads);
 
+/* FULL-mode routing, topkgating_full (src/hunyuan_moe_full.cpp:119-350), routing part:
+ * softmax per token (probs, before any masking); optionally group-limited greedy (groups of
+ * E/n_group experts scored by their largest probability, clamped below at 0; the topk_group
+ * best groups kept, the others' probabilities zeroed); top-K of the (masked) probabilities;
+ * capacity = max(K, (uint32)(capacity_factor*K*T/E)) when drop_tokens, else the largest
+ * per-expert pair count, in both cases at least min_capacity; each pair's priority = its
+ * position among the pairs of its expert in k-major order (every token's first choice, then
+ * every token's second, ...), kept when below capacity; weights renormalised over the K
+ * choices (sum clamped at 1e-8) when norm_topk_prob and K > 1, else scaled by
+ * routed_scaling_factor.  Ties everywhere go to the lower index.
+ * Outputs: probs [T,E], idx/w [T,K] (rank order; w is the combine weight of a kept pair),
+ * keep [T,K], exp_counts [E] (all pairs), *capacity.  The auxiliary loss (training only) is
+ * not restated.  E and n_group at most 256 (*capacity = 0 otherwise). */
+void oracle_topkgating_full(const float* logits, uint32_t T, uint32_t E, uint32_t K,
+                            int group_limited, uint32_t n_group, uint32_t topk_group,
+                            int drop_tokens, float capacity_factor, uint32_t min_capacity,
+                            int norm_topk_prob, float routed_scaling_factor, float* probs,
+                            int32_t* idx, float* w, uint8_t* keep, int32_t* exp_counts,
+                            uint32_t* capacity);
+
 #ifdef __cplusplus
 }
 #endif

@@ -78,6 +78,10 @@ class Oracle:
         L.oracle_synth_tensor.argtypes = [i32, _u8p, u64, u64, u64, C.c_float, i32]
         L.oracle_synth_tensor_f32.argtypes = [i32, _fp, u64, u64, u64, C.c_float, i32]
         L.oracle_rms_norm.argtypes = [_fp, _fp, _fp, u32, u32, C.c_float]
+        L.oracle_topkgating_full.argtypes = [_fp, u32, u32, u32, C.c_int, u32, u32, C.c_int, C.c_float,
+                                             u32, C.c_int, C.c_float, _fp, _i32p, _fp, _u8p, _i32p,
+                                             C.POINTER(u32)]
+        L.oracle_topkgating_full.restype = None
         L.oracle_swiglu_ffn.argtypes = [_fp, _fp, _fp, _fp, u32, u32, u32, i32]
         L.oracle_router.argtypes = [_fp, u32, u32, u32, u32, _fp, _fp, _fp, _fp, _fp, _i32p, i32]
         L.oracle_moe_forward.argtypes = [_fp, _fp, u32, u32, u32, u32, u32, _fp, _fp, _fp, _fp,
@@ -126,6 +130,27 @@ class Oracle:
         out = np.empty_like(x)
         self.L.oracle_rms_norm(_ptr(x, _fp), _ptr(w, _fp), _ptr(out, _fp), T, H, eps)
         return out
+
+    def topkgating_full(self, logits: np.ndarray, K: int, group=None, drop=None, min_capacity: int = 8,
+                        norm_topk_prob: bool = True, scale: float = 1.0) -> dict:
+        """FULL-mode routing (topkgating_full, src/hunyuan_moe_full.cpp:119-350).
+        group = (n_group, topk_group) for group-limited greedy; drop = capacity_factor to
+        drop pairs beyond a fixed capacity (None: capacity = the largest expert count)."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        T, E = logits.shape
+        probs = np.empty((T, E), np.float32)
+        idx = np.empty((T, K), np.int32)
+        w = np.empty((T, K), np.float32)
+        keep = np.empty((T, K), np.uint8)
+        cnt = np.empty(E, np.int32)
+        cap = C.c_uint32()
+        ng, tg = group if group else (0, 0)
+        self.L.oracle_topkgating_full(_ptr(logits, _fp), T, E, K, 1 if group else 0, ng, tg,
+                                      0 if drop is None else 1, 1.0 if drop is None else drop,
+                                      min_capacity, 1 if norm_topk_prob else 0, scale, _ptr(probs, _fp),
+                                      _ptr(idx, _i32p), _ptr(w, _fp), _ptr(keep, _u8p), _ptr(cnt, _i32p),
+                                      C.byref(cap))
+        return dict(probs=probs, idx=idx, w=w, keep=keep.astype(bool), exp_counts=cnt, capacity=cap.value)
 
     def swiglu_ffn(self, x, gu, dn, I: int) -> np.ndarray:
         n, H = x.shape
@@ -186,6 +211,12 @@ class RefMoE:
                                         _i32p]
         L.hyref_swiglu_ffn.argtypes = [_fp, _fp, _fp, _fp, u32, u32, u32]
         L.hyref_rms_norm.argtypes = [_fp, _fp, _fp, u32, u32, C.c_float]
+        L.hyref_full_capacity_bound.argtypes = [u32, u32, u32, C.c_int, C.c_float, u32]
+        L.hyref_full_capacity_bound.restype = u32
+        L.hyref_topkgating_full.argtypes = [_fp, u32, u32, u32, C.c_int, u32, u32, C.c_int, C.c_float, u32,
+                                            C.c_int, C.c_float, _fp, _u8p, _fp, _i32p, C.POINTER(u32),
+                                            C.POINTER(C.c_float)]
+        L.hyref_topkgating_full.restype = C.c_int
 
     @staticmethod
     def available() -> bool:
@@ -211,6 +242,33 @@ class RefMoE:
         self.L.hyref_moe_forward(_ptr(x, _fp), handle, T, H, I, K, _ptr(out, _fp),
                                  _ptr(probs, _fp), _ptr(tw, _fp), _ptr(ti, _i32p))
         return dict(out=out, probs=probs, w=tw, idx=ti)
+
+    def topkgating_full(self, logits: np.ndarray, K: int, group=None, drop=None, min_capacity: int = 8,
+                        norm_topk_prob: bool = True, scale: float = 1.0) -> dict:
+        """The reference's topkgating_full (src/hunyuan_moe_full.cpp:119-350): probs, the
+        dispatch mask and combine weights [T, E, capacity], expert counts, capacity, rate."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        T, E = logits.shape
+        dt = 0 if drop is None else 1
+        cf = 1.0 if drop is None else drop
+        bound = self.L.hyref_full_capacity_bound(T, E, K, dt, cf, min_capacity)
+        probs = np.empty((T, E), np.float32)
+        mask = np.zeros(T * E * bound, np.uint8)
+        comb = np.zeros(T * E * bound, np.float32)
+        cnt = np.empty(E, np.int32)
+        cap = C.c_uint32()
+        rate = C.c_float()
+        ng, tg = group if group else (0, 0)
+        rc = self.L.hyref_topkgating_full(_ptr(logits, _fp), T, E, K, 1 if group else 0, ng, tg, dt, cf,
+                                          min_capacity, 1 if norm_topk_prob else 0, scale, _ptr(probs, _fp),
+                                          _ptr(mask, _u8p), _ptr(comb, _fp), _ptr(cnt, _i32p), C.byref(cap),
+                                          C.byref(rate))
+        if rc != 0:
+            raise RuntimeError("topkgating_full computed a capacity above the bound")
+        c = cap.value
+        return dict(probs=probs, mask=mask[:T * E * c].reshape(T, E, c).astype(bool),
+                    combine=comb[:T * E * c].reshape(T, E, c), exp_counts=cnt, capacity=c,
+                    rate=rate.value)
 
     def rms_norm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
         """The reference's rms_norm_f32 (src/rms_norm.cpp:9-33)."""

@@ -10,8 +10,12 @@
 //   moe_forward_cpu   (src/attention.cpp:191-313, decl src/hunyuan_model.h:147-156)
 //   swiglu_ffn_f32    (src/rms_norm.cpp:39-91)
 //   rms_norm_f32      (src/rms_norm.cpp:9-33)
+//   topkgating_full   (src/hunyuan_moe_full.cpp:119-350)
 // unchanged.
 #include "hunyuan_model.h"
+#include "hunyuan_moe_full.h"
+
+#include <algorithm>
 
 #include <cstdint>
 #include <cstring>
@@ -73,6 +77,50 @@ void hyref_swiglu_ffn(const float* x, const float* gate_up, const float* down, f
 void hyref_rms_norm(const float* x, const float* weight, float* out, uint32_t T, uint32_t H,
                     float eps) {
     rms_norm_f32(x, weight, out, T, H, eps);
+}
+
+// The largest capacity topkgating_full can compute for these arguments.  It writes its
+// dispatch mask with the capacity it computes, so the buffers are sized for this bound
+// (moe_forward_full sizes them smaller, which is the heap overflow noted at
+// src/hunyuan_moe_full.cpp:296).
+uint32_t hyref_full_capacity_bound(uint32_t T, uint32_t E, uint32_t K, int drop_tokens,
+                                   float capacity_factor, uint32_t min_capacity) {
+    uint32_t c = drop_tokens ? std::max(K, (uint32_t)(capacity_factor * K * T / E)) : T;
+    return std::max(c, min_capacity);
+}
+
+// Calls topkgating_full; mask / combine receive [T][E][capacity] with the capacity the call
+// computed (returned in *capacity; at most hyref_full_capacity_bound).
+int hyref_topkgating_full(const float* logits, uint32_t T, uint32_t E, uint32_t K,
+                          int group_limited, uint32_t n_group, uint32_t topk_group,
+                          int drop_tokens, float capacity_factor, uint32_t min_capacity,
+                          int norm_topk_prob, float routed_scaling_factor, float* probs,
+                          uint8_t* mask, float* combine, int32_t* exp_counts,
+                          uint32_t* capacity, float* capacity_rate) {
+    MoERoutingConfig cfg;
+    cfg.num_experts = E;
+    cfg.moe_topk = K;
+    cfg.group_limited_greedy = group_limited != 0;
+    cfg.n_group = n_group;
+    cfg.topk_group = topk_group;
+    cfg.drop_tokens = drop_tokens != 0;
+    cfg.capacity_factor = capacity_factor;
+    cfg.min_capacity = min_capacity;
+    cfg.norm_topk_prob = norm_topk_prob != 0;
+    cfg.routed_scaling_factor = routed_scaling_factor;
+    const uint32_t bound = hyref_full_capacity_bound(T, E, K, drop_tokens, capacity_factor, min_capacity);
+    MoEGateOutput out;
+    out.alloc(T, E, K, bound, true);
+    topkgating_full(logits, T, cfg, out);
+    if (out.expert_capacity > bound) return -1;
+    const size_t n = (size_t)T * E * out.expert_capacity;
+    for (size_t i = 0; i < n; ++i) mask[i] = out.dispatch_mask[i] ? 1 : 0;
+    std::memcpy(combine, out.combine_weights, n * sizeof(float));
+    std::memcpy(probs, out.router_probs, (size_t)T * E * sizeof(float));
+    std::memcpy(exp_counts, out.exp_counts, E * sizeof(int32_t));
+    *capacity = out.expert_capacity;
+    *capacity_rate = out.exp_capacity_rate;
+    return 0;
 }
 
 }  // extern "C"

@@ -76,6 +76,44 @@ def run_rms_norm(orc: O.Oracle, ref: O.RefMoE) -> None:
     print(f"rms_norm: {os.path.getsize(path)} bytes")
 
 
+# FULL-mode routing cases: name, T, E, K, options of topkgating_full
+ROUTING_CASES = [
+    ("plain", 37, 64, 8, {}),
+    ("group", 37, 64, 8, {"group": (8, 3)}),
+    ("drop", 64, 64, 8, {"drop": 1.0}),
+    ("group_drop_scaled", 20, 16, 4, {"group": (4, 2), "drop": 1.25, "norm_topk_prob": False, "scale": 2.5}),
+    ("top1_drop", 9, 64, 1, {"drop": 1.0, "min_capacity": 1}),
+]
+
+
+def routing_options(opts: dict) -> np.ndarray:
+    g = opts.get("group") or (0, 0)
+    return np.array([1 if opts.get("group") else 0, g[0], g[1], 0 if opts.get("drop") is None else 1,
+                     opts.get("drop") or 1.0, opts.get("min_capacity", 8),
+                     1 if opts.get("norm_topk_prob", True) else 0, opts.get("scale", 1.0)], np.float64)
+
+
+def run_routing_full(ref: O.RefMoE) -> None:
+    """topkgating_full (src/hunyuan_moe_full.cpp:119-350) on seeded logits, half of them
+    rounded to steps of 0.5 so that ties occur."""
+    rng = np.random.default_rng(17)
+    arrays = {}
+    for name, T, E, K, opts in ROUTING_CASES:
+        for tie in (False, True):
+            lg = (rng.standard_normal((T, E)) * 2).astype(np.float32)
+            if tie:
+                lg = (np.round(lg * 2) / 2).astype(np.float32)
+            r = ref.topkgating_full(lg, K, **opts)
+            key = f"{name}{'_ties' if tie else ''}"
+            arrays.update({f"{key}_logits": lg, f"{key}_k": np.int64(K), f"{key}_opts": routing_options(opts),
+                           f"{key}_probs": r["probs"], f"{key}_mask": r["mask"], f"{key}_combine": r["combine"],
+                           f"{key}_counts": r["exp_counts"], f"{key}_capacity": np.int64(r["capacity"]),
+                           f"{key}_rate": np.float32(r["rate"])})
+    path = os.path.join(HERE, "routing_full.npz")
+    np.savez_compressed(path, **arrays)
+    print(f"routing_full: {os.path.getsize(path)} bytes")
+
+
 def main():
     orc = O.Oracle()
     ref = O.RefMoE()
@@ -85,6 +123,8 @@ def main():
             run_case(orc, ref, *c)
     if not only or "rms_norm" in only:
         run_rms_norm(orc, ref)
+    if not only or "routing_full" in only:
+        run_routing_full(ref)
 
 
 if __name__ == "__main__":

@@ -88,3 +88,30 @@ def fixture_inputs(orc: O.Oracle, fx: dict):
     _, _, _, ti = orc.router(x, rw, K)
     w = O.synth_layer_f32(orc, seed, 0, H, I, E, wt, experts=np.unique(ti))
     return x, w, input_checksum(x, rw)
+
+
+def check_full_routing(mine: dict, ref: dict, K: int) -> None:
+    """The FULL-mode routing restatement (idx, w, keep per pair) against the reference's
+    topkgating_full outputs (probs, dispatch mask and combine weights [T, E, capacity],
+    expert counts, capacity, capacity rate): every kept pair has exactly one mask entry whose
+    combine weight is its w; dropped and unselected (token, expert) pairs have none."""
+    T, E = ref["probs"].shape
+    assert np.array_equal(mine["probs"], ref["probs"])
+    assert mine["capacity"] == ref["capacity"]
+    assert np.array_equal(mine["exp_counts"], ref["exp_counts"])
+    m, cw = ref["mask"], ref["combine"]
+    assert m.shape == (T, E, ref["capacity"])
+    seen = np.zeros((T, E), bool)
+    for t in range(T):
+        for k in range(K):
+            e = int(mine["idx"][t, k])
+            assert not seen[t, e], "an expert chosen twice"
+            seen[t, e] = True
+            hits = np.nonzero(m[t, e])[0]
+            if mine["keep"][t, k]:
+                assert len(hits) == 1 and cw[t, e, hits[0]] == mine["w"][t, k], (t, k)
+            else:
+                assert len(hits) == 0, (t, k)
+    assert not m[~seen].any()
+    # the reference divides in single precision: kept pairs / (T * K)
+    assert np.float32(mine["keep"].sum()) / np.float32(T * K) == np.float32(ref["rate"])

@@ -138,3 +138,41 @@ def test_rms_norm_restatement_matches_compiled_reference(orc):
         x = (rng.standard_normal((T, H)) * 10.0 ** rng.integers(-5, 5, size=(T, 1))).astype(np.float32)
         w = rng.standard_normal(H).astype(np.float32)
         assert np.array_equal(orc.rms_norm(x, w, eps), ref.rms_norm(x, w, eps))
+
+
+def _routing_opts(v: np.ndarray) -> dict:
+    opts = {"min_capacity": int(v[5]), "norm_topk_prob": bool(v[6]), "scale": float(v[7])}
+    if v[0]:
+        opts["group"] = (int(v[1]), int(v[2]))
+    if v[3]:
+        opts["drop"] = float(v[4])
+    return opts
+
+
+def test_full_routing_restatement_matches_reference_golden(orc):
+    """FULL-mode routing (topkgating_full, src/hunyuan_moe_full.cpp:119-350: group-limited
+    greedy, capacity with k-major drop priority, renormalisation or scaling) against the
+    reference's outputs stored in tests/golden/routing_full.npz, ties included."""
+    from moe_cases import check_full_routing
+    d = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "routing_full.npz"))
+    keys = sorted({k[: -len("_logits")] for k in d.files if k.endswith("_logits")})
+    assert len(keys) == 10
+    for key in keys:
+        K = int(d[f"{key}_k"])
+        mine = orc.topkgating_full(d[f"{key}_logits"], K, **_routing_opts(d[f"{key}_opts"]))
+        ref = {"probs": d[f"{key}_probs"], "mask": d[f"{key}_mask"], "combine": d[f"{key}_combine"],
+               "exp_counts": d[f"{key}_counts"], "capacity": int(d[f"{key}_capacity"]),
+               "rate": float(d[f"{key}_rate"])}
+        check_full_routing(mine, ref, K)
+
+
+@pytest.mark.skipif(not O.RefMoE.available(), reason="reference checker not built here")
+@pytest.mark.parametrize("opts", [{}, {"group": (8, 3)}, {"drop": 1.0}, {"drop": 0.5, "min_capacity": 2},
+                                  {"group": (4, 1), "drop": 2.0, "norm_topk_prob": False, "scale": 0.7}])
+def test_full_routing_restatement_matches_compiled_reference(orc, opts):
+    from moe_cases import check_full_routing
+    ref = O.RefMoE()
+    rng = np.random.default_rng(len(opts))
+    for T in (1, 16, 130):
+        lg = (rng.standard_normal((T, 64)) * 3).astype(np.float32)
+        check_full_routing(orc.topkgating_full(lg, 8, **opts), ref.topkgating_full(lg, 8, **opts), 8)
