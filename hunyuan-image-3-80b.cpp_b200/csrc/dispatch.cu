@@ -151,7 +151,7 @@ __global__ __launch_bounds__(1024) void topk_plan_kernel(const float* __restrict
     const int tid = threadIdx.x, warp = tid >> 5;
     if (tid < kMaxE) gcnt_s[tid] = 0;
     __syncthreads();
-    if (warp < T) topk_token(logits, warp, a.E, K, probs_out, topk_w, topk_idx, pbuf[warp], gcnt_s, a.slot_of);
+    if (warp < T) topk_token(logits, warp, a.E, K, probs_out, topk_w, topk_idx, pbuf[warp], gcnt_s, a.slot_of, a.mode);
     __syncthreads();
     if (tid < 64) goff_s[tid] = tid < a.E ? gcnt_s[tid] : 0;
     __syncthreads();

@@ -27,6 +27,7 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cmath>
 #include <cstdlib>
 #include <thread>
 
@@ -161,6 +162,7 @@ struct hymoe_ctx {
     std::vector<float*> norm_w;
     std::vector<float> norm_eps;
     float* x_norm = nullptr;
+    RouteMode route;  // routing variant (hymoe_set_routing); default: moe_forward_cpu's
     int expert_at(uint32_t layer, int slot) const {
         return expert_of_slot[layer].empty() ? slot : expert_of_slot[layer][slot];
     }
@@ -983,6 +985,34 @@ hymoe_status hymoe_set_norm(hymoe_ctx* c, uint32_t layer, const float* weight, f
     return HYMOE_OK;
 }
 
+hymoe_status hymoe_set_routing(hymoe_ctx* c, const hymoe_routing* r) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    RouteMode m;  // NULL: moe_forward_cpu's routing
+    if (r) {
+        if (r->drop_tokens)
+            return c->fail(HYMOE_ERR_UNSUPPORTED, "capacity drops (drop_tokens) are not implemented");
+        if (r->group_limited_greedy) {
+            if (r->n_group == 0 || r->n_group > 32 || c->E % static_cast<int>(r->n_group) != 0 ||
+                r->topk_group == 0 || r->topk_group > r->n_group)
+                return c->fail(HYMOE_ERR_INVALID_ARG, "group-limited routing: n_group %u (1..32, dividing E=%d), "
+                               "topk_group %u (1..n_group)", r->n_group, c->E, r->topk_group);
+            m.n_group = static_cast<int>(r->n_group);
+            m.topk_group = static_cast<int>(r->topk_group);
+        }
+        if (!std::isfinite(r->routed_scaling_factor))
+            return c->fail(HYMOE_ERR_INVALID_ARG, "routed_scaling_factor is not finite");
+        // topkgating_full renormalises only when K > 1 (src/hunyuan_moe_full.cpp:229-243)
+        m.norm = r->norm_topk_prob && c->K > 1 ? 1 : 0;
+        m.clamp = 1;
+        m.scale = r->routed_scaling_factor;
+    }
+    HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    HY_CUDA(c, cudaStreamSynchronize(c->stream));
+    c->clear_graphs();  // the mode is baked into captured launches
+    c->route = m;
+    return HYMOE_OK;
+}
+
 hymoe_status hymoe_set_placement(hymoe_ctx* c, uint32_t layer, const int32_t* slot_of_expert) {
     if (!c) return HYMOE_ERR_INVALID_ARG;
     if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
@@ -1208,7 +1238,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             const bool fused = n_chunks == 1;
             c->phase_begin();
             HY_CUDA(c, launch_router(dxn, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
-                                     c->topk_w, c->topk_idx, c->chunk_counts, slot_of, !fused, st));
+                                     c->topk_w, c->topk_idx, c->chunk_counts, slot_of, c->route, !fused, st));
             c->phase_end(HYMOE_PHASE_ROUTER, fused ? 1 : 2);
             PlanArgs pa{};
             pa.chunk_counts = c->chunk_counts;
@@ -1223,6 +1253,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             pa.n_segs = c->n_segs;
             pa.shared_apart = shared_apart ? 1 : 0;
             pa.slot_of = slot_of;
+            pa.mode = c->route;
             pa.items = items_args(gemv);
             c->phase_begin();
             if (fused)

@@ -20,15 +20,25 @@ cudaError_t launch_synth_gguf(uint8_t* dst, int type, uint64_t n, uint64_t seed,
 cudaError_t launch_synth_f32(float* dst, uint64_t n, uint64_t seed, uint64_t stream, float scale,
                              cudaStream_t st);
 
+// Routing variant (FULL mode, topkgating_full, src/hunyuan_moe_full.cpp:119-243, without
+// capacity drops).  The default is moe_forward_cpu's routing (src/attention.cpp:224-275).
+struct RouteMode {
+    int n_group = 0;     // > 0: group-limited greedy over n_group groups of E/n_group experts
+    int topk_group = 0;  //      groups kept
+    int norm = 1;        // weights = p / sum of the K selected p (else p * scale)
+    int clamp = 0;       //      sum clamped below at 1e-8 (FULL mode)
+    float scale = 1.f;   // routed_scaling_factor when norm == 0
+};
+
 // ---- router.cu
 constexpr int kRouterTok = 16;  // tokens per router CTA (= dispatch chunk)
 constexpr int kGemvMaxRows = 64; // token rows per GEMV work item
 // Logits, then (topk = true) the top-K kernel with per-chunk slot counts (slot_of: expert ->
-// placement slot, nullptr for slot = expert; topk_idx holds slots).
+// placement slot, nullptr for slot = expert; topk_idx holds slots; mode: routing variant).
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
-                          int* topk_idx, int* chunk_counts, const int* slot_of, bool topk,
-                          cudaStream_t st);
+                          int* topk_idx, int* chunk_counts, const int* slot_of,
+                          const RouteMode& mode, bool topk, cudaStream_t st);
 
 // ---- dispatch.cu
 constexpr int kMaxSegs = 80;  // >= E + 1 (E <= 64)
@@ -52,6 +62,7 @@ struct PlanArgs {
     int* n_segs;              // (segs == NULL: expert-parallel mode, items built later)
     int shared_apart;         // 1: the shared expert runs as its own launch (no segment here)
     const int* slot_of;       // fused top-K: expert -> placement slot (nullptr: identity)
+    RouteMode mode;           // fused top-K: routing variant
     ItemsArgs items;
 };
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);

@@ -219,14 +219,14 @@ __global__ __launch_bounds__(64) void router_logits_small_kernel(
 __global__ __launch_bounds__(32 * kRouterTok) void router_topk_kernel(
     const float* __restrict__ logits, int T, int E, int K, float* __restrict__ probs_out,
     float* __restrict__ topk_w, int* __restrict__ topk_idx, int* __restrict__ chunk_counts,
-    const int* __restrict__ slot_of) {
+    const int* __restrict__ slot_of, RouteMode mode) {
     __shared__ float pbuf[kRouterTok][kMaxE];
     __shared__ int cnt[kMaxE];
     const int warp = threadIdx.x >> 5;
     if (threadIdx.x < kMaxE) cnt[threadIdx.x] = 0;
     __syncthreads();
     const int t = blockIdx.x * kRouterTok + warp;
-    if (t < T) topk_token(logits, t, E, K, probs_out, topk_w, topk_idx, pbuf[warp], cnt, slot_of);
+    if (t < T) topk_token(logits, t, E, K, probs_out, topk_w, topk_idx, pbuf[warp], cnt, slot_of, mode);
     __syncthreads();
     if (threadIdx.x < E) chunk_counts[static_cast<size_t>(blockIdx.x) * E + threadIdx.x] = cnt[threadIdx.x];
 }
@@ -235,8 +235,8 @@ __global__ __launch_bounds__(32 * kRouterTok) void router_topk_kernel(
 
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
-                          int* topk_idx, int* chunk_counts, const int* slot_of, bool topk,
-                          cudaStream_t st) {
+                          int* topk_idx, int* chunk_counts, const int* slot_of,
+                          const RouteMode& mode, bool topk, cudaStream_t st) {
     cudaError_t e;
     if (T <= kDecodeMaxT) {
         const size_t smem = sizeof(float) * static_cast<size_t>(H) * (1 + T);
@@ -262,7 +262,7 @@ cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, 
     e = cudaGetLastError();
     if (e != cudaSuccess || !topk) return e;
     router_topk_kernel<<<(T + kRouterTok - 1) / kRouterTok, 32 * kRouterTok, 0, st>>>(
-        logits, T, E, K, probs, topk_w, topk_idx, chunk_counts, slot_of);
+        logits, T, E, K, probs, topk_w, topk_idx, chunk_counts, slot_of, mode);
     return cudaGetLastError();
 }
 

@@ -7,6 +7,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "kernels.h"
 
 namespace hymoe {
 
@@ -16,11 +17,11 @@ constexpr int kMaxE = 64;
 // per-slot counters of the caller's chunk (incremented for the token's K selections).
 // slot_of: expert -> placement slot (nullptr: slot = expert).  Selection, ties and weights are
 // decided on expert ids; topk_idx and cnt receive the selected experts' slots, so every later
-// step (sort, dispatch, GEMM groups, combine) works in slot order.
+// step (sort, dispatch, GEMM groups, combine) works in slot order.  mode: the routing variant.
 __device__ __forceinline__ void topk_token(const float* __restrict__ logits, int t, int E, int K,
                                            float* __restrict__ probs_out, float* __restrict__ topk_w,
                                            int* __restrict__ topk_idx, float* pbuf, int* cnt,
-                                           const int* __restrict__ slot_of) {
+                                           const int* __restrict__ slot_of, const RouteMode& mode) {
     const int lane = threadIdx.x & 31;
     const bool v0 = lane < E, v1 = lane + 32 < E;
     const float l0 = v0 ? logits[static_cast<size_t>(t) * E + lane] : -INFINITY;
@@ -42,6 +43,41 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ logits, int
     if (probs_out != nullptr) {
         if (v0) probs_out[static_cast<size_t>(t) * E + lane] = p0;
         if (v1) probs_out[static_cast<size_t>(t) * E + lane + 32] = p1;
+    }
+    if (mode.n_group > 0) {
+        // Group-limited greedy (src/hunyuan_moe_full.cpp:137-170): groups of gs experts scored
+        // by their largest probability (at least 0); the topk_group best (ties: lower group)
+        // keep their probabilities, every other expert's becomes 0.  probs_out keeps the
+        // unmasked softmax, as the reference's router_probs does.
+        const int gs = E / mode.n_group;
+        __syncwarp();  // lane 0 is done reading the exponentials
+        pbuf[lane] = p0;
+        pbuf[lane + 32] = p1;
+        __syncwarp();
+        float sc = 0.f;
+        if (lane < mode.n_group)
+            for (int e = 0; e < gs; ++e) {
+                const float v = pbuf[lane * gs + e];
+                if (v > sc) sc = v;
+            }
+        bool gtaken = lane >= mode.n_group, gsel = false;
+        for (int r = 0; r < mode.topk_group; ++r) {
+            float bv = gtaken ? -1.f : sc;
+            int bi = gtaken ? (1 << 30) : lane;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if (bi == lane) gtaken = gsel = true;
+        }
+        const unsigned kept = __ballot_sync(0xffffffffu, gsel);  // bit g: group g kept
+        if (v0 && !((kept >> (lane / gs)) & 1u)) p0 = 0.f;
+        if (v1 && !((kept >> ((lane + 32) / gs)) & 1u)) p1 = 0.f;
     }
     bool taken0 = !v0, taken1 = !v1;
     float selp = 0.f;  // lane k keeps the k-th selection
@@ -79,7 +115,12 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ logits, int
     float sw = 0.f;
     for (int k = 0; k < K; ++k) sw = __fadd_rn(sw, __shfl_sync(0xffffffffu, selp, k));
     if (lane < K) {
-        topk_w[static_cast<size_t>(t) * K + lane] = __fdiv_rn(selp, sw);
+        float wv;
+        if (mode.norm)
+            wv = __fdiv_rn(selp, mode.clamp && sw < 1e-8f ? 1e-8f : sw);
+        else
+            wv = __fmul_rn(selp, mode.scale);
+        topk_w[static_cast<size_t>(t) * K + lane] = wv;
         const int slot = slot_of != nullptr ? __ldg(slot_of + sele) : sele;
         topk_idx[static_cast<size_t>(t) * K + lane] = slot;
         atomicAdd(&cnt[slot], 1);

@@ -31,7 +31,7 @@ EXPORTS = ["hymoe_version", "hymoe_nccl_unique_id", "hymoe_create", "hymoe_destr
            "hymoe_ffn_noalloc", "hymoe_set_placement", "hymoe_balance_placement",
            "hymoe_gguf_open", "hymoe_gguf_close", "hymoe_gguf_last_error", "hymoe_gguf_tensor",
            "hymoe_gguf_get_u32", "hymoe_gguf_moe_tensors", "hymoe_load_layer_gguf",
-           "hymoe_set_norm"]
+           "hymoe_set_norm", "hymoe_set_routing"]
 
 PHASES = ["router", "plan", "dispatch", "gate_up", "down", "combine", "ep_dispatch",
           "ep_combine"]
@@ -47,6 +47,12 @@ class Config(C.Structure):
 class Tensor(C.Structure):
     _fields_ = [("data", C.c_void_p), ("ggml_type", C.c_int32), ("ne", C.c_int64 * 2),
                 ("nbytes", C.c_size_t)]
+
+
+class Routing(C.Structure):
+    _fields_ = [("group_limited_greedy", C.c_int32), ("n_group", C.c_uint32), ("topk_group", C.c_uint32),
+                ("drop_tokens", C.c_int32), ("capacity_factor", C.c_float), ("min_capacity", C.c_uint32),
+                ("norm_topk_prob", C.c_int32), ("routed_scaling_factor", C.c_float)]
 
 
 class Debug(C.Structure):
@@ -104,6 +110,7 @@ def lib() -> C.CDLL:
                                              C.POINTER(Tensor), C.POINTER(Tensor), C.POINTER(Tensor)]
         L.hymoe_load_layer_gguf.argtypes = [vp, u32, vp, u32]
         L.hymoe_set_norm.argtypes = [vp, u32, vp, C.c_float, C.c_int]
+        L.hymoe_set_routing.argtypes = [vp, C.POINTER(Routing)]
         for f in EXPORTS:
             if f not in ("hymoe_version", "hymoe_destroy", "hymoe_last_error", "hymoe_gguf_close",
                          "hymoe_gguf_last_error"):
@@ -272,6 +279,18 @@ class MoE:
             raise ValueError(f"placement needs {self.E} entries, got {len(slot_of_expert)}")
         arr = (C.c_int32 * self.E)(*[int(v) for v in slot_of_expert])
         self._check(self.L.hymoe_set_placement(self.h, layer, arr))
+
+    def set_routing(self, group=None, drop=None, min_capacity: int = 8, norm_topk_prob: bool = True,
+                    scale: float = 1.0, plain: bool = False) -> None:
+        """FULL-mode routing variant (hymoe_set_routing); plain=True restores the default.
+        group = (n_group, topk_group); drop = capacity_factor (not implemented: raises)."""
+        if plain:
+            self._check(self.L.hymoe_set_routing(self.h, None))
+            return
+        ng, tg = group if group else (0, 0)
+        r = Routing(1 if group else 0, ng, tg, 0 if drop is None else 1, 1.0 if drop is None else drop,
+                    min_capacity, 1 if norm_topk_prob else 0, scale)
+        self._check(self.L.hymoe_set_routing(self.h, C.byref(r)))
 
     def set_norm(self, layer: int, weight, eps: float) -> None:
         """Post-attention RMSNorm weights [H] (host numpy float32; None removes them)."""

@@ -166,6 +166,30 @@ hymoe_status hymoe_synth_layer(hymoe_ctx* ctx, uint32_t layer, int32_t ggml_type
  * them.  The first call also allocates a [max_tokens, H] F32 buffer for the normalised rows. */
 hymoe_status hymoe_set_norm(hymoe_ctx* ctx, uint32_t layer, const float* weight, float eps, int flags);
 
+/* Routing variant of the FULL-mode router, topkgating_full (MoERoutingConfig,
+ * src/hunyuan_moe_full.h:25-47; src/hunyuan_moe_full.cpp:119-243), for every later call of the
+ * context (every rank of an expert-parallel job sets the same):
+ *   group_limited_greedy: experts in n_group groups of E/n_group (n_group <= 32 dividing E),
+ *     each group scored by its largest probability; only the topk_group best groups'
+ *     experts can be selected (ties: lower group);
+ *   norm_topk_prob: weights = p / sum of the K selected p, the sum clamped below at 1e-8
+ *     (with K > 1); otherwise weights = p * routed_scaling_factor;
+ *   drop_tokens (capacity_factor, min_capacity): capacity-limited routing is not implemented
+ *     (HYMOE_ERR_UNSUPPORTED); without it topkgating_full's capacity keeps every pair.
+ * The debug probabilities stay the unmasked softmax (the reference's router_probs).
+ * NULL restores moe_forward_cpu's routing (the default). */
+typedef struct {
+    int32_t group_limited_greedy;
+    uint32_t n_group;
+    uint32_t topk_group;
+    int32_t drop_tokens;
+    float capacity_factor;
+    uint32_t min_capacity;
+    int32_t norm_topk_prob;
+    float routed_scaling_factor;
+} hymoe_routing;
+hymoe_status hymoe_set_routing(hymoe_ctx* ctx, const hymoe_routing* routing);
+
 /* Expert placement of one layer for expert parallelism.  slot_of_expert[e] (a
  * permutation of 0..E-1; NULL = identity, the default) puts expert e in slot s, held by
  * rank s / (E/ep_size) as its local expert s % (E/ep_size).  Every rank must set the same

@@ -381,3 +381,50 @@ def test_layer_stack_in_place_matches_the_oracle(orc):
     for l in range(L):
         x = _oracle(orc, lays[l], orc.rms_norm(x, ws[l], 1e-5), K, I, resid=x)["out"]
     assert rel_l2(got, x) <= REL_L2_TOL
+
+
+def _block_with_routing(orc, lay, x, idx, w, I):
+    """shared(x) + sum_k w[t,k] * expert_{idx[t,k]}(x[t]) through the oracle's FFN."""
+    out = orc.swiglu_ffn(x, lay["sgu_f"], lay["sdn_f"], I).astype(np.float64)
+    for e in np.unique(idx):
+        rows = np.nonzero((idx == e).any(axis=1))[0]
+        y = orc.swiglu_ffn(np.ascontiguousarray(x[rows]), lay["egu_f"][e], lay["edn_f"][e], I)
+        wk = np.where(idx[rows] == e, w[rows], 0).sum(axis=1)
+        out[rows] += wk[:, None] * y
+    return out.astype(np.float32)
+
+
+@pytest.mark.parametrize("opts", [{"group": (8, 3)}, {"norm_topk_prob": False, "scale": 2.5},
+                                  {"group": (4, 1), "norm_topk_prob": False, "scale": 0.7}])
+@pytest.mark.parametrize("T", [5, 40, 300])
+def test_full_mode_routing_variants_vs_oracle(orc, opts, T):
+    """hymoe_set_routing (group-limited greedy, unnormalised scaling) against the oracle's
+    topkgating_full on the GPU's own logits (bit-identical to the reference's): same experts in
+    the same rank order (a difference only where two probabilities lie within 1e-6 of each
+    other, expf's last place), same weights within 1e-5; the output equals the block under
+    that routing within the parity tolerance; the plain routing comes back bit-identical."""
+    H, I, E, K, seed, wt = 512, 256, 64, 8, 61, O.Q4_0
+    lay = host_layer(orc, seed, 0, H, I, E, wt)
+    m = _ctx(H, I, E, K, T)
+    _load(m, lay, wt)
+    x = O.synth_x(orc, seed + T, T, H)
+    plain = m.forward_host(0, x)["out"]
+    m.set_routing(**opts)
+    r = m.forward_host(0, x, debug=True)
+    a = orc.topkgating_full(r["logits"], K, **opts)
+    np.testing.assert_allclose(r["probs"], a["probs"], rtol=1e-6, atol=1e-12)
+    for t in range(T):
+        if not np.array_equal(r["idx"][t], a["idx"][t]):
+            diff = set(r["idx"][t]) ^ set(a["idx"][t])
+            kth = a["probs"][t, a["idx"][t]].min()
+            assert all(abs(a["probs"][t, e] - kth) <= 1e-6 * kth for e in diff), f"token {t}"
+        else:
+            np.testing.assert_allclose(r["w"][t], a["w"][t], rtol=1e-5)
+    ref = _block_with_routing(orc, lay, x, r["idx"], r["w"], I)
+    assert rel_l2(r["out"], ref) <= REL_L2_TOL
+    with pytest.raises(hymoe.HymoeError) as ei:
+        m.set_routing(drop=1.0)
+    assert ei.value.status == 4
+    m.set_routing(plain=True)
+    assert np.array_equal(m.forward_host(0, x)["out"], plain)
+    m.close()
