@@ -44,6 +44,10 @@ def test_null_arguments_are_rejected():
     assert L.hymoe_create(None, None) == 1
     assert L.hymoe_synchronize(None) == 1
     assert L.hymoe_forward(None, 0, None, None, None, 0, None, None, 0) == 1
+    assert L.hymoe_set_routing(None, None) == 1
+    assert L.hymoe_set_norm(None, 0, None, 1e-5, 0) == 1
+    assert L.hymoe_set_placement(None, 0, None) == 1
+    assert L.hymoe_load_layer_gguf(None, 0, None, 0) == 1
     L.hymoe_destroy(None)
 
 
