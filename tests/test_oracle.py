@@ -107,9 +107,13 @@ def test_bias_zero_equals_no_bias(orc):
 
 
 @pytest.mark.skipif(not O.RefMoE.available(), reason="reference checker not built here")
-@pytest.mark.parametrize("seed", [11, 12])
-def test_restatement_matches_compiled_reference(orc, seed):
-    H, I, E, K, T = 256, 128, 32, 8, 13
+@pytest.mark.parametrize("seed,H,I,E,K,T", [(11, 256, 128, 32, 8, 13), (12, 256, 128, 32, 8, 13),
+                                            (13, 128, 64, 8, 1, 5), (14, 384, 192, 16, 2, 33),
+                                            (15, 128, 128, 32, 6, 1), (16, 256, 64, 64, 8, 9)])
+def test_restatement_matches_compiled_reference(orc, seed, H, I, E, K, T):
+    """Every output of moe_forward_cpu (output, probabilities, top-K weights and indices) is
+    bit-identical between the restatement and the reference compiled from its sources, over
+    expert counts 8..64, K 1..8, hidden sizes 128..384 and 1..33 tokens."""
     rw, sgu, sdn, egu, edn = O.synth_layer_f32(orc, seed, 0, H, I, E, O.Q4_0)
     x = O.synth_x(orc, seed, T, H)
     ref = O.RefMoE()
