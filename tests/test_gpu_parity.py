@@ -428,3 +428,21 @@ def test_full_mode_routing_variants_vs_oracle(orc, opts, T):
     m.set_routing(plain=True)
     assert np.array_equal(m.forward_host(0, x)["out"], plain)
     m.close()
+
+
+@pytest.mark.parametrize("H,I,E,K,wt,Ts", [(256, 128, 8, 1, O.Q4_0, (1, 7, 100)),
+                                             (384, 192, 16, 2, O.Q8_0, (3, 70)),
+                                             (256, 128, 32, 6, O.Q4_0, (1, 33, 130))])
+def test_other_expert_counts_and_top_k_vs_oracle(orc, H, I, E, K, wt, Ts):
+    """Expert counts 8/16/32 with K = 1/2/6 on the decode and tensor-core paths: logits
+    bit-identical, experts equal outside near ties, output within the parity tolerance."""
+    lay = host_layer(orc, 71 + E, 0, H, I, E, wt)
+    m = _ctx(H, I, E, K, max(Ts))
+    _load(m, lay, wt)
+    for T in Ts:
+        x = O.synth_x(orc, 71 + T, T, H)
+        r = m.forward_host(0, x, debug=True)
+        o = _oracle(orc, lay, x, K, I)
+        assert np.array_equal(r["logits"], o["logits"]), T
+        _check(r, o["out"], o["idx"], o["logits"], K)
+    m.close()
