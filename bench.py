@@ -1,20 +1,26 @@
 #!/usr/bin/env python
 """bench.py — MoE-layer tokens/s of the B200 MoE block (BASELINE metric), plus the decode
-HBM bandwidth sub-metric.
+HBM bandwidth sub-metric and the other BASELINE configurations as sub-blocks of the line.
 
-Default workload (N=1): one HunyuanImage-3.0 MoE block (H=4096, I=3072, 64 routed + 1
-shared SwiGLU expert, top-8), GGUF Q4_0 expert weights, 4096 tokens per step,
-activations ~N(0,1), router bias ~N(0,0.5) (seeded synthetic data, random-init weights
-generated on the device).  A step is one hymoe_forward over the 4096 tokens.
+Headline workload (N=1, cfg3): one HunyuanImage-3.0 MoE block (H=4096, I=3072, 64 routed + 1
+shared SwiGLU expert, top-8), GGUF Q4_0 expert weights, 4096 tokens per step, activations
+~N(0,1), router bias ~N(0,0.5) (seeded synthetic data, random-init weights generated on the
+device).  A step is one hymoe_forward over the 4096 tokens.
 
   value  tokens/s with inputs resident in HBM, device time by CUDA events, L2 flushed
          between steps (a 256 MiB write outside the timed events)
   e2e    the same call through the C ABI with pinned HOST buffers: H2D of x and the bias,
          compute, D2H of the output inside the timed region
-  roofline  the dominant kernel (grouped gate_up GEMM): algorithmic FLOP per launch /
-         its CUDA-event duration, against MEASURED_PEAKS.json bf16 (sustained)
+  roofline  the dominant kernel (grouped gate_up GEMM): algorithmic FLOP per launch / its
+         CUDA-event duration, against MEASURED_PEAKS.json bf16 burst (the kernel runs at the
+         maximum SM clock inside a 3 ms step)
+  parity  rows of the timed 4096-token call against the oracle (N=1), or every row of every
+         rank against a single-GPU context of the same layer (N>1)
   cpu_baseline  the reference's own moe_forward_cpu (oracle/_ref, compiled from the
-         reference sources) on a bounded token sample, one host core as written
+         reference sources) on the same sampled token rows, one host core as written
+Sub-blocks: `cfg1` (F32 weights, 256 tokens; N=1), `cfg4` (8192 tokens split over the ranks,
+Zipf(1.1) router bias, balanced placement; every N), `stack` (cfg5: 32 Q4_0 blocks layer by
+layer on a 4160-token sequence; every N), `decode` (cfg2: Q8_0, 1/8/64 tokens; N=1).
 
 --impl reference times the reference's CPU implementation with all host cores (token
 sharded over processes; the MoE is per-token independent) on the same workload.
@@ -22,8 +28,7 @@ Under torchrun (N > 1) the layer runs expert-parallel: rank r owns 64/N experts 
 router and the shared expert) — by default those of its slots in a placement that balances
 the experts' routed rows on a calibration batch (--placement contiguous: experts
 [r*64/N, (r+1)*64/N)) — processes its own 4096 tokens, and token rows and results move over
-NVLink peer memory inside the timed step (weak scaling: per-GPU tokens fixed).  --bias zipf
-gives the skewed-load variant of the expert-parallel config.
+NVLink peer memory inside the timed step (weak scaling: per-GPU tokens fixed).
 """
 from __future__ import annotations
 
@@ -31,9 +36,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -47,6 +50,12 @@ FLOP_PER_PAIR_DN = 2 * H * I          # down
 FLOP_ROUTER_PER_TOKEN = 2 * E * H
 FFN_BYTES = {2: 2 * I * H // 32 * 18 + H * I // 32 * 18, 8: 2 * I * H // 32 * 34 + H * I // 32 * 34}
 METRIC = "MoE-layer tokens/s (Q4_0, 4096 tok) at 1/2/4/8 B200; decode HBM GB/s"
+CFG1_TOKENS = 256
+CFG4_TOKENS = 8192
+STACK_LAYERS, STACK_SEQ = 32, 4160
+STACK_METRIC = "MoE-stack tokens/s (32 Q4_0 MoE blocks, 4160-token sequence, layer by layer)"
+PARITY_ROWS = 12          # oracle-checked rows of the timed call (N=1)
+PARITY_ROWS_EP = 4        # oracle-checked rows of rank 0's expert-parallel output (N>1)
 
 
 def peaks():
@@ -111,6 +120,99 @@ class Clocks:
                 "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples)}
 
 
+# --------------------------------------------------------------------------- GPU helpers
+
+def _context(hymoe, torch, T: int, rank: int, world: int, local_rank: int, layers: int = 1):
+    """A hymoe context for up to T tokens per call: expert parallel over the job's ranks (rank 0
+    makes the NCCL id) or, on one GPU, the whole layer."""
+    if world > 1:
+        box = [hymoe.nccl_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(box, src=0)
+        return hymoe.MoE(H, I, E, K, layers, T, device=local_rank, ep_rank=rank, ep_size=world,
+                         nccl_id=box[0])
+    return hymoe.MoE(H, I, E, K, layers, T, device=local_rank)
+
+
+def _balance(m, hymoe, torch, xc, bias, wtype: int, seed: int, world: int, layer: int = 0):
+    """Expert placement from a calibration batch xc (its own seed, not the timed tokens): each
+    expert's routed rows over all ranks, balanced greedily over the ranks; then every rank
+    loads the experts of its slots."""
+    T = xc.shape[0]
+    out = torch.empty_like(xc)
+    idx = torch.empty(T, K, dtype=torch.int32, device=xc.device)
+    m.forward_device(layer, xc.data_ptr(), out.data_ptr(), T, bias_ptr=bias.data_ptr(),
+                     dbg=hymoe.Debug(None, None, None, idx.data_ptr()))
+    torch.cuda.synchronize()
+    cal = torch.bincount(idx.flatten().long(), minlength=E)
+    torch.distributed.all_reduce(cal)
+    place = hymoe.balance_placement(cal.cpu().tolist(), world)
+    m.set_placement(layer, place)
+    m.synth_layer(layer, wtype, seed, 0.02)
+    return place
+
+
+def _max_over_ranks(torch, dev, *vals):
+    t = torch.tensor(list(vals), device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
+def _time_steps(torch, stream, step, steps: int, flush, world: int, local_rank: int, dev):
+    """`steps` steps, each bracketed by CUDA events on `stream` (an L2 flush outside them when
+    `flush` is given), clocks sampled meanwhile; returns (total device ms, max over ranks;
+    clock record)."""
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    clocks = Clocks(local_rank)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    for s in range(steps):
+        if flush is not None:
+            flush.zero_()
+        ev[s][0].record(stream)
+        step()
+        ev[s][1].record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        ms = _max_over_ranks(torch, dev, ms)[0]
+    return ms, clk
+
+
+def _row_parity(torch, hymoe, ref1, x, out, idx, bias, world: int, dev) -> dict:
+    """Expert-parallel rows against a single-GPU context `ref1` holding all E experts of the
+    same seeded layer (the single-GPU path is pinned to the oracle by the N=1 line and the GPU
+    tests): this rank's tokens through ref1, compared with the expert-parallel output `out`
+    and top-K `idx` of the same tokens; summed over the ranks."""
+    T = x.shape[0]
+    out1 = torch.empty_like(x)
+    lg1 = torch.empty(T, E, device=dev)
+    idx1 = torch.empty(T, K, dtype=torch.int32, device=dev)
+    ref1.forward_device(0, x.data_ptr(), out1.data_ptr(), T, bias_ptr=bias.data_ptr(),
+                        dbg=hymoe.Debug(lg1.data_ptr(), None, None, idx1.data_ptr()))
+    torch.cuda.synchronize()
+    same_rows = (out1 == out).all(dim=1).sum()
+    num = ((out.double() - out1.double()) ** 2).sum()
+    den = (out1.double() ** 2).sum()
+    srt = torch.sort(lg1, dim=1, descending=True).values
+    gap = srt[:, K - 1] - srt[:, K]
+    differ = (torch.sort(idx, dim=1).values != torch.sort(idx1, dim=1).values).any(dim=1)
+    bad = (differ & (gap > 1e-4)).sum()
+    ties = (differ & (gap <= 1e-4)).sum()
+    t = torch.stack([same_rows.double(), torch.tensor(float(T), device=dev, dtype=torch.float64),
+                     num, den, bad.double(), ties.double()])
+    if world > 1:
+        torch.distributed.all_reduce(t)
+    same_rows, rows, num, den, bad, ties = t.tolist()
+    rel = (num / den) ** 0.5 if den > 0 else 0.0
+    return {"against": "single-GPU hymoe context holding all 64 experts of the same layer, every row of every rank",
+            "rows": int(rows), "bit_identical_rows": int(same_rows), "rel_l2": rel, "rel_l2_tol": 1e-3,
+            "topk_mismatches": int(bad), "near_ties_excluded": int(ties),
+            "ok": int(bad) == 0 and rel <= 1e-3}
+
+
 # --------------------------------------------------------------------------- GPU arm
 
 def run_gpu(args, rank: int, world: int, local_rank: int):
@@ -121,15 +223,9 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     T = args.tokens
-    if world > 1:
-        # Expert parallelism: rank 0 makes the NCCL id, every rank owns E/world experts.
-        box = [hymoe.nccl_unique_id() if rank == 0 else None]
-        torch.distributed.broadcast_object_list(box, src=0)
-        m = hymoe.MoE(H, I, E, K, 1, T, device=local_rank, ep_rank=rank, ep_size=world,
-                      nccl_id=box[0])
-    else:
-        m = hymoe.MoE(H, I, E, K, 1, T, device=local_rank)
-    m.synth_layer(0, hymoe.TYPE_Q8_0 if args.wtype == "q8_0" else hymoe.TYPE_Q4_0, args.seed, 0.02)
+    wtype = hymoe.TYPE_Q8_0 if args.wtype == "q8_0" else hymoe.TYPE_Q4_0
+    m = _context(hymoe, torch, T, rank, world, local_rank)
+    m.synth_layer(0, wtype, args.seed, 0.02)
     # A dedicated stream: torch's default stream has handle 0, which the C ABI reads as
     # "the context's own stream".  Every torch op and event below runs on this stream.
     stream = torch.cuda.Stream(device=dev)
@@ -138,9 +234,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     g = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank)
     x = torch.randn(T, H, device=dev, generator=g, dtype=torch.float32)
     if args.bias == "zipf":
-        sys.path.insert(0, ORACLE)
-        from oracle import zipf_bias  # the seeded Zipf(1.1) expert skew of the EP workload
-        bias = torch.from_numpy(zipf_bias(args.seed, E)).to(dev)
+        bias = torch.from_numpy(hymoe.zipf_router_bias(args.seed, E)).to(dev)
     else:
         gb = torch.Generator(device=dev).manual_seed(args.seed)
         bias = (torch.randn(E, device=dev, generator=gb) * 0.5).contiguous()
@@ -152,21 +246,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
 
     place = None
     if world > 1 and args.placement == "balanced":
-        # Expert placement from a calibration batch (its own seed, not the timed tokens): the
-        # routed rows of every expert over all ranks, balanced greedily over the ranks; then
-        # every rank loads the experts of its slots.
         gc = torch.Generator(device=dev).manual_seed(args.seed * 1000 + rank + 500)
         xc = torch.randn(T, H, device=dev, generator=gc, dtype=torch.float32)
-        cal_idx = torch.empty(T, K, dtype=torch.int32, device=dev)
-        m.forward_device(0, xc.data_ptr(), out.data_ptr(), T, bias_ptr=bias.data_ptr(),
-                         dbg=hymoe.Debug(None, None, None, cal_idx.data_ptr()))
-        torch.cuda.synchronize()
-        cal = torch.bincount(cal_idx.flatten().long(), minlength=E)
-        torch.distributed.all_reduce(cal)
-        place = hymoe.balance_placement(cal.cpu().tolist(), world)
-        m.set_placement(0, place)
-        m.synth_layer(0, hymoe.TYPE_Q8_0 if args.wtype == "q8_0" else hymoe.TYPE_Q4_0, args.seed, 0.02)
-        del xc, cal_idx
+        place = _balance(m, hymoe, torch, xc, bias, wtype, args.seed, world)
+        del xc
 
     for _ in range(args.warmup):
         step()
@@ -212,13 +295,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     if world > 1:
         torch.distributed.barrier()
     dev_ms = sum(a.elapsed_time(b) for a, b in ev)
-    t_max = dev_ms
-    if world > 1:
-        tt = torch.tensor([dev_ms], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        t_max = float(tt.item())
+    t_max = _max_over_ranks(torch, dev, dev_ms)[0] if world > 1 else dev_ms
     ms_per_step = t_max / args.steps
     value = world * T * args.steps / (t_max / 1e3)
+    # `out` now holds the last timed step's output: the rows the parity below checks
 
     # ---- e2e through the C ABI with pinned host buffers
     xh = x.cpu().pin_memory()
@@ -238,9 +318,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         b.synchronize()
         e2e_ms += a.elapsed_time(b)
     if world > 1:
-        tt = torch.tensor([e2e_ms], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
+        e2e_ms = _max_over_ranks(torch, dev, e2e_ms)[0]
     e2e_value = world * T * args.steps / (e2e_ms / 1e3)
 
     pk = peaks()
@@ -249,9 +327,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     achieved = flop_gu / (gu_launch_ms / 1e3) / 1e12
     tr = ncu_traffic().get("gate_up_q4_0_t4096", {})
     roofline = {"kernel": "gemm_tc_kernel<Q4_0> (grouped gate_up + SwiGLU)", "bound": "tensor",
-                "achieved": round(achieved, 1), "peak": pk["tf_sus"], "unit": "TFLOP/s",
-                "frac": round(achieved / pk["tf_sus"], 4),
-                "peak_src": f"{pk['src']} bf16 sustained (burst {pk['tf']})",
+                "achieved": round(achieved, 1), "peak": pk["tf"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["tf"], 4),
+                "peak_src": f"{pk['src']} bf16 burst (the step is 3 ms at the maximum SM clock; "
+                            f"sustained {pk['tf_sus']})",
                 "traffic": tr.get("dram_bytes_per_launch"),
                 "algorithmic_flop_per_launch": flop_gu}
     phases = {k: round(v[0] / args.steps, 4) for k, v in prof.items() if v[1]}
@@ -265,7 +344,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
         "data": f"synthetic (seeded; random-init {args.wtype.upper()} weights generated on device)",
-        "config": {"workload": f"cfg3/cfg4: one MoE block, {args.wtype.upper()} experts, {T} tokens/step/GPU, "
+        "config": {"workload": f"cfg3: one MoE block, {args.wtype.upper()} experts, {T} tokens/step/GPU, "
                                f"router bias {'Zipf(1.1) over a seeded expert permutation' if args.bias == 'zipf' else '~N(0,0.5)'}",
                    "model": "HunyuanImage-3.0 MoE block H=4096 I=3072 E=64+1 shared top-8",
                    "global_batch": T * world, "seq_len": T,
@@ -274,7 +353,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                                  if place is not None else "contiguous (rank r owns experts [r*E/N, (r+1)*E/N))") if world > 1 else None,
                    "l2": "flushed between steps (256 MiB write outside the timed events)"},
         "tflops_total": round(flop_total / (ms_per_step / 1e3) / 1e12, 1),
-        "frac_of_peak_total": round(flop_total / (ms_per_step / 1e3) / 1e12 / pk["tf_sus"], 4),
+        "frac_of_peak_total": round(flop_total / (ms_per_step / 1e3) / 1e12 / pk["tf"], 4),
         "phases_ms_per_step": phases,
         "roofline": roofline,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
@@ -287,28 +366,183 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     }
     if per_rank is not None:
         res["ep_ranks"] = per_rank
-    if args.cpu and world == 1:
-        # the reference on a token sample of the same seeded layer; the GPU runs the same tokens
-        gf = (lambda xs: m.forward_host(0, xs, debug=True)) if args.wtype == "q4_0" else None
-        res["cpu_baseline"], res["parity"] = cpu_baseline_single(args.seed, gpu_forward=gf)
+
+    # ---- parity of the timed call's rows
+    sample = np.sort(np.random.default_rng(args.seed + 77).choice(T, size=PARITY_ROWS if world == 1
+                                                                  else PARITY_ROWS_EP, replace=False))
+    sel = torch.from_numpy(sample).to(dev)
+    xs = x.index_select(0, sel).cpu().numpy()
+    outs = out.index_select(0, sel).cpu().numpy()
+    idxs = dbg_idx.index_select(0, sel).cpu().numpy()
+    bias_np = bias.cpu().numpy()
+    ref1 = None
+    if world > 1:
+        # every row of every rank against a single-GPU context of the same layer
+        ref1 = hymoe.MoE(H, I, E, K, 1, CFG4_TOKENS, device=local_rank)
+        ref1.synth_layer(0, wtype, args.seed, 0.02)
+        ref1.set_stream(stream.cuda_stream)
+        res["parity"] = _row_parity(torch, hymoe, ref1, x, out, dbg_idx, bias, world, dev)
+        if args.cpu:  # and a few of rank 0's rows against the oracle
+            if rank == 0:
+                res["parity"]["oracle_rows"] = oracle_rows(args.seed, wtype, xs, outs, idxs, bias_np,
+                                                           time_reference=False)[1]
+            torch.distributed.barrier()
+        res["parity"]["ok"] = res["parity"]["ok"] and res["parity"].get("oracle_rows", {}).get("ok", True)
+    elif args.cpu:
+        res["cpu_baseline"], res["parity"] = oracle_rows(args.seed, wtype, xs, outs, idxs, bias_np)
+        res["parity"]["rows_of"] = f"the last timed {T}-token call (rows {sample.tolist()})"
     m.close()
+    del x, out, flush
+
+    if args.subblocks:
+        res["cfg4"] = run_cfg4(args, rank, world, local_rank, stream, ref1)
+        if ref1 is not None:
+            ref1.close()
+        if world == 1:
+            res["cfg1"] = run_cfg1(args, local_rank, stream)
+        res["stack"] = run_stack(args, rank, world, local_rank, sub=True)
+    elif ref1 is not None:
+        ref1.close()
     if args.decode and world == 1:
         res["decode"] = run_decode(args, local_rank)
     return res
 
 
-STACK_LAYERS, STACK_SEQ = 32, 4160
-STACK_METRIC = "MoE-stack tokens/s (32 Q4_0 MoE blocks, 4160-token sequence, layer by layer)"
+def run_cfg4(args, rank: int, world: int, local_rank: int, stream, ref1=None) -> dict:
+    """cfg4: one Q4_0 block on 8192 tokens in total, split evenly over the ranks (strong
+    scaling), router bias Zipf(1.1) over a seeded expert permutation, experts placed by the
+    balanced placement of a calibration batch.  At N>1 rank 0 also times the same 8192 tokens
+    on its own GPU through a single-GPU context (the other ranks wait), which gives the
+    sub-block's own scaling efficiency, and every rank's rows are compared with that context."""
+    import torch
+    import hymoe
+
+    dev = torch.device("cuda", local_rank)
+    per = CFG4_TOKENS // world
+    wtype = hymoe.TYPE_Q4_0
+    m = _context(hymoe, torch, per, rank, world, local_rank)
+    m.synth_layer(0, wtype, args.seed, 0.02)
+    m.set_stream(stream.cuda_stream)
+    bias = torch.from_numpy(hymoe.zipf_router_bias(args.seed, E)).to(dev)
+    g = torch.Generator(device=dev).manual_seed(args.seed * 1000 + 4242)
+    xall = torch.randn(CFG4_TOKENS, H, device=dev, generator=g, dtype=torch.float32)
+    x = xall[rank * per:(rank + 1) * per].contiguous()
+    out = torch.empty_like(x)
+    if world > 1:
+        gc = torch.Generator(device=dev).manual_seed(args.seed * 1000 + 4243)
+        xc = torch.randn(CFG4_TOKENS, H, device=dev, generator=gc, dtype=torch.float32)
+        _balance(m, hymoe, torch, xc[rank * per:(rank + 1) * per].contiguous(), bias, wtype, args.seed, world)
+        del xc
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        m.forward_device(0, x.data_ptr(), out.data_ptr(), per, bias_ptr=bias.data_ptr())
+
+    for _ in range(args.warmup):
+        step()
+    idx = torch.empty(per, K, dtype=torch.int32, device=dev)
+    m.forward_device(0, x.data_ptr(), out.data_ptr(), per, bias_ptr=bias.data_ptr(),
+                     dbg=hymoe.Debug(None, None, None, idx.data_ptr()))
+    torch.cuda.synchronize()
+    steps = args.steps
+    ms, clk = _time_steps(torch, stream, step, steps, flush, world, local_rank, dev)
+    load = torch.bincount(idx.flatten().long(), minlength=E)
+    if world > 1:
+        torch.distributed.all_reduce(load)
+    value = CFG4_TOKENS * steps / (ms / 1e3)
+    res = {"metric": "MoE-layer tokens/s (Q4_0, 8192 tokens in total, Zipf(1.1) router bias)",
+           "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+           "ms_per_step": round(ms / steps, 4), "scaling": "strong",
+           "config": {"workload": f"cfg4: {CFG4_TOKENS} tokens split over {world} GPU(s) ({per} each), "
+                                  "Zipf(1.1) bias over a seeded expert permutation",
+                      "placement": "balanced on a calibration batch" if world > 1 else None,
+                      "l2": "flushed between steps"},
+           "expert_rows": {"max": int(load.max()), "min": int(load.min()), "mean": float(load.double().mean())},
+           "clocks": clk}
+    if world > 1 and ref1 is not None:
+        ref1.set_stream(stream.cuda_stream)
+        res["parity"] = _row_parity(torch, hymoe, ref1, x, out, idx, bias, world, dev)
+        m.close()
+        one = torch.zeros(1, device=dev, dtype=torch.float64)
+        if rank == 0:
+            o1 = torch.empty_like(xall)
+
+            def step1():
+                ref1.forward_device(0, xall.data_ptr(), o1.data_ptr(), CFG4_TOKENS, bias_ptr=bias.data_ptr())
+
+            for _ in range(args.warmup):
+                step1()
+            ms1, _ = _time_steps(torch, stream, step1, steps, flush, 1, local_rank, dev)
+            one[0] = CFG4_TOKENS * steps / (ms1 / 1e3)
+        torch.distributed.broadcast(one, src=0)
+        v1 = float(one.item())
+        res["one_gpu_value"] = round(v1, 1)
+        res["efficiency"] = round(value / (world * v1), 4)
+    else:
+        m.close()
+    return res
 
 
-def run_stack(args, rank: int, world: int, local_rank: int) -> dict:
+def run_cfg1(args, local_rank: int, stream) -> dict:
+    """cfg1: the reference's own weight type, F32 (stored on the device as F16 tiles for the
+    fp16 tensor cores), 256 tokens, no router bias; timed like the headline, with the parity of
+    8 sampled rows against the oracle on the F32 weights."""
+    import numpy as np
+    import torch
+    import hymoe
+
+    dev = torch.device("cuda", local_rank)
+    T = CFG1_TOKENS
+    m = hymoe.MoE(H, I, E, K, 1, T, device=local_rank)
+    m.synth_layer(0, hymoe.TYPE_F32, args.seed, 0.02)
+    m.set_stream(stream.cuda_stream)
+    g = torch.Generator(device=dev).manual_seed(args.seed * 1000 + 256)
+    x = torch.randn(T, H, device=dev, generator=g, dtype=torch.float32)
+    out = torch.empty_like(x)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        m.forward_device(0, x.data_ptr(), out.data_ptr(), T)
+
+    for _ in range(args.warmup):
+        step()
+    idx = torch.empty(T, K, dtype=torch.int32, device=dev)
+    m.forward_device(0, x.data_ptr(), out.data_ptr(), T, dbg=hymoe.Debug(None, None, None, idx.data_ptr()))
+    torch.cuda.synchronize()
+    m.profile(True)
+    ms, clk = _time_steps(torch, stream, step, args.steps, flush, 1, local_rank, dev)
+    m.profile(False)
+    prof = m.profile_read()
+    m.close()
+    pk = peaks()
+    flop = T * (K + 1) * (FLOP_PER_PAIR_GU + FLOP_PER_PAIR_DN) + T * FLOP_ROUTER_PER_TOKEN
+    tf = flop / (ms / args.steps / 1e3) / 1e12
+    res = {"metric": "MoE-layer tokens/s (F32 weights, 256 tokens)",
+           "value": round(T * args.steps / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": 1,
+           "steps": args.steps, "ms_per_step": round(ms / args.steps, 4),
+           "config": {"workload": "cfg1: one MoE block, F32 weights (F16 tiles on the device), 256 tokens, no bias",
+                      "l2": "flushed between steps"},
+           "tflops_total": round(tf, 1), "frac_of_peak_total": round(tf / pk["tf"], 4),
+           "phases_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in prof.items() if v[1]},
+           "clocks": clk}
+    if args.cpu:
+        sample = np.sort(np.random.default_rng(args.seed + 1).choice(T, size=8, replace=False))
+        sel = torch.from_numpy(sample).to(dev)
+        res["parity"] = oracle_rows(args.seed, hymoe.TYPE_F32, x.index_select(0, sel).cpu().numpy(),
+                                    out.index_select(0, sel).cpu().numpy(),
+                                    idx.index_select(0, sel).cpu().numpy(), None, time_reference=False)[1]
+    return res
+
+
+def run_stack(args, rank: int, world: int, local_rank: int, sub: bool = False) -> dict:
     """cfg5: 32 MoE blocks (Q4_0, random-init per layer from one seed) applied layer by layer to
     one 4160-token sequence, x <- x + MoE_l(RMSNorm(x)) with unit RMSNorm weights (the
     post-attention half of src/decoder_layer.cpp:34-42; eps 1e-5), in place
     (HYMOE_PRE_NORM, residual = out = x).  The sequence is split over the ranks, each of which
     holds E/N experts of every layer.  A step is the whole stack; `value` = sequence tokens per
     second (device time, max over ranks); `e2e` adds the upload of x and the download of the
-    result through the host API."""
+    result through the host API.  As a sub-block of the default line (`sub`) it runs at most
+    5 timed steps of about 0.1 s."""
     import numpy as np
     import torch
     import hymoe
@@ -316,14 +550,10 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> dict:
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     L = STACK_LAYERS
+    steps = min(args.steps, 5) if sub else args.steps
     per = (STACK_SEQ + world - 1) // world
     T = max(0, min(per, STACK_SEQ - rank * per))  # this rank's slice of the sequence
-    if world > 1:
-        box = [hymoe.nccl_unique_id() if rank == 0 else None]
-        torch.distributed.broadcast_object_list(box, src=0)
-        m = hymoe.MoE(H, I, E, K, L, per, device=local_rank, ep_rank=rank, ep_size=world, nccl_id=box[0])
-    else:
-        m = hymoe.MoE(H, I, E, K, L, per, device=local_rank)
+    m = _context(hymoe, torch, per, rank, world, local_rank, layers=L)
     ones = np.ones(H, np.float32)
     for l in range(L):
         m.synth_layer(l, hymoe.TYPE_Q4_0, args.seed, 0.02)
@@ -344,13 +574,13 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> dict:
         stack(x.data_ptr())
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
+          for _ in range(steps)]
     clocks = Clocks(local_rank)
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     m.profile(True)
-    for s in range(args.steps):
+    for s in range(steps):
         x.copy_(x0)  # every step starts from the same sequence (outside the timed events)
         ev[s][0].record(stream)
         stack(x.data_ptr())
@@ -366,7 +596,7 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> dict:
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    for s in range(args.steps):
+    for s in range(steps):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         x.copy_(xh, non_blocking=True)
@@ -376,14 +606,15 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> dict:
         b.synchronize()
         e2e_ms += a.elapsed_time(b)
     if world > 1:
-        tt = torch.tensor([dev_ms, e2e_ms], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        dev_ms, e2e_ms = (float(v) for v in tt.tolist())
+        dev_ms, e2e_ms = _max_over_ranks(torch, dev, dev_ms, e2e_ms)
     m.close()
-    ms = dev_ms / args.steps
+    ms = dev_ms / steps
+    pk = peaks()
+    flop = STACK_SEQ * L * ((K + 1) * (FLOP_PER_PAIR_GU + FLOP_PER_PAIR_DN) + FLOP_ROUTER_PER_TOKEN)
+    tf = flop / (ms / 1e3) / 1e12 / world
     return {
-        "metric": STACK_METRIC, "value": round(STACK_SEQ * args.steps / (dev_ms / 1e3), 1),
-        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "metric": STACK_METRIC, "value": round(STACK_SEQ * steps / (dev_ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "fp16",
         "data": "synthetic (seeded; random-init Q4_0 weights of 32 layers generated on device)",
@@ -393,10 +624,13 @@ def run_stack(args, rank: int, world: int, local_rank: int) -> dict:
                    "global_batch": STACK_SEQ, "seq_len": STACK_SEQ,
                    "parallelism": f"ep{world}" if world > 1 else "single",
                    "l2": "weights of 32 layers (44 GB at N=1) far exceed L2"},
-        "phases_ms_per_step": {k: round(v[0] / args.steps, 4) for k, v in prof.items() if v[1]},
-        "e2e": {"value": round(STACK_SEQ * args.steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+        "tflops_per_gpu": round(tf, 1),
+        "frac_of_peak_per_gpu": round(tf / pk["tf_sus"], 4),
+        "peak_src": f"{pk['src']} bf16 sustained (a 100 ms GEMM loop under the power cap)",
+        "phases_ms_per_step": {k: round(v[0] / steps, 4) for k, v in prof.items() if v[1]},
+        "e2e": {"value": round(STACK_SEQ * steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": xh.numel() * 4, "d2h_bytes_per_step": oh.numel() * 4,
-                "ms_per_step": round(e2e_ms / args.steps, 4)},
+                "ms_per_step": round(e2e_ms / steps, 4)},
         "gpu_launches": sum(v[1] for v in prof.values()),
         "clocks": clk,
     }
@@ -480,7 +714,7 @@ def _cpu_inputs(n_tokens: int, seed: int):
 def parity_stats(gpu: dict, ref_out, ref_idx, k: int, tol: float = 1e-3, gap: float = 1e-4) -> dict:
     """Bench-line parity of a GPU call against the reference on the same tokens: output
     relative L2 (tolerance 1e-3) and top-K agreement, tokens whose K-th/(K+1)-th logit gap is
-    at most 1e-4 excluded as near ties (the GPU's pre-softmax logits equal the reference's)."""
+    at most 1e-4 excluded as near ties (the reference's pre-softmax logits decide)."""
     import numpy as np
     out = np.asarray(gpu["out"], np.float64)
     ref = np.asarray(ref_out, np.float64)
@@ -500,37 +734,52 @@ def parity_stats(gpu: dict, ref_out, ref_idx, k: int, tol: float = 1e-3, gap: fl
             "near_ties_excluded": ties, "topk_mismatches": bad, "ok": bad == 0 and rel <= tol}
 
 
-def cpu_baseline_single(seed: int, n_tokens: int = 12, gpu_forward=None):
-    """The reference's own moe_forward_cpu, one core (as written), on a token sample; with
-    gpu_forward (tokens -> forward_host result with debug outputs) also the parity of the GPU
-    on the same tokens.  Returns (cpu_baseline, parity or None)."""
-    O, orc, x, w = _cpu_inputs(n_tokens, seed)
-    if O.RefMoE.available():
-        ref = O.RefMoE()
-        h = ref.weights(H, I, *w)
-        t0 = time.perf_counter()
-        r = ref.moe_forward(x, h, E, H, I, K)
-        dt = time.perf_counter() - t0
-        ref.free(h)
-        kind = "reference"
-    else:
-        one = O.Oracle(nthreads=1)
-        t0 = time.perf_counter()
-        r = one.moe_forward(x, *w, K, I)
-        dt = time.perf_counter() - t0
-        kind = "port"
-    base = {"value": round(n_tokens / dt, 3), "unit": "tokens/s", "cores": 1, "kind": kind,
-            "sample": f"{n_tokens} tokens of the cfg3 workload through moe_forward_cpu "
-                      f"(src/attention.cpp:191-313), F32-dequantised Q4_0 weights, no router bias "
-                      f"(the reference has none; same per-token cost), "
-                      f"{dt:.2f} s; host has {os.cpu_count()} cores"}
-    parity = None
-    if gpu_forward is not None:
-        try:
-            parity = parity_stats(gpu_forward(x), r["out"], r["idx"], K)
-            parity["against"] = kind
-        except Exception as e:  # reported, never fatal to the bench line
-            parity = {"error": repr(e)[:200]}
+def oracle_rows(seed: int, wtype: int, xs, gpu_out, gpu_idx, bias, time_reference: bool = True):
+    """Sampled rows of a timed GPU call against the CPU checkers, on the same seeded layer.
+    parity: the oracle (the C restatement, bit-identical to the reference's moe_forward_cpu) with
+    the call's router bias, against the GPU's rows and top-K.  cpu_baseline (time_reference):
+    the reference's own moe_forward_cpu (oracle/_ref) on the same rows, one host core as written
+    and without the bias it has no input for (same per-token cost); its output must equal the
+    oracle's at bias 0 bit for bit.  Returns (cpu_baseline or None, parity)."""
+    sys.path.insert(0, ORACLE)
+    import numpy as np
+    import oracle as O
+    orc = O.Oracle()
+    xs = np.ascontiguousarray(xs, np.float32)
+    n = xs.shape[0]
+    rw = orc.fill_normal(E * H, seed, O.stream_id(0, O.KIND_ROUTER), 0.02).reshape(E, H)
+    logits, _, _, ti = orc.router(xs, rw, K, bias=bias)
+    need = np.unique(ti)
+    use_ref = time_reference and O.RefMoE.available()
+    if time_reference:
+        need = np.union1d(need, orc.router(xs, rw, K)[3])
+    w = O.synth_layer_f32(orc, seed, 0, H, I, E, wtype, experts=need)
+    o = orc.moe_forward(xs, *w, K, I, bias=bias)
+    parity = parity_stats({"out": gpu_out, "idx": gpu_idx, "logits": logits}, o["out"], o["idx"], K)
+    parity["against"] = ("oracle: C restatement of moe_forward_cpu (bit-identical to the reference at "
+                         "bias 0) with the call's router bias")
+    base = None
+    if time_reference:
+        if use_ref:
+            ref = O.RefMoE()
+            h = ref.weights(H, I, *w)
+            t0 = time.perf_counter()
+            r = ref.moe_forward(xs, h, E, H, I, K)
+            dt = time.perf_counter() - t0
+            ref.free(h)
+            o0 = orc.moe_forward(xs, *w, K, I)
+            parity["oracle_equals_reference_at_bias0"] = bool(np.array_equal(o0["out"], r["out"]))
+            kind = "reference"
+        else:
+            one = O.Oracle(nthreads=1)
+            t0 = time.perf_counter()
+            one.moe_forward(xs, *w, K, I)
+            dt = time.perf_counter() - t0
+            kind = "port"
+        base = {"value": round(n / dt, 3), "unit": "tokens/s", "cores": 1, "kind": kind,
+                "sample": f"the same {n} token rows through moe_forward_cpu (src/attention.cpp:191-313), "
+                          f"F32-dequantised weights, no router bias (the reference has none; same "
+                          f"per-token cost), {dt:.2f} s; host has {os.cpu_count()} cores"}
     return base, parity
 
 
@@ -618,13 +867,15 @@ def main():
     ap.add_argument("--bias", default="normal", choices=["normal", "zipf"])
     ap.add_argument("--no-cpu", dest="cpu", action="store_false")
     ap.add_argument("--no-decode", dest="decode", action="store_false")
+    ap.add_argument("--no-subblocks", dest="subblocks", action="store_false",
+                    help="skip the cfg1 / cfg4 / stack sub-blocks of the default line")
     # weights of the main (timed) workload: cfg3/cfg4 use Q4_0; q8_0 with --tokens 1..64 runs the
     # decode workload through the same path (used for kernel captures)
     ap.add_argument("--wtype", default="q4_0", choices=["q4_0", "q8_0"])
     ap.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                     help="expert placement across ranks (N > 1)")
     ap.add_argument("--stack", action="store_true",
-                    help="cfg5 instead: 32 MoE blocks layer by layer on a 4160-token sequence")
+                    help="cfg5 alone: 32 MoE blocks layer by layer on a 4160-token sequence")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -642,7 +893,7 @@ def main():
 
         import torch
         torch.cuda.set_device(local_rank)
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                              device_id=torch.device("cuda", local_rank))
     res = run_stack(args, rank, world, local_rank) if args.stack else run_gpu(args, rank, world, local_rank)
     if rank == 0:

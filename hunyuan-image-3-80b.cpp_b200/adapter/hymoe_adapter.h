@@ -30,12 +30,21 @@ struct MoEWeightsGGUF {
 // Releases the adapter's GPU context (device memory, weights).  Optional at exit.
 void release();
 
+// Makes the next call upload its weights again.  The adapter tells weight sets apart by a
+// fingerprint of sampled bytes of every tensor (never by their addresses, which the
+// reference's layer-streaming loop reuses from layer to layer); call this after editing a
+// few weights of a set in place between two calls.
+void invalidate();
+
 }  // namespace hymoe_adapter
 
 // Same contract as moe_forward_cpu: output = shared + routed MoE of the (post-attention
 // RMS-normalised) hidden states; debug_router_logits receives the softmax probabilities,
-// as the reference writes them.  Weights (F32 MoEWeights) are uploaded when a different
-// weight set is passed; GPU errors are thrown as std::runtime_error.
+// as the reference writes them.  Weights (F32 MoEWeights) are uploaded whenever their content
+// differs from the set on the device (sizes and sampled bytes of every tensor), so one
+// MoEWeights object refilled layer after layer is uploaded for each layer.  Any n_tokens is
+// accepted: calls above 8192 tokens run as 8192-token chunks.  GPU errors are thrown as
+// std::runtime_error.
 void hymoe_moe_forward_cpu(const float* hidden_states, const MoEWeights& w, uint32_t n_tokens,
                            const HunyuanConfig& cfg, float* output,
                            float* debug_router_logits = nullptr,

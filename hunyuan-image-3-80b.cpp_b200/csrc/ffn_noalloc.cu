@@ -169,13 +169,17 @@ cudaError_t scratch_for_current_device(float** out) {
     return cudaSuccess;
 }
 
-bool on_device(const void* p) {
+// Memory the kernels, which run on the current device `dev`, may read and write directly:
+// device memory of that device, or managed memory.  Another GPU's memory is refused (it would
+// turn into peer traffic, or an illegal access without a peer mapping).
+bool on_device(const void* p, int dev) {
     cudaPointerAttributes a{};
     if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
         cudaGetLastError();
         return false;
     }
-    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+    if (a.type == cudaMemoryTypeManaged) return true;
+    return a.type == cudaMemoryTypeDevice && a.device == dev;
 }
 
 size_t gguf_bytes(int type, int64_t n) {
@@ -228,8 +232,11 @@ extern "C" hymoe_status hymoe_ffn_noalloc(const hymoe_tensor* gate_up, const hym
                    "hymoe_ffn_noalloc: intermediate size exceeds HYMOE_NOALLOC_MAX_INTERMEDIATE (16384)");
     if (gate_up->nbytes != gguf_bytes(t, H * I2) || down->nbytes != gguf_bytes(t, H * I2 / 2))
         return bad(HYMOE_ERR_INVALID_ARG, "hymoe_ffn_noalloc: nbytes does not match the GGUF size");
-    if (!on_device(gate_up->data) || !on_device(down->data) || !on_device(x) || !on_device(y))
-        return bad(HYMOE_ERR_INVALID_ARG, "hymoe_ffn_noalloc: every pointer must be device memory");
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return bad(HYMOE_ERR_CUDA, "hymoe_ffn_noalloc: cudaGetDevice failed");
+    if (!on_device(gate_up->data, dev) || !on_device(down->data, dev) || !on_device(x, dev) || !on_device(y, dev))
+        return bad(HYMOE_ERR_INVALID_ARG, "hymoe_ffn_noalloc: every pointer must be device memory of the "
+                                          "current device (or managed memory)");
     if (!aligned16(gate_up->data) || !aligned16(down->data) || !aligned16(x) || !aligned16(y))
         return bad(HYMOE_ERR_INVALID_ARG, "hymoe_ffn_noalloc: pointers must be 16-byte aligned");
     float* h = nullptr;

@@ -344,3 +344,18 @@ class MoE:
         flags = (HOST_PTRS if host else 0) | (USE_GRAPH if graph else 0) | (PRE_NORM if pre_norm else 0)
         self._check(self.L.hymoe_forward(self.h, layer, x_ptr, resid_ptr, out_ptr, T, bias_ptr,
                                          C.byref(dbg) if dbg else None, flags))
+
+
+def zipf_router_bias(seed: int, E: int, s: float = 1.1):
+    """Router bias of the skewed expert-parallel workload: expected load follows a Zipf(s) law
+    over a seeded permutation of the experts, p_r ∝ r^-s, bias_e = ln(E * p_rank(e)).  A
+    workload generator (no reference counterpart: the reference has no router bias)."""
+    import numpy as np
+    rng = np.random.Generator(np.random.Philox(seed))
+    perm = rng.permutation(E)
+    r = np.arange(1, E + 1, dtype=np.float64)
+    p = r ** (-s)
+    p /= p.sum()
+    bias = np.empty(E, np.float64)
+    bias[perm] = np.log(E * p)
+    return bias.astype(np.float32)

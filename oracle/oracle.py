@@ -46,15 +46,28 @@ def default_threads() -> int:
     return max(1, len(os.sched_getaffinity(0)))
 
 
+def reference_dir() -> str | None:
+    """The reference checkout the checkers compile: $HYMOE_REFERENCE, else a checkout named
+    `reference` beside this repository; None when neither holds the reference's src/."""
+    env = os.environ.get("HYMOE_REFERENCE")
+    cands = [env] if env else [os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")]
+    for d in cands:
+        if d and os.path.isdir(os.path.join(d, "src")):
+            return d
+    return None
+
+
 def build(ref: bool | None = None) -> None:
     """Compile liboracle.so (and the reference checker when its sources exist)."""
     targets = ["oracle"]
-    refdir = os.environ.get("HYMOE_REFERENCE", "/root/reference")
+    refdir = reference_dir()
     if ref is None:
-        ref = os.path.isdir(os.path.join(refdir, "src"))
+        ref = refdir is not None
+    if ref and refdir is None:
+        raise RuntimeError("the reference checkout was not found: set HYMOE_REFERENCE")
     if ref:
         targets += ["ref", "ref-gpu"]
-    subprocess.run(["make", "-s", "-C", HERE, f"REF={refdir}", *targets], check=True)
+    subprocess.run(["make", "-s", "-C", HERE, *([f"REF={refdir}"] if ref else []), *targets], check=True)
 
 
 class Oracle:

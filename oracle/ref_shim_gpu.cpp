@@ -7,7 +7,9 @@
 //                                 so its MoE call (src/decoder_layer.cpp:38) runs on the GPU
 //                                 through the C++ adapter and libhymoe.so
 // — plus C entry points for tests.  Built into oracle/_ref/libhyref_gpu.so by oracle/Makefile.
+#include <algorithm>
 #include <cstdint>
+#include <cstdio>
 #include <vector>
 
 #include "hunyuan_model.h"
@@ -66,6 +68,49 @@ void* hyref_layer_create(uint32_t H, uint32_t I, uint32_t E, const float* in_ln,
 }
 
 void hyref_layer_destroy(void* w) { delete static_cast<DecoderLayerWeights*>(w); }
+
+// Puts another layer's MoE weights into the same DecoderLayerWeights object.
+// in_place = 0: the reference's per-layer streaming on one object
+//   (src/hunyuan_full_model.cpp:195-207): release_layer clears and shrinks every vector
+//   (:119-130), then the next load fills vectors of the same sizes;
+// in_place = 1: the new values are written over the old ones, so every address stays.
+// Returns 1 when the router's data sits at its previous address afterwards, else 0.
+int hyref_layer_reload_moe(void* wp, uint32_t H, uint32_t I, uint32_t E, const float* router_w,
+                           const float* shared_gu, const float* shared_down,
+                           const float* const* experts_gu, const float* const* experts_down,
+                           int in_place) {
+    MoEWeights& m = static_cast<DecoderLayerWeights*>(wp)->moe;
+    const void* before = m.router_weight.data();
+    const size_t gu = static_cast<size_t>(2) * I * H, dn = static_cast<size_t>(H) * I;
+    if (in_place) {
+        std::copy(router_w, router_w + static_cast<size_t>(E) * H, m.router_weight.begin());
+        std::copy(shared_gu, shared_gu + gu, m.shared_gate_up.begin());
+        std::copy(shared_down, shared_down + dn, m.shared_down.begin());
+        for (uint32_t e = 0; e < E; ++e) {
+            std::copy(experts_gu[e], experts_gu[e] + gu, m.experts[e].gate_up.begin());
+            std::copy(experts_down[e], experts_down[e] + dn, m.experts[e].down.begin());
+        }
+    } else {
+        m.shared_gate_up.clear(); m.shared_gate_up.shrink_to_fit();
+        m.shared_down.clear(); m.shared_down.shrink_to_fit();
+        m.router_weight.clear(); m.router_weight.shrink_to_fit();
+        for (auto& e : m.experts) {
+            e.gate_up.clear(); e.gate_up.shrink_to_fit();
+            e.down.clear(); e.down.shrink_to_fit();
+        }
+        m.experts.clear();
+        fill(m.router_weight, router_w, static_cast<size_t>(E) * H);
+        fill(m.shared_gate_up, shared_gu, gu);
+        fill(m.shared_down, shared_down, dn);
+        m.num_experts = E;
+        m.experts.resize(E);
+        for (uint32_t e = 0; e < E; ++e) {
+            fill(m.experts[e].gate_up, experts_gu[e], gu);
+            fill(m.experts[e].down, experts_down[e], dn);
+        }
+    }
+    return m.router_weight.data() == before ? 1 : 0;
+}
 
 // which = 0: the reference layer as written; 1: the same source with the GPU MoE.
 // Returns 0, or 1 when the GPU path threw (the message goes to stderr).

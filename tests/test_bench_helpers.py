@@ -48,3 +48,13 @@ def test_output_error_above_tolerance_fails():
     noisy = out * np.float32(1.01)
     p = bench.parity_stats({"out": noisy, "idx": idx, "logits": logits}, out, idx, 4)
     assert not p["ok"] and abs(p["rel_l2"] - 0.01) < 1e-4
+
+
+def test_workload_zipf_bias_equals_the_oracle_restatement():
+    """The package's Zipf(1.1) router bias (what bench.py feeds the GPU) is the oracle's
+    zipf_bias (what the parity tests feed the checker)."""
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle"))
+    import hymoe
+    import oracle as O
+    for seed in (0, 5, 104):
+        assert np.array_equal(hymoe.zipf_router_bias(seed, 64), O.zipf_bias(seed, 64))

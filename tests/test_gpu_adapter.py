@@ -31,6 +31,8 @@ def _lib():
     L.hyref_layer_forward.argtypes = [_fp, C.c_void_p, u32, u32, u32, u32, C.c_int, _fp]
     L.hyref_moe_forward.argtypes = [_fp, C.c_void_p, u32, u32, u32, u32, C.c_int, _fp, _fp, _fp,
                                     C.POINTER(C.c_int32)]
+    L.hyref_layer_reload_moe.argtypes = [C.c_void_p, u32, u32, u32, _fp, _fp, _fp, C.POINTER(_fp),
+                                         C.POINTER(_fp), C.c_int]
     return L
 
 
@@ -95,3 +97,67 @@ def test_reference_decoder_layer_with_gpu_moe(orc, layer):
     # only the MoE differs, so the layer agrees to the MoE tolerance.
     assert rel_l2(outs[1], outs[0]) <= REL_L2_TOL
     assert rel_l2(outs[1] - x, outs[0] - x) <= 2 * REL_L2_TOL
+
+
+def _moe_both(L, h, x, H, I, E, K):
+    """moe_forward_cpu (0) and the adapter (1) on the same MoEWeights object."""
+    T = x.shape[0]
+    res = {}
+    for which in (0, 1):
+        out = np.empty((T, H), np.float32)
+        probs = np.empty((T, E), np.float32)
+        w = np.empty((T, K), np.float32)
+        idx = np.empty((T, K), np.int32)
+        rc = L.hyref_moe_forward(_p(x), h, T, H, I, K, which, _p(out), _p(probs), _p(w),
+                                 idx.ctypes.data_as(C.POINTER(C.c_int32)))
+        assert rc == 0
+        res[which] = dict(out=out, probs=probs, w=w, idx=idx)
+    return res
+
+
+@pytest.mark.parametrize("in_place", [0, 1])
+def test_adapter_follows_a_weight_object_refilled_layer_by_layer(orc, layer, in_place):
+    """The reference's layer-streaming loop keeps ONE DecoderLayerWeights object and refills
+    it for every layer (src/hunyuan_full_model.cpp:195-207; release_layer's clear +
+    shrink_to_fit at :119-130), so consecutive layers' weights often sit at the same
+    addresses.  in_place=1 forces that case (new values written over the old ones).  The
+    adapter must run each layer on that layer's weights: after the refill it matches
+    moe_forward_cpu on the new weights, and its output differs from the previous layer's."""
+    L, h, H, I, E, K, seed = (layer[k] for k in ("L", "h", "H", "I", "E", "K", "seed"))
+    x = O.synth_x(orc, seed + 2, 17, H)
+    first = _moe_both(L, h, x, H, I, E, K)
+    assert rel_l2(first[1]["out"], first[0]["out"]) <= REL_L2_TOL
+    keep = O.synth_layer_f32(orc, seed, 1, H, I, E, O.F32)  # decoder layer 1 of the same seed
+    rw, sgu, sdn, egu, edn = keep
+    same_addr = L.hyref_layer_reload_moe(h, H, I, E, _p(rw), _p(sgu), _p(sdn),
+                                         (_fp * E)(*[_p(a) for a in egu]),
+                                         (_fp * E)(*[_p(a) for a in edn]), in_place)
+    if in_place:
+        assert same_addr == 1
+    second = _moe_both(L, h, x, H, I, E, K)
+    logits = orc.router(x, np.ascontiguousarray(rw), K)[0]
+    bad, _ = topk_mismatches(second[1]["idx"], second[0]["idx"], logits, K)
+    assert bad == 0
+    assert rel_l2(second[1]["out"], second[0]["out"]) <= REL_L2_TOL
+    assert rel_l2(second[0]["out"], first[0]["out"]) > 0.1  # the layers really differ
+    # put layer 0 back for the other tests of this module
+    rw0, sgu0, sdn0, egu0, edn0 = layer["keep"][:5]
+    L.hyref_layer_reload_moe(h, H, I, E, _p(rw0), _p(sgu0), _p(sdn0), (_fp * E)(*[_p(a) for a in egu0]),
+                             (_fp * E)(*[_p(a) for a in edn0]), 1)
+
+
+def test_adapter_takes_more_tokens_than_one_context(orc, layer):
+    """moe_forward_cpu accepts any n_tokens; the adapter runs calls above the context's
+    8192-token bound as 8192-token chunks (output and every debug array sliced alike)."""
+    L, h, H, I, E, K, seed = (layer[k] for k in ("L", "h", "H", "I", "E", "K", "seed"))
+    x = O.synth_x(orc, seed + 3, 8192 + 131, H)
+    r = _moe_both(L, h, x, H, I, E, K)
+    logits = orc.router(x, np.ascontiguousarray(layer["keep"][0]), K)[0]
+    bad, _ = topk_mismatches(r[1]["idx"], r[0]["idx"], logits, K)
+    assert bad == 0
+    np.testing.assert_allclose(r[1]["probs"], r[0]["probs"], rtol=2e-6, atol=1e-9)
+    same = (r[1]["idx"] == r[0]["idx"]).all(axis=1)
+    np.testing.assert_allclose(r[1]["w"][same], r[0]["w"][same], rtol=2e-6)
+    assert rel_l2(r[1]["out"], r[0]["out"]) <= REL_L2_TOL
+    tail = slice(8192, None)  # the second chunk on its own
+    assert rel_l2(r[1]["out"][tail], r[0]["out"][tail]) <= REL_L2_TOL
