@@ -59,6 +59,8 @@ __device__ void build_items(const int4* seg, int ns, const ItemsArgs& a, int* pr
             const int ntt = pre[lo + 1] - pre[lo];
             const int rb = local / ntt, tt = local - rb * ntt;
             items[i] = make_int4(sg.x, rb, sg.y + tt * tn, min(tn, sg.z - tt * tn));
+            int2* aux = which ? a.aux_dn : a.aux_gu;
+            if (aux != nullptr) aux[i] = make_int2(sg.w, a.seg_ret[lo] + tt * tn);
         }
     }
 }
@@ -261,6 +263,35 @@ __global__ void ep_segments_kernel(const int* __restrict__ C, int ld, int N, int
     *n_segs = n;
 }
 
+// Fused expert parallel: the receive segments of ep_segments_kernel (rows stay source-major)
+// listed shared first, then this rank's own rows, then sources rank-1, rank-2, ...; each with
+// its source rank (w) and, in seg_ret, the source's expert-sorted position of its first row:
+// sum of the source's counts of every slot before this rank's local expert le.
+__global__ void ep_segments_fused_kernel(const int* __restrict__ C, int ld, int N, int rank, int el,
+                                         int T, int4* __restrict__ segs, int* __restrict__ seg_ret,
+                                         int* __restrict__ n_segs) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    segs[0] = make_int4(el, 0, T, rank);
+    seg_ret[0] = 0;
+    int n = 1;
+    for (int j = 0; j < N; ++j) {
+        const int s = (rank - j + N) % N;
+        int row = T;  // first row of source s: after the rows of sources 0..s-1
+        for (int s2 = 0; s2 < s; ++s2)
+            for (int le = 0; le < el; ++le) row += C[s2 * ld + rank * el + le];
+        int ret = 0;  // source s's pairs of slots before rank * el
+        for (int e = 0; e < rank * el; ++e) ret += C[s * ld + e];
+        for (int le = 0; le < el; ++le) {
+            const int cnt = C[s * ld + rank * el + le];
+            segs[n] = make_int4(le, row, cnt, s);
+            seg_ret[n++] = ret;
+            row += cnt;
+            ret += cnt;
+        }
+    }
+    *n_segs = n;
+}
+
 __global__ void unmap_slots_kernel(int* __restrict__ idx, const int* __restrict__ expert_of_slot, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) idx[i] = __ldg(expert_of_slot + idx[i]);
@@ -303,6 +334,12 @@ cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, co
 cudaError_t launch_shared_prep(const float* x, int T, int H, __half* xp, int group, int n_rb_gu,
                                int n_rb_dn, int4* items_gu, int4* items_dn, int* n_items, cudaStream_t st) {
     shared_prep_kernel<<<1, 256, 0, st>>>(x, T, H, xp, group, n_rb_gu, n_rb_dn, items_gu, items_dn, n_items);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_segments_fused(const int* C, int ld, int N, int rank, int el, int T, int4* segs,
+                                     int* seg_ret, int* n_segs, cudaStream_t st) {
+    ep_segments_fused_kernel<<<1, 32, 0, st>>>(C, ld, N, rank, el, T, segs, seg_ret, n_segs);
     return cudaGetLastError();
 }
 

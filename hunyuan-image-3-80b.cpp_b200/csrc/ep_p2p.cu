@@ -1,28 +1,35 @@
 // ep_p2p.cu — expert-parallel dispatch and combine over NVLink peer memory.
 //
 // Every rank maps the other ranks' activation matrix (xp, fp16), routed-result matrix (yr,
-// fp16) and metadata block (count matrix + flags) into its address space (CUDA IPC).  One call:
+// fp16), return matrix (yret, fp16) and metadata block (count matrix + flags) into its address
+// space (CUDA IPC).  One call, on every rank:
 //
 //   ep_counts_kernel    my per-expert pair counts and my token count -> C[me] of every rank;
 //                       count flag; wait for every rank's count flag (bounded)
-//   ep_scatter_kernel   each token row, converted to fp16 once, goes straight into the
-//                       owner's xp at its final row (P2P stores); the last CTA raises this
-//                       rank's delivery flag on every rank
-//   ep_wait_kernel      wait for every rank's delivery flag (bounded): xp is complete
-//   (local GEMMs over rows [0, T + received))
-//   ep_raise_kernel     raise this rank's "results ready" flag on every rank
-//   ep_combine_kernel   wait for every owner's ready flag (bounded), then the weighted sum
-//                       reads each routed result directly from its owner's yr (P2P loads)
+//   dispatch            each pair's token row (fp16) goes straight into its owner's xp at its
+//                       final receive row (P2P stores), then this rank's delivery flag is
+//                       raised on every rank.  Tensor-core calls: ep_local_kernel writes the
+//                       local rows before the GEMM and the gate_up GEMM's communication warps
+//                       send the rest while it computes; decode-size calls: ep_scatter_kernel
+//   (local GEMMs over rows [0, T + received); the tensor-core producer waits per source for
+//    its delivery flag, the decode path waits for all of them first, ep_wait_kernel)
+//   return              each routed result row goes back into its source's yret at the
+//                       source's expert-sorted position of the pair, then this rank's ready
+//                       flag is raised on every rank: the down GEMM's communication warps
+//                       (tensor core) or ep_push_kernel (decode)
+//   combine             wait for every rank's ready flag (bounded), then the local combine
+//                       over yret (the same kernel and operation order as on one GPU)
 //
-// Receive layout (same as the NCCL path): rows [0, T) the shared expert's local tokens, then
-// the rows of source rank 0, 1, ..., each in (local expert, source token) order.  A source
-// places its pair (t, k) with expert e (owner d = e / el) at
-//   base(d, me) + (sorted position of the pair among my pairs) - goff[d * el]
-//   base(d, me) = T_d + sum_{s < me} sum_{le} C[s][d * el + le]
+// Receive layout: rows [0, T) the shared expert's local tokens, then the rows of source rank
+// 0, 1, ..., each in (local expert, source token) order.  A source places its pair (t, k)
+// with slot e (owner d = e / el) and expert-sorted position p at
+//   base(d, me) + p - goff[d * el],  base(d, me) = T_d + sum_{s < me} sum_{le} C[s][d * el + le]
 // Flags carry the call's epoch (strictly increasing, the same on every rank) and are compared
 // with >=, so they never need resetting.  Ordering between calls needs no extra flags: a rank
-// starts writing a peer's xp (next call) only after its own combine finished reading every
-// owner's yr, which waited for every owner's ready flag, raised after that owner's GEMMs.
+// starts writing a peer's xp (next call) only after its own combine of this call, which waited
+// for every rank's ready flag, raised after that rank's GEMMs read their xp; an owner writes a
+// source's yret in the next call only for rows that source delivered in the next call, i.e.
+// after that source's combine of this call.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -75,7 +82,7 @@ __global__ void ep_counts_kernel(EpPeers peers, int N, int me, int E, int T, con
 }
 
 // Grid (router chunk of 16 tokens, column slice of 256); 128 threads.  slot_pos[t, k]
-// receives the pair's row in its owner's matrices.
+// receives the pair's expert-sorted position (its row in this rank's yret).
 constexpr int kEpCols = 256;
 
 __global__ __launch_bounds__(128) void ep_scatter_kernel(
@@ -108,9 +115,9 @@ __global__ __launch_bounds__(128) void ep_scatter_kernel(
             for (int p = 0; p < tt; ++p)
                 for (int kk = 0; kk < K; ++kk) rank += sidx[p][kk] == e;
             const int d = e / el;
-            const int row = base[d] + chunk_base[c * E + e] + rank - goff[d * el];
-            srow[tt][k] = row;
-            if (blockIdx.y == 0) slot_pos[(t0 + tt) * K + k] = row;
+            const int pos = chunk_base[c * E + e] + rank;  // expert-sorted position of the pair
+            srow[tt][k] = base[d] + pos - goff[d * el];
+            if (blockIdx.y == 0) slot_pos[(t0 + tt) * K + k] = pos;
         }
     }
     __syncthreads();
@@ -146,6 +153,68 @@ __global__ __launch_bounds__(128) void ep_scatter_kernel(
     }
 }
 
+// Fused expert parallel, before the GEMMs.  Grid (router chunk, column slice of 256), 128
+// threads.  slot_pos[t, k] = the pair's expert-sorted position p (the row its result returns
+// to in this rank's yret); every token row goes to rows [0, T) of this rank's xp (the shared
+// expert's rows) and each pair this rank owns to its receive row
+//   T + sum_{s < me} sum_{le} C[s][me * el + le] + p - goff[me * el];
+// pairs owned elsewhere are sent by the gate_up GEMM's communication warps.
+__global__ __launch_bounds__(128) void ep_local_kernel(
+    EpPeers peers, int N, int me, int E, int el, int T, int H, int K, const float* __restrict__ x,
+    const int* __restrict__ topk_idx, const int* __restrict__ chunk_base, const int* __restrict__ goff,
+    int* __restrict__ slot_pos) {
+    __shared__ int sidx[kRouterTok][8];
+    __shared__ int srow[kRouterTok][8];
+    __shared__ int base;
+    const int c = blockIdx.x, t0 = c * kRouterTok, tid = threadIdx.x;
+    const int nt = min(kRouterTok, T - t0);
+    if (tid == 0) {
+        const int* C = peers.meta[me] + kEpCountOff;
+        int b = T;
+        for (int s = 0; s < me; ++s)
+            for (int le = 0; le < el; ++le) b += C[s * (E + 1) + me * el + le];
+        base = b - goff[me * el];
+    }
+    {
+        const int tt = tid >> 3, k = tid & 7;
+        sidx[tt][k] = (tt < nt && k < K) ? topk_idx[(t0 + tt) * K + k] : -1;
+    }
+    __syncthreads();
+    {
+        const int tt = tid >> 3, k = tid & 7;
+        if (tt < nt && k < K) {
+            const int e = sidx[tt][k];
+            int rank = 0;
+            for (int p = 0; p < tt; ++p)
+                for (int kk = 0; kk < K; ++kk) rank += sidx[p][kk] == e;
+            const int pos = chunk_base[c * E + e] + rank;
+            srow[tt][k] = e / el == me ? base + pos : -1;
+            if (blockIdx.y == 0) slot_pos[(t0 + tt) * K + k] = pos;
+        }
+    }
+    __syncthreads();
+    const int j = blockIdx.y * kEpCols + (tid & 31) * 8;
+    if (j >= H) return;
+    __half* xp = peers.xp[me];
+    for (int tt = tid >> 5; tt < nt; tt += 4) {
+        const float* xr = x + static_cast<size_t>(t0 + tt) * H;
+        const float4 a = *reinterpret_cast<const float4*>(xr + j);
+        const float4 b = *reinterpret_cast<const float4*>(xr + j + 4);
+        const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+        const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
+        uint4 v;
+        v.x = *reinterpret_cast<const uint32_t*>(&h0);
+        v.y = *reinterpret_cast<const uint32_t*>(&h1);
+        v.z = *reinterpret_cast<const uint32_t*>(&h2);
+        v.w = *reinterpret_cast<const uint32_t*>(&h3);
+        for (int k = 0; k < K; ++k) {
+            const int row = srow[tt][k];
+            if (row >= 0) *reinterpret_cast<uint4*>(xp + static_cast<size_t>(row) * H + j) = v;
+        }
+        *reinterpret_cast<uint4*>(xp + static_cast<size_t>(t0 + tt) * H + j) = v;
+    }
+}
+
 __global__ void ep_wait_kernel(EpPeers peers, int N, int me, int flag_off, uint32_t epoch, uint64_t budget_ns,
                                int* err) {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
@@ -159,64 +228,33 @@ __global__ void ep_raise_kernel(EpPeers peers, int N, int me, int flag_off, uint
         st_release_sys(reinterpret_cast<uint32_t*>(peers.meta[threadIdx.x]) + flag_off + me, epoch);
 }
 
-// out[t] = resid[t] + (y_shared[t] + sum_k w[t,k] * yr_owner(k)[slot_pos[t,k]]), the owners'
-// fp16 rows read over NVLink (16 bytes per load); the same operation order as combine_kernel.
-// Grid (H / 1024, T), 128 threads x 8 columns.
-__global__ __launch_bounds__(128) void ep_combine_kernel(EpPeers peers, int N, int me, int el,
-                                                         const int* __restrict__ topk_idx,
-                                                         const int* __restrict__ slot_pos,
-                                                         const float* __restrict__ topk_w,
-                                                         const float* __restrict__ y_shared,
-                                                         const float* resid, float* out, int H, int K,
-                                                         uint32_t epoch, uint64_t budget_ns, int* err) {
-    __shared__ int ok;
-    if (threadIdx.x == 0)
-        ok = wait_flags(reinterpret_cast<const uint32_t*>(peers.meta[me]) + kEpFlagReady, N, epoch, budget_ns, err)
-                 ? 1 : 0;
+// Decode-size calls: every received segment's result rows (yr, fp16) into its source's yret
+// at the source's expert-sorted positions (seg_ret), then the last CTA raises this rank's ready
+// flag on every rank.  segs[0] is the shared expert's (local, not returned).
+__global__ __launch_bounds__(256) void ep_push_kernel(EpPeers peers, int N, int me, const int4* __restrict__ segs,
+                                                      const int* __restrict__ seg_ret,
+                                                      const int* __restrict__ n_segs, int H,
+                                                      unsigned int* done_ctas, uint32_t epoch) {
+    __shared__ bool last;
+    const int ns = *n_segs;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (int i = 1; i < ns; ++i) {
+        const int4 sg = segs[i];
+        const uint4* src = reinterpret_cast<const uint4*>(peers.yr[me] + static_cast<size_t>(sg.y) * H);
+        uint4* dst = reinterpret_cast<uint4*>(peers.yret[sg.w] + static_cast<size_t>(seg_ret[i]) * H);
+        const size_t n16 = static_cast<size_t>(sg.z) * H / 8;
+        for (size_t q = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < n16; q += stride)
+            dst[q] = __ldcg(src + q);
+    }
+    __threadfence_system();
     __syncthreads();
-    if (!ok) return;
-    const int t = blockIdx.y;
-    const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
-    if (j >= H) return;
-    uint4 u[8];
-    float w[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        if (k < K) {
-            const int d = __ldg(topk_idx + t * K + k) / el;
-            const int row = __ldg(slot_pos + t * K + k);
-            w[k] = __ldg(topk_w + t * K + k);
-            u[k] = *reinterpret_cast<const uint4*>(peers.yr[d] + static_cast<size_t>(row) * H + j);
-        }
+    if (threadIdx.x == 0) last = atomicAdd(done_ctas, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (last) {
+        __threadfence_system();
+        if (threadIdx.x < N) st_release_sys(reinterpret_cast<uint32_t*>(peers.meta[threadIdx.x]) + kEpFlagReady + me, epoch);
+        if (threadIdx.x == 0) *done_ctas = 0u;
     }
-    const float* sr = y_shared + static_cast<size_t>(t) * H + j;
-    const float4 s0 = *reinterpret_cast<const float4*>(sr), s1 = *reinterpret_cast<const float4*>(sr + 4);
-    const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-    float h[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (resid != nullptr) {
-        const float* hr = resid + static_cast<size_t>(t) * H + j;
-        const float4 h0 = *reinterpret_cast<const float4*>(hr), h1 = *reinterpret_cast<const float4*>(hr + 4);
-        h[0] = h0.x; h[1] = h0.y; h[2] = h0.z; h[3] = h0.w;
-        h[4] = h1.x; h[5] = h1.y; h[6] = h1.z; h[7] = h1.w;
-    }
-    float o[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        float r = 0.f;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            if (k < K) {
-                const uint32_t wd = i < 2 ? u[k].x : i < 4 ? u[k].y : i < 6 ? u[k].z : u[k].w;
-                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wd));
-                r = __fadd_rn(r, __fmul_rn(w[k], (i & 1) ? f.y : f.x));
-            }
-        }
-        o[i] = __fadd_rn(s[i], r);
-        if (resid != nullptr) o[i] = __fadd_rn(h[i], o[i]);
-    }
-    float* orow = out + static_cast<size_t>(t) * H + j;
-    *reinterpret_cast<float4*>(orow) = make_float4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<float4*>(orow + 4) = make_float4(o[4], o[5], o[6], o[7]);
 }
 
 }  // namespace
@@ -238,6 +276,16 @@ cudaError_t launch_ep_scatter(const EpPeers& p, int N, int me, int E, int el, in
     return cudaGetLastError();
 }
 
+cudaError_t launch_ep_local(const EpPeers& p, int N, int me, int E, int el, int T, int H, int K, const float* x,
+                            const int* topk_idx, const int* chunk_base, const int* goff, int* slot_pos,
+                            cudaStream_t st) {
+    (void)N;
+    if (T <= 0) return cudaSuccess;
+    dim3 grid((T + kRouterTok - 1) / kRouterTok, (H + kEpCols - 1) / kEpCols);
+    ep_local_kernel<<<grid, 128, 0, st>>>(p, N, me, E, el, T, H, K, x, topk_idx, chunk_base, goff, slot_pos);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_ep_wait(const EpPeers& p, int N, int me, int flag_off, uint32_t epoch, uint64_t budget_ns,
                            int* err, cudaStream_t st) {
     ep_wait_kernel<<<1, 32, 0, st>>>(p, N, me, flag_off, epoch, budget_ns, err);
@@ -249,13 +297,9 @@ cudaError_t launch_ep_raise(const EpPeers& p, int N, int me, int flag_off, uint3
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_combine(const EpPeers& p, int N, int me, int el, const int* topk_idx, const int* slot_pos,
-                              const float* topk_w, const float* y_shared, const float* resid, float* out, int T,
-                              int H, int K, uint32_t epoch, uint64_t budget_ns, int* err, cudaStream_t st) {
-    if (K > 8) return cudaErrorInvalidValue;
-    dim3 grid((H / 8 + 127) / 128, T);
-    ep_combine_kernel<<<grid, 128, 0, st>>>(p, N, me, el, topk_idx, slot_pos, topk_w, y_shared, resid, out, H, K,
-                                            epoch, budget_ns, err);
+cudaError_t launch_ep_push(const EpPeers& p, int N, int me, const int4* segs, const int* seg_ret, const int* n_segs,
+                           int H, unsigned int* done_ctas, uint32_t epoch, int n_sms, cudaStream_t st) {
+    ep_push_kernel<<<n_sms, 256, 0, st>>>(p, N, me, segs, seg_ret, n_segs, H, done_ctas, epoch);
     return cudaGetLastError();
 }
 

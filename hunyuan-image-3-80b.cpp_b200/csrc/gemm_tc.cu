@@ -29,6 +29,12 @@
 //   warps 6..13 dequantisers, two groups of four on alternate stages: GGUF Q4_0/Q8_0/F16
 //               tile -> fp16 A half in the canonical K-major 128B-swizzled layout, two
 //               (row, GGUF block) entries per thread; then arrive on the leader's a_ready[s]
+//   warps 14..17 (fused expert parallel only, 576 threads) communication, beside the MMA
+//               pipeline: in gate_up they store this rank's token rows owned by other ranks
+//               into the owners' activation matrices (NVLink peer stores), and the producer
+//               loads a remote source's rows only after that source's delivery flag; in down
+//               they copy each finished item's routed result rows back to the source rank
+//               (peer stores into its return matrix), then raise this rank's ready flag.
 // Barriers: full[s] (local), a_ready[s] (leader, 8 warp arrivals: the 4 dequant warps of
 // the stage's group in each CTA),
 // empty[s] / acc_full[b] (both CTAs, from the leader's multicast commits), acc_empty[b]
@@ -63,6 +69,8 @@ namespace hymoe {
 namespace {
 
 constexpr int kThreads = 448;
+constexpr int kEpThreads = 576;    // + four communication warps (fused expert parallel)
+constexpr int kEpSendCols = 1024;  // columns per send work unit: 128 threads x 8 fp16
 constexpr int kABytes = kTileRows * 128;        // 16 KB fp16 A half
 constexpr int kBBytes = kMaxBoxRows * 128;      // 16 KB fp16 B half (largest box)
 constexpr int kAccCols = 256;
@@ -161,9 +169,129 @@ __device__ __forceinline__ void dequant_entry<W_F16>(const uint8_t* raw, uint8_t
 }
 
 
-template <int WT, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs a) {
+// ---- fused expert parallel: communication warps (128 threads, named barrier 2)
+
+// Bounded wait for a system-scope flag to reach `epoch` (another GPU raises it).
+__device__ bool wait_flag_sys(const uint32_t* flag, uint32_t epoch, uint64_t budget_ns, int* err) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (ld_acquire_sys_u32(flag) < epoch) {
+        if ((++spins & 255u) == 0) {
+            if (*(volatile int*)err != 0) return false;
+            if (globaltimer_ns() - t0 > budget_ns) {
+                atomicOr(err, DEVERR_TIMEOUT_PEER);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// gate_up: this rank's pairs owned by other ranks, as fp16 rows of x, into the owners' xp at
+// their receive rows  T_d + sum_{s < me} sum_{le} C[s][d * el + le] + p - goff[d * el]
+// (p = slot_pos, the pair's expert-sorted position).  Work units: (16-token router chunk,
+// 1024-column slice), spread over the grid's CTAs; each thread moves 8 columns of 4 tokens
+// at a time (loads first, then the stores).
+__device__ void ep_send_rows(const EpFuse& f, int ct, int cta, int n_ctas, int* base_s) {
+    const int* C = f.peers.meta[f.me] + kEpCountOff;
+    const int ld = f.E + 1;
+    if (ct < f.N) {
+        int b = C[ct * ld + f.E];  // T of rank ct: its shared rows come first
+        for (int s = 0; s < f.me; ++s)
+            for (int le = 0; le < f.el; ++le) b += C[s * ld + ct * f.el + le];
+        base_s[ct] = b - f.goff[ct * f.el];
+    }
+    named_bar_sync(2, 128);
+    const int n_chunks = (f.T + kRouterTok - 1) / kRouterTok;
+    const int n_sl = (f.H + kEpSendCols - 1) / kEpSendCols;
+    for (int vb = cta; vb < n_chunks * n_sl; vb += n_ctas) {
+        const int c = vb / n_sl, sl = vb - c * n_sl;
+        const int t0 = c * kRouterTok, nt = min(kRouterTok, f.T - t0);
+        const int j = sl * kEpSendCols + ct * 8;
+        if (j >= f.H) continue;
+        for (int tb = 0; tb < nt; tb += 4) {
+            float4 xv[4][2];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (tb + u < nt) {
+                    const float4* xr = reinterpret_cast<const float4*>(f.x + static_cast<size_t>(t0 + tb + u) * f.H + j);
+                    xv[u][0] = xr[0];
+                    xv[u][1] = xr[1];
+                }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (tb + u >= nt) break;
+                const int t = t0 + tb + u;
+                const __half2 h0 = __floats2half2_rn(xv[u][0].x, xv[u][0].y), h1 = __floats2half2_rn(xv[u][0].z, xv[u][0].w);
+                const __half2 h2 = __floats2half2_rn(xv[u][1].x, xv[u][1].y), h3 = __floats2half2_rn(xv[u][1].z, xv[u][1].w);
+                uint4 v;
+                v.x = *reinterpret_cast<const uint32_t*>(&h0);
+                v.y = *reinterpret_cast<const uint32_t*>(&h1);
+                v.z = *reinterpret_cast<const uint32_t*>(&h2);
+                v.w = *reinterpret_cast<const uint32_t*>(&h3);
+                for (int k = 0; k < f.K; ++k) {
+                    const int d = __ldg(f.topk_idx + t * f.K + k) / f.el;
+                    if (d == f.me) continue;
+                    const int row = base_s[d] + __ldg(f.slot_pos + t * f.K + k);
+                    *reinterpret_cast<uint4*>(f.peers.xp[d] + static_cast<size_t>(row) * f.H + j) = v;
+                }
+            }
+        }
+    }
+}
+
+// down: after the epilogue has finished item tc (4 warp arrivals on done_items per item), its
+// routed result rows [row0, row0 + rows) x this CTA's 128 columns go from yr to the source's
+// yret at the source's expert-sorted positions (aux.y + r).  Shared-expert rows stay local.
+__device__ bool ep_push_results(const GemmArgs& a, const EpFuse& f, int ct, int cid, int ncl, int rank,
+                                int n_items, const uint32_t* done_items, int* err) {
+    uint32_t tc = 0;
+    for (int w = cid; w < n_items; w += ncl, ++tc) {
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t spins = 0;
+        while (ld_acquire_cta_u32(done_items) < 4u * (tc + 1)) {
+            if ((++spins & 63u) == 0) {
+                if (*(volatile int*)err != 0) return false;
+                if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+                    atomicOr(err, DEVERR_TIMEOUT_EPILOGUE);
+                    return false;
+                }
+            }
+            __nanosleep(100);
+        }
+        const int4 item = a.items[w];
+        const int rb = 2 * item.y + rank;
+        if (rb >= a.n_rb || item.z < a.shared_rows) continue;
+        const int2 ax = f.aux[w];
+        const __half* src = a.out_r + static_cast<size_t>(item.z) * a.out_ld + rb * kTileRows;
+        __half* dst = f.peers.yret[ax.x] + static_cast<size_t>(ax.y) * a.out_ld + rb * kTileRows;
+        const int n16 = item.w * (kTileRows / 8);
+        for (int i = ct; i < n16; i += 128) {
+            const int r = i >> 4, col = (i & 15) * 8;
+            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * a.out_ld + col));
+            *reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * a.out_ld + col) = v;
+        }
+    }
+    return true;
+}
+
+// Every CTA's communication warps are done: the last CTA raises this rank's flag at
+// flag_off on every rank (after a system-scope fence of every CTA's peer stores).
+__device__ void ep_finish(const EpFuse& f, int ct, int n_ctas, int flag_off, int* last_s) {
+    __threadfence_system();
+    named_bar_sync(2, 128);
+    if (ct == 0) *last_s = atomicAdd(f.done, 1u) == static_cast<unsigned>(n_ctas - 1);
+    named_bar_sync(2, 128);
+    if (*last_s) {
+        __threadfence_system();
+        if (ct < f.N) st_release_sys_u32(reinterpret_cast<uint32_t*>(f.peers.meta[ct]) + flag_off + f.me, f.epoch);
+        if (ct == 0) *f.done = 0u;  // every CTA of this launch has counted
+    }
+}
+
+template <int WT, int STAGES, bool EP>
+__global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs a, const __grid_constant__ EpFuse ep) {
     constexpr int RAW = tile_bytes(WT);
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -179,6 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* mma_done = acc_empty + 2;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+    uint32_t* done_items = tmem_holder + 1;  // epilogue warp arrivals (fused down: 4 per item)
+    int* comm_s = reinterpret_cast<int*>(tmem_holder + 2);  // [kEpMaxRanks + 1] comm scratch
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t rank = cluster_ctarank();
@@ -194,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&acc_empty[b], 8);
         }
         mbar_init(mma_done, 1);
+        if constexpr (EP) *done_items = 0u;
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -214,8 +345,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
+            uint32_t delivered = 0;  // sources whose rows of this call have landed (fused gate_up)
             for (int w = cid; ok && w < n_items; w += ncl) {
                 const int4 item = a.items[w];
+                if constexpr (EP) {
+                    if (a.ep_mode == 1) {
+                        const int src = ep.aux[w].x;
+                        if (src != ep.me && !((delivered >> src) & 1u)) {
+                            const uint32_t* flag = reinterpret_cast<const uint32_t*>(ep.peers.meta[ep.me]) +
+                                                   kEpFlagDeliver + src;
+                            if (!wait_flag_sys(flag, ep.epoch, ep.budget_ns, err)) {
+                                ok = false;
+                                break;
+                            }
+                            fence_proxy_async_global();
+                            delivered |= 1u << src;
+                        }
+                    }
+                }
                 const int rb = 2 * item.y + static_cast<int>(rank);
                 const bool has_tile = rb < a.n_rb;
                 const int n = pair_n(item.w), half = n >> 1;
@@ -346,8 +493,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (t < nj) o[static_cast<size_t>(t) * a.out_ld] = __float2half_rn(silu_mul(gt, up));
                 }
             }
+            if constexpr (EP) {
+                if (a.ep_mode == 2) {  // this item's result rows are written: hand them to the comm warps
+                    __threadfence_block();
+                    __syncwarp();
+                    if (lane == 0) red_release_cta_add(done_items, 1u);
+                }
+            }
         }
-    } else {
+    } else if (!EP || warp < 14) {
         // ------------------------------------------------------------ dequantisers
         // Two groups of four warps take alternate stages, so two stages are converted
         // concurrently; each thread converts entries e and e + 128 of its stage.
@@ -378,6 +532,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive_cluster(mapa_shared(&aready[s], 0));
             }
         }
+    } else {
+        // ------------------------------------------------------------ communication (EP)
+        if constexpr (EP) {
+            const int ct = tid - kThreads;  // 0..127
+            if (a.ep_mode == 1) {
+                ep_send_rows(ep, ct, blockIdx.x, gridDim.x, comm_s);
+                ep_finish(ep, ct, gridDim.x, kEpFlagDeliver, comm_s + kEpMaxRanks);
+            } else if (a.ep_mode == 2) {
+                // every wait inside is bounded, so all 128 threads arrive here; they agree before
+                // the completion barriers (a thread that gave up must not leave the others waiting)
+                const bool pushed = ep_push_results(a, ep, ct, cid, ncl, static_cast<int>(rank), n_items,
+                                                    done_items, err);
+                if (named_bar_and(2, 128, pushed)) ep_finish(ep, ct, gridDim.x, kEpFlagReady, comm_s + kEpMaxRanks);
+            }
+        }
     }
 
     tc_fence_before();
@@ -391,15 +560,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int WT, int STAGES>
 constexpr size_t smem_bytes() {
+    // tiles, barriers, then tmem_holder, done_items and the comm scratch (kEpMaxRanks + 1 ints)
     return 1024 + STAGES * (kABytes + kBBytes + tile_bytes(WT)) +
-           (3 * STAGES + 5) * 8 + 16;
+           (3 * STAGES + 5) * 8 + 8 + 4 * (kEpMaxRanks + 1);
 }
 
-template <int WT, int STAGES>
-cudaError_t launch_typed(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st) {
+template <int WT, int STAGES, bool EP>
+cudaError_t launch_typed(const GemmMaps& maps, const GemmArgs& a, const EpFuse& ep, int n_sms, cudaStream_t st) {
     constexpr size_t smem = smem_bytes<WT, STAGES>();
     static_assert(smem <= 232448, "shared memory budget");
-    auto kern = gemm_tc_kernel<WT, STAGES>;
+    auto kern = gemm_tc_kernel<WT, STAGES, EP>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
@@ -409,16 +579,14 @@ cudaError_t launch_typed(const GemmMaps& maps, const GemmArgs& a, int n_sms, cud
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(EP ? kEpThreads : kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     // Persistent grid: as many pairs as can be resident at once.
-    static int max_clusters[16] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int& mc = max_clusters[WT & 15];
+    static int max_clusters[2][16] = {};
+    int& mc = max_clusters[EP ? 1 : 0][WT & 15];
     if (mc == 0) {
         cfg.gridDim = dim3(2 * (n_sms / 2));
         if (cudaOccupancyMaxActiveClusters(&mc, kern, &cfg) != cudaSuccess || mc <= 0) {
@@ -427,18 +595,29 @@ cudaError_t launch_typed(const GemmMaps& maps, const GemmArgs& a, int n_sms, cud
         }
     }
     cfg.gridDim = dim3(2 * std::min(mc, n_sms / 2));
-    e = cudaLaunchKernelEx(&cfg, kern, maps, a);
+    e = cudaLaunchKernelEx(&cfg, kern, maps, a, ep);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_gemm_tc(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st) {
+cudaError_t launch_gemm_tc(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st,
+                           const EpFuse* ep) {
+    if (a.ep_mode != 0) {
+        if (!ep || ep->N > kEpMaxRanks || ep->K > 8 || ep->aux == nullptr) return cudaErrorInvalidValue;
+        switch (a.wtype) {
+            case W_Q4_0: return launch_typed<W_Q4_0, 6, true>(maps, a, *ep, n_sms, st);
+            case W_Q8_0: return launch_typed<W_Q8_0, 5, true>(maps, a, *ep, n_sms, st);
+            case W_F16: return launch_typed<W_F16, 4, true>(maps, a, *ep, n_sms, st);
+            default: return cudaErrorInvalidValue;
+        }
+    }
+    const EpFuse none{};
     switch (a.wtype) {
-        case W_Q4_0: return launch_typed<W_Q4_0, 6>(maps, a, n_sms, st);
-        case W_Q8_0: return launch_typed<W_Q8_0, 5>(maps, a, n_sms, st);
-        case W_F16: return launch_typed<W_F16, 4>(maps, a, n_sms, st);
+        case W_Q4_0: return launch_typed<W_Q4_0, 6, false>(maps, a, none, n_sms, st);
+        case W_Q8_0: return launch_typed<W_Q8_0, 5, false>(maps, a, none, n_sms, st);
+        case W_F16: return launch_typed<W_F16, 4, false>(maps, a, none, n_sms, st);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -10,15 +10,17 @@
 //   scatter_gather_kernel    stable counting sort of (token, rank) pairs into fp16 rows;
 //                            shared-expert rows go to rows [0, T) of the GEMM input
 //   [expert parallel]        peer memory: counts to every rank, rows stored straight into
-//                            the owners' matrices (ep_p2p.cu); or NCCL: all-gather of counts
-//                            and grouped ncclSend/ncclRecv of the routed rows
+//                            the owners' matrices (ep_p2p.cu; tensor-core calls send them from
+//                            inside the gate_up GEMM, overlapped with its MMAs); or NCCL:
+//                            all-gather of counts and grouped ncclSend/ncclRecv of the rows
 //   items_kernel             GEMM work items from the row segments (expert parallel)
 //   gate_up GEMM             tcgen05 grouped GEMM + SwiGLU epilogue -> h (fp16); decode
 //                            sizes (groups <= 64 rows): weight-streaming kernels, the shared
 //                            expert on a forked stream for 4-8 tokens
 //   down GEMM                -> y (shared expert, fp32) and yr (routed, fp16)
-//   [expert parallel]        peer memory: ready flags, the combine reads owners' yr; or
-//                            NCCL: routed results back to their sources
+//   [expert parallel]        peer memory: results pushed back into each source's return
+//                            matrix (tensor-core calls: from inside the down GEMM, item by
+//                            item), ready flags; or NCCL: routed results back to their sources
 //   combine_kernel           out = residual + shared + sum_k w_k y_k
 //   [D2H out, debug]         (HYMOE_HOST_PTRS only)
 #include <cuda.h>
@@ -186,13 +188,16 @@ struct hymoe_ctx {
     float* bias_dev = nullptr;
     int4* segs = nullptr;
     int* n_segs = nullptr;
+    int* seg_ret = nullptr;     // expert parallel (peer memory): return row of each segment
+    int2 *aux_gu = nullptr, *aux_dn = nullptr;  // ... and per item {source, return row}
     int* gcnt = nullptr;
 
     // expert parallelism
     ncclComm_t comm = nullptr;
     bool comm_broken = false;
     __half* xp_send = nullptr;   // [T*K, H] routed rows in destination order
-    __half* y_ret = nullptr;     // [T*K, H] routed results back from their ranks (fp16)
+    __half* y_ret = nullptr;     // [T*K, H] routed results back from their ranks (fp16), in this
+                                 // rank's expert-sorted pair order (peers write it directly)
     int* C_dev = nullptr;        // [N][E] gathered per-expert counts
     int* C_host = nullptr;       // pinned copy
     cudaEvent_t ev_counts = nullptr;
@@ -453,21 +458,23 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
     HY_CUDA(c, cudaMemset(c->ep_meta, 0, meta_ints * sizeof(int)));
     HY_CUDA(c, dalloc(&c->done_ctas, 1));
     HY_CUDA(c, cudaMemset(c->done_ctas, 0, sizeof(unsigned int)));
+    constexpr int kBufs = 4;     // xp, yr, metadata, y_ret
+    constexpr size_t kRec = 512;  // bytes per rank in the gathered buffer
     struct Rec {
         unsigned char uuid[16];
         uint32_t max_tokens, ok, pad[2];
-        uint64_t off[3];  // offset of each buffer inside the allocation its handle maps
-        cudaIpcMemHandle_t h[3];
+        uint64_t off[kBufs];  // offset of each buffer inside the allocation its handle maps
+        cudaIpcMemHandle_t h[kBufs];
     };
-    static_assert(sizeof(Rec) <= 256, "record");
+    static_assert(sizeof(Rec) <= kRec, "record");
     Rec mine{};
     cudaDeviceProp prop{};
     HY_CUDA(c, cudaGetDeviceProperties(&prop, c->cfg.device));
     memcpy(mine.uuid, &prop.uuid, 16);
     mine.max_tokens = c->cfg.max_tokens;
     mine.ok = 1;
-    const void* bufs[3] = {c->xp, c->yr, c->ep_meta};
-    for (int i = 0; i < 3; ++i) {
+    const void* bufs[kBufs] = {c->xp, c->yr, c->ep_meta, c->y_ret};
+    for (int i = 0; i < kBufs; ++i) {
         uintptr_t base = 0;
         if (!allocation_base(bufs[i], &base) || cudaIpcGetMemHandle(&mine.h[i], reinterpret_cast<void*>(base)) != cudaSuccess) {
             cudaGetLastError();
@@ -477,11 +484,11 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
         mine.off[i] = reinterpret_cast<uintptr_t>(bufs[i]) - base;
     }
     char* dbuf = nullptr;
-    HY_CUDA(c, dalloc(&dbuf, 256 * (N + 1)));
+    HY_CUDA(c, dalloc(&dbuf, kRec * (N + 1)));
     std::vector<Rec> recs(N);
     auto gather = [&]() -> hymoe_status {
         HY_CUDA(c, cudaMemcpy(dbuf, &mine, sizeof(Rec), cudaMemcpyHostToDevice));
-        ncclResult_t r = ncclAllGather(dbuf, dbuf + 256, 256, ncclChar, c->comm, c->stream);
+        ncclResult_t r = ncclAllGather(dbuf, dbuf + kRec, kRec, ncclChar, c->comm, c->stream);
         if (r != ncclSuccess && r != ncclInProgress)
             return c->fail(HYMOE_ERR_NCCL, "ncclAllGather(peer handles): %s", ncclGetErrorString(r));
         hymoe_status s2 = ep_poll(c, "peer handle exchange");
@@ -492,7 +499,7 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
         c->ev_pool.push_back(ev);
         if (s2 != HYMOE_OK) return s2;
         for (int s = 0; s < N; ++s)
-            HY_CUDA(c, cudaMemcpy(&recs[s], dbuf + 256 * (s + 1), sizeof(Rec), cudaMemcpyDeviceToHost));
+            HY_CUDA(c, cudaMemcpy(&recs[s], dbuf + kRec * (s + 1), sizeof(Rec), cudaMemcpyDeviceToHost));
         return HYMOE_OK;
     };
     hymoe_status st = gather();
@@ -519,10 +526,11 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
     P.xp[me] = c->xp;
     P.yr[me] = c->yr;
     P.meta[me] = c->ep_meta;
+    P.yret[me] = c->y_ret;
     for (int s = 0; s < N && all_ok && mine.ok; ++s) {
         if (s == me) continue;
-        void* ptr[3] = {nullptr, nullptr, nullptr};
-        for (int i = 0; i < 3; ++i) {
+        void* ptr[kBufs] = {nullptr, nullptr, nullptr, nullptr};
+        for (int i = 0; i < kBufs; ++i) {
             if (cudaIpcOpenMemHandle(&ptr[i], recs[s].h[i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
                 cudaGetLastError();
                 mine.ok = 0;
@@ -534,6 +542,7 @@ hymoe_status ep_p2p_setup(hymoe_ctx* c) {
         P.xp[s] = reinterpret_cast<__half*>(static_cast<char*>(ptr[0]) + recs[s].off[0]);
         P.yr[s] = reinterpret_cast<__half*>(static_cast<char*>(ptr[1]) + recs[s].off[1]);
         P.meta[s] = reinterpret_cast<int*>(static_cast<char*>(ptr[2]) + recs[s].off[2]);
+        P.yret[s] = reinterpret_cast<__half*>(static_cast<char*>(ptr[3]) + recs[s].off[3]);
     }
     // second round: every rank learns whether every rank mapped every peer
     if (all_ok) {
@@ -642,12 +651,17 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     A(dalloc(&c->gcnt, E));
     A(dalloc(&c->segs, kMaxSegs));
     A(dalloc(&c->n_segs, 1));
+    A(dalloc(&c->seg_ret, kMaxSegs));
     A(dalloc(&c->bias_dev, E));
     A(dalloc(&c->slot_pos, T * K));
     A(dalloc(&c->n_items, 2));
     A(dalloc(&c->err_word, 1));
     A(dalloc(&c->items_gu, c->max_items));
     A(dalloc(&c->items_dn, c->max_items));
+    if (N > 1) {
+        A(dalloc(&c->aux_gu, c->max_items));
+        A(dalloc(&c->aux_dn, c->max_items));
+    }
     A(dalloc(&c->items_sh_gu, n_rb));
     A(dalloc(&c->items_sh_dn, n_rb));
     A(dalloc(&c->n_items_sh, 2));
@@ -756,6 +770,9 @@ void hymoe_destroy(hymoe_ctx* c) {
     cudaFree(c->gcnt);
     cudaFree(c->segs);
     cudaFree(c->n_segs);
+    cudaFree(c->seg_ret);
+    cudaFree(c->aux_gu);
+    cudaFree(c->aux_dn);
     c->clear_graphs();
     c->prof_clear();
     for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
@@ -1212,6 +1229,13 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             ia.items_gu = c->items_gu;
             ia.items_dn = c->items_dn;
             ia.n_items = c->n_items;
+            if (p2p) {  // segments carry their sources and return rows; tensor-core items too
+                ia.seg_ret = c->seg_ret;
+                if (!gv) {
+                    ia.aux_gu = c->aux_gu;
+                    ia.aux_dn = c->aux_dn;
+                }
+            }
             return ia;
         };
         // Decode sizes on one GPU: the shared expert needs no routing, so it streams its weights
@@ -1274,19 +1298,27 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
 
         std::vector<size_t> send_cnt(N, 0), send_off(N, 0), recv_cnt(N, 0), recv_off(N, 0);
         if (p2p) {
-            // Counts to every rank, rows straight into their owners' matrices, then wait until
-            // every rank's rows have landed here (bounded device-side waits).
+            // Counts to every rank (bounded wait for theirs).  Tensor-core calls: this rank's
+            // token rows and the pairs it owns into its own xp now; the pairs other ranks own
+            // leave from inside the gate_up GEMM.  Decode-size calls: every row to its owner now,
+            // then wait until every rank's rows have landed here.  Either way the receive
+            // segments come from the count matrix on the device.
             c->phase_begin();
             HY_CUDA(c, launch_ep_counts(c->peers, N, rank, E, T, c->gcnt, epoch, budget_ns, c->err_word, st));
-            if (T > 0)
-                HY_CUDA(c, launch_ep_scatter(c->peers, N, rank, E, el, T, H, K, dxn, c->topk_idx, c->chunk_base,
-                                             c->goff, c->slot_pos, c->done_ctas, epoch, st));
-            else
-                HY_CUDA(c, launch_ep_raise(c->peers, N, rank, kEpFlagDeliver, epoch, st));
-            HY_CUDA(c, launch_ep_wait(c->peers, N, rank, kEpFlagDeliver, epoch, budget_ns, c->err_word, st));
-            HY_CUDA(c, launch_ep_segments(c->ep_meta + kEpCountOff, E + 1, N, rank, el, E, T, c->segs, c->n_segs,
-                                          st));
-            c->phase_end(HYMOE_PHASE_EP_DISPATCH, 4);
+            if (!gemv) {
+                HY_CUDA(c, launch_ep_local(c->peers, N, rank, E, el, T, H, K, dxn, c->topk_idx, c->chunk_base,
+                                           c->goff, c->slot_pos, st));
+            } else {
+                if (T > 0)
+                    HY_CUDA(c, launch_ep_scatter(c->peers, N, rank, E, el, T, H, K, dxn, c->topk_idx, c->chunk_base,
+                                                 c->goff, c->slot_pos, c->done_ctas, epoch, st));
+                else
+                    HY_CUDA(c, launch_ep_raise(c->peers, N, rank, kEpFlagDeliver, epoch, st));
+                HY_CUDA(c, launch_ep_wait(c->peers, N, rank, kEpFlagDeliver, epoch, budget_ns, c->err_word, st));
+            }
+            HY_CUDA(c, launch_ep_segments_fused(c->ep_meta + kEpCountOff, E + 1, N, rank, el, T, c->segs,
+                                                c->seg_ret, c->n_segs, st));
+            c->phase_end(HYMOE_PHASE_EP_DISPATCH, gemv ? 4 : 3);
             // Received counts stay on the device: size the decode kernel for full 64-row items.
             gemv_rows = kGemvMaxRows;
         } else if (ep) {
@@ -1362,6 +1394,24 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         }
         const size_t rows_in_use = p2p ? c->rows_cap
                                    : ep ? recv_off[N - 1] + recv_cnt[N - 1] : static_cast<size_t>(T) * (K + 1);
+        EpFuse fuse{};
+        if (p2p && !gemv) {
+            fuse.peers = c->peers;
+            fuse.N = N;
+            fuse.me = rank;
+            fuse.el = el;
+            fuse.E = E;
+            fuse.K = K;
+            fuse.T = T;
+            fuse.H = H;
+            fuse.x = dxn;
+            fuse.topk_idx = c->topk_idx;
+            fuse.slot_pos = c->slot_pos;
+            fuse.goff = c->goff;
+            fuse.done = c->done_ctas;
+            fuse.epoch = epoch;
+            fuse.budget_ns = budget_ns;
+        }
         if (gemv) {
             const int max_it = static_cast<int>(std::min<size_t>(
                 c->max_items, static_cast<size_t>(tiles_gu) * ((rows_in_use + kGemvMaxRows - 1) / kGemvMaxRows + kMaxSegs)));
@@ -1374,6 +1424,12 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             HY_CUDA(c, launch_gemv(c->gmaps_h, c->items_dn, c->n_items + 1, max_it, L.d_dn_ptrs, L.wtype,
                                    I / kTileK, 0, mr, c->y, H, c->yr, T, c->err_word, c->n_sms, st));
             c->phase_end(HYMOE_PHASE_DOWN);
+            if (p2p) {  // routed results back into their sources' return matrices, ready flags
+                c->phase_begin();
+                HY_CUDA(c, launch_ep_push(c->peers, N, rank, c->segs, c->seg_ret, c->n_segs, H, c->done_ctas, epoch,
+                                          c->n_sms, st));
+                c->phase_end(HYMOE_PHASE_EP_COMBINE);
+            }
         } else {
             GemmArgs ga{};
             ga.items = c->items_gu;
@@ -1386,8 +1442,10 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             ga.out = c->hbuf;
             ga.out_ld = I;
             ga.err = c->err_word;
+            ga.ep_mode = p2p ? 1 : 0;  // fused: the remote rows leave and arrive during the GEMM
+            fuse.aux = c->aux_gu;
             c->phase_begin();
-            HY_CUDA(c, launch_gemm_tc(c->maps_xp, ga, c->n_sms, st));
+            HY_CUDA(c, launch_gemm_tc(c->maps_xp, ga, c->n_sms, st, p2p ? &fuse : nullptr));
             c->phase_end(HYMOE_PHASE_GATE_UP);
             ga.items = c->items_dn;
             ga.n_items = c->n_items + 1;
@@ -1399,22 +1457,22 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             ga.out_r = c->yr;
             ga.shared_rows = T;
             ga.out_ld = H;
+            ga.ep_mode = p2p ? 2 : 0;  // fused: results go back to their sources item by item
+            fuse.aux = c->aux_dn;
             c->phase_begin();
-            HY_CUDA(c, launch_gemm_tc(c->maps_h, ga, c->n_sms, st));
+            HY_CUDA(c, launch_gemm_tc(c->maps_h, ga, c->n_sms, st, p2p ? &fuse : nullptr));
             c->phase_end(HYMOE_PHASE_DOWN);
         }
 
         const __half* y_routed = c->yr + static_cast<size_t>(T) * H;
         if (p2p) {
-            // Results ready here; the combine reads every routed result from its owner's y.
+            // Every owner has pushed this rank's results into y_ret: wait for their ready flags
+            // (a rank without tokens waits too, so the next call's writes follow every owner's
+            // GEMMs).
             c->phase_begin();
-            HY_CUDA(c, launch_ep_raise(c->peers, N, rank, kEpFlagReady, epoch, st));
-            if (T > 0)
-                HY_CUDA(c, launch_ep_combine(c->peers, N, rank, el, c->topk_idx, c->slot_pos, c->topk_w, c->y, dres,
-                                             dout, T, H, K, epoch, budget_ns, c->err_word, st));
-            else  // no tokens to combine: still wait, so that the next call's writes follow every owner's GEMMs
-                HY_CUDA(c, launch_ep_wait(c->peers, N, rank, kEpFlagReady, epoch, budget_ns, c->err_word, st));
-            c->phase_end(HYMOE_PHASE_EP_COMBINE, 2);
+            HY_CUDA(c, launch_ep_wait(c->peers, N, rank, kEpFlagReady, epoch, budget_ns, c->err_word, st));
+            c->phase_end(HYMOE_PHASE_EP_COMBINE);
+            y_routed = c->y_ret;
         } else if (ep) {
             // Routed results back to the ranks their tokens came from (fp16, H per row).
             c->phase_begin();
@@ -1435,11 +1493,9 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         }
         if (shared_apart) HY_CUDA(c, cudaStreamWaitEvent(st, c->ev_join, 0));  // the shared expert's rows of y
         if (T > 0) {
-            if (!p2p) {
-                c->phase_begin();
-                HY_CUDA(c, launch_combine(c->y, y_routed, c->slot_pos, c->topk_w, dres, dout, T, H, K, st));
-                c->phase_end(HYMOE_PHASE_COMBINE);
-            }
+            c->phase_begin();
+            HY_CUDA(c, launch_combine(c->y, y_routed, c->slot_pos, c->topk_w, dres, dout, T, H, K, st));
+            c->phase_end(HYMOE_PHASE_COMBINE);
             if (dbg) {
                 const cudaMemcpyKind kd = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
                 if (dbg->topk_weights)

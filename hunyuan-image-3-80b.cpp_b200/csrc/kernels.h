@@ -43,8 +43,12 @@ cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, 
 // ---- dispatch.cu
 constexpr int kMaxSegs = 80;  // >= E + 1 (E <= 64)
 struct ItemsArgs {
-    const int4* segs;         // {weight group, first row, rows, -}
+    const int4* segs;         // {weight group, first row, rows, source rank (expert parallel)}
     const int* n_segs;
+    const int* seg_ret;       // fused expert parallel: the source's return row of each
+                              // segment's first row (nullptr otherwise)
+    int2* aux_gu;             // fused expert parallel: per item {source rank, first return row}
+    int2* aux_dn;
     int n_rb_gu, n_rb_dn;     // row blocks per item for gate_up / down
     int tile_n;               // token rows per tensor-core item
     int gemv;                 // 1: items of at most kGemvMaxRows rows for the GEMV path
@@ -85,6 +89,11 @@ cudaError_t launch_shared_prep(const float* x, int T, int H, __half* xp, int gro
 // C: [N][ld] per-expert counts of every source rank (ld >= E).
 cudaError_t launch_ep_segments(const int* C, int ld, int N, int rank, int el, int E, int T, int4* segs,
                                int* n_segs, cudaStream_t st);
+// Fused expert parallel: the same receive segments listed local source first, then sources
+// rank-1, rank-2, ... (rows stay where they are); seg_ret[i] = the source's position of the
+// segment's first row among that source's expert-sorted pairs.
+cudaError_t launch_ep_segments_fused(const int* C, int ld, int N, int rank, int el, int T, int4* segs,
+                                     int* seg_ret, int* n_segs, cudaStream_t st);
 
 // ---- ep_p2p.cu (expert-parallel dispatch / combine over NVLink peer memory)
 constexpr int kEpMaxRanks = 8;
@@ -96,18 +105,50 @@ struct EpPeers {  // every rank's buffers as mapped in this process (own entry: 
     __half* xp[kEpMaxRanks];   // activation matrices
     __half* yr[kEpMaxRanks];   // routed-result matrices (fp16, same rows as xp)
     int* meta[kEpMaxRanks];
+    __half* yret[kEpMaxRanks]; // results returned to each source, in its expert-sorted pair order
 };
 cudaError_t launch_ep_counts(const EpPeers& p, int N, int me, int E, int T, const int* gcnt, uint32_t epoch,
                              uint64_t budget_ns, int* err, cudaStream_t st);
+// Decode-size calls: every pair's row (fp16) into its owner's xp and the token rows into rows
+// [0, T) of this rank's xp; slot_pos = expert-sorted positions; then this rank's delivery flag.
 cudaError_t launch_ep_scatter(const EpPeers& p, int N, int me, int E, int el, int T, int H, int K, const float* x,
                               const int* topk_idx, const int* chunk_base, const int* goff, int* slot_pos,
                               unsigned int* done_ctas, uint32_t epoch, cudaStream_t st);
 cudaError_t launch_ep_wait(const EpPeers& p, int N, int me, int flag_off, uint32_t epoch, uint64_t budget_ns,
                            int* err, cudaStream_t st);
 cudaError_t launch_ep_raise(const EpPeers& p, int N, int me, int flag_off, uint32_t epoch, cudaStream_t st);
-cudaError_t launch_ep_combine(const EpPeers& p, int N, int me, int el, const int* topk_idx, const int* slot_pos,
-                              const float* topk_w, const float* y_shared, const float* resid, float* out, int T,
-                              int H, int K, uint32_t epoch, uint64_t budget_ns, int* err, cudaStream_t st);
+// Decode-size calls: the received segments' result rows back into their sources' yret (at
+// seg_ret), then this rank's ready flag on every rank.
+cudaError_t launch_ep_push(const EpPeers& p, int N, int me, const int4* segs, const int* seg_ret, const int* n_segs,
+                           int H, unsigned int* done_ctas, uint32_t epoch, int n_sms, cudaStream_t st);
+// Fused expert parallel, before the GEMMs: slot_pos[t, k] = the pair's expert-sorted position
+// (chunk_base + rank in chunk); every token row (fp16) into rows [0, T) of this rank's xp, and
+// the pairs this rank owns into their rows of its xp.  The other pairs leave inside the gate_up
+// GEMM (EpFuse).
+cudaError_t launch_ep_local(const EpPeers& p, int N, int me, int E, int el, int T, int H, int K, const float* x,
+                            const int* topk_idx, const int* chunk_base, const int* goff, int* slot_pos,
+                            cudaStream_t st);
+
+// What the grouped GEMM's communication warps need in fused expert-parallel mode.
+//   gate_up (mode 1): they store this rank's pairs owned elsewhere (fp16 rows of x) into the
+//     owners' xp at their receive rows, then the last CTA raises this rank's delivery flag on
+//     every rank; the producer loads an item's token rows from a source only after that
+//     source's delivery flag of this call (bounded wait).
+//   down (mode 2): after each item's epilogue they copy its routed result rows (this CTA's
+//     128 columns) into the source rank's yret at the source's expert-sorted positions; the
+//     last CTA then raises this rank's ready flag on every rank.
+struct EpFuse {
+    EpPeers peers;
+    const int2* aux;         // per item {source rank, first return row}
+    int N, me, el, E, K, T, H;
+    const float* x;          // [T, H] fp32 token rows (after the pre-norm when there is one)
+    const int* topk_idx;     // [T, K] placement slots
+    const int* slot_pos;     // [T, K] expert-sorted positions
+    const int* goff;         // [E + 1] expert-sorted offsets of this rank's pairs
+    unsigned int* done;      // CTA completion counter (reset to 0 by the last CTA)
+    uint32_t epoch;
+    uint64_t budget_ns;
+};
 
 // ---- gemm_tc.cu (tcgen05 grouped GEMM, 2-SM pairs)
 constexpr int kNumBoxes = 3;
@@ -129,8 +170,11 @@ struct GemmArgs {
     int shared_rows;
     int out_ld;
     int* err;
+    int ep_mode;                   // 0: none; 1: gate_up with the token-row sends; 2: down with
+                                   // the result pushes (fused expert parallel, `ep`)
 };
-cudaError_t launch_gemm_tc(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st);
+cudaError_t launch_gemm_tc(const GemmMaps& maps, const GemmArgs& a, int n_sms, cudaStream_t st,
+                           const EpFuse* ep = nullptr);
 
 // ---- gemv.cu (decode path: weight streaming, mma.sync)
 constexpr int kGemvBoxes = 4;

@@ -56,3 +56,34 @@ def recv_segments(C: np.ndarray, Ts, d: int, el: int):
 def rows_cap(max_tokens: int, N: int, K: int, el: int) -> int:
     """Receive capacity the library allocates: T + N*T*min(K, el) rows (N = 1: T + T*K)."""
     return max_tokens + (max_tokens * K if N == 1 else N * max_tokens * min(K, el))
+
+
+def fused_segments(C: np.ndarray, Ts, d: int, el: int):
+    """Owner d's segments as the fused expert-parallel path lists them (csrc/dispatch.cu
+    ep_segments_fused_kernel): shared first, then sources d, d-1, d-2, ... (rows stay
+    source-major); each (group, first row, rows, source, return row), where the return row is
+    the source's expert-sorted position of the segment's first row."""
+    N = C.shape[0]
+    segs = [(el, 0, Ts[d], d, 0)]
+    for j in range(N):
+        s = (d - j) % N
+        row = Ts[d] + sum(int(C[s2, d * el:(d + 1) * el].sum()) for s2 in range(s))
+        ret = int(C[s, :d * el].sum())
+        for le in range(el):
+            cnt = int(C[s, d * el + le])
+            segs.append((le, row, cnt, s, ret))
+            row += cnt
+            ret += cnt
+    return segs
+
+
+def build_items(segs, n_rb: int, tile_n: int = 256):
+    """Work items of the tensor-core path (csrc/dispatch.cu build_items): segment-major, then
+    row block, then token tile; each (group, row block, first row, rows, source, return row)."""
+    items = []
+    for g, r0, n, src, ret in segs:
+        ntt = (n + tile_n - 1) // tile_n if n > 0 else 0
+        for rb in range(n_rb):
+            for tt in range(ntt):
+                items.append((g, rb, r0 + tt * tile_n, min(tile_n, n - tt * tile_n), src, ret + tt * tile_n))
+    return items

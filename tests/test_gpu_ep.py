@@ -1,7 +1,9 @@
 """Expert-parallel GPU tests (2+ GPUs): one child process per GPU; rank r owns experts
 [r*E/N, (r+1)*E/N) and receives the rows routed to them.  Both transports run: peer memory
-(rows written straight into the owners' matrices, results read from them by the combine)
-and the NCCL send/recv exchange (HYMOE_EP_TRANSPORT=nccl).
+(rows written straight into the owners' matrices and results pushed back into the sources'
+return matrices — from inside the GEMMs on the tensor-core path, by separate kernels on the
+decode path, the two mixing freely between ranks) and the NCCL send/recv exchange
+(HYMOE_EP_TRANSPORT=nccl).
 
 Every output row's arithmetic is independent of how rows are tiled, so when both runs use
 the tensor-core path the expert-parallel output must be bit-identical to the single-GPU
@@ -105,7 +107,10 @@ def _run_ep(world, tokens_per_rank, transport="p2p", place=None, pre_norm=False)
 @pytest.mark.parametrize("transport", ["p2p", "nccl"])
 @pytest.mark.parametrize("tokens,placed", [([[200, 3], [150, 0]], False), ([[64], [5]], False),
                                            ([[300], [300]], False), ([[200, 3], [150, 0]], True),
-                                           ([[300], [300]], True)])
+                                           ([[300], [300]], True),
+                                           # one rank on the tensor-core path, the other on the
+                                           # decode path in the same call, three calls in a row
+                                           ([[200, 40, 300], [5, 300, 70]], False)])
 def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens, placed, transport):
     """placed: experts on ranks by hymoe_balance_placement (not the contiguous split)."""
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
