@@ -310,6 +310,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     if world > 1:
         torch.distributed.barrier()
     e2e_ms = 0.0
+    m.profile(True)  # copy phases: each host<->device copy bracketed by events on its stream
     for s in range(args.steps):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -317,7 +318,16 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         b.record(stream)
         b.synchronize()
         e2e_ms += a.elapsed_time(b)
+    m.profile(False)
+    pe = m.profile_read()
+    mine_e2e = {"rank": rank, "e2e_ms": round(e2e_ms / args.steps, 4),
+                "copy_in_ms": round(pe["copy_in"][0] / args.steps, 4),
+                "copy_out_ms": round(pe["copy_out"][0] / args.steps, 4),
+                "copies_per_step": (pe["copy_in"][1] + pe["copy_out"][1]) // args.steps}
+    e2e_ranks = [mine_e2e]
     if world > 1:
+        e2e_ranks = [None] * world
+        torch.distributed.all_gather_object(e2e_ranks, mine_e2e)
         e2e_ms = _max_over_ranks(torch, dev, e2e_ms)[0]
     e2e_value = world * T * args.steps / (e2e_ms / 1e3)
 
@@ -358,7 +368,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         "roofline": roofline,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": xh.numel() * 4 + bh.numel() * 4,
-                "d2h_bytes_per_step": oh.numel() * 4, "ms_per_step": round(e2e_ms / args.steps, 4)},
+                "d2h_bytes_per_step": oh.numel() * 4, "ms_per_step": round(e2e_ms / args.steps, 4),
+                "note": "host-pointer calls run in token chunks whose copies overlap the compute; "
+                        "copy_in/copy_out are the copies' summed device time per step on each rank",
+                "ranks": e2e_ranks},
         "gpu_launches": launches,
         "clocks": clk,
         "expert_load": {"max": int(counts.max()), "min": int(counts.min()),

@@ -89,6 +89,13 @@ __device__ __forceinline__ bool named_bar_and(int id, int n, bool p) {
     return r != 0;
 }
 
+// Item of round j for SM pair cid of ncl: rounds deal consecutive runs of ncl items, in
+// alternating direction ("snake"), so with a size-ordered list every pair's total work stays
+// close to the mean.  Every role of a pair walks the same sequence.
+__device__ __forceinline__ int gemm_item(int j, int cid, int ncl) {
+    return j * ncl + ((j & 1) ? ncl - 1 - cid : cid);
+}
+
 // Pair tile width: the item's token count rounded up to the MMA's granularity (16).
 __device__ __forceinline__ int pair_n(int rows) {
     const int n = (rows + 15) & ~15;
@@ -246,7 +253,7 @@ __device__ void ep_send_rows(const EpFuse& f, int ct, int cta, int n_ctas, int* 
 __device__ bool ep_push_results(const GemmArgs& a, const EpFuse& f, int ct, int cid, int ncl, int rank,
                                 int n_items, const uint32_t* done_items, int* err) {
     uint32_t tc = 0;
-    for (int w = cid; w < n_items; w += ncl, ++tc) {
+    for (int w; (w = gemm_item(static_cast<int>(tc), cid, ncl)) < n_items; ++tc) {
         const uint64_t t0 = globaltimer_ns();
         uint32_t spins = 0;
         while (ld_acquire_cta_u32(done_items) < 4u * (tc + 1)) {
@@ -346,7 +353,7 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
             uint32_t it = 0;
             bool ok = true;
             uint32_t delivered = 0;  // sources whose rows of this call have landed (fused gate_up)
-            for (int w = cid; ok && w < n_items; w += ncl) {
+            for (int j = 0, w; ok && (w = gemm_item(j, cid, ncl)) < n_items; ++j) {
                 const int4 item = a.items[w];
                 if constexpr (EP) {
                     if (a.ep_mode == 1) {
@@ -394,7 +401,7 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
         if (leader && lane == 0) {
             uint32_t it = 0, tc = 0;
             bool ok = true;
-            for (int w = cid; ok && w < n_items; w += ncl, ++tc) {
+            for (int w; ok && (w = gemm_item(static_cast<int>(tc), cid, ncl)) < n_items; ++tc) {
                 const int4 item = a.items[w];
                 const uint32_t idesc = idesc_f16_f32(2 * kTileRows, pair_n(item.w));
                 const uint32_t ab = tc & 1, aph = (tc >> 1) & 1;
@@ -435,7 +442,7 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
         const uint32_t acc_empty_leader0 = mapa_shared(&acc_empty[0], 0);
         const uint32_t acc_empty_leader1 = mapa_shared(&acc_empty[1], 0);
         uint32_t tc = 0;
-        for (int w = cid; w < n_items; w += ncl, ++tc) {
+        for (int w; (w = gemm_item(static_cast<int>(tc), cid, ncl)) < n_items; ++tc) {
             const int4 item = a.items[w];
             const int rb = 2 * item.y + static_cast<int>(rank);
             const bool has_tile = rb < a.n_rb;
@@ -510,7 +517,7 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
         const int e = dq & 127;
         uint32_t it = 0;
         bool ok = true;
-        for (int w = cid; ok && w < n_items; w += ncl) {
+        for (int j = 0, w; ok && (w = gemm_item(j, cid, ncl)) < n_items; ++j) {
             const int4 item = a.items[w];
             const bool has_tile = 2 * item.y + static_cast<int>(rank) < a.n_rb;
             for (int ks = 0; ks < a.n_ks; ++ks, ++it) {

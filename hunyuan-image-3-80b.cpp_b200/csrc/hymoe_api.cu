@@ -190,6 +190,8 @@ struct hymoe_ctx {
     int* n_segs = nullptr;
     int* seg_ret = nullptr;     // expert parallel (peer memory): return row of each segment
     int2 *aux_gu = nullptr, *aux_dn = nullptr;  // ... and per item {source, return row}
+    float* dbg_w = nullptr;     // pipelined expert-parallel host calls: debug top-K weights
+    int* dbg_idx = nullptr;     // and indices of every chunk (allocated on first use)
     int* gcnt = nullptr;
 
     // expert parallelism
@@ -248,6 +250,25 @@ struct hymoe_ctx {
         prof_ev[phase].emplace_back(prof_open, e);
         prof_launches[phase] += launches;
         prof_open = nullptr;
+    }
+    // An asynchronous copy on `s`, bracketed by profile events (phase COPY_IN / COPY_OUT) while
+    // profiling is on.
+    cudaError_t timed_copy(int phase, void* dst, const void* src, size_t bytes, cudaMemcpyKind kind,
+                           cudaStream_t s) {
+        if (bytes == 0) return cudaSuccess;
+        cudaEvent_t a = nullptr;
+        if (prof) {
+            a = take_event();
+            cudaEventRecord(a, s);
+        }
+        const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, kind, s);
+        if (prof) {
+            cudaEvent_t b = take_event();
+            cudaEventRecord(b, s);
+            prof_ev[phase].emplace_back(a, b);
+            prof_launches[phase] += 1;
+        }
+        return e;
     }
     void prof_clear() {
         for (auto& v : prof_ev) {
@@ -773,6 +794,8 @@ void hymoe_destroy(hymoe_ctx* c) {
     cudaFree(c->seg_ret);
     cudaFree(c->aux_gu);
     cudaFree(c->aux_dn);
+    cudaFree(c->dbg_w);
+    cudaFree(c->dbg_idx);
     c->clear_graphs();
     c->prof_clear();
     for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
@@ -1115,20 +1138,31 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     cudaStream_t st = c->stream;
     const size_t xbytes = static_cast<size_t>(T) * H * sizeof(float);
 
-    // Host buffers, one GPU, no debug outputs, at least 2048 tokens: the call runs in token
-    // chunks so that the copies overlap the compute — every upload is queued at once on one
-    // copy stream, each chunk computes when its upload has landed, and its download (second
-    // copy stream) starts when it is done.  Every token's result is independent of the
-    // others', so the output is the same as one call's.
-    if (host && !ep && !dbg && T >= kChunkMinTokens && !(flags & HYMOE_USE_GRAPH)) {
-        // ~2048-token chunks: smaller ones lose more GEMM efficiency than the overlap gains
-        const int n_ch = std::min(4, T / kChunkMinTokens);
+    // Host-pointer calls in token chunks, so that the copies overlap the compute: every upload
+    // is queued at once on one copy stream, each chunk computes when its upload has landed, and
+    // its download (second copy stream) starts when it is done.  Every token's result is
+    // independent of the others', so the output is the same as one call's.
+    //   One GPU: calls of >= 2048 tokens without debug outputs, ~2048-token chunks (smaller ones
+    //   lose more GEMM efficiency than the overlap gains).
+    //   Expert parallel: every rank must run the same number of exchanges, so the chunk count
+    //   comes from the job-wide max_tokens (>= 4096: max_tokens / 2048 chunks, at most 4), each
+    //   rank splitting its own tokens (a chunk may have none); debug outputs go through device
+    //   scratch.
+    const int max_tok = static_cast<int>(c->cfg.max_tokens);
+    const bool chunk_one = host && !ep && !dbg && T >= kChunkMinTokens && !(flags & HYMOE_USE_GRAPH);
+    const bool chunk_ep = host && ep && max_tok >= 2 * kChunkMinTokens && !(flags & HYMOE_USE_GRAPH);
+    if (chunk_one || chunk_ep) {
+        const int n_ch = chunk_ep ? std::min(4, max_tok / kChunkMinTokens) : std::min(4, T / kChunkMinTokens);
         const int per = (T + n_ch - 1) / n_ch;
         cudaStream_t up = c->copy_stream, down = c->down_stream;
         const float* dbias = nullptr;
         if (router_bias) {
             HY_CUDA(c, cudaMemcpyAsync(c->bias_dev, router_bias, sizeof(float) * E, cudaMemcpyHostToDevice, st));
             dbias = c->bias_dev;
+        }
+        if (dbg && (dbg->topk_weights || dbg->topk_indices) && !c->dbg_w) {
+            HY_CUDA(c, dalloc(&c->dbg_w, static_cast<size_t>(max_tok) * K));
+            HY_CUDA(c, dalloc(&c->dbg_idx, static_cast<size_t>(max_tok) * K));
         }
         // both copy streams follow earlier work on the compute stream (they rewrite x_dev / out_dev)
         std::vector<cudaEvent_t> evs;
@@ -1142,28 +1176,46 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         HY_CUDA(c, cudaStreamWaitEvent(down, ev0, 0));
         std::vector<cudaEvent_t> in(n_ch, nullptr);
         for (int ch = 0; ch < n_ch; ++ch) {
-            const int t0 = ch * per, n = std::min(per, T - t0);
-            if (n <= 0) break;
+            const int t0 = std::min(T, ch * per), n = std::min(per, T - t0);
             const size_t off = static_cast<size_t>(t0) * H, bytes = static_cast<size_t>(n) * H * sizeof(float);
-            HY_CUDA(c, cudaMemcpyAsync(c->x_dev + off, x + off, bytes, cudaMemcpyHostToDevice, up));
+            HY_CUDA(c, c->timed_copy(HYMOE_PHASE_COPY_IN, c->x_dev + off, x + off, bytes, cudaMemcpyHostToDevice, up));
             if (residual && residual != x)
-                HY_CUDA(c, cudaMemcpyAsync(c->resid_dev + off, residual + off, bytes, cudaMemcpyHostToDevice, up));
+                HY_CUDA(c, c->timed_copy(HYMOE_PHASE_COPY_IN, c->resid_dev + off, residual + off, bytes,
+                                         cudaMemcpyHostToDevice, up));
             in[ch] = ev();
             HY_CUDA(c, cudaEventRecord(in[ch], up));
         }
         hymoe_status result = HYMOE_OK;
         for (int ch = 0; ch < n_ch && result == HYMOE_OK; ++ch) {
-            const int t0 = ch * per, n = std::min(per, T - t0);
-            if (n <= 0) break;
+            const int t0 = std::min(T, ch * per), n = std::min(per, T - t0);
             const size_t off = static_cast<size_t>(t0) * H, bytes = static_cast<size_t>(n) * H * sizeof(float);
             HY_CUDA(c, cudaStreamWaitEvent(st, in[ch], 0));
             const float* r = !residual ? nullptr : residual == x ? c->x_dev + off : c->resid_dev + off;
-            result = hymoe_forward(c, layer, c->x_dev + off, r, c->out_dev + off,
-                                   static_cast<uint32_t>(n), dbias, nullptr, flags & ~HYMOE_HOST_PTRS);
+            hymoe_debug d2{};
+            if (dbg) {
+                d2.router_logits = dbg->router_logits ? c->logits + static_cast<size_t>(t0) * E : nullptr;
+                d2.router_probs = dbg->router_probs ? c->probs + static_cast<size_t>(t0) * E : nullptr;
+                d2.topk_weights = dbg->topk_weights ? c->dbg_w + static_cast<size_t>(t0) * K : nullptr;
+                d2.topk_indices = dbg->topk_indices ? c->dbg_idx + static_cast<size_t>(t0) * K : nullptr;
+            }
+            result = hymoe_forward(c, layer, c->x_dev + off, r, c->out_dev + off, static_cast<uint32_t>(n), dbias,
+                                   dbg ? &d2 : nullptr, flags & ~HYMOE_HOST_PTRS);
             cudaEvent_t done = ev();
             HY_CUDA(c, cudaEventRecord(done, st));
             HY_CUDA(c, cudaStreamWaitEvent(down, done, 0));
-            HY_CUDA(c, cudaMemcpyAsync(out + off, c->out_dev + off, bytes, cudaMemcpyDeviceToHost, down));
+            HY_CUDA(c, c->timed_copy(HYMOE_PHASE_COPY_OUT, out + off, c->out_dev + off, bytes, cudaMemcpyDeviceToHost,
+                                     down));
+        }
+        if (dbg && result == HYMOE_OK && T > 0) {
+            const size_t te = static_cast<size_t>(T) * E, tk = static_cast<size_t>(T) * K;
+            if (dbg->router_logits)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->router_logits, c->logits, te * sizeof(float), cudaMemcpyDeviceToHost, down));
+            if (dbg->router_probs)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->router_probs, c->probs, te * sizeof(float), cudaMemcpyDeviceToHost, down));
+            if (dbg->topk_weights)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->topk_weights, c->dbg_w, tk * sizeof(float), cudaMemcpyDeviceToHost, down));
+            if (dbg->topk_indices)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->topk_indices, c->dbg_idx, tk * sizeof(int), cudaMemcpyDeviceToHost, down));
         }
         cudaEvent_t fin = ev();
         HY_CUDA(c, cudaEventRecord(fin, down));
@@ -1180,12 +1232,12 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     float* dlog = dbg ? dbg->router_logits : nullptr;
     float* dprob = dbg ? dbg->router_probs : nullptr;
     if (host) {
-        if (T > 0) HY_CUDA(c, cudaMemcpyAsync(c->x_dev, x, xbytes, cudaMemcpyHostToDevice, st));
+        if (T > 0) HY_CUDA(c, c->timed_copy(HYMOE_PHASE_COPY_IN, c->x_dev, x, xbytes, cudaMemcpyHostToDevice, st));
         dx = c->x_dev;
         if (residual && residual == x) {
             dres = c->x_dev;  // decoder_layer form out = h + moe(...): one upload
         } else if (residual && T > 0) {
-            HY_CUDA(c, cudaMemcpyAsync(c->resid_dev, residual, xbytes, cudaMemcpyHostToDevice, st));
+            HY_CUDA(c, c->timed_copy(HYMOE_PHASE_COPY_IN, c->resid_dev, residual, xbytes, cudaMemcpyHostToDevice, st));
             dres = c->resid_dev;
         }
         dout = c->out_dev;
@@ -1543,7 +1595,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         HY_CUDA(c, cudaGraphLaunch(hit->second, st));
     }
     if (host) {
-        if (T > 0) HY_CUDA(c, cudaMemcpyAsync(out, dout, xbytes, cudaMemcpyDeviceToHost, st));
+        if (T > 0) HY_CUDA(c, c->timed_copy(HYMOE_PHASE_COPY_OUT, out, dout, xbytes, cudaMemcpyDeviceToHost, st));
         return hymoe_synchronize(c);
     }
     return HYMOE_OK;

@@ -34,7 +34,7 @@ EXPORTS = ["hymoe_version", "hymoe_nccl_unique_id", "hymoe_create", "hymoe_destr
            "hymoe_set_norm", "hymoe_set_routing"]
 
 PHASES = ["router", "plan", "dispatch", "gate_up", "down", "combine", "ep_dispatch",
-          "ep_combine"]
+          "ep_combine", "copy_in", "copy_out"]
 
 
 class Config(C.Structure):

@@ -217,7 +217,12 @@ hymoe_status hymoe_balance_placement(uint32_t n_experts, uint32_t ep_size, const
  * softmax (no reference counterpart; 0 reproduces the reference).  In expert-parallel
  * mode every rank calls this with its own tokens (n_tokens may differ per rank).
  * With HYMOE_HOST_PTRS the call copies in, computes and copies out before returning;
- * otherwise it is asynchronous on the context's stream. */
+ * otherwise it is asynchronous on the context's stream.  Host-pointer calls run as token
+ * chunks whose copies overlap the compute: on one GPU calls of >= 2048 tokens without debug
+ * outputs (up to 4 chunks of >= 2048 tokens); with expert parallelism every host-pointer call
+ * of a context whose max_tokens is >= 4096 (max_tokens / 2048 chunks, at most 4, each rank
+ * splitting its own tokens; every rank must pass HYMOE_HOST_PTRS on the same calls).  The
+ * results equal one call's: every token's output is independent of the others'. */
 hymoe_status hymoe_forward(hymoe_ctx* ctx, uint32_t layer, const float* x,
                            const float* residual, float* out, uint32_t n_tokens,
                            const float* router_bias, hymoe_debug* dbg, int flags);
@@ -232,16 +237,20 @@ enum {
     HYMOE_PHASE_GATE_UP = 3,  /* grouped gate_up GEMM + SwiGLU               */
     HYMOE_PHASE_DOWN = 4,     /* grouped down GEMM                           */
     HYMOE_PHASE_COMBINE = 5,  /* weighted combine + residual                 */
-    HYMOE_PHASE_EP_DISPATCH = 6, /* expert-parallel token exchange (NCCL)    */
-    HYMOE_PHASE_EP_COMBINE = 7,  /* expert-parallel result exchange (NCCL)   */
-    HYMOE_NUM_PHASES = 8
+    HYMOE_PHASE_EP_DISPATCH = 6, /* expert-parallel token exchange           */
+    HYMOE_PHASE_EP_COMBINE = 7,  /* expert-parallel result exchange          */
+    HYMOE_PHASE_COPY_IN = 8,     /* HYMOE_HOST_PTRS: host -> device copies (summed over the
+                                    copies; on pipelined calls they overlap the compute)  */
+    HYMOE_PHASE_COPY_OUT = 9,    /* HYMOE_HOST_PTRS: device -> host copies                */
+    HYMOE_NUM_PHASES = 10
 };
 
 /* enable != 0 clears the accumulators and starts recording; 0 stops. */
 hymoe_status hymoe_profile(hymoe_ctx* ctx, int enable);
 
 /* Waits for the context's stream, then writes for each of the first n phases the total
- * device milliseconds and the number of kernel launches recorded since recording began. */
+ * device milliseconds and the number of kernel launches (copies, for the copy phases)
+ * recorded since recording began. */
 hymoe_status hymoe_profile_read(hymoe_ctx* ctx, float* total_ms, int32_t* launches, int n);
 
 /* Limits of hymoe_ffn_noalloc: its scratch is one fixed array per device. */

@@ -80,12 +80,13 @@ def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p", pla
         q.put((rank, f"error: {e!r}", None))
 
 
-def _run_ep(world, tokens_per_rank, transport="p2p", place=None, pre_norm=False):
+def _run_ep(world, tokens_per_rank, transport="p2p", place=None, pre_norm=False, max_tokens=None):
     import hymoe
     nccl_id = hymoe.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    max_tokens = max(16, max(max(t) for t in tokens_per_rank))  # job-wide bound
+    if max_tokens is None:
+        max_tokens = max(16, max(max(t) for t in tokens_per_rank))  # job-wide bound
     procs = [ctx.Process(target=_ep_worker,
                          args=(r, world, nccl_id, tokens_per_rank[r], max_tokens, q, transport, place,
                                pre_norm))
@@ -143,6 +144,36 @@ def test_expert_parallel_matches_single_gpu_and_oracle(orc, tokens, placed, tran
                 o = orc.moe_forward(x, lay["router"], lay["sgu_f"], lay["sdn_f"], lay["egu_f"],
                                     lay["edn_f"], K, I, bias=bias)
                 assert rel_l2(ep_out["out"], o["out"]) <= REL_L2_TOL
+    single.close()
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
+def test_expert_parallel_pipelined_host_calls(orc, transport):
+    """A context with max_tokens >= 4096 runs every host-pointer call as max_tokens / 2048 token
+    chunks on every rank (copies overlapping the compute; a rank's chunk may be empty), debug
+    outputs included: the same bits as the single-GPU call where every chunk is on the
+    tensor-core path, the parity tolerance otherwise."""
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    tokens = [[300, 0, 4096], [2100, 5, 130]]
+    res = _run_ep(2, tokens, transport, max_tokens=4096)
+    import hymoe
+    lay = _layer(orc)
+    single = hymoe.MoE(H, I, E, K, 1, 4096, device=0)
+    single.load_layer(0, lay["router"], lay["sgu"], lay["sdn"], lay["egu"], lay["edn"], WT)
+    for call in range(3):
+        bias = O.zipf_bias(SEED + call, E)
+        for rank in range(2):
+            t = tokens[rank][call]
+            x = O.synth_x(orc, SEED + 100 * call + rank, t, H)
+            ref = single.forward_host(0, x, bias=bias, debug=True)
+            got = res[rank][call]
+            for k in ("idx", "w", "logits", "probs"):
+                assert np.array_equal(got[k], ref[k]), (rank, call, k)
+            if all(tokens[r][call] // 2 > 64 for r in range(2)):
+                assert np.array_equal(got["out"], ref["out"]), f"rank {rank} call {call}"
+            elif t:
+                assert rel_l2(got["out"], ref["out"]) <= REL_L2_TOL
     single.close()
 
 
