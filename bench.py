@@ -381,8 +381,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         res["ep_ranks"] = per_rank
 
     # ---- parity of the timed call's rows
-    sample = np.sort(np.random.default_rng(args.seed + 77).choice(T, size=PARITY_ROWS if world == 1
-                                                                  else PARITY_ROWS_EP, replace=False))
+    n_rows = min(T, PARITY_ROWS if world == 1 else PARITY_ROWS_EP)
+    sample = np.sort(np.random.default_rng(args.seed + 77).choice(T, size=n_rows, replace=False))
     sel = torch.from_numpy(sample).to(dev)
     xs = x.index_select(0, sel).cpu().numpy()
     outs = out.index_select(0, sel).cpu().numpy()

@@ -29,9 +29,10 @@ __global__ __launch_bounds__(128, 10) void combine_kernel(const float* __restric
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
         if (k < K) {
-            const int pos = __ldg(slot_pos + t * K + k);
+            const int pos = __ldg(slot_pos + t * K + k);  // < 0: a pair dropped by the capacity
             w[k] = __ldg(topk_w + t * K + k);
-            u[k] = *reinterpret_cast<const uint4*>(y_routed + static_cast<size_t>(pos) * H + j);
+            u[k] = pos >= 0 ? *reinterpret_cast<const uint4*>(y_routed + static_cast<size_t>(pos) * H + j)
+                            : make_uint4(0u, 0u, 0u, 0u);
         }
     }
     const float* sr = y_shared + static_cast<size_t>(t) * H + j;
@@ -50,7 +51,7 @@ __global__ __launch_bounds__(128, 10) void combine_kernel(const float* __restric
         float r = 0.f;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            if (k < K) {
+            if (k < K && w[k] != 0.f) {  // a dropped pair (weight 0) adds nothing
                 const uint32_t wd = i < 2 ? u[k].x : i < 4 ? u[k].y : i < 6 ? u[k].z : u[k].w;
                 const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wd));
                 r = __fadd_rn(r, __fmul_rn(w[k], (i & 1) ? f.y : f.x));

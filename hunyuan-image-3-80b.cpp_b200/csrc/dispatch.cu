@@ -225,17 +225,21 @@ __global__ __launch_bounds__(128) void scatter_gather_kernel(
     const int nt = min(kRouterTok, T - t0);
     {
         const int tt = tid >> 3, k = tid & 7;  // 128 threads = 16 tokens x 8 ranks
-        sidx[tt][k] = (tt < nt && k < K) ? topk_idx[(t0 + tt) * K + k] : -1;
+        const int v = (tt < nt && k < K) ? topk_idx[(t0 + tt) * K + k] : -1;
+        sidx[tt][k] = v >= 0 && (v & kDroppedPair) ? -1 : v;  // a dropped pair takes no row
     }
     __syncthreads();
     {
         const int tt = tid >> 3, k = tid & 7;
         if (tt < nt && k < K) {
             const int e = sidx[tt][k];
-            int rank = 0;
-            for (int p = 0; p < tt; ++p)
-                for (int kk = 0; kk < K; ++kk) rank += sidx[p][kk] == e;
-            const int pos = chunk_base[c * E + e] + rank;
+            int pos = -1;
+            if (e >= 0) {
+                int rank = 0;
+                for (int p = 0; p < tt; ++p)
+                    for (int kk = 0; kk < K; ++kk) rank += sidx[p][kk] == e;
+                pos = chunk_base[c * E + e] + rank;
+            }
             spos[tt][k] = pos;
             if (blockIdx.y == 0) slot_pos[(t0 + tt) * K + k] = pos;
         }
@@ -256,7 +260,7 @@ __global__ __launch_bounds__(128) void scatter_gather_kernel(
         v.z = *reinterpret_cast<const uint32_t*>(&h2);
         v.w = *reinterpret_cast<const uint32_t*>(&h3);
         for (int k = 0; k < K; ++k)
-            *reinterpret_cast<uint4*>(xp_routed + static_cast<size_t>(spos[tt][k]) * H + j) = v;
+            if (spos[tt][k] >= 0) *reinterpret_cast<uint4*>(xp_routed + static_cast<size_t>(spos[tt][k]) * H + j) = v;
         if (xp_shared != nullptr) *reinterpret_cast<uint4*>(xp_shared + static_cast<size_t>(t0 + tt) * H + j) = v;
     }
 }
@@ -331,7 +335,51 @@ __global__ void ep_segments_fused_kernel(const int* __restrict__ C, int ld, int 
 
 __global__ void unmap_slots_kernel(int* __restrict__ idx, const int* __restrict__ expert_of_slot, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) idx[i] = __ldg(expert_of_slot + idx[i]);
+    if (i >= n) return;
+    const int slot = idx[i] & ~kDroppedPair;
+    idx[i] = expert_of_slot != nullptr ? __ldg(expert_of_slot + slot) : slot;
+}
+
+// k-major priorities (one CTA of 1024 threads).  For each choice k, tokens in blocks of 1024:
+// a lane's rank among its warp's lanes of the same slot (warp match), plus the counts of the
+// same slot in earlier warps of the block, plus the slot's running count over earlier blocks
+// and earlier choices.
+__global__ __launch_bounds__(1024) void capacity_kernel(int* __restrict__ topk_idx, float* __restrict__ topk_w,
+                                                        int* __restrict__ chunk_counts, int T, int K, int E,
+                                                        int capacity) {
+    __shared__ int run[kMaxE];
+    __shared__ int wcnt[32][kMaxE];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid < kMaxE) run[tid] = 0;
+    const unsigned lt = (1u << lane) - 1u;
+    for (int k = 0; k < K; ++k) {
+        for (int t0 = 0; t0 < T; t0 += 1024) {
+            const int t = t0 + tid;
+            const bool valid = t < T;
+            const int slot = valid ? topk_idx[t * K + k] : -1;
+            const unsigned peers = __match_any_sync(0xffffffffu, slot);
+            for (int e = lane; e < kMaxE; e += 32) wcnt[warp][e] = 0;
+            __syncwarp();
+            if (valid && (peers & lt) == 0) wcnt[warp][slot] = __popc(peers);
+            __syncthreads();
+            if (tid < E) {  // exclusive scan over the block's warps, continued from `run`
+                int acc = run[tid];
+                for (int w = 0; w < 32; ++w) {
+                    const int cnt = wcnt[w][tid];
+                    wcnt[w][tid] = acc;
+                    acc += cnt;
+                }
+                run[tid] = acc;
+            }
+            __syncthreads();
+            if (valid && wcnt[warp][slot] + __popc(peers & lt) >= capacity) {
+                topk_idx[t * K + k] = slot | kDroppedPair;
+                topk_w[t * K + k] = 0.f;
+                atomicSub(chunk_counts + static_cast<size_t>(t / kRouterTok) * E + slot, 1);
+            }
+            __syncthreads();  // wcnt is rewritten by the next block
+        }
+    }
 }
 
 }  // namespace
@@ -350,6 +398,14 @@ cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, fl
 
 cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st) {
     items_kernel<<<1, 1024, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_capacity(int* topk_idx, float* topk_w, int* chunk_counts, int T, int K, int E, int capacity,
+                            cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (E > kMaxE) return cudaErrorInvalidValue;
+    capacity_kernel<<<1, 1024, 0, st>>>(topk_idx, topk_w, chunk_counts, T, K, E, capacity);
     return cudaGetLastError();
 }
 

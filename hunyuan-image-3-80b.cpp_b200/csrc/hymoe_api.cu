@@ -1029,8 +1029,15 @@ hymoe_status hymoe_set_routing(hymoe_ctx* c, const hymoe_routing* r) {
     if (!c) return HYMOE_ERR_INVALID_ARG;
     RouteMode m;  // NULL: moe_forward_cpu's routing
     if (r) {
-        if (r->drop_tokens)
-            return c->fail(HYMOE_ERR_UNSUPPORTED, "capacity drops (drop_tokens) are not implemented");
+        if (r->drop_tokens) {
+            if (c->cfg.ep_size > 1)
+                return c->fail(HYMOE_ERR_UNSUPPORTED, "capacity drops (drop_tokens) run on one GPU only");
+            if (!(r->capacity_factor >= 0.f) || !std::isfinite(r->capacity_factor))
+                return c->fail(HYMOE_ERR_INVALID_ARG, "capacity_factor %g", static_cast<double>(r->capacity_factor));
+            m.drop = 1;
+            m.capacity_factor = r->capacity_factor;
+            m.min_capacity = static_cast<int>(std::min<uint32_t>(r->min_capacity, 1u << 30));
+        }
         if (r->group_limited_greedy) {
             if (r->n_group == 0 || r->n_group > 32 || c->E % static_cast<int>(r->n_group) != 0 ||
                 r->topk_group == 0 || r->topk_group > r->n_group)
@@ -1310,12 +1317,25 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         }
         if (T > 0) {
             const int n_chunks = (T + kRouterTok - 1) / kRouterTok;
-            // T <= 16 (one router chunk): the top-K runs inside the plan launch.
-            const bool fused = n_chunks == 1;
+            // T <= 16 (one router chunk): the top-K runs inside the plan launch (not with
+            // capacity drops, which need every token's choices before the plan).
+            const bool fused = n_chunks == 1 && !c->route.drop;
             c->phase_begin();
             HY_CUDA(c, launch_router(dxn, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
                                      c->topk_w, c->topk_idx, c->chunk_counts, slot_of, c->route, !fused, st));
             c->phase_end(HYMOE_PHASE_ROUTER, fused ? 1 : 2);
+            if (c->route.drop) {
+                // topkgating_full's capacity with drop_tokens (src/hunyuan_moe_full.cpp:205-224):
+                // floor(capacity_factor * K * T / E) in single precision, at least K and
+                // min_capacity; pairs beyond it in k-major order are dropped
+                const uint32_t f = static_cast<uint32_t>(c->route.capacity_factor * static_cast<float>(K) *
+                                                         static_cast<float>(T) / static_cast<float>(E));
+                const int cap = std::max(std::max<int>(static_cast<int>(std::min<uint32_t>(f, 1u << 30)), K),
+                                         c->route.min_capacity);
+                c->phase_begin();
+                HY_CUDA(c, launch_capacity(c->topk_idx, c->topk_w, c->chunk_counts, T, K, E, cap, st));
+                c->phase_end(HYMOE_PHASE_ROUTER);
+            }
             PlanArgs pa{};
             pa.chunk_counts = c->chunk_counts;
             pa.n_chunks = n_chunks;
@@ -1553,8 +1573,11 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
                 if (dbg->topk_weights)
                     HY_CUDA(c, cudaMemcpyAsync(dbg->topk_weights, c->topk_w, sizeof(float) * T * K, kd, st));
                 if (dbg->topk_indices) {
-                    if (slot_of)  // slots back to expert ids (topk_idx is not read again in this call)
-                        HY_CUDA(c, launch_unmap_slots(c->topk_idx, slot_of + E, static_cast<int>(T * K), st));
+                    // slots back to expert ids, dropped-pair marks cleared (topk_idx is not read
+                    // again in this call)
+                    if (slot_of || c->route.drop)
+                        HY_CUDA(c, launch_unmap_slots(c->topk_idx, slot_of ? slot_of + E : nullptr,
+                                                      static_cast<int>(T * K), st));
                     HY_CUDA(c, cudaMemcpyAsync(dbg->topk_indices, c->topk_idx, sizeof(int) * T * K, kd, st));
                 }
                 if (host && dlog)

@@ -28,7 +28,14 @@ struct RouteMode {
     int norm = 1;        // weights = p / sum of the K selected p (else p * scale)
     int clamp = 0;       //      sum clamped below at 1e-8 (FULL mode)
     float scale = 1.f;   // routed_scaling_factor when norm == 0
+    int drop = 0;        // capacity-limited routing (one GPU): pairs beyond `capacity` dropped
+    float capacity_factor = 1.f;
+    int min_capacity = 0;
 };
+
+// Top-K entries of a pair dropped by the capacity limit carry this bit (the slot stays in the
+// low bits for the debug output); the sort, the GEMMs and the combine skip them.
+constexpr int kDroppedPair = 1 << 30;
 
 // ---- router.cu
 constexpr int kRouterTok = 16;  // tokens per router CTA (= dispatch chunk)
@@ -75,7 +82,14 @@ cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, fl
                              int* topk_idx, const PlanArgs& a, cudaStream_t st);
 
 cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st);
-// idx[i] = expert_of_slot[idx[i]] for i < n (top-K slots back to expert ids for the caller).
+// Capacity-limited routing (topkgating_full with drop_tokens, src/hunyuan_moe_full.cpp:205-305):
+// every pair's priority among its slot's pairs in k-major order (all tokens' first choices
+// before any second choice, tokens in order); pairs at or beyond `capacity` get kDroppedPair in
+// topk_idx, weight 0, and leave their chunk's count.  One CTA.
+cudaError_t launch_capacity(int* topk_idx, float* topk_w, int* chunk_counts, int T, int K, int E, int capacity,
+                            cudaStream_t st);
+// idx[i] = expert_of_slot[idx[i]] for i < n (top-K slots back to expert ids for the caller);
+// the dropped-pair bit is cleared; expert_of_slot == nullptr: identity (only the bit is cleared).
 cudaError_t launch_unmap_slots(int* idx, const int* expert_of_slot, int n, cudaStream_t st);
 
 // xp_shared == nullptr: the shared expert's rows are written elsewhere (launch_shared_prep).

@@ -283,7 +283,8 @@ class MoE:
     def set_routing(self, group=None, drop=None, min_capacity: int = 8, norm_topk_prob: bool = True,
                     scale: float = 1.0, plain: bool = False) -> None:
         """FULL-mode routing variant (hymoe_set_routing); plain=True restores the default.
-        group = (n_group, topk_group); drop = capacity_factor (not implemented: raises)."""
+        group = (n_group, topk_group); drop = capacity_factor of capacity-limited routing (one
+        GPU; the pairs beyond each expert's capacity in k-major order are dropped)."""
         if plain:
             self._check(self.L.hymoe_set_routing(self.h, None))
             return

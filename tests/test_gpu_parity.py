@@ -422,11 +422,38 @@ def test_full_mode_routing_variants_vs_oracle(orc, opts, T):
             np.testing.assert_allclose(r["w"][t], a["w"][t], rtol=1e-5)
     ref = _block_with_routing(orc, lay, x, r["idx"], r["w"], I)
     assert rel_l2(r["out"], ref) <= REL_L2_TOL
-    with pytest.raises(hymoe.HymoeError) as ei:
-        m.set_routing(drop=1.0)
-    assert ei.value.status == 4
     m.set_routing(plain=True)
     assert np.array_equal(m.forward_host(0, x)["out"], plain)
+    m.close()
+
+
+@pytest.mark.parametrize("opts", [{"drop": 1.0}, {"drop": 0.5, "group": (8, 3)},
+                                  {"drop": 1.25, "min_capacity": 4, "norm_topk_prob": False, "scale": 1.5}])
+@pytest.mark.parametrize("T", [5, 17, 300, 700])
+def test_capacity_drops_vs_oracle(orc, opts, T):
+    """hymoe_set_routing with drop_tokens: the capacity floor(cf * K * T / E) (at least K and
+    min_capacity), each expert's first pairs in k-major order kept, the others dropped — the
+    same pairs as the oracle's topkgating_full (pinned to the reference's), their debug weight
+    0, their rows out of the GEMMs; the output equals the block over the kept pairs.  T = 5 and
+    17 run the decode kernels (17: more than one router chunk), 300 and 700 the tensor cores."""
+    H, I, E, K, seed, wt = 512, 256, 64, 8, 67, O.Q4_0
+    lay = host_layer(orc, seed, 0, H, I, E, wt)
+    m = _ctx(H, I, E, K, T)
+    _load(m, lay, wt)
+    x = O.synth_x(orc, seed + T, T, H)
+    bias = O.zipf_bias(seed, E)  # skewed load: hot experts overflow their capacity
+    m.set_routing(**opts)
+    r = m.forward_host(0, x, bias=bias, debug=True)
+    a = orc.topkgating_full(r["logits"], K, **opts)
+    assert np.array_equal(r["idx"], a["idx"])
+    np.testing.assert_allclose(r["w"], a["w"] * a["keep"], rtol=1e-5, atol=0)
+    assert np.array_equal(r["w"] == 0, ~a["keep"])
+    if T >= 300 and opts["drop"] <= 1.0:
+        assert (~a["keep"]).any()  # the case really drops pairs
+    ref = _block_with_routing(orc, lay, x, r["idx"], r["w"], I)
+    assert rel_l2(r["out"], ref) <= REL_L2_TOL
+    m.set_routing(plain=True)
+    assert (m.forward_host(0, x, bias=bias, debug=True)["w"] > 0).all()
     m.close()
 
 
