@@ -34,7 +34,9 @@
 #include <thread>
 
 #include <algorithm>
+#include <condition_variable>
 #include <cstdarg>
+#include <deque>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -90,6 +92,31 @@ EncodeTiledFn get_encode_fn() {
             fn = reinterpret_cast<EncodeTiledFn>(p);
     });
     return fn;
+}
+
+using WaitValueFn = PFN_cuStreamWaitValue32_v11070;
+using WriteValueFn = PFN_cuStreamWriteValue32_v11070;
+
+// Stream memory operations (the wait happens in the GPU's front end: no kernel, no SM).
+struct StreamMemOps {
+    WaitValueFn wait = nullptr;
+    WriteValueFn write = nullptr;
+};
+const StreamMemOps& stream_mem_ops() {
+    static StreamMemOps ops;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuStreamWaitValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            ops.wait = reinterpret_cast<WaitValueFn>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            ops.write = reinterpret_cast<WriteValueFn>(p);
+    });
+    return ops;
 }
 
 using AddressRangeFn = PFN_cuMemGetAddressRange_v3020;
@@ -215,6 +242,34 @@ struct hymoe_ctx {
     unsigned int* done_ctas = nullptr;  // dispatch completion counter
     uint32_t epoch = 0;                 // calls made; flags carry it
     std::vector<void*> ipc_opened;
+
+    // Asynchronous layer loads (hymoe_load_layer_async): the caller's thread validates and queues
+    // a job; the loader thread issues the job's copies and re-tiling on load_stream (pageable
+    // host copies block only that thread), then writes ready[layer] = the job's epoch with a
+    // stream memory operation; a forward of that layer makes its stream wait (in the GPU's front
+    // end) for ready[layer] >= the last epoch issued for it.
+    struct LoadJob {
+        uint32_t layer = 0, epoch = 0;
+        int wt = 0;
+        float* d_router = nullptr;
+        uint8_t *d_gu = nullptr, *d_dn = nullptr;
+        size_t gu_bytes = 0, dn_bytes = 0;
+        hymoe_tensor router{};
+        std::vector<hymoe_tensor> gu, dn;  // per weight group (local experts, then shared)
+        std::vector<float> router_f32;     // a router decoded on the host (GGUF)
+        cudaEvent_t prior = nullptr;       // the caller's stream at the time of the call
+    };
+    std::thread loader;
+    std::mutex lmu;
+    std::condition_variable lcv, ldone;
+    std::deque<LoadJob> jobs;
+    bool lstop = false;
+    cudaStream_t load_stream = nullptr;
+    uint8_t* load_tmp = nullptr;        // one GGUF tensor in flight (the job's stream orders reuse)
+    uint32_t* ready = nullptr;          // device [num_layers]: last completed load epoch per layer
+    std::vector<uint32_t> issued, done;  // per layer: last epoch queued / finished (host)
+    std::vector<hymoe_status> lstatus;  // per layer: status of the last finished load
+    std::string lerr;                   // message of the last failed load
 
     std::map<GraphKey, cudaGraphExec_t> graphs;  // HYMOE_USE_GRAPH replays
     void clear_graphs() {
@@ -391,6 +446,128 @@ hymoe_status load_matrix(hymoe_ctx* c, const hymoe_tensor* t, uint8_t* dst, int 
     }
     HY_CUDA(c, launch_repack(src, t->ggml_type, dst, dst_type, rows, K, glu_I, c->stream));
     if (host) HY_CUDA(c, cudaStreamSynchronize(c->stream));  // tmp is reused by the next tensor
+    return HYMOE_OK;
+}
+
+// Validates one layer's tensors for this rank (hymoe_load_layer's rules); *wt = the device tile
+// type.
+hymoe_status check_layer_tensors(hymoe_ctx* c, uint32_t layer, const hymoe_tensor* router,
+                                 const hymoe_tensor* shared_gate_up, const hymoe_tensor* shared_down,
+                                 const hymoe_tensor* experts_gate_up, const hymoe_tensor* experts_down, int* wt) {
+    const int H = c->H, I = c->I, E = c->E;
+    if (!tensor_ok(router, E, H, HYMOE_TYPE_F32))
+        return c->fail(HYMOE_ERR_INVALID_ARG, "router must be F32 [E=%d, H=%d]", E, H);
+    if (!shared_gate_up || !shared_down || !experts_gate_up || !experts_down)
+        return c->fail(HYMOE_ERR_INVALID_ARG, "null tensor array");
+    const int gt = shared_gate_up->ggml_type;
+    if (gt != HYMOE_TYPE_F32 && gt != HYMOE_TYPE_F16 && gt != HYMOE_TYPE_Q4_0 && gt != HYMOE_TYPE_Q8_0)
+        return c->fail(HYMOE_ERR_INVALID_ARG, "unsupported GGUF type %d", gt);
+    if (!tensor_ok(shared_gate_up, 2 * I, H, gt) || !tensor_ok(shared_down, H, I, gt))
+        return c->fail(HYMOE_ERR_INVALID_ARG, "shared expert tensors: bad shape/type/size");
+    for (int le = 0; le < c->e_local; ++le) {
+        const int ge = c->expert_at(layer, c->e_first + le);
+        if (!tensor_ok(&experts_gate_up[ge], 2 * I, H, gt) || !tensor_ok(&experts_down[ge], H, I, gt))
+            return c->fail(HYMOE_ERR_INVALID_ARG,
+                           "expert %d tensors: bad shape/size or type differs from the shared expert", ge);
+    }
+    *wt = tile_type_for(gt);
+    return HYMOE_OK;
+}
+
+// Loader thread: one job at a time, in queue order.  Every step is issued on load_stream; the
+// ready flag is written even after a failure (the waiting forward must not wait forever), and
+// the failure is kept for hymoe_wait_layer / hymoe_forward / hymoe_synchronize.
+hymoe_status run_load_job(hymoe_ctx* c, hymoe_ctx::LoadJob& j, std::string* msg) {
+    cudaStream_t s = c->load_stream;
+    const int H = c->H, I = c->I;
+    cudaError_t e = cudaStreamWaitEvent(s, j.prior, 0);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(j.d_router, j.router.data, j.router.nbytes, cudaMemcpyHostToDevice, s);
+    for (size_t g = 0; g < j.gu.size() && e == cudaSuccess; ++g) {
+        e = cudaMemcpyAsync(c->load_tmp, j.gu[g].data, j.gu[g].nbytes, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess)
+            e = launch_repack(c->load_tmp, j.gu[g].ggml_type, j.d_gu + j.gu_bytes * g, j.wt, 2 * I, H, I, s);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(c->load_tmp, j.dn[g].data, j.dn[g].nbytes, cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess)
+            e = launch_repack(c->load_tmp, j.dn[g].ggml_type, j.d_dn + j.dn_bytes * g, j.wt, H, I, 0, s);
+    }
+    const CUresult w = stream_mem_ops().write(reinterpret_cast<CUstream>(s),
+                                              reinterpret_cast<CUdeviceptr>(c->ready + j.layer), j.epoch,
+                                              CU_STREAM_WRITE_VALUE_DEFAULT);
+    const cudaError_t sync = cudaStreamSynchronize(s);  // the caller's host buffers are free after this
+    if (e != cudaSuccess || sync != cudaSuccess || w != CUDA_SUCCESS) {
+        cudaGetLastError();
+        *msg = std::string("asynchronous load of layer ") + std::to_string(j.layer) + ": " +
+               (w != CUDA_SUCCESS && e == cudaSuccess && sync == cudaSuccess
+                    ? "cuStreamWriteValue32 failed"
+                    : cudaGetErrorString(e != cudaSuccess ? e : sync));
+        return HYMOE_ERR_CUDA;
+    }
+    return HYMOE_OK;
+}
+
+void loader_main(hymoe_ctx* c) {
+    cudaSetDevice(c->cfg.device);
+    while (true) {
+        hymoe_ctx::LoadJob job;
+        {
+            std::unique_lock<std::mutex> lk(c->lmu);
+            c->lcv.wait(lk, [&] { return c->lstop || !c->jobs.empty(); });
+            if (c->jobs.empty()) return;
+            job = std::move(c->jobs.front());
+            c->jobs.pop_front();
+        }
+        std::string msg;
+        const hymoe_status st = run_load_job(c, job, &msg);
+        cudaEventDestroy(job.prior);
+        {
+            std::lock_guard<std::mutex> lk(c->lmu);
+            c->done[job.layer] = job.epoch;
+            c->lstatus[job.layer] = st;
+            if (st != HYMOE_OK) c->lerr = msg;
+        }
+        c->ldone.notify_all();
+    }
+}
+
+// Starts the loader thread and its stream, staging buffer and ready flags (first use).
+hymoe_status ensure_loader(hymoe_ctx* c) {
+    if (c->loader.joinable()) return HYMOE_OK;
+    const StreamMemOps& ops = stream_mem_ops();
+    if (!ops.wait || !ops.write)
+        return c->fail(HYMOE_ERR_UNSUPPORTED, "stream memory operations (cuStreamWaitValue32) are unavailable");
+    const size_t n = c->layers.size();
+    if (!c->load_stream) HY_CUDA(c, cudaStreamCreateWithFlags(&c->load_stream, cudaStreamNonBlocking));
+    if (!c->load_tmp) HY_CUDA(c, dalloc(&c->load_tmp, c->tmp_bytes));
+    if (!c->ready) {
+        HY_CUDA(c, dalloc(&c->ready, n));
+        HY_CUDA(c, cudaMemset(c->ready, 0, sizeof(uint32_t) * n));
+    }
+    c->issued.assign(n, 0);
+    c->done.assign(n, 0);
+    c->lstatus.assign(n, HYMOE_OK);
+    c->lstop = false;
+    c->loader = std::thread(loader_main, c);
+    return HYMOE_OK;
+}
+
+// Waits until every queued load of `layer` (every layer: layer == UINT32_MAX) has finished;
+// returns the status of the last finished load of that layer (HYMOE_OK for all layers unless
+// one failed).
+hymoe_status wait_loads(hymoe_ctx* c, uint32_t layer) {
+    if (!c->loader.joinable()) return HYMOE_OK;
+    std::unique_lock<std::mutex> lk(c->lmu);
+    auto finished = [&](uint32_t l) { return c->done[l] >= c->issued[l]; };
+    c->ldone.wait(lk, [&] {
+        if (layer != UINT32_MAX) return finished(layer);
+        for (uint32_t l = 0; l < c->issued.size(); ++l)
+            if (!finished(l)) return false;
+        return true;
+    });
+    if (layer != UINT32_MAX) return c->lstatus[layer];
+    for (hymoe_status st : c->lstatus)
+        if (st != HYMOE_OK) return st;
     return HYMOE_OK;
 }
 
@@ -734,6 +911,14 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
 void hymoe_destroy(hymoe_ctx* c) {
     if (!c) return;
     cudaSetDevice(c->cfg.device);
+    if (c->loader.joinable()) {  // queued loads finish first
+        {
+            std::lock_guard<std::mutex> lk(c->lmu);
+            c->lstop = true;
+        }
+        c->lcv.notify_all();
+        c->loader.join();
+    }
     if (c->p2p && c->comm && !c->comm_broken) {
         // Peers may still read this rank's y (their combine) or write its xp: a bounded barrier
         // over the communicator orders the frees after every rank's last call.
@@ -803,6 +988,9 @@ void hymoe_destroy(hymoe_ctx* c) {
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     if (c->down_stream) cudaStreamDestroy(c->down_stream);
     if (c->side_stream) cudaStreamDestroy(c->side_stream);
+    if (c->load_stream) cudaStreamDestroy(c->load_stream);
+    cudaFree(c->load_tmp);
+    cudaFree(c->ready);
     if (c->ev_fork) cudaEventDestroy(c->ev_fork);
     if (c->ev_join) cudaEventDestroy(c->ev_join);
     cudaFree(c->items_sh_gu);
@@ -846,25 +1034,14 @@ hymoe_status hymoe_load_layer(hymoe_ctx* c, uint32_t layer, const hymoe_tensor* 
     if (!c) return HYMOE_ERR_INVALID_ARG;
     if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
     HY_CUDA(c, cudaSetDevice(c->cfg.device));
-    const int H = c->H, I = c->I, E = c->E;
-    if (!tensor_ok(router, E, H, HYMOE_TYPE_F32))
-        return c->fail(HYMOE_ERR_INVALID_ARG, "router must be F32 [E=%d, H=%d]", E, H);
-    if (!shared_gate_up || !shared_down || !experts_gate_up || !experts_down)
-        return c->fail(HYMOE_ERR_INVALID_ARG, "null tensor array");
-    const int gt = shared_gate_up->ggml_type;
-    if (gt != HYMOE_TYPE_F32 && gt != HYMOE_TYPE_F16 && gt != HYMOE_TYPE_Q4_0 && gt != HYMOE_TYPE_Q8_0)
-        return c->fail(HYMOE_ERR_INVALID_ARG, "unsupported GGUF type %d", gt);
-    if (!tensor_ok(shared_gate_up, 2 * I, H, gt) || !tensor_ok(shared_down, H, I, gt))
-        return c->fail(HYMOE_ERR_INVALID_ARG, "shared expert tensors: bad shape/type/size");
-    for (int le = 0; le < c->e_local; ++le) {
-        const int ge = c->expert_at(layer, c->e_first + le);
-        if (!tensor_ok(&experts_gate_up[ge], 2 * I, H, gt) || !tensor_ok(&experts_down[ge], H, I, gt))
-            return c->fail(HYMOE_ERR_INVALID_ARG,
-                           "expert %d tensors: bad shape/size or type differs from the shared expert", ge);
-    }
-    const int wt = tile_type_for(gt);
+    const int H = c->H, I = c->I;
+    int wt = 0;
+    hymoe_status st = check_layer_tensors(c, layer, router, shared_gate_up, shared_down, experts_gate_up,
+                                          experts_down, &wt);
+    if (st != HYMOE_OK) return st;
+    wait_loads(c, layer);  // an asynchronous load of this slot finishes first
     c->clear_graphs();
-    hymoe_status st = ensure_layer(c, layer, wt);
+    st = ensure_layer(c, layer, wt);
     if (st != HYMOE_OK) return st;
     LayerStore& L = c->layers[layer];
     L.loaded = false;
@@ -895,6 +1072,7 @@ hymoe_status hymoe_synth_layer(hymoe_ctx* c, uint32_t layer, int32_t ggml_type, 
     HY_CUDA(c, cudaSetDevice(c->cfg.device));
     const int H = c->H, I = c->I, E = c->E;
     const int wt = tile_type_for(ggml_type);
+    wait_loads(c, layer);  // an asynchronous load of this slot finishes first
     c->clear_graphs();
     hymoe_status st = ensure_layer(c, layer, wt);
     if (st != HYMOE_OK) return st;
@@ -1004,6 +1182,106 @@ hymoe_status hymoe_load_layer_gguf(hymoe_ctx* c, uint32_t layer, const hymoe_ggu
     return hymoe_load_layer(c, layer, &router, &sgu, &sdn, egu.data(), edn.data(), HYMOE_HOST_PTRS);
 }
 
+// Queues an asynchronous load (the tensors are validated already; router_f32 holds a router
+// decoded on the host, kept alive by the job).
+static hymoe_status queue_load(hymoe_ctx* c, uint32_t layer, const hymoe_tensor* router,
+                               const hymoe_tensor* shared_gate_up, const hymoe_tensor* shared_down,
+                               const hymoe_tensor* experts_gate_up, const hymoe_tensor* experts_down, int wt,
+                               std::vector<float>&& router_f32) {
+    hymoe_status st = ensure_loader(c);
+    if (st != HYMOE_OK) return st;
+    c->clear_graphs();
+    LayerStore& L0 = c->layers[layer];
+    if (L0.gu && L0.wtype != wt) {  // the slot is reallocated for another type: nothing may use it
+        wait_loads(c, layer);
+        HY_CUDA(c, cudaStreamSynchronize(c->stream));
+    }
+    st = ensure_layer(c, layer, wt);
+    if (st != HYMOE_OK) return st;
+    LayerStore& L = c->layers[layer];
+    hymoe_ctx::LoadJob j;
+    j.layer = layer;
+    j.wt = wt;
+    j.d_router = L.router;
+    j.d_gu = L.gu;
+    j.d_dn = L.dn;
+    j.gu_bytes = c->gu_group_bytes;
+    j.dn_bytes = c->dn_group_bytes;
+    j.router = *router;
+    j.router_f32 = std::move(router_f32);
+    if (!j.router_f32.empty()) j.router.data = j.router_f32.data();
+    for (int g = 0; g < c->groups; ++g) {
+        const bool shared = g == c->e_local;
+        const int ge = shared ? 0 : c->expert_at(layer, c->e_first + g);
+        j.gu.push_back(shared ? *shared_gate_up : experts_gate_up[ge]);
+        j.dn.push_back(shared ? *shared_down : experts_down[ge]);
+    }
+    // the slot is rewritten only after every call queued so far on the context's stream
+    HY_CUDA(c, cudaEventCreateWithFlags(&j.prior, cudaEventDisableTiming));
+    const cudaError_t e = cudaEventRecord(j.prior, c->stream);
+    if (e != cudaSuccess) {
+        cudaEventDestroy(j.prior);
+        return c->cuda_fail(e, "cudaEventRecord");
+    }
+    {
+        std::lock_guard<std::mutex> lk(c->lmu);
+        j.epoch = ++c->issued[layer];
+        c->jobs.push_back(std::move(j));
+    }
+    c->lcv.notify_one();
+    L.loaded = true;
+    return HYMOE_OK;
+}
+
+hymoe_status hymoe_load_layer_async(hymoe_ctx* c, uint32_t layer, const hymoe_tensor* router,
+                                    const hymoe_tensor* shared_gate_up, const hymoe_tensor* shared_down,
+                                    const hymoe_tensor* experts_gate_up, const hymoe_tensor* experts_down) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
+    HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    int wt = 0;
+    const hymoe_status st = check_layer_tensors(c, layer, router, shared_gate_up, shared_down, experts_gate_up,
+                                                experts_down, &wt);
+    if (st != HYMOE_OK) return st;
+    return queue_load(c, layer, router, shared_gate_up, shared_down, experts_gate_up, experts_down, wt, {});
+}
+
+hymoe_status hymoe_load_layer_gguf_async(hymoe_ctx* c, uint32_t layer, const hymoe_gguf* file, uint32_t layer_idx) {
+    if (!c || !file) return HYMOE_ERR_INVALID_ARG;
+    if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
+    HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    const int E = c->E;
+    std::vector<hymoe_tensor> egu(E), edn(E);
+    hymoe_tensor router{}, sgu{}, sdn{};
+    hymoe_status st = hymoe_gguf_moe_tensors(file, layer_idx, E, &router, &sgu, &sdn, egu.data(), edn.data());
+    if (st != HYMOE_OK) return c->fail(st, "GGUF layer %u: %s", layer_idx, hymoe_gguf_last_error());
+    std::vector<float> rf;
+    if (router.ggml_type != HYMOE_TYPE_F32) {
+        if (router.ne[0] != c->H || router.ne[1] != E ||
+            router.nbytes != gguf_nbytes(router.ggml_type, static_cast<int64_t>(E) * c->H) || !dequant_router(&router, &rf))
+            return c->fail(HYMOE_ERR_INVALID_ARG, "GGUF layer %u: router [%lld, %lld] of type %d", layer_idx,
+                           static_cast<long long>(router.ne[1]), static_cast<long long>(router.ne[0]), router.ggml_type);
+        router.data = rf.data();
+        router.ggml_type = HYMOE_TYPE_F32;
+        router.nbytes = rf.size() * sizeof(float);
+    }
+    int wt = 0;
+    st = check_layer_tensors(c, layer, &router, &sgu, &sdn, egu.data(), edn.data(), &wt);
+    if (st != HYMOE_OK) return st;
+    return queue_load(c, layer, &router, &sgu, &sdn, egu.data(), edn.data(), wt, std::move(rf));
+}
+
+hymoe_status hymoe_wait_layer(hymoe_ctx* c, uint32_t layer) {
+    if (!c) return HYMOE_ERR_INVALID_ARG;
+    if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
+    const hymoe_status st = wait_loads(c, layer);
+    if (st != HYMOE_OK) {
+        std::lock_guard<std::mutex> lk(c->lmu);
+        return c->fail(st, "%s", c->lerr.c_str());
+    }
+    return HYMOE_OK;
+}
+
 hymoe_status hymoe_set_norm(hymoe_ctx* c, uint32_t layer, const float* weight, float eps, int flags) {
     if (!c) return HYMOE_ERR_INVALID_ARG;
     if (layer >= c->layers.size()) return c->fail(HYMOE_ERR_INVALID_ARG, "layer %u out of range", layer);
@@ -1077,6 +1355,7 @@ hymoe_status hymoe_set_placement(hymoe_ctx* c, uint32_t layer, const int32_t* sl
         }
     }
     HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    wait_loads(c, layer);
     HY_CUDA(c, cudaStreamSynchronize(c->stream));  // no call of this layer still reads the old map
     c->clear_graphs();
     c->layers[layer].loaded = false;  // the experts of this rank's slots change: load again
@@ -1137,6 +1416,34 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     if (ep && (c->comm_broken || !c->comm))
         return c->fail(HYMOE_ERR_STATE, "expert-parallel communicator is unusable after an earlier failure");
     HY_CUDA(c, cudaSetDevice(c->cfg.device));
+    if (c->loader.joinable()) {
+        // An asynchronous load of this layer still in flight: the call's device work waits for it
+        // (a wait in the stream's front end, no host wait); a finished load that failed fails the
+        // call.  Captured graphs are not given such a wait: the host waits for the load first.
+        uint32_t want = 0;
+        bool finished = true;
+        hymoe_status lst = HYMOE_OK;
+        {
+            std::lock_guard<std::mutex> lk(c->lmu);
+            want = c->issued[layer];
+            finished = c->done[layer] >= want;
+            if (finished) lst = c->lstatus[layer];
+        }
+        if (!finished && (flags & HYMOE_USE_GRAPH)) {
+            lst = wait_loads(c, layer);
+            finished = true;
+        }
+        if (lst != HYMOE_OK) {
+            std::lock_guard<std::mutex> lk(c->lmu);
+            return c->fail(lst, "%s", c->lerr.c_str());
+        }
+        if (!finished) {
+            const CUresult r = stream_mem_ops().wait(reinterpret_cast<CUstream>(c->stream),
+                                                     reinterpret_cast<CUdeviceptr>(c->ready + layer), want,
+                                                     CU_STREAM_WAIT_VALUE_GEQ);
+            if (r != CUDA_SUCCESS) return c->fail(HYMOE_ERR_CUDA, "cuStreamWaitValue32 failed (%d)", static_cast<int>(r));
+        }
+    }
     const LayerStore& L = c->layers[layer];
     const int* slot_of = c->place_dev[layer];  // nullptr: identity placement
     const int T = static_cast<int>(n_tokens), H = c->H, I = c->I, E = c->E, K = c->K;

@@ -31,7 +31,8 @@ EXPORTS = ["hymoe_version", "hymoe_nccl_unique_id", "hymoe_create", "hymoe_destr
            "hymoe_ffn_noalloc", "hymoe_set_placement", "hymoe_balance_placement",
            "hymoe_gguf_open", "hymoe_gguf_close", "hymoe_gguf_last_error", "hymoe_gguf_tensor",
            "hymoe_gguf_get_u32", "hymoe_gguf_moe_tensors", "hymoe_load_layer_gguf",
-           "hymoe_set_norm", "hymoe_set_routing"]
+           "hymoe_set_norm", "hymoe_set_routing", "hymoe_load_layer_async", "hymoe_wait_layer",
+           "hymoe_load_layer_gguf_async"]
 
 PHASES = ["router", "plan", "dispatch", "gate_up", "down", "combine", "ep_dispatch",
           "ep_combine", "copy_in", "copy_out"]
@@ -109,6 +110,10 @@ def lib() -> C.CDLL:
         L.hymoe_gguf_moe_tensors.argtypes = [vp, u32, u32, C.POINTER(Tensor), C.POINTER(Tensor),
                                              C.POINTER(Tensor), C.POINTER(Tensor), C.POINTER(Tensor)]
         L.hymoe_load_layer_gguf.argtypes = [vp, u32, vp, u32]
+        L.hymoe_load_layer_async.argtypes = [vp, u32, C.POINTER(Tensor), C.POINTER(Tensor),
+                                             C.POINTER(Tensor), C.POINTER(Tensor), C.POINTER(Tensor)]
+        L.hymoe_wait_layer.argtypes = [vp, u32]
+        L.hymoe_load_layer_gguf_async.argtypes = [vp, u32, vp, u32]
         L.hymoe_set_norm.argtypes = [vp, u32, vp, C.c_float, C.c_int]
         L.hymoe_set_routing.argtypes = [vp, C.POINTER(Routing)]
         for f in EXPORTS:
@@ -268,6 +273,28 @@ class MoE:
         ed = (Tensor * E)(*[_tensor(a, wtype, H, I) for a in experts_dn])
         self._check(self.L.hymoe_load_layer(self.h, layer, C.byref(r), C.byref(sg), C.byref(sd),
                                             eg, ed, HOST_PTRS))
+
+    def load_layer_async(self, layer: int, router, shared_gu, shared_dn, experts_gu, experts_dn,
+                         wtype: int) -> None:
+        """hymoe_load_layer_async: returns at once; the arrays must stay alive and unchanged until
+        wait_layer(layer) (this object keeps references to them until then)."""
+        H, I, E = self.H, self.I, self.E
+        r = _tensor(router, TYPE_F32, E, H)
+        sg = _tensor(shared_gu, wtype, 2 * I, H)
+        sd = _tensor(shared_dn, wtype, H, I)
+        eg = (Tensor * E)(*[_tensor(a, wtype, 2 * I, H) for a in experts_gu])
+        ed = (Tensor * E)(*[_tensor(a, wtype, H, I) for a in experts_dn])
+        self._check(self.L.hymoe_load_layer_async(self.h, layer, C.byref(r), C.byref(sg), C.byref(sd), eg, ed))
+        self._pending = getattr(self, "_pending", {})
+        self._pending.setdefault(layer, []).append((router, shared_gu, shared_dn, experts_gu, experts_dn))
+
+    def load_layer_gguf_async(self, layer: int, file: "GGUF", layer_idx: int) -> None:
+        """hymoe_load_layer_gguf_async: keep `file` open until wait_layer(layer)."""
+        self._check(self.L.hymoe_load_layer_gguf_async(self.h, layer, file.h, layer_idx))
+
+    def wait_layer(self, layer: int) -> None:
+        self._check(self.L.hymoe_wait_layer(self.h, layer))
+        getattr(self, "_pending", {}).pop(layer, None)
 
     def set_placement(self, layer: int, slot_of_expert) -> None:
         """Expert placement (a permutation of 0..E-1, or None for identity); load the layer

@@ -150,6 +150,26 @@ hymoe_status hymoe_load_layer(hymoe_ctx* ctx, uint32_t layer, const hymoe_tensor
                               const hymoe_tensor* experts_gate_up,
                               const hymoe_tensor* experts_down, int flags);
 
+/* Asynchronous hymoe_load_layer (host pointers) for layer streaming: the reference's loop
+ * loads a layer, runs it and releases it (src/hunyuan_full_model.cpp:195-207); with this call the
+ * next layer's upload runs while the current layer computes.  The tensors are checked and the
+ * call returns at once: a loader thread of the context copies them to the device and re-tiles
+ * them on its own stream, in the order of the calls.  The host bytes must stay valid and
+ * unchanged until hymoe_wait_layer(ctx, layer) returns.  hymoe_forward on this layer may follow
+ * immediately: its device work waits for the load on the GPU (no host wait).  The slot is
+ * rewritten only after every call already queued on the context's stream, so "load layer l+1
+ * into the other slot, then run layer l" overlaps the two.  A failed load makes
+ * hymoe_wait_layer and later hymoe_forward calls on that layer fail. */
+hymoe_status hymoe_load_layer_async(hymoe_ctx* ctx, uint32_t layer, const hymoe_tensor* router,
+                                    const hymoe_tensor* shared_gate_up,
+                                    const hymoe_tensor* shared_down,
+                                    const hymoe_tensor* experts_gate_up,
+                                    const hymoe_tensor* experts_down);
+
+/* Waits until every asynchronous load queued for `layer` has finished (its host buffers may then
+ * be freed or reused) and returns the last one's status. */
+hymoe_status hymoe_wait_layer(hymoe_ctx* ctx, uint32_t layer);
+
 /* Fills a layer with synthetic weights generated on the device: every tensor ~N(0,std)
  * by the library's Philox4x32-10 / Irwin-Hall generator (one stream per tensor: layer in
  * the high 32 bits, kind 1 router / 2 gate_up / 3 down in bits 16-31, expert index or
@@ -323,6 +343,11 @@ hymoe_status hymoe_gguf_moe_tensors(const hymoe_gguf* file, uint32_t layer_idx, 
  * converter gives every tensor of a layer one type) is decoded to F32 on the host first. */
 hymoe_status hymoe_load_layer_gguf(hymoe_ctx* ctx, uint32_t layer, const hymoe_gguf* file,
                                    uint32_t layer_idx);
+
+/* hymoe_load_layer_gguf through hymoe_load_layer_async: the file must stay open until
+ * hymoe_wait_layer(ctx, layer) returns. */
+hymoe_status hymoe_load_layer_gguf_async(hymoe_ctx* ctx, uint32_t layer, const hymoe_gguf* file,
+                                         uint32_t layer_idx);
 
 #ifdef __cplusplus
 }
