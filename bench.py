@@ -310,7 +310,6 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
     if world > 1:
         torch.distributed.barrier()
     e2e_ms = 0.0
-    m.profile(True)  # copy phases: each host<->device copy bracketed by events on its stream
     for s in range(args.steps):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -318,12 +317,19 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
         b.record(stream)
         b.synchronize()
         e2e_ms += a.elapsed_time(b)
+    # copy breakdown from separate profiled calls (events around every copy; not the timed loop)
+    if world > 1:
+        torch.distributed.barrier()
+    m.profile(True)
+    n_prof = 3
+    for s in range(n_prof):
+        m.forward_device(0, xh.data_ptr(), oh.data_ptr(), T, bias_ptr=bh.data_ptr(), host=True)
     m.profile(False)
     pe = m.profile_read()
     mine_e2e = {"rank": rank, "e2e_ms": round(e2e_ms / args.steps, 4),
-                "copy_in_ms": round(pe["copy_in"][0] / args.steps, 4),
-                "copy_out_ms": round(pe["copy_out"][0] / args.steps, 4),
-                "copies_per_step": (pe["copy_in"][1] + pe["copy_out"][1]) // args.steps}
+                "copy_in_ms": round(pe["copy_in"][0] / n_prof, 4),
+                "copy_out_ms": round(pe["copy_out"][0] / n_prof, 4),
+                "copies_per_step": (pe["copy_in"][1] + pe["copy_out"][1]) // n_prof}
     e2e_ranks = [mine_e2e]
     if world > 1:
         e2e_ranks = [None] * world
@@ -370,7 +376,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int):
                 "h2d_bytes_per_step": xh.numel() * 4 + bh.numel() * 4,
                 "d2h_bytes_per_step": oh.numel() * 4, "ms_per_step": round(e2e_ms / args.steps, 4),
                 "note": "host-pointer calls run in token chunks whose copies overlap the compute; "
-                        "copy_in/copy_out are the copies' summed device time per step on each rank",
+                        "copy_in/copy_out: the copies' summed device time per call on each rank, from "
+                        "separate profiled calls after the timed loop",
                 "ranks": e2e_ranks},
         "gpu_launches": launches,
         "clocks": clk,

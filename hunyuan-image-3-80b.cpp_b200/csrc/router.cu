@@ -10,9 +10,11 @@
 // and adds in h order - the operations the reference performs - so the logits equal the
 // reference's bit for bit.  The add chain bounds a call at roughly 4 x H cycles; beyond
 // that the kernels are organised for operand reuse:
-//   router_logits_tiled_kernel (T > 64): CTA = 16 tokens x 32 experts, 128 threads with
-//     2 tokens x 2 experts (4 independent chains) each; x and Wr slabs of 128 columns
-//     stream through a 3-stage cp.async ring in shared memory.
+//   router_logits_wide_kernel (T > 64): CTA = 16 tokens x all experts, 128 threads; warp w
+//     owns 4 tokens, lane l experts l and l + 32 (8 independent chains per lane); token slabs
+//     broadcast, router rows by conflict-free lane reads, 2 stages of 128 columns in shared
+//     memory (an earlier 16 x 32 tile with 4 chains per thread was shared-memory-latency
+//     bound: 163 us against 0.137 ms for this kernel plus the top-K at 4096 tokens).
 //   router_logits_small_kernel (8 < T <= 64): CTA = 8 tokens x 8 experts, one chain per
 //     thread, deeper ring: the latency-bound chains spread over many CTAs.
 //   router_logits_decode_kernel (T <= 8): CTA = one expert; its router row and the T
@@ -31,11 +33,8 @@ namespace hymoe {
 
 namespace {
 
-constexpr int kTT = 16;     // tokens per tiled CTA
-constexpr int kTE = 32;     // experts per tiled CTA
 constexpr int kKC = 128;    // columns per stage
 constexpr int kLd = kKC + 4;  // padded smem row (floats): 16-byte rows offset by 4 banks
-constexpr int kStages = 3;
 constexpr int kDecodeMaxT = 8;
 constexpr int kSmallMaxT = 64;
 
@@ -62,73 +61,73 @@ __device__ __forceinline__ float chain4(float acc, float4 a, float4 b) {
     return __fadd_rn(acc, p23.y);
 }
 
-__global__ __launch_bounds__(128) void router_logits_tiled_kernel(
+// T > 64: CTA = 16 tokens (one dispatch chunk) x all E experts, 4 warps; warp w owns tokens
+// 4w..4w+3 and lane l experts l and l + 32 (8 independent chains per lane).  Token slabs are
+// read by broadcast, router rows by conflict-free 16-byte lane reads (rows padded to 132
+// floats); two stages of 128 columns (84 KB: two CTAs per SM, the whole grid in one wave at
+// 4096 tokens).
+constexpr int kWTok = 16, kWExp = 64, kWStages = 2;
+
+__global__ __launch_bounds__(128) void router_logits_wide_kernel(
     const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
     const float* __restrict__ bias, float* __restrict__ logits) {
     extern __shared__ float4 rsm4[];
     float* sm = reinterpret_cast<float*>(rsm4);
-    float* Xs = sm;                          // [stages][kTT][kLd]
-    float* Ws = sm + kStages * kTT * kLd;    // [stages][kTE][kLd]
-    const int tid = threadIdx.x;
-    const int t0 = blockIdx.x * kTT, e0 = blockIdx.y * kTE;
-    const int tq = tid >> 4, eq = tid & 15;  // tokens 2tq, 2tq+1; experts eq, eq+16
+    float* Xs = sm;
+    float* Ws = sm + kWStages * kWTok * kLd;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.x * kWTok;
     const int nst = H / kKC;
-
     auto load_stage = [&](int st, int ks) {
-        float* xs = Xs + st * kTT * kLd;
-        float* ws = Ws + st * kTE * kLd;
+        float* xs = Xs + st * kWTok * kLd;
+        float* ws = Ws + st * kWExp * kLd;
         const int c0 = ks * kKC;
-        for (int i = tid; i < kTT * (kKC / 4); i += 128) {
+        for (int i = tid; i < kWTok * (kKC / 4); i += 128) {
             const int r = i / (kKC / 4), c = (i % (kKC / 4)) * 4;
-            const int t = min(t0 + r, T - 1);
-            cp_async16(xs + r * kLd + c, x + static_cast<size_t>(t) * H + c0 + c);
+            cp_async16(xs + r * kLd + c, x + static_cast<size_t>(min(t0 + r, T - 1)) * H + c0 + c);
         }
-        for (int i = tid; i < kTE * (kKC / 4); i += 128) {
+        for (int i = tid; i < E * (kKC / 4); i += 128) {
             const int r = i / (kKC / 4), c = (i % (kKC / 4)) * 4;
-            const int e = min(e0 + r, E - 1);
-            cp_async16(ws + r * kLd + c, Wr + static_cast<size_t>(e) * H + c0 + c);
+            cp_async16(ws + r * kLd + c, Wr + static_cast<size_t>(r) * H + c0 + c);
         }
     };
-
-    float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;  // [token][expert]
+    float acc[4][2];
 #pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) {
-        if (s < nst) load_stage(s, s);
-        cp_async_commit();
-    }
+    for (int u = 0; u < 4; ++u) acc[u][0] = acc[u][1] = 0.f;
+    load_stage(0, 0);
+    cp_async_commit();
     for (int ks = 0; ks < nst; ++ks) {
-        cp_async_wait<kStages - 2>();
-        __syncthreads();
-        if (ks + kStages - 1 < nst) load_stage((ks + kStages - 1) % kStages, ks + kStages - 1);
+        if (ks + 1 < nst) load_stage((ks + 1) % kWStages, ks + 1);
         cp_async_commit();
-        const int st = ks % kStages;
-        const float* x0 = Xs + st * kTT * kLd + (2 * tq) * kLd;
-        const float* x1 = x0 + kLd;
-        const float* w0 = Ws + st * kTE * kLd + eq * kLd;
-        const float* w1 = w0 + 16 * kLd;
-#pragma unroll 8
+        cp_async_wait<1>();
+        __syncthreads();
+        const int st = ks % kWStages;
+        const float* xs = Xs + st * kWTok * kLd + (4 * warp) * kLd;
+        const float* w0 = Ws + st * kWExp * kLd + lane * kLd;
+        const float* w1 = w0 + 32 * kLd;
+#pragma unroll 4
         for (int k = 0; k < kKC; k += 4) {
-            const float4 xa = *reinterpret_cast<const float4*>(x0 + k);
-            const float4 xb = *reinterpret_cast<const float4*>(x1 + k);
             const float4 wa = *reinterpret_cast<const float4*>(w0 + k);
             const float4 wb = *reinterpret_cast<const float4*>(w1 + k);
-            a00 = chain4(a00, xa, wa);
-            a01 = chain4(a01, xa, wb);
-            a10 = chain4(a10, xb, wa);
-            a11 = chain4(a11, xb, wb);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float4 xv = *reinterpret_cast<const float4*>(xs + u * kLd + k);
+                acc[u][0] = chain4(acc[u][0], xv, wa);
+                acc[u][1] = chain4(acc[u][1], xv, wb);
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int t = t0 + 4 * warp + u;
+        if (t >= T) continue;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int e = lane + 32 * h;
+            if (e < E) logits[static_cast<size_t>(t) * E + e] = bias != nullptr ? __fadd_rn(acc[u][h], bias[e]) : acc[u][h];
         }
     }
-    cp_async_wait<0>();
-    const int ta = t0 + 2 * tq, ea = e0 + eq;
-    const float b0 = (bias != nullptr && ea < E) ? bias[ea] : 0.f;
-    const float b1 = (bias != nullptr && ea + 16 < E) ? bias[ea + 16] : 0.f;
-    auto put = [&](int t, int e, float v, float b) {
-        if (t < T && e < E) logits[static_cast<size_t>(t) * E + e] = bias ? __fadd_rn(v, b) : v;
-    };
-    put(ta, ea, a00, b0);
-    put(ta, ea + 16, a01, b1);
-    put(ta + 1, ea, a10, b0);
-    put(ta + 1, ea + 16, a11, b1);
 }
 
 // T <= 8: CTA = one expert; its router row and the T token rows are staged in shared memory
@@ -252,12 +251,11 @@ cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, 
         dim3 g((T + kSmallTT - 1) / kSmallTT, (E + kSmallTE - 1) / kSmallTE);
         router_logits_small_kernel<<<g, 64, smem, st>>>(x, T, H, Wr, E, bias, logits);
     } else {
-        const size_t smem = sizeof(float) * kStages * (kTT + kTE) * kLd;
-        e = cudaFuncSetAttribute(router_logits_tiled_kernel,
+        const size_t smem = sizeof(float) * kWStages * (kWTok + kWExp) * kLd;
+        e = cudaFuncSetAttribute(router_logits_wide_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        dim3 g((T + kTT - 1) / kTT, (E + kTE - 1) / kTE);
-        router_logits_tiled_kernel<<<g, 128, smem, st>>>(x, T, H, Wr, E, bias, logits);
+        router_logits_wide_kernel<<<(T + kWTok - 1) / kWTok, 128, smem, st>>>(x, T, H, Wr, E, bias, logits);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess || !topk) return e;
