@@ -186,7 +186,7 @@ constexpr int kScatterCols = 256;
 __global__ __launch_bounds__(128) void scatter_gather_kernel(
     const float* __restrict__ x, int T, int H, int E, int K, const int* __restrict__ topk_idx,
     const int* __restrict__ chunk_base, int* __restrict__ slot_pos, __half* __restrict__ xp_routed,
-    __half* __restrict__ xp_shared) {
+    __half* __restrict__ xp_shared, RowNorm nrm) {
     __shared__ int sidx[kRouterTok][8];
     __shared__ int spos[kRouterTok][8];
     const int c = blockIdx.x, t0 = c * kRouterTok, tid = threadIdx.x;
@@ -218,8 +218,8 @@ __global__ __launch_bounds__(128) void scatter_gather_kernel(
     if (j >= H) return;
     for (int tt = tid >> 5; tt < nt; tt += 4) {
         const float* xr = x + static_cast<size_t>(t0 + tt) * H;
-        const float4 a = *reinterpret_cast<const float4*>(xr + j);
-        const float4 b = *reinterpret_cast<const float4*>(xr + j + 4);
+        const float4 a = norm_row4(*reinterpret_cast<const float4*>(xr + j), nrm, t0 + tt, j);
+        const float4 b = norm_row4(*reinterpret_cast<const float4*>(xr + j + 4), nrm, t0 + tt, j + 4);
         const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
         const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
         uint4 v;
@@ -237,7 +237,7 @@ __global__ __launch_bounds__(128) void scatter_gather_kernel(
 __global__ __launch_bounds__(256) void shared_prep_kernel(const float* __restrict__ x, int T, int H,
                                                           __half* __restrict__ xp, int group, int n_rb_gu,
                                                           int n_rb_dn, int4* items_gu, int4* items_dn,
-                                                          int* n_items) {
+                                                          int* n_items, RowNorm nrm) {
     const int tid = threadIdx.x;
     for (int i = tid; i < n_rb_gu; i += blockDim.x) items_gu[i] = make_int4(group, i, 0, T);
     for (int i = tid; i < n_rb_dn; i += blockDim.x) items_dn[i] = make_int4(group, i, 0, T);
@@ -246,7 +246,7 @@ __global__ __launch_bounds__(256) void shared_prep_kernel(const float* __restric
         n_items[1] = n_rb_dn;
     }
     for (int i = tid * 4; i < T * H; i += blockDim.x * 4) {
-        const float4 a = *reinterpret_cast<const float4*>(x + i);
+        const float4 a = norm_row4(*reinterpret_cast<const float4*>(x + i), nrm, i / H, i % H);
         const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
         uint2 v;
         v.x = *reinterpret_cast<const uint32_t*>(&h0);
@@ -385,16 +385,17 @@ cudaError_t launch_unmap_slots(int* idx, const int* expert_of_slot, int n, cudaS
 
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
                                   const int* chunk_base, int* slot_pos, __half* xp_routed,
-                                  __half* xp_shared, cudaStream_t st) {
+                                  __half* xp_shared, cudaStream_t st, const RowNorm& nrm) {
     dim3 grid((T + kRouterTok - 1) / kRouterTok, (H + kScatterCols - 1) / kScatterCols);
     scatter_gather_kernel<<<grid, 128, 0, st>>>(x, T, H, E, K, topk_idx, chunk_base, slot_pos,
-                                                  xp_routed, xp_shared);
+                                                  xp_routed, xp_shared, nrm);
     return cudaGetLastError();
 }
 
 cudaError_t launch_shared_prep(const float* x, int T, int H, __half* xp, int group, int n_rb_gu,
-                               int n_rb_dn, int4* items_gu, int4* items_dn, int* n_items, cudaStream_t st) {
-    shared_prep_kernel<<<1, 256, 0, st>>>(x, T, H, xp, group, n_rb_gu, n_rb_dn, items_gu, items_dn, n_items);
+                               int n_rb_dn, int4* items_gu, int4* items_dn, int* n_items, cudaStream_t st,
+                               const RowNorm& nrm) {
+    shared_prep_kernel<<<1, 256, 0, st>>>(x, T, H, xp, group, n_rb_gu, n_rb_dn, items_gu, items_dn, n_items, nrm);
     return cudaGetLastError();
 }
 

@@ -88,7 +88,7 @@ constexpr int kEpCols = 256;
 __global__ __launch_bounds__(128) void ep_scatter_kernel(
     EpPeers peers, int N, int me, int E, int el, int T, int H, int K, const float* __restrict__ x,
     const int* __restrict__ topk_idx, const int* __restrict__ chunk_base, const int* __restrict__ goff,
-    int* __restrict__ slot_pos, unsigned int* done_ctas, uint32_t epoch) {
+    int* __restrict__ slot_pos, unsigned int* done_ctas, uint32_t epoch, RowNorm nrm) {
     __shared__ int sidx[kRouterTok][8];
     __shared__ int srow[kRouterTok][8];
     __shared__ int base[kEpMaxRanks];
@@ -125,8 +125,8 @@ __global__ __launch_bounds__(128) void ep_scatter_kernel(
     if (j < H) {
         for (int tt = tid >> 5; tt < nt; tt += 4) {
             const float* xr = x + static_cast<size_t>(t0 + tt) * H;
-            const float4 a = *reinterpret_cast<const float4*>(xr + j);
-            const float4 b = *reinterpret_cast<const float4*>(xr + j + 4);
+            const float4 a = norm_row4(*reinterpret_cast<const float4*>(xr + j), nrm, t0 + tt, j);
+            const float4 b = norm_row4(*reinterpret_cast<const float4*>(xr + j + 4), nrm, t0 + tt, j + 4);
             const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
             const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
             uint4 v;
@@ -162,7 +162,7 @@ __global__ __launch_bounds__(128) void ep_scatter_kernel(
 __global__ __launch_bounds__(128) void ep_local_kernel(
     EpPeers peers, int N, int me, int E, int el, int T, int H, int K, const float* __restrict__ x,
     const int* __restrict__ topk_idx, const int* __restrict__ chunk_base, const int* __restrict__ goff,
-    int* __restrict__ slot_pos) {
+    int* __restrict__ slot_pos, RowNorm nrm) {
     __shared__ int sidx[kRouterTok][8];
     __shared__ int srow[kRouterTok][8];
     __shared__ int base;
@@ -198,8 +198,8 @@ __global__ __launch_bounds__(128) void ep_local_kernel(
     __half* xp = peers.xp[me];
     for (int tt = tid >> 5; tt < nt; tt += 4) {
         const float* xr = x + static_cast<size_t>(t0 + tt) * H;
-        const float4 a = *reinterpret_cast<const float4*>(xr + j);
-        const float4 b = *reinterpret_cast<const float4*>(xr + j + 4);
+        const float4 a = norm_row4(*reinterpret_cast<const float4*>(xr + j), nrm, t0 + tt, j);
+        const float4 b = norm_row4(*reinterpret_cast<const float4*>(xr + j + 4), nrm, t0 + tt, j + 4);
         const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
         const __half2 h2 = __floats2half2_rn(b.x, b.y), h3 = __floats2half2_rn(b.z, b.w);
         uint4 v;
@@ -268,21 +268,21 @@ cudaError_t launch_ep_counts(const EpPeers& p, int N, int me, int E, int T, cons
 
 cudaError_t launch_ep_scatter(const EpPeers& p, int N, int me, int E, int el, int T, int H, int K, const float* x,
                               const int* topk_idx, const int* chunk_base, const int* goff, int* slot_pos,
-                              unsigned int* done_ctas, uint32_t epoch, cudaStream_t st) {
+                              unsigned int* done_ctas, uint32_t epoch, cudaStream_t st, const RowNorm& nrm) {
     if (T <= 0) return cudaErrorInvalidValue;  // a rank without tokens raises its flag directly
     dim3 grid((T + kRouterTok - 1) / kRouterTok, (H + kEpCols - 1) / kEpCols);
     ep_scatter_kernel<<<grid, 128, 0, st>>>(p, N, me, E, el, T, H, K, x, topk_idx, chunk_base, goff, slot_pos,
-                                            done_ctas, epoch);
+                                            done_ctas, epoch, nrm);
     return cudaGetLastError();
 }
 
 cudaError_t launch_ep_local(const EpPeers& p, int N, int me, int E, int el, int T, int H, int K, const float* x,
                             const int* topk_idx, const int* chunk_base, const int* goff, int* slot_pos,
-                            cudaStream_t st) {
+                            cudaStream_t st, const RowNorm& nrm) {
     (void)N;
     if (T <= 0) return cudaSuccess;
     dim3 grid((T + kRouterTok - 1) / kRouterTok, (H + kEpCols - 1) / kEpCols);
-    ep_local_kernel<<<grid, 128, 0, st>>>(p, N, me, E, el, T, H, K, x, topk_idx, chunk_base, goff, slot_pos);
+    ep_local_kernel<<<grid, 128, 0, st>>>(p, N, me, E, el, T, H, K, x, topk_idx, chunk_base, goff, slot_pos, nrm);
     return cudaGetLastError();
 }
 

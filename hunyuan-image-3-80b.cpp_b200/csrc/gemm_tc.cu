@@ -222,8 +222,8 @@ __device__ void ep_send_rows(const EpFuse& f, int ct, int cta, int n_ctas, int* 
             for (int u = 0; u < 4; ++u)
                 if (tb + u < nt) {
                     const float4* xr = reinterpret_cast<const float4*>(f.x + static_cast<size_t>(t0 + tb + u) * f.H + j);
-                    xv[u][0] = xr[0];
-                    xv[u][1] = xr[1];
+                    xv[u][0] = norm_row4(xr[0], f.nrm, t0 + tb + u, j);
+                    xv[u][1] = norm_row4(xr[1], f.nrm, t0 + tb + u, j + 4);
                 }
 #pragma unroll
             for (int u = 0; u < 4; ++u) {

@@ -187,10 +187,11 @@ struct hymoe_ctx {
     std::vector<std::vector<int>> expert_of_slot;
     std::vector<int*> place_dev;
     // Post-attention RMSNorm per layer (hymoe_set_norm): [H] weights on the device (nullptr:
-    // none) and eps; x_norm holds the normalised rows of a HYMOE_PRE_NORM call.
+    // none) and eps; rms_buf holds a HYMOE_PRE_NORM call's per-token factors (the kernels that
+    // read the token rows normalise them on the fly).
     std::vector<float*> norm_w;
     std::vector<float> norm_eps;
-    float* x_norm = nullptr;
+    float* rms_buf = nullptr;
     RouteMode route;  // routing variant (hymoe_set_routing); default: moe_forward_cpu's
     int expert_at(uint32_t layer, int slot) const {
         return expert_of_slot[layer].empty() ? slot : expert_of_slot[layer][slot];
@@ -939,7 +940,7 @@ void hymoe_destroy(hymoe_ctx* c) {
     for (auto& L : c->layers) free_layer(L);
     for (int* p : c->place_dev) cudaFree(p);
     for (float* p : c->norm_w) cudaFree(p);
-    cudaFree(c->x_norm);
+    cudaFree(c->rms_buf);
     cudaFree(c->x_dev);
     cudaFree(c->resid_dev);
     cudaFree(c->out_dev);
@@ -1294,7 +1295,7 @@ hymoe_status hymoe_set_norm(hymoe_ctx* c, uint32_t layer, const float* weight, f
         c->norm_w[layer] = nullptr;
         return HYMOE_OK;
     }
-    if (!c->x_norm) HY_CUDA(c, dalloc(&c->x_norm, static_cast<size_t>(c->cfg.max_tokens) * c->H));
+    if (!c->rms_buf) HY_CUDA(c, dalloc(&c->rms_buf, static_cast<size_t>(c->cfg.max_tokens)));
     if (!c->norm_w[layer]) HY_CUDA(c, dalloc(&c->norm_w[layer], static_cast<size_t>(c->H)));
     const bool host = (flags & HYMOE_HOST_PTRS) != 0;
     HY_CUDA(c, cudaMemcpy(c->norm_w[layer], weight, sizeof(float) * c->H,
@@ -1572,12 +1573,19 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     auto device_part = [&]() -> hymoe_status {
         // HYMOE_PRE_NORM: the layer's RMSNorm first; everything below reads the normalised rows
         // (the residual stays the caller's).  Timed with the router phase.
+        // HYMOE_PRE_NORM: the layer's RMSNorm.  One kernel computes each token's factor
+        // 1 / rms (the reference's chain); every kernel that reads the token rows (router,
+        // dispatch, expert-parallel sends) applies (x * rms) * w as it loads them, so the
+        // normalised rows are never written out.  The residual stays the caller's x.  Timed with
+        // the router phase.
         const float* dxn = dx;
+        RowNorm nrm{};
         if (pre_norm && T > 0) {
             c->phase_begin();
-            HY_CUDA(c, launch_rmsnorm(dx, c->norm_w[layer], c->norm_eps[layer], T, H, c->x_norm, st));
+            HY_CUDA(c, launch_rms(dx, c->norm_eps[layer], T, H, c->rms_buf, st));
             c->phase_end(HYMOE_PHASE_ROUTER);
-            dxn = c->x_norm;
+            nrm.rms = c->rms_buf;
+            nrm.w = c->norm_w[layer];
         }
         // Decode regime: every group has at most kGemvMaxRows rows (on one GPU a group has
         // at most T rows: the shared expert T, a routed expert at most one row per token).
@@ -1615,7 +1623,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             HY_CUDA(c, cudaEventRecord(c->ev_fork, st));
             HY_CUDA(c, cudaStreamWaitEvent(side, c->ev_fork, 0));
             HY_CUDA(c, launch_shared_prep(dxn, T, H, c->xp, el, tiles_gu, tiles_dn, c->items_sh_gu, c->items_sh_dn,
-                                          c->n_items_sh, side));
+                                          c->n_items_sh, side, nrm));
             HY_CUDA(c, launch_gemv(c->gmaps_xp, c->items_sh_gu, c->n_items_sh, tiles_gu, L.d_gu_ptrs, L.wtype,
                                    H / kTileK, 1, T, c->hbuf, I, nullptr, 0, c->err_word, std::min(c->n_sms, tiles_gu), side));
             HY_CUDA(c, launch_gemv(c->gmaps_h, c->items_sh_dn, c->n_items_sh + 1, tiles_dn, L.d_dn_ptrs, L.wtype,
@@ -1629,7 +1637,8 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             const bool fused = n_chunks == 1 && !c->route.drop;
             c->phase_begin();
             HY_CUDA(c, launch_router(dxn, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
-                                     c->topk_w, c->topk_idx, c->chunk_counts, slot_of, c->route, !fused, st));
+                                     c->topk_w, c->topk_idx, c->chunk_counts, slot_of, c->route, !fused, st,
+                                     nrm));
             c->phase_end(HYMOE_PHASE_ROUTER, fused ? 1 : 2);
             if (c->route.drop) {
                 // topkgating_full's capacity with drop_tokens (src/hunyuan_moe_full.cpp:205-224):
@@ -1668,7 +1677,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
                 c->phase_begin();
                 HY_CUDA(c, launch_scatter_gather(dxn, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
                                                  ep ? c->xp_send : c->xp + static_cast<size_t>(T) * H,
-                                                 shared_apart ? nullptr : c->xp, st));
+                                                 shared_apart ? nullptr : c->xp, st, nrm));
                 c->phase_end(HYMOE_PHASE_DISPATCH);
             }
         } else {
@@ -1686,11 +1695,11 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             HY_CUDA(c, launch_ep_counts(c->peers, N, rank, E, T, c->gcnt, epoch, budget_ns, c->err_word, st));
             if (!gemv) {
                 HY_CUDA(c, launch_ep_local(c->peers, N, rank, E, el, T, H, K, dxn, c->topk_idx, c->chunk_base,
-                                           c->goff, c->slot_pos, st));
+                                           c->goff, c->slot_pos, st, nrm));
             } else {
                 if (T > 0)
                     HY_CUDA(c, launch_ep_scatter(c->peers, N, rank, E, el, T, H, K, dxn, c->topk_idx, c->chunk_base,
-                                                 c->goff, c->slot_pos, c->done_ctas, epoch, st));
+                                                 c->goff, c->slot_pos, c->done_ctas, epoch, st, nrm));
                 else
                     HY_CUDA(c, launch_ep_raise(c->peers, N, rank, kEpFlagDeliver, epoch, st));
                 HY_CUDA(c, launch_ep_wait(c->peers, N, rank, kEpFlagDeliver, epoch, budget_ns, c->err_word, st));
@@ -1784,6 +1793,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             fuse.T = T;
             fuse.H = H;
             fuse.x = dxn;
+            fuse.nrm = nrm;
             fuse.topk_idx = c->topk_idx;
             fuse.slot_pos = c->slot_pos;
             fuse.goff = c->goff;

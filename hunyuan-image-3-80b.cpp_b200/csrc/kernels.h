@@ -37,6 +37,23 @@ struct RouteMode {
 // low bits for the debug output); the sort, the GEMMs and the combine skip them.
 constexpr int kDroppedPair = 1 << 30;
 
+// Token rows read through the decoder layer's post-attention RMSNorm applied on the fly:
+// x[t][j] -> (x[t][j] * rms[t]) * w[j], each product rounded in that order (rms_norm_f32,
+// src/rms_norm.cpp:9-33); rms == nullptr reads the rows as they are.
+struct RowNorm {
+    const float* rms = nullptr;  // [T] 1 / sqrt(sum of squares / H + eps) per token
+    const float* w = nullptr;    // [H]
+};
+#ifdef __CUDACC__
+__device__ __forceinline__ float4 norm_row4(float4 v, const RowNorm& n, int t, int j) {
+    if (n.rms == nullptr) return v;
+    const float s = __ldg(n.rms + t);
+    const float4 g = __ldg(reinterpret_cast<const float4*>(n.w + j));
+    return make_float4(__fmul_rn(__fmul_rn(v.x, s), g.x), __fmul_rn(__fmul_rn(v.y, s), g.y),
+                       __fmul_rn(__fmul_rn(v.z, s), g.z), __fmul_rn(__fmul_rn(v.w, s), g.w));
+}
+#endif
+
 // ---- router.cu
 constexpr int kRouterTok = 16;  // tokens per router CTA (= dispatch chunk)
 constexpr int kGemvMaxRows = 64; // token rows per GEMV work item
@@ -45,7 +62,7 @@ constexpr int kGemvMaxRows = 64; // token rows per GEMV work item
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
                           int* topk_idx, int* chunk_counts, const int* slot_of,
-                          const RouteMode& mode, bool topk, cudaStream_t st);
+                          const RouteMode& mode, bool topk, cudaStream_t st, const RowNorm& nrm = {});
 
 // ---- dispatch.cu
 constexpr int kMaxSegs = 80;  // >= E + 1 (E <= 64)
@@ -95,11 +112,12 @@ cudaError_t launch_unmap_slots(int* idx, const int* expert_of_slot, int n, cudaS
 // xp_shared == nullptr: the shared expert's rows are written elsewhere (launch_shared_prep).
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
                                   const int* chunk_base, int* slot_pos, __half* xp_routed,
-                                  __half* xp_shared, cudaStream_t st);
+                                  __half* xp_shared, cudaStream_t st, const RowNorm& nrm = {});
 // The shared expert as its own launch: its fp16 rows xp[0, T) and its work items (one per
 // 128-row block, all T rows) for gate_up and down; n_items[2].
 cudaError_t launch_shared_prep(const float* x, int T, int H, __half* xp, int group, int n_rb_gu,
-                               int n_rb_dn, int4* items_gu, int4* items_dn, int* n_items, cudaStream_t st);
+                               int n_rb_dn, int4* items_gu, int4* items_dn, int* n_items, cudaStream_t st,
+                               const RowNorm& nrm = {});
 // C: [N][ld] per-expert counts of every source rank (ld >= E).
 cudaError_t launch_ep_segments(const int* C, int ld, int N, int rank, int el, int E, int T, int4* segs,
                                int* n_segs, cudaStream_t st);
@@ -127,7 +145,7 @@ cudaError_t launch_ep_counts(const EpPeers& p, int N, int me, int E, int T, cons
 // [0, T) of this rank's xp; slot_pos = expert-sorted positions; then this rank's delivery flag.
 cudaError_t launch_ep_scatter(const EpPeers& p, int N, int me, int E, int el, int T, int H, int K, const float* x,
                               const int* topk_idx, const int* chunk_base, const int* goff, int* slot_pos,
-                              unsigned int* done_ctas, uint32_t epoch, cudaStream_t st);
+                              unsigned int* done_ctas, uint32_t epoch, cudaStream_t st, const RowNorm& nrm = {});
 cudaError_t launch_ep_wait(const EpPeers& p, int N, int me, int flag_off, uint32_t epoch, uint64_t budget_ns,
                            int* err, cudaStream_t st);
 cudaError_t launch_ep_raise(const EpPeers& p, int N, int me, int flag_off, uint32_t epoch, cudaStream_t st);
@@ -141,7 +159,7 @@ cudaError_t launch_ep_push(const EpPeers& p, int N, int me, const int4* segs, co
 // GEMM (EpFuse).
 cudaError_t launch_ep_local(const EpPeers& p, int N, int me, int E, int el, int T, int H, int K, const float* x,
                             const int* topk_idx, const int* chunk_base, const int* goff, int* slot_pos,
-                            cudaStream_t st);
+                            cudaStream_t st, const RowNorm& nrm = {});
 
 // What the grouped GEMM's communication warps need in fused expert-parallel mode.
 //   gate_up (mode 1): they store this rank's pairs owned elsewhere (fp16 rows of x) into the
@@ -155,7 +173,8 @@ struct EpFuse {
     EpPeers peers;
     const int2* aux;         // per item {source rank, first return row}
     int N, me, el, E, K, T, H;
-    const float* x;          // [T, H] fp32 token rows (after the pre-norm when there is one)
+    const float* x;          // [T, H] fp32 token rows
+    RowNorm nrm;             // the pre-norm applied while reading them (rms == nullptr: none)
     const int* topk_idx;     // [T, K] placement slots
     const int* slot_pos;     // [T, K] expert-sorted positions
     const int* goff;         // [E + 1] expert-sorted offsets of this rank's pairs
@@ -213,6 +232,9 @@ cudaError_t launch_combine(const float* y_shared, const __half* y_routed, const 
 
 // ---- norm.cu
 // out = rms_norm_f32(x, w, eps) over T rows of H (H % 128 == 0), the reference's rounding.
+// Only the per-token factor rms[t] = 1 / sqrt(sum of squares / H + eps) (the same chain); the
+// consumers apply (x * rms) * w while reading x (RowNorm).
+cudaError_t launch_rms(const float* x, float eps, int T, int H, float* rms, cudaStream_t st);
 cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int T, int H, float* out,
                            cudaStream_t st);
 

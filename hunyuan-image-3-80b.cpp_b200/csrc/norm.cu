@@ -27,9 +27,11 @@ constexpr int kNormThreads = 256;
 constexpr int kNormCopies = kNormTok * kNormCols / 4 / kNormThreads;  // 16-byte copies per thread per chunk
 constexpr int kNormUnroll = 4;
 
+// out == nullptr: only the per-token factor, into rms_out[T] (the consumers apply it).
 __global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const float* __restrict__ x,
                                                                const float* __restrict__ w, float eps,
-                                                               int T, int H, float* __restrict__ out) {
+                                                               int T, int H, float* __restrict__ out,
+                                                               float* __restrict__ rms_out) {
     __shared__ __align__(16) float tile[kNormStages][kNormTok * kNormLd];
     __shared__ float rms_s[kNormTok];
     const int t0 = blockIdx.x * kNormTok;
@@ -73,6 +75,10 @@ __global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const float* __re
     cp_async_wait<0>();
     if (tid < kNormTok)
         rms_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(H)), eps)));
+    if (out == nullptr) {
+        if (tid < kNormTok && t0 + tid < T) rms_out[t0 + tid] = rms_s[tid];
+        return;
+    }
     __syncthreads();
     const int n4 = H / 4;
     const int rows = min(kNormTok, T - t0);
@@ -111,7 +117,14 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int T, int
                            cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (H % kNormCols != 0) return cudaErrorInvalidValue;
-    rmsnorm_kernel<<<(T + kNormTok - 1) / kNormTok, kNormThreads, 0, st>>>(x, w, eps, T, H, out);
+    rmsnorm_kernel<<<(T + kNormTok - 1) / kNormTok, kNormThreads, 0, st>>>(x, w, eps, T, H, out, nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rms(const float* x, float eps, int T, int H, float* rms, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (H % kNormCols != 0) return cudaErrorInvalidValue;
+    rmsnorm_kernel<<<(T + kNormTok - 1) / kNormTok, kNormThreads, 0, st>>>(x, nullptr, eps, T, H, nullptr, rms);
     return cudaGetLastError();
 }
 

@@ -68,9 +68,20 @@ __device__ __forceinline__ float chain4(float acc, float4 a, float4 b) {
 // 4096 tokens).
 constexpr int kWTok = 16, kWExp = 64, kWStages = 2;
 
+// Token rows normalised on the fly (RowNorm): each landed stage of the token slab is
+// normalised in place before the chains read it.
+__device__ __forceinline__ void norm_slab(float* xs, int rows, int cols, int ld, int t0, int T, int c0,
+                                          const RowNorm& nrm, int nthreads) {
+    for (int i = threadIdx.x; i < rows * cols; i += nthreads) {
+        const int r = i / cols, c = i - r * cols;
+        const float s = __ldg(nrm.rms + min(t0 + r, T - 1));
+        xs[r * ld + c] = __fmul_rn(__fmul_rn(xs[r * ld + c], s), __ldg(nrm.w + c0 + c));
+    }
+}
+
 __global__ __launch_bounds__(128) void router_logits_wide_kernel(
     const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
-    const float* __restrict__ bias, float* __restrict__ logits) {
+    const float* __restrict__ bias, float* __restrict__ logits, RowNorm nrm) {
     extern __shared__ float4 rsm4[];
     float* sm = reinterpret_cast<float*>(rsm4);
     float* Xs = sm;
@@ -102,6 +113,10 @@ __global__ __launch_bounds__(128) void router_logits_wide_kernel(
         cp_async_wait<1>();
         __syncthreads();
         const int st = ks % kWStages;
+        if (nrm.rms != nullptr) {
+            norm_slab(Xs + st * kWTok * kLd, kWTok, kKC, kLd, t0, T, ks * kKC, nrm, 128);
+            __syncthreads();
+        }
         const float* xs = Xs + st * kWTok * kLd + (4 * warp) * kLd;
         const float* w0 = Ws + st * kWExp * kLd + lane * kLd;
         const float* w1 = w0 + 32 * kLd;
@@ -134,7 +149,7 @@ __global__ __launch_bounds__(128) void router_logits_wide_kernel(
 // once, then T threads run their chains without further synchronisation.
 __global__ __launch_bounds__(128) void router_logits_decode_kernel(
     const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
-    const float* __restrict__ bias, float* __restrict__ logits) {
+    const float* __restrict__ bias, float* __restrict__ logits, RowNorm nrm) {
     extern __shared__ float4 rsm4[];
     float* ws = reinterpret_cast<float*>(rsm4);  // [H]
     float* xs = ws + H;                           // [T][H]
@@ -145,6 +160,10 @@ __global__ __launch_bounds__(128) void router_logits_decode_kernel(
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
+    if (nrm.rms != nullptr) {
+        norm_slab(xs, T, H, H, 0, T, 0, nrm, 128);
+        __syncthreads();
+    }
     const int t = threadIdx.x;
     if (t >= T) return;
     const float* xr = xs + static_cast<size_t>(t) * H;
@@ -164,7 +183,7 @@ constexpr int kSmallKC = 256, kSmallLd = kSmallKC + 4, kSmallStages = 6;
 
 __global__ __launch_bounds__(64) void router_logits_small_kernel(
     const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
-    const float* __restrict__ bias, float* __restrict__ logits) {
+    const float* __restrict__ bias, float* __restrict__ logits, RowNorm nrm) {
     extern __shared__ float4 rsm4[];
     float* sm = reinterpret_cast<float*>(rsm4);
     float* Xs = sm;                                 // [stages][kSmallTT][kSmallLd]
@@ -201,6 +220,11 @@ __global__ __launch_bounds__(64) void router_logits_small_kernel(
         if (ks + kSmallStages - 1 < nst) load_stage((ks + kSmallStages - 1) % kSmallStages, ks + kSmallStages - 1);
         cp_async_commit();
         const int st = ks % kSmallStages;
+        if (nrm.rms != nullptr) {
+            norm_slab(Xs + st * kSmallTT * kSmallLd, nt, min(kSmallKC, H - ks * kSmallKC), kSmallLd, t0, T,
+                      ks * kSmallKC, nrm, 64);
+            __syncthreads();
+        }
         const float* xr = Xs + st * kSmallTT * kSmallLd + tt * kSmallLd;
         const float* wr = Ws + st * kSmallTE * kSmallLd + ee * kSmallLd;
         const int ncol = min(kSmallKC, H - ks * kSmallKC);
@@ -235,27 +259,27 @@ __global__ __launch_bounds__(32 * kRouterTok) void router_topk_kernel(
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
                           int* topk_idx, int* chunk_counts, const int* slot_of,
-                          const RouteMode& mode, bool topk, cudaStream_t st) {
+                          const RouteMode& mode, bool topk, cudaStream_t st, const RowNorm& nrm) {
     cudaError_t e;
     if (T <= kDecodeMaxT) {
         const size_t smem = sizeof(float) * static_cast<size_t>(H) * (1 + T);
         e = cudaFuncSetAttribute(router_logits_decode_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        router_logits_decode_kernel<<<E, 128, smem, st>>>(x, T, H, Wr, E, bias, logits);
+        router_logits_decode_kernel<<<E, 128, smem, st>>>(x, T, H, Wr, E, bias, logits, nrm);
     } else if (T <= kSmallMaxT) {
         const size_t smem = sizeof(float) * kSmallStages * (kSmallTT + kSmallTE) * kSmallLd;
         e = cudaFuncSetAttribute(router_logits_small_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         dim3 g((T + kSmallTT - 1) / kSmallTT, (E + kSmallTE - 1) / kSmallTE);
-        router_logits_small_kernel<<<g, 64, smem, st>>>(x, T, H, Wr, E, bias, logits);
+        router_logits_small_kernel<<<g, 64, smem, st>>>(x, T, H, Wr, E, bias, logits, nrm);
     } else {
         const size_t smem = sizeof(float) * kWStages * (kWTok + kWExp) * kLd;
         e = cudaFuncSetAttribute(router_logits_wide_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        router_logits_wide_kernel<<<(T + kWTok - 1) / kWTok, 128, smem, st>>>(x, T, H, Wr, E, bias, logits);
+        router_logits_wide_kernel<<<(T + kWTok - 1) / kWTok, 128, smem, st>>>(x, T, H, Wr, E, bias, logits, nrm);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess || !topk) return e;
