@@ -45,6 +45,7 @@ enum DevErr : int {
     DEVERR_TIMEOUT_EPILOGUE = 8,
     DEVERR_BAD_ITEM = 16,
     DEVERR_TIMEOUT_PEER = 32,  // a peer GPU's flag did not arrive in time
+    DEVERR_TIMEOUT_DECODE = 64,  // the one-kernel decode path: a counter did not arrive in time
 };
 
 // ------------------------------------------------------------------ PTX wrappers

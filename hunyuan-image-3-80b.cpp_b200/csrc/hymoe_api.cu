@@ -212,6 +212,13 @@ struct hymoe_ctx {
     size_t tmp_bytes = 0;
     GemmMaps maps_xp{}, maps_h{};
     GemvMaps gmaps_xp{}, gmaps_h{};
+    // One-kernel decode path (1..8 tokens on one GPU): its scratch, counters and maps.
+    bool dec_ok = false;
+    __half* dec_h = nullptr;   // [(el + 1) * 8, I]
+    __half* dec_yr = nullptr;  // [el * 8, H]
+    float* dec_ysh = nullptr;  // [8, H]
+    DecodeSync* dec_sync = nullptr;
+    DecodeMaps dec_maps{};
 
     float* bias_dev = nullptr;
     int4* segs = nullptr;
@@ -883,6 +890,31 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
     hymoe_status st = make_maps(c, &c->maps_xp, &c->gmaps_xp, c->xp, H, rows);
     if (st == HYMOE_OK) st = make_maps(c, &c->maps_h, &c->gmaps_h, c->hbuf, I, rows);
     if (st != HYMOE_OK) return bail(st);
+    {
+        // The one-kernel decode path: one GPU, a device that launches cooperative grids, and
+        // switched on by HYMOE_DECODE_FUSED=1 (default: off, the multi-kernel path serves every
+        // size; it is faster on the measured B200s until the one-kernel path's front end is
+        // hidden).
+        int coop = 0;
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, cfg->device);
+        const char* df = getenv("HYMOE_DECODE_FUSED");
+        const bool fused_on = df && strcmp(df, "1") == 0;
+        if (N == 1 && coop && fused_on && E <= kDecodeMaxE && H / kTileRows <= kDecodeMaxRb) {
+            const size_t hrows = static_cast<size_t>(el + 1) * 8;
+            A(dalloc(&c->dec_h, hrows * I));
+            A(dalloc(&c->dec_yr, static_cast<size_t>(el) * 8 * H));
+            A(dalloc(&c->dec_ysh, static_cast<size_t>(8) * H));
+            A(dalloc(&c->dec_sync, 1));
+            if (e == cudaSuccess) A(cudaMemset(c->dec_sync, 0, sizeof(DecodeSync)));
+            if (e == cudaSuccess) A(cudaMemset(c->dec_h, 0, sizeof(__half) * hrows * I));
+            if (e == cudaSuccess) A(cudaMemset(c->xp, 0, sizeof(__half) * 8 * H));
+            if (e != cudaSuccess) return bail(c->cuda_fail(e, "decode scratch allocation"));
+            c->dec_maps.x = c->gmaps_xp.x[0];  // rows 0..7 of xp, box {64, 8}
+            st = make_tmap(c, &c->dec_maps.h, c->dec_h, I, hrows, 8);
+            if (st != HYMOE_OK) return bail(st);
+            c->dec_ok = true;
+        }
+    }
     if (N > 1) {
         if (!cfg->nccl_unique_id) return bail(c->fail(HYMOE_ERR_INVALID_ARG, "ep_size > 1 needs nccl_unique_id"));
         if (const char* v = getenv("HYMOE_EP_TIMEOUT_S")) c->ep_timeout_s = atof(v);
@@ -959,6 +991,10 @@ void hymoe_destroy(hymoe_ctx* c) {
     cudaFree(c->items_dn);
     cudaFree(c->xp);
     cudaFree(c->hbuf);
+    cudaFree(c->dec_h);
+    cudaFree(c->dec_yr);
+    cudaFree(c->dec_ysh);
+    cudaFree(c->dec_sync);
     cudaFree(c->y);
     cudaFree(c->yr);
     cudaFree(c->tmp);
@@ -1420,7 +1456,10 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     if (c->loader.joinable()) {
         // An asynchronous load of this layer still in flight: the call's device work waits for it
         // (a wait in the stream's front end, no host wait); a finished load that failed fails the
-        // call.  Captured graphs are not given such a wait: the host waits for the load first.
+        // call.  Captured graphs are not given such a wait, and neither are host-pointer calls:
+        // their copies from pageable memory synchronise the stream on the host first, which
+        // must not depend on the loader thread making progress (its own pageable copies): the
+        // host waits for the load instead.
         uint32_t want = 0;
         bool finished = true;
         hymoe_status lst = HYMOE_OK;
@@ -1430,7 +1469,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             finished = c->done[layer] >= want;
             if (finished) lst = c->lstatus[layer];
         }
-        if (!finished && (flags & HYMOE_USE_GRAPH)) {
+        if (!finished && (flags & (HYMOE_USE_GRAPH | HYMOE_HOST_PTRS))) {
             lst = wait_loads(c, layer);
             finished = true;
         }
@@ -1586,6 +1625,62 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             c->phase_end(HYMOE_PHASE_ROUTER);
             nrm.rms = c->rms_buf;
             nrm.w = c->norm_w[layer];
+        }
+        // Debug outputs (the multi-kernel and the one-kernel paths alike).
+        auto debug_out = [&]() -> hymoe_status {
+            if (!dbg || T <= 0) return HYMOE_OK;
+            const cudaMemcpyKind kd = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+            if (dbg->topk_weights)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->topk_weights, c->topk_w, sizeof(float) * T * K, kd, st));
+            if (dbg->topk_indices) {
+                // slots back to expert ids, dropped-pair marks cleared (topk_idx is not read
+                // again in this call)
+                if (slot_of || c->route.drop)
+                    HY_CUDA(c, launch_unmap_slots(c->topk_idx, slot_of ? slot_of + E : nullptr,
+                                                  static_cast<int>(T * K), st));
+                HY_CUDA(c, cudaMemcpyAsync(dbg->topk_indices, c->topk_idx, sizeof(int) * T * K, kd, st));
+            }
+            if (host && dlog)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->router_logits, dlog, sizeof(float) * T * E, kd, st));
+            if (host && dprob)
+                HY_CUDA(c, cudaMemcpyAsync(dbg->router_probs, dprob, sizeof(float) * T * E, kd, st));
+            return HYMOE_OK;
+        };
+        // 1..8 tokens on one GPU (Q4_0 / Q8_0, no capacity drops): the whole block is one
+        // cooperative kernel (decode.cu), timed as the gate_up phase.
+        if (c->dec_ok && !ep && T >= 1 && T <= kDecodeMaxT && !c->route.drop &&
+            (L.wtype == W_Q4_0 || L.wtype == W_Q8_0) && K <= 8 && decode_smem(L.wtype, T, H, E) != 0) {
+            DecodeArgs da{};
+            da.x = dx;
+            da.nrm = nrm;
+            da.resid = dres;
+            da.out = dout;
+            da.T = T;
+            da.H = H;
+            da.I = I;
+            da.E = E;
+            da.K = K;
+            da.el = el;
+            da.Wr = L.router;
+            da.bias = dbias;
+            da.mode = c->route;
+            da.slot_of = slot_of;
+            da.gu = L.d_gu_ptrs;
+            da.dn = L.d_dn_ptrs;
+            da.logits = dlog ? dlog : c->logits;
+            da.probs = dprob;
+            da.topk_w = c->topk_w;
+            da.topk_idx = c->topk_idx;
+            da.xp = c->xp;
+            da.hb = c->dec_h;
+            da.ysh = c->dec_ysh;
+            da.yr = c->dec_yr;
+            da.sync = c->dec_sync;
+            da.err = c->err_word;
+            c->phase_begin();
+            HY_CUDA(c, launch_decode(c->dec_maps, da, L.wtype, c->n_sms, st));
+            c->phase_end(HYMOE_PHASE_GATE_UP);
+            return debug_out();
         }
         // Decode regime: every group has at most kGemvMaxRows rows (on one GPU a group has
         // at most T rows: the shared expert T, a routed expert at most one row per token).
@@ -1885,23 +1980,8 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             c->phase_begin();
             HY_CUDA(c, launch_combine(c->y, y_routed, c->slot_pos, c->topk_w, dres, dout, T, H, K, st));
             c->phase_end(HYMOE_PHASE_COMBINE);
-            if (dbg) {
-                const cudaMemcpyKind kd = host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
-                if (dbg->topk_weights)
-                    HY_CUDA(c, cudaMemcpyAsync(dbg->topk_weights, c->topk_w, sizeof(float) * T * K, kd, st));
-                if (dbg->topk_indices) {
-                    // slots back to expert ids, dropped-pair marks cleared (topk_idx is not read
-                    // again in this call)
-                    if (slot_of || c->route.drop)
-                        HY_CUDA(c, launch_unmap_slots(c->topk_idx, slot_of ? slot_of + E : nullptr,
-                                                      static_cast<int>(T * K), st));
-                    HY_CUDA(c, cudaMemcpyAsync(dbg->topk_indices, c->topk_idx, sizeof(int) * T * K, kd, st));
-                }
-                if (host && dlog)
-                    HY_CUDA(c, cudaMemcpyAsync(dbg->router_logits, dlog, sizeof(float) * T * E, kd, st));
-                if (host && dprob)
-                    HY_CUDA(c, cudaMemcpyAsync(dbg->router_probs, dprob, sizeof(float) * T * E, kd, st));
-            }
+            hymoe_status sd = debug_out();
+            if (sd != HYMOE_OK) return sd;
         }
         return HYMOE_OK;
     };

@@ -224,6 +224,58 @@ cudaError_t launch_gemv(const GemvMaps& maps, const int4* items, const int* n_it
                         void* out, int out_ld, __half* out_r, int shared_rows, int* err, int n_sms,
                         cudaStream_t st);
 
+// ---- decode.cu
+// The whole block for 1..8 tokens on one GPU (Q4_0 / Q8_0 weights) as one persistent
+// cooperative kernel: router chains, top-K and plan, the shared and routed experts' weight
+// streams and the combine, with device-side counters in place of kernel boundaries.
+constexpr int kDecodeMaxT = 8;
+constexpr int kDecodeMaxE = 64;
+constexpr int kDecodeMaxRb = 64;  // H / 128
+struct DecodeSync {               // zero between calls (the kernel's last CTA resets it)
+    uint32_t router_done;         // router CTAs finished
+    uint32_t xp_ready;            // the fp16 token rows are written
+    uint32_t plan_ready;          // top-K, weights and the active slots are published
+    uint32_t n_act;               // routed slots hit by the call
+    uint32_t exit_cnt;            // CTAs finished
+    uint32_t ticket;              // next list position to hand out
+    uint32_t pad[2];
+    uint32_t gu_done[kDecodeMaxE + 1];  // gate_up items done, per group (0: shared, 1 + j: routed)
+    uint32_t dn_done[kDecodeMaxRb];     // groups done, per down row block
+    int32_t act_slot[kDecodeMaxE];      // active routed index j -> placement slot
+    int32_t j_of[kDecodeMaxE];          // placement slot -> j (-1: not hit)
+};
+struct DecodeMaps {
+    CUtensorMap x;  // fp16 token rows (rows 0..7 used), box {64, 8}, SW128
+    CUtensorMap h;  // fp16 SwiGLU rows of group g at rows 8g..8g+7, box {64, 8}, SW128
+};
+struct DecodeArgs {
+    const float* x;         // [T, H]
+    RowNorm nrm;            // the pre-norm (rms == nullptr: none)
+    const float* resid;     // [T, H] or nullptr
+    float* out;             // [T, H]
+    int T, H, I, E, K, el;  // el: routed slots; the shared expert's tiles are group el
+    const float* Wr;        // [E, H] router
+    const float* bias;      // [E] or nullptr
+    RouteMode mode;
+    const int* slot_of;     // expert -> slot, or nullptr
+    const uint8_t* const* gu;  // [el + 1] gate_up tiles per slot (shared last)
+    const uint8_t* const* dn;  // [el + 1] down tiles
+    float* logits;          // [T, E]
+    float* probs;           // [T, E] or nullptr
+    float* topk_w;          // [T, K]
+    int* topk_idx;          // [T, K] (slots)
+    __half* xp;             // [>= 8, H] fp16 token rows (DecodeMaps::x)
+    __half* hb;             // [(el + 1) * 8, I] (DecodeMaps::h)
+    float* ysh;             // [8, H] shared expert's result
+    __half* yr;             // [el * 8, H] routed results, group 1 + j at rows 8j..8j+7
+    DecodeSync* sync;
+    int* err;
+};
+// Dynamic shared memory of the kernel (0: the shape does not fit it).
+size_t decode_smem(int wtype, int T, int H, int E);
+// cudaErrorNotSupported when the kernel cannot hold one CTA per SM (cooperative launch).
+cudaError_t launch_decode(const DecodeMaps& maps, const DecodeArgs& a, int wtype, int n_sms, cudaStream_t st);
+
 // ---- combine.cu
 // out[t] = resid[t] + y_shared[t] + sum_k w[t,k] * y_routed[slot_pos[t,k]] (routed rows fp16)
 cudaError_t launch_combine(const float* y_shared, const __half* y_routed, const int* slot_pos,
@@ -231,11 +283,8 @@ cudaError_t launch_combine(const float* y_shared, const __half* y_routed, const 
                            int K, cudaStream_t st);
 
 // ---- norm.cu
-// out = rms_norm_f32(x, w, eps) over T rows of H (H % 128 == 0), the reference's rounding.
-// Only the per-token factor rms[t] = 1 / sqrt(sum of squares / H + eps) (the same chain); the
-// consumers apply (x * rms) * w while reading x (RowNorm).
+// rms[t] = 1 / sqrt(sum of squares / H + eps) over T rows of H (H % 64 == 0), the reference's
+// rounding (rms_norm_f32's chain); the consumers apply (x * rms) * w while reading x (RowNorm).
 cudaError_t launch_rms(const float* x, float eps, int T, int H, float* rms, cudaStream_t st);
-cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int T, int H, float* out,
-                           cudaStream_t st);
 
 }  // namespace hymoe

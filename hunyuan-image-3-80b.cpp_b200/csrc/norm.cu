@@ -1,16 +1,20 @@
-// norm.cu — the decoder layer's post-attention RMSNorm ahead of the MoE block
-// (rms_norm_f32, src/rms_norm.cpp:9-33, applied at src/decoder_layer.cpp:34), with the
-// reference's rounding: each token's sum of squares is one sequential chain in column order
-// (every product rounded, then added: no fused multiply-add), rms = 1 / sqrt(sum / H + eps)
-// with IEEE-rounded division and square root, and out = (x * rms) * w[j] rounded left to right.
+// norm.cu — the per-token factor of the decoder layer's post-attention RMSNorm
+// (rms_norm_f32, src/rms_norm.cpp:9-33, applied at src/decoder_layer.cpp:34):
+//   rms[t] = 1 / sqrt(sum_j x[t,j]^2 / H + eps)
+// with the reference's rounding: the sum of squares is one sequential chain in column order
+// (every product rounded, then added: no fused multiply-add), then IEEE-rounded division and
+// square root.  The kernels that read the token rows (router, dispatch, expert-parallel sends)
+// apply (x * rms[t]) * w[j] as they load them (RowNorm), so the normalised rows are never
+// written: the norm costs one 4 * T * H byte read.
 //
-// The chain is inherently serial per token (H dependent adds), so tokens run in parallel: a CTA
-// owns 16 tokens, one chain per lane of its first half-warp, fed from shared memory.  All 256
-// threads copy 16 x 128-column chunks into a 4-stage ring with 16-byte cp.async (three chunks in
-// flight while the current one is summed); rows are padded to 132 floats so the chain lanes'
-// 16-byte reads hit distinct banks.  The normalised rows are then written by all threads, four
-// independent 16-byte loads in flight per thread (x re-read, mostly from L2).  HBM bound: 8 bytes
-// per element (x read once from HBM, out written).
+// The chain is serial per token (H dependent adds, ~4 cycles each), so its latency bounds the
+// kernel and tokens run in parallel: a CTA is ONE warp owning 32 tokens, a lane per token.  The
+// warp streams 64-column chunks of its 32 rows through an 8-stage cp.async ring (each copy
+// instruction covers 256 contiguous bytes of two rows: coalesced), waits with its own
+// cp.async groups plus a warp barrier (no CTA barrier), and each lane runs its token's chain
+// over the chunk.  Rows are padded to 68 floats so the lanes' 16-byte reads of 32 different
+// rows take the minimum 4 shared-memory wavefronts.  Seven chunks (61 KB) in flight per warp
+// keep its HBM stream ahead of the chain.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -19,112 +23,68 @@
 namespace hymoe {
 namespace {
 
-constexpr int kNormTok = 16;            // tokens per CTA
-constexpr int kNormCols = 128;          // columns per staged chunk
-constexpr int kNormLd = kNormCols + 4;  // padded row stride (floats)
-constexpr int kNormStages = 4;
-constexpr int kNormThreads = 256;
-constexpr int kNormCopies = kNormTok * kNormCols / 4 / kNormThreads;  // 16-byte copies per thread per chunk
-constexpr int kNormUnroll = 4;
+constexpr int kRmsTok = 32;             // tokens per CTA (one warp, a lane each)
+constexpr int kRmsCols = 64;            // columns per chunk
+constexpr int kRmsLd = kRmsCols + 4;    // padded row stride (floats)
+constexpr int kRmsStages = 8;
+constexpr int kRmsCopies = kRmsTok * kRmsCols / 4 / 32;  // 16-byte copies per lane per chunk (16)
+constexpr size_t kRmsSmem = sizeof(float) * kRmsStages * kRmsTok * kRmsLd;
 
-// out == nullptr: only the per-token factor, into rms_out[T] (the consumers apply it).
-__global__ __launch_bounds__(kNormThreads) void rmsnorm_kernel(const float* __restrict__ x,
-                                                               const float* __restrict__ w, float eps,
-                                                               int T, int H, float* __restrict__ out,
-                                                               float* __restrict__ rms_out) {
-    __shared__ __align__(16) float tile[kNormStages][kNormTok * kNormLd];
-    __shared__ float rms_s[kNormTok];
-    const int t0 = blockIdx.x * kNormTok;
-    const int tid = threadIdx.x;
-    const int n_chunks = H / kNormCols;
+__global__ __launch_bounds__(32) void rms_kernel(const float* __restrict__ x, float eps, int T, int H,
+                                                 float* __restrict__ rms) {
+    extern __shared__ float4 rms_smem4[];
+    float* tile = reinterpret_cast<float*>(rms_smem4);  // [stages][32 rows][kRmsLd]
+    const int lane = threadIdx.x;
+    const int t0 = blockIdx.x * kRmsTok;
+    const int n_chunks = H / kRmsCols;
+    // copy i of a chunk: rows 2i and 2i + 1, lanes 0-15 and 16-31, 16 bytes each
+    const int sub = lane >> 4, q = lane & 15;
     auto issue = [&](int c) {
-        float* dst = tile[c % kNormStages];
+        float* dst = tile + (c % kRmsStages) * kRmsTok * kRmsLd;
 #pragma unroll
-        for (int i = 0; i < kNormCopies; ++i) {
-            const int idx = tid + i * kNormThreads;
-            const int row = idx / (kNormCols / 4), q = idx % (kNormCols / 4);
+        for (int i = 0; i < kRmsCopies; ++i) {
+            const int row = 2 * i + sub;
             const int t = min(t0 + row, T - 1);  // rows past T copy a valid row; never written out
-            cp_async16(dst + row * kNormLd + 4 * q, x + static_cast<size_t>(t) * H + c * kNormCols + 4 * q);
+            cp_async16(dst + row * kRmsLd + 4 * q, x + static_cast<size_t>(t) * H + c * kRmsCols + 4 * q);
         }
     };
 #pragma unroll
-    for (int c = 0; c < kNormStages - 1; ++c) {
+    for (int c = 0; c < kRmsStages - 1; ++c) {
         if (c < n_chunks) issue(c);
         cp_async_commit();
     }
     float ss = 0.f;
     for (int c = 0; c < n_chunks; ++c) {
-        cp_async_wait<kNormStages - 2>();  // this thread's copies of chunk c have landed
-        // every thread's copies of chunk c have landed, and the chain lanes are done with chunk
-        // c-1, whose stage the next issue reuses
-        __syncthreads();
-        if (c + kNormStages - 1 < n_chunks) issue(c + kNormStages - 1);
+        cp_async_wait<kRmsStages - 2>();  // this lane's copies of chunk c have landed
+        // every lane's copies of chunk c have landed, and every lane is done with chunk c - 1,
+        // whose stage the next issue reuses
+        __syncwarp();
+        if (c + kRmsStages - 1 < n_chunks) issue(c + kRmsStages - 1);
         cp_async_commit();  // possibly empty: keeps the group count per iteration fixed
-        if (tid < kNormTok) {
-            const float* row = &tile[c % kNormStages][tid * kNormLd];
-#pragma unroll 8
-            for (int j = 0; j < kNormCols; j += 4) {
-                const float4 v = *reinterpret_cast<const float4*>(row + j);
-                ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
-                ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
-                ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
-                ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
-            }
+        const float* row = tile + (c % kRmsStages) * kRmsTok * kRmsLd + lane * kRmsLd;
+#pragma unroll
+        for (int j = 0; j < kRmsCols; j += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(row + j);
+            ss = __fadd_rn(ss, __fmul_rn(v.x, v.x));
+            ss = __fadd_rn(ss, __fmul_rn(v.y, v.y));
+            ss = __fadd_rn(ss, __fmul_rn(v.z, v.z));
+            ss = __fadd_rn(ss, __fmul_rn(v.w, v.w));
         }
     }
     cp_async_wait<0>();
-    if (tid < kNormTok)
-        rms_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(H)), eps)));
-    if (out == nullptr) {
-        if (tid < kNormTok && t0 + tid < T) rms_out[t0 + tid] = rms_s[tid];
-        return;
-    }
-    __syncthreads();
-    const int n4 = H / 4;
-    const int rows = min(kNormTok, T - t0);
-    const int total = rows * n4;
-    for (int base = tid; base < total; base += kNormUnroll * kNormThreads) {
-        float4 v[kNormUnroll], g[kNormUnroll];
-#pragma unroll
-        for (int u = 0; u < kNormUnroll; ++u) {
-            const int i = base + u * kNormThreads;
-            if (i < total) {
-                const int row = i / n4, q = i - row * n4;
-                v[u] = __ldg(reinterpret_cast<const float4*>(x + static_cast<size_t>(t0 + row) * H) + q);
-                g[u] = __ldg(reinterpret_cast<const float4*>(w) + q);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < kNormUnroll; ++u) {
-            const int i = base + u * kNormThreads;
-            if (i < total) {
-                const int row = i / n4, q = i - row * n4;
-                const float s = rms_s[row];
-                float4 o;
-                o.x = __fmul_rn(__fmul_rn(v[u].x, s), g[u].x);
-                o.y = __fmul_rn(__fmul_rn(v[u].y, s), g[u].y);
-                o.z = __fmul_rn(__fmul_rn(v[u].z, s), g[u].z);
-                o.w = __fmul_rn(__fmul_rn(v[u].w, s), g[u].w);
-                reinterpret_cast<float4*>(out + static_cast<size_t>(t0 + row) * H)[q] = o;
-            }
-        }
-    }
+    if (t0 + lane < T)
+        rms[t0 + lane] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(H)), eps)));
 }
 
 }  // namespace
 
-cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int T, int H, float* out,
-                           cudaStream_t st) {
-    if (T <= 0) return cudaSuccess;
-    if (H % kNormCols != 0) return cudaErrorInvalidValue;
-    rmsnorm_kernel<<<(T + kNormTok - 1) / kNormTok, kNormThreads, 0, st>>>(x, w, eps, T, H, out, nullptr);
-    return cudaGetLastError();
-}
-
 cudaError_t launch_rms(const float* x, float eps, int T, int H, float* rms, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    if (H % kNormCols != 0) return cudaErrorInvalidValue;
-    rmsnorm_kernel<<<(T + kNormTok - 1) / kNormTok, kNormThreads, 0, st>>>(x, nullptr, eps, T, H, nullptr, rms);
+    if (H % kRmsCols != 0) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(rms_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kRmsSmem));
+    if (e != cudaSuccess) return e;
+    rms_kernel<<<(T + kRmsTok - 1) / kRmsTok, 32, kRmsSmem, st>>>(x, eps, T, H, rms);
     return cudaGetLastError();
 }
 

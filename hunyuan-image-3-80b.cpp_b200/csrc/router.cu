@@ -27,39 +27,18 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "router_chain.cuh"
 #include "topk.cuh"
 
 namespace hymoe {
 
 namespace {
 
+using namespace rchain;
+
 constexpr int kKC = 128;    // columns per stage
 constexpr int kLd = kKC + 4;  // padded smem row (floats): 16-byte rows offset by 4 banks
-constexpr int kDecodeMaxT = 8;
 constexpr int kSmallMaxT = 64;
-
-// Two IEEE single-precision products, each rounded to nearest, in one packed instruction
-// (sm_100 f32x2): the same results as two __fmul_rn.
-__device__ __forceinline__ float2 mul2_rn(float ax, float ay, float bx, float by) {
-    unsigned long long a, b, p;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(ax), "f"(ay));
-    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(bx), "f"(by));
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(p) : "l"(a), "l"(b));
-    float2 r;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(p));
-    return r;
-}
-
-// acc + a.x*b.x + a.y*b.y + a.z*b.z + a.w*b.w, every product and sum separately rounded, in
-// that order (the reference's loop).
-__device__ __forceinline__ float chain4(float acc, float4 a, float4 b) {
-    const float2 p01 = mul2_rn(a.x, a.y, b.x, b.y);
-    const float2 p23 = mul2_rn(a.z, a.w, b.z, b.w);
-    acc = __fadd_rn(acc, p01.x);
-    acc = __fadd_rn(acc, p01.y);
-    acc = __fadd_rn(acc, p23.x);
-    return __fadd_rn(acc, p23.y);
-}
 
 // T > 64: CTA = 16 tokens (one dispatch chunk) x all E experts, 4 warps; warp w owns tokens
 // 4w..4w+3 and lane l experts l and l + 32 (8 independent chains per lane).  Token slabs are
@@ -68,17 +47,6 @@ __device__ __forceinline__ float chain4(float acc, float4 a, float4 b) {
 // 4096 tokens).
 constexpr int kWTok = 16, kWExp = 64, kWStages = 2;
 
-// Token rows normalised on the fly (RowNorm): each landed stage of the token slab is
-// normalised in place before the chains read it.
-__device__ __forceinline__ void norm_slab(float* xs, int rows, int cols, int ld, int t0, int T, int c0,
-                                          const RowNorm& nrm, int nthreads) {
-    for (int i = threadIdx.x; i < rows * cols; i += nthreads) {
-        const int r = i / cols, c = i - r * cols;
-        const float s = __ldg(nrm.rms + min(t0 + r, T - 1));
-        xs[r * ld + c] = __fmul_rn(__fmul_rn(xs[r * ld + c], s), __ldg(nrm.w + c0 + c));
-    }
-}
-
 __global__ __launch_bounds__(128) void router_logits_wide_kernel(
     const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
     const float* __restrict__ bias, float* __restrict__ logits, RowNorm nrm) {
@@ -86,9 +54,13 @@ __global__ __launch_bounds__(128) void router_logits_wide_kernel(
     float* sm = reinterpret_cast<float*>(rsm4);
     float* Xs = sm;
     float* Ws = sm + kWStages * kWTok * kLd;
+    float* Ns = Ws + kWStages * kWExp * kLd;  // [stages][kKC] norm weights of the stage's columns
+    __shared__ float rs[kWTok];                // the slab's per-token norm factors
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = blockIdx.x * kWTok;
     const int nst = H / kKC;
+    const bool norm = nrm.rms != nullptr;
+    if (norm && tid < kWTok) rs[tid] = nrm.rms[min(t0 + tid, T - 1)];
     auto load_stage = [&](int st, int ks) {
         float* xs = Xs + st * kWTok * kLd;
         float* ws = Ws + st * kWExp * kLd;
@@ -101,6 +73,7 @@ __global__ __launch_bounds__(128) void router_logits_wide_kernel(
             const int r = i / (kKC / 4), c = (i % (kKC / 4)) * 4;
             cp_async16(ws + r * kLd + c, Wr + static_cast<size_t>(r) * H + c0 + c);
         }
+        if (norm && tid < kKC / 4) cp_async16(Ns + st * kKC + 4 * tid, nrm.w + c0 + 4 * tid);
     };
     float acc[4][2];
 #pragma unroll
@@ -113,8 +86,8 @@ __global__ __launch_bounds__(128) void router_logits_wide_kernel(
         cp_async_wait<1>();
         __syncthreads();
         const int st = ks % kWStages;
-        if (nrm.rms != nullptr) {
-            norm_slab(Xs + st * kWTok * kLd, kWTok, kKC, kLd, t0, T, ks * kKC, nrm, 128);
+        if (norm) {
+            norm_slab(Xs + st * kWTok * kLd, kWTok, kKC, kLd, rs, Ns + st * kKC, 128);
             __syncthreads();
         }
         const float* xs = Xs + st * kWTok * kLd + (4 * warp) * kLd;
@@ -153,15 +126,22 @@ __global__ __launch_bounds__(128) void router_logits_decode_kernel(
     extern __shared__ float4 rsm4[];
     float* ws = reinterpret_cast<float*>(rsm4);  // [H]
     float* xs = ws + H;                           // [T][H]
+    float* ns = xs + static_cast<size_t>(T) * H;  // [H] norm weights (pre-norm calls)
+    __shared__ float rs[kDecodeMaxT];
     const int e = blockIdx.x;
+    const bool norm = nrm.rms != nullptr;
     for (int i = threadIdx.x * 4; i < H; i += 128 * 4)
         cp_async16(ws + i, Wr + static_cast<size_t>(e) * H + i);
     for (int i = threadIdx.x * 4; i < T * H; i += 128 * 4) cp_async16(xs + i, x + i);
+    if (norm) {
+        for (int i = threadIdx.x * 4; i < H; i += 128 * 4) cp_async16(ns + i, nrm.w + i);
+        if (threadIdx.x < T) rs[threadIdx.x] = nrm.rms[threadIdx.x];
+    }
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    if (nrm.rms != nullptr) {
-        norm_slab(xs, T, H, H, 0, T, 0, nrm, 128);
+    if (norm) {
+        norm_slab(xs, T, H, H, rs, ns, 128);
         __syncthreads();
     }
     const int t = threadIdx.x;
@@ -188,11 +168,15 @@ __global__ __launch_bounds__(64) void router_logits_small_kernel(
     float* sm = reinterpret_cast<float*>(rsm4);
     float* Xs = sm;                                 // [stages][kSmallTT][kSmallLd]
     float* Ws = sm + kSmallStages * kSmallTT * kSmallLd;      // [stages][kSmallTE][kSmallLd]
+    float* Ns = Ws + kSmallStages * kSmallTE * kSmallLd;      // [stages][kSmallKC] norm weights
+    __shared__ float rs[kSmallTT];
     const int tid = threadIdx.x;
     const int t0 = blockIdx.x * kSmallTT, e0 = blockIdx.y * kSmallTE;
     const int nt = min(kSmallTT, T - t0), ne = min(kSmallTE, E - e0);
     const int tt = tid / kSmallTE, ee = tid % kSmallTE;
     const int nst = (H + kSmallKC - 1) / kSmallKC;  // H is a multiple of 128
+    const bool norm = nrm.rms != nullptr;
+    if (norm && tid < kSmallTT) rs[tid] = nrm.rms[min(t0 + tid, T - 1)];
 
     auto load_stage = [&](int st, int ks) {
         float* xs = Xs + st * kSmallTT * kSmallLd;
@@ -206,6 +190,8 @@ __global__ __launch_bounds__(64) void router_logits_small_kernel(
             const int r = i / q, c = (i % q) * 4;
             cp_async16(ws + r * kSmallLd + c, Wr + static_cast<size_t>(e0 + r) * H + c0 + c);
         }
+        if (norm)
+            for (int i = tid; i < q; i += 64) cp_async16(Ns + st * kSmallKC + 4 * i, nrm.w + c0 + 4 * i);
     };
 
     float acc = 0.f;
@@ -220,9 +206,9 @@ __global__ __launch_bounds__(64) void router_logits_small_kernel(
         if (ks + kSmallStages - 1 < nst) load_stage((ks + kSmallStages - 1) % kSmallStages, ks + kSmallStages - 1);
         cp_async_commit();
         const int st = ks % kSmallStages;
-        if (nrm.rms != nullptr) {
-            norm_slab(Xs + st * kSmallTT * kSmallLd, nt, min(kSmallKC, H - ks * kSmallKC), kSmallLd, t0, T,
-                      ks * kSmallKC, nrm, 64);
+        if (norm) {
+            norm_slab(Xs + st * kSmallTT * kSmallLd, nt, min(kSmallKC, H - ks * kSmallKC), kSmallLd, rs,
+                      Ns + st * kSmallKC, 64);
             __syncthreads();
         }
         const float* xr = Xs + st * kSmallTT * kSmallLd + tt * kSmallLd;
@@ -262,20 +248,20 @@ cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, 
                           const RouteMode& mode, bool topk, cudaStream_t st, const RowNorm& nrm) {
     cudaError_t e;
     if (T <= kDecodeMaxT) {
-        const size_t smem = sizeof(float) * static_cast<size_t>(H) * (1 + T);
+        const size_t smem = sizeof(float) * static_cast<size_t>(H) * (2 + T);
         e = cudaFuncSetAttribute(router_logits_decode_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         router_logits_decode_kernel<<<E, 128, smem, st>>>(x, T, H, Wr, E, bias, logits, nrm);
     } else if (T <= kSmallMaxT) {
-        const size_t smem = sizeof(float) * kSmallStages * (kSmallTT + kSmallTE) * kSmallLd;
+        const size_t smem = sizeof(float) * kSmallStages * ((kSmallTT + kSmallTE) * kSmallLd + kSmallKC);
         e = cudaFuncSetAttribute(router_logits_small_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         dim3 g((T + kSmallTT - 1) / kSmallTT, (E + kSmallTE - 1) / kSmallTE);
         router_logits_small_kernel<<<g, 64, smem, st>>>(x, T, H, Wr, E, bias, logits, nrm);
     } else {
-        const size_t smem = sizeof(float) * kWStages * (kWTok + kWExp) * kLd;
+        const size_t smem = sizeof(float) * kWStages * ((kWTok + kWExp) * kLd + kKC);
         e = cudaFuncSetAttribute(router_logits_wide_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;

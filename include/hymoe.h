@@ -156,7 +156,10 @@ hymoe_status hymoe_load_layer(hymoe_ctx* ctx, uint32_t layer, const hymoe_tensor
  * call returns at once: a loader thread of the context copies them to the device and re-tiles
  * them on its own stream, in the order of the calls.  The host bytes must stay valid and
  * unchanged until hymoe_wait_layer(ctx, layer) returns.  hymoe_forward on this layer may follow
- * immediately: its device work waits for the load on the GPU (no host wait).  The slot is
+ * immediately: a device-pointer call's work waits for the load on the GPU (no host wait); a
+ * host-pointer or graph call waits on the host.  While a load is in flight, do not queue
+ * copies from pageable host memory on the stream of a device-pointer call that waits for it
+ * (such a copy first synchronises that stream on the host).  The slot is
  * rewritten only after every call already queued on the context's stream, so "load layer l+1
  * into the other slot, then run layer l" overlaps the two.  A failed load makes
  * hymoe_wait_layer and later hymoe_forward calls on that layer fail. */
