@@ -46,6 +46,7 @@ enum DevErr : int {
     DEVERR_BAD_ITEM = 16,
     DEVERR_TIMEOUT_PEER = 32,  // a peer GPU's flag did not arrive in time
     DEVERR_TIMEOUT_DECODE = 64,  // the one-kernel decode path: a counter did not arrive in time
+    DEVERR_SPEC_MISMATCH = 128,  // the certified routing pass disagreed with the chains (a defect)
 };
 
 // ------------------------------------------------------------------ PTX wrappers

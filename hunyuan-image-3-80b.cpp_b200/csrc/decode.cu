@@ -55,6 +55,12 @@ using namespace rchain;
 constexpr int kDThreads = 256, kDWarps = 8;
 constexpr int kDRedLd = 9;        // token pitch (floats) of the cross-warp partials
 constexpr int kDRouterCtas = 32;  // router CTAs (E / this many experts each)
+constexpr int kDSpecCtas = 32;    // CTAs of the certified routing pass
+// Certified selection: the K-th selected logit's lower bound must exceed every other expert's
+// upper bound by this much (covers the softmax's roundings, see certify_token) and lie within
+// this distance of the largest logit (probabilities stay normal numbers).
+constexpr double kSpecMargin = 3e-5;
+constexpr double kSpecRange = 80.0;
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
     uint32_t v;
@@ -115,7 +121,7 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
     float* red = reinterpret_cast<float*>(wbuf + kDWarps * R * TB);      // [8][128][kDRedLd]
     // The router CTAs stage their rows over the ring before it runs: the barriers live apart.
     __shared__ __align__(8) uint64_t bars[kDWarps * R];
-    __shared__ int s_abort, s_last, s_comb;
+    __shared__ int s_abort, s_last, s_comb, s_claim;
     __shared__ int s_pos[2];  // list positions (tickets) of the current and the next item
     __shared__ int s_cnt[kMaxE];
     __shared__ float s_rs[kDecodeMaxT];
@@ -133,6 +139,10 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
     const int epc = (E + n_router - 1) / n_router;
     const int router0 = G - n_router;      // router CTAs: [router0, G)
     const int xp_cta = NSH % router0;      // writes the fp16 token rows
+    // CTAs of the certified routing pass: [spec0, router0), below the router CTAs and above the
+    // fp16-row CTA (plain top-K only: the group-limited variants wait for the chains).
+    const int n_spec = a.mode.n_group > 0 ? 0 : max(0, min(kDSpecCtas, router0 - xp_cta - 1));
+    const int spec0 = router0 - n_spec;
 
     uint64_t* wb = bars + warp * R;
     uint8_t* wx = xbox + warp * R * 1024;
@@ -193,29 +203,217 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
                 topk_token(s_logit, warp, E, a.K, a.probs, a.topk_w, a.topk_idx, s_pbuf[warp], s_cnt, a.slot_of,
                            a.mode);
             __syncthreads();
-            if (warp == 0) {  // the routed slots hit, in slot order (el <= 64: two ballots)
-                int n = 0;
+            // The plan comes from here unless the certified pass has published it already; then
+            // the chains' selection must be the certified one.
+            if (tid == 0) s_claim = static_cast<int>(atomicCAS(&sy->plan_claim, 0u, 2u));
+            __syncthreads();
+            if (s_claim == 0) {
+                if (warp == 0) {  // the routed slots hit, in slot order (el <= 64: two ballots)
+                    int n = 0;
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int sl = lane + 32 * h;
-                    const bool hit = sl < a.el && s_cnt[sl] > 0;
-                    const unsigned b = __ballot_sync(0xffffffffu, hit);
-                    const int rank = n + __popc(b & ((1u << lane) - 1u));
-                    if (sl < a.el) {
-                        sy->j_of[sl] = hit ? rank : -1;
-                        if (hit) sy->act_slot[rank] = sl;
+                    for (int h = 0; h < 2; ++h) {
+                        const int sl = lane + 32 * h;
+                        const bool hit = sl < a.el && s_cnt[sl] > 0;
+                        const unsigned b = __ballot_sync(0xffffffffu, hit);
+                        const int rank = n + __popc(b & ((1u << lane) - 1u));
+                        if (sl < a.el) {
+                            sy->j_of[sl] = hit ? rank : -1;
+                            if (hit) sy->act_slot[rank] = sl;
+                        }
+                        n += __popc(b);
                     }
-                    n += __popc(b);
+                    if (lane == 0) sy->n_act = static_cast<uint32_t>(n);
+                    __syncwarp();
+                    // release of the warp's stores and (through the barrier) the top-K outputs
+                    if (lane == 0) st_release_gpu_u32(&sy->plan_ready, 1u);
                 }
-                if (lane == 0) sy->n_act = static_cast<uint32_t>(n);
-                __syncwarp();
-                // release of the warp's stores and (through the barrier) the top-K outputs
-                if (lane == 0) st_release_gpu_u32(&sy->plan_ready, 1u);
+            } else if (warp < T) {
+                // the certified pass published the plan (its masks happen before plan_ready)
+                bool ok = true;
+                if (lane == 0) ok = wait_geq(&sy->plan_ready, 1u, a.err);
+                if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+                    const int sl = lane < a.K ? __ldcg(a.topk_idx + warp * a.K + lane) : -1;
+                    uint64_t bit = sl >= 0 ? (1ull << sl) : 0ull;
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) bit |= __shfl_xor_sync(0xffffffffu, bit, o);
+                    if (lane == 0 && bit != __ldcg(reinterpret_cast<const unsigned long long*>(sy->spec_mask + warp)))
+                        atomicOr(a.err, DEVERR_SPEC_MISMATCH);
+                }
             }
+            __syncthreads();
+            if (tid == 0) st_release_gpu_u32(&sy->weights_ready, 1u);  // after every top-K store
         }
         // The staging area becomes the ring: order these generic accesses before the copies.
         fence_proxy_async_smem();
         __syncthreads();
+    }
+
+    // ---------------------------------------------------------------- certified routing
+    // Speculation without risk: every (token, expert) logit is computed in fp64 from the same
+    // rounded products the chain adds (x * w rounded to fp32; pre-norm rows normalised with the
+    // same roundings), together with a bound on how far the chain's recursive fp32 sum can lie
+    // from it: |chain - sum| <= u/(1-u) * sum_k |partial_k| (each rounding of an add is at most
+    // u times the rounded partial sum), the partial sums bounded by the fp64 prefix sums plus
+    // H*gamma_H*sum|p| (u = 2^-24, gamma_H = H u / (1 - H u)), plus one rounding of the bias add.
+    // A token whose K-th selected lower bound exceeds every other upper bound by kSpecMargin has
+    // the chains' selection for certain: softmax is monotone, and two logits that far apart
+    // (both within kSpecRange of the largest) keep distinct probabilities through fl(l - m), expf
+    // (2 ulp) and the division.  If every token is certified, the plan is published from here,
+    // long before the chains end; the chains then only supply the weights and their rank order
+    // (and check the selection).  A warp per (token, expert) pair, lanes over 32 column chunks.
+    if (cta >= spec0 && cta < router0) {
+        const int per = H / 32;  // columns per lane (H % 128 == 0)
+        const bool norm = a.nrm.rms != nullptr;
+        const int n_pairs = T * E, n_w = n_spec * kDWarps;
+        for (int pr = (cta - spec0) * kDWarps + warp; pr < n_pairs; pr += n_w) {
+            const int t = pr / E, e = pr - t * E;
+            const int c0 = lane * per;
+            const float* xr = a.x + static_cast<size_t>(t) * H + c0;
+            const float* wr = a.Wr + static_cast<size_t>(e) * H + c0;
+            const float rms = norm ? __ldg(a.nrm.rms + t) : 1.f;
+            auto prod4 = [&](int k, float (&p)[4]) {
+                float4 xv = __ldg(reinterpret_cast<const float4*>(xr + k));
+                const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + k));
+                if (norm) {
+                    const float4 g = __ldg(reinterpret_cast<const float4*>(a.nrm.w + c0 + k));
+                    xv = make_float4(__fmul_rn(__fmul_rn(xv.x, rms), g.x), __fmul_rn(__fmul_rn(xv.y, rms), g.y),
+                                     __fmul_rn(__fmul_rn(xv.z, rms), g.z), __fmul_rn(__fmul_rn(xv.w, rms), g.w));
+                }
+                p[0] = __fmul_rn(xv.x, wv.x);
+                p[1] = __fmul_rn(xv.y, wv.y);
+                p[2] = __fmul_rn(xv.z, wv.z);
+                p[3] = __fmul_rn(xv.w, wv.w);
+            };
+            double loc = 0.0, pabs = 0.0;
+            for (int k = 0; k < per; k += 4) {
+                float p[4];
+                prod4(k, p);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    loc += static_cast<double>(p[i]);
+                    pabs += fabs(static_cast<double>(p[i]));
+                }
+            }
+            double inc = loc;  // inclusive prefix of the chunk sums over lanes (column order)
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const double v = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += v;
+            }
+            double run = inc - loc, sabs = 0.0;
+            for (int k = 0; k < per; k += 4) {
+                float p[4];
+                prod4(k, p);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    run += static_cast<double>(p[i]);
+                    sabs += fabs(run);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                pabs += __shfl_xor_sync(0xffffffffu, pabs, o);
+                sabs += __shfl_xor_sync(0xffffffffu, sabs, o);
+            }
+            const double L = __shfl_sync(0xffffffffu, inc, 31);
+            int last = 0;
+            if (lane == 0) {
+                const double u = 5.9604644775390625e-8;  // 2^-24
+                const double gH = H * u / (1.0 - H * u);
+                const double bc = u / (1.0 - u) * (sabs + H * gH * pabs) + 1e-9 * (pabs + fabs(L));
+                const double lb = L + (a.bias != nullptr ? static_cast<double>(a.bias[e]) : 0.0);
+                sy->spec_lb[t * E + e] = lb;
+                sy->spec_bd[t * E + e] = bc + u * (fabs(lb) + bc) + 1e-12 * (fabs(lb) + 1.0);
+                last = atom_acq_rel_gpu_add(sy->spec_tok + t, 1u) == static_cast<uint32_t>(E - 1);
+            }
+            if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+            // This warp completed token t's bounds: certify its selection.
+            double lb0 = -1e300, lb1 = -1e300, bd0 = 0.0, bd1 = 0.0;
+            if (lane < E) {
+                lb0 = __ldcg(sy->spec_lb + t * E + lane);
+                bd0 = __ldcg(sy->spec_bd + t * E + lane);
+            }
+            if (lane + 32 < E) {
+                lb1 = __ldcg(sy->spec_lb + t * E + lane + 32);
+                bd1 = __ldcg(sy->spec_bd + t * E + lane + 32);
+            }
+            bool sel0 = false, sel1 = false;
+            for (int k = 0; k < a.K; ++k) {  // K rounds of arg-max, ties to the lower expert
+                double bv = -1e300;
+                int bi = 1 << 30;
+                if (!sel0 && lane < E) {
+                    bv = lb0;
+                    bi = lane;
+                }
+                if (!sel1 && lane + 32 < E && (lb1 > bv || bi == (1 << 30))) {
+                    bv = lb1;
+                    bi = lane + 32;
+                }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) {
+                    const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (ov > bv || (ov == bv && oi < bi)) {
+                        bv = ov;
+                        bi = oi;
+                    }
+                }
+                if (bi == lane) sel0 = true;
+                if (bi == lane + 32) sel1 = true;
+            }
+            double lo = 1e300, hi = -1e300, top = -1e300;
+            if (lane < E) {
+                top = lb0 + bd0;
+                if (sel0) lo = lb0 - bd0;
+                else hi = lb0 + bd0;
+            }
+            if (lane + 32 < E) {
+                top = fmax(top, lb1 + bd1);
+                if (sel1) lo = fmin(lo, lb1 - bd1);
+                else hi = fmax(hi, lb1 + bd1);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                lo = fmin(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+                hi = fmax(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+                top = fmax(top, __shfl_xor_sync(0xffffffffu, top, o));
+            }
+            const bool ok = lo - hi > kSpecMargin && lo - top > -kSpecRange;
+            uint64_t mask = 0;
+            if (sel0) mask |= 1ull << (a.slot_of != nullptr ? __ldg(a.slot_of + lane) : lane);
+            if (sel1) mask |= 1ull << (a.slot_of != nullptr ? __ldg(a.slot_of + lane + 32) : lane + 32);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mask |= __shfl_xor_sync(0xffffffffu, mask, o);
+            int all = 0;
+            if (lane == 0) {
+                sy->spec_mask[t] = mask;
+                if (!ok) atomicOr(&sy->spec_fail, 1u);
+                all = atom_acq_rel_gpu_add(&sy->spec_cert, 1u) == static_cast<uint32_t>(T - 1);
+                // every token decided, none failed, and the chains have not published yet
+                if (all) all = __ldcg(&sy->spec_fail) == 0 && atomicCAS(&sy->plan_claim, 0u, 1u) == 0u;
+            }
+            if (!__shfl_sync(0xffffffffu, all, 0)) continue;
+            // Publish the plan: the union of the certified selections, in slot order.
+            uint64_t uni = 0;
+            for (int tt = 0; tt < T; ++tt)
+                uni |= __ldcg(reinterpret_cast<const unsigned long long*>(sy->spec_mask + tt));
+            int n = 0;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int sl = lane + 32 * h;
+                const bool hit = sl < a.el && ((uni >> sl) & 1ull);
+                const unsigned b = __ballot_sync(0xffffffffu, hit);
+                const int rank = n + __popc(b & ((1u << lane) - 1u));
+                if (sl < a.el) {
+                    sy->j_of[sl] = hit ? rank : -1;
+                    if (hit) sy->act_slot[rank] = sl;
+                }
+                n += __popc(b);
+            }
+            if (lane == 0) sy->n_act = static_cast<uint32_t>(n);
+            __syncwarp();
+            if (lane == 0) st_release_gpu_u32(&sy->plan_ready, 1u);
+        }
     }
 
     // ---------------------------------------------------------------- fp16 token rows
@@ -444,15 +642,26 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
                 failed = true;
                 break;
             }
+            // The tile's words into registers, then the slot goes back to the copy engine
+            // (the next copy overlaps this tile's conversion and MMAs).
             const int s = cq % R;  // cq: lane 0's count, the same in every lane here
             const uint8_t* tile = ww + s * TB;
             uint32_t bx[2][2][2];
             x_frags<WT>(wx + s * 1024 + 128 * tok_b, tok_b & 7, c4, bx);
+            RawGroup<WT> raw[8];
+#pragma unroll
+            for (int g = 0; g < 8; ++g) tile_raw<WT>(tile, 16 * g + gq, c4, raw[g]);
+            __syncwarp();  // every lane has read the slot
+            ++cq;
+            if (lane == 0) {
+                poll_apply(pp, ptarget, pv);
+                top_up();
+            }
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
                 uint32_t af[2][2][4];
                 float d[2][2];
-                tile_frags<WT, false>(tile, 16 * g + gq, c4, af, d);
+                raw_frags<WT>(raw[g], af, d);
 #pragma unroll
                 for (int b = 0; b < 2; ++b) {
                     float blk[4] = {0.f, 0.f, 0.f, 0.f};
@@ -463,12 +672,6 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
                     acc[g][2] = fmaf(d[b][1], blk[2], acc[g][2]);
                     acc[g][3] = fmaf(d[b][1], blk[3], acc[g][3]);
                 }
-            }
-            __syncwarp();  // every lane is done with the slot
-            ++cq;
-            if (lane == 0) {
-                poll_apply(pp, ptarget, pv);
-                top_up();
             }
         }
         if (failed && lane == 0) s_abort = 1;
@@ -525,7 +728,11 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
         __syncthreads();
         if (s_abort) break;
         if (s_comb) {
-            // out = resid + (shared + sum_k w_k y_k), each step rounded (combine.cu's order).
+            // out = resid + (shared + sum_k w_k y_k), each step rounded (combine.cu's order).  The
+            // weights and their rank order come from the chains.
+            if (tid == 0 && !wait_geq(&sy->weights_ready, 1u, a.err)) s_abort = 1;
+            __syncthreads();
+            if (s_abort) break;
             const int K = a.K;
             for (int e = tid; e < kTileRows * T; e += kDThreads) {
                 const int r = e % kTileRows, t = e / kTileRows;
@@ -566,6 +773,11 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
             sy->plan_ready = 0;
             sy->n_act = 0;
             sy->ticket = 0;
+            sy->plan_claim = 0;
+            sy->weights_ready = 0;
+            sy->spec_cert = 0;
+            sy->spec_fail = 0;
+            for (int t = 0; t < kDecodeMaxT; ++t) sy->spec_tok[t] = 0;
             for (int g = 0; g <= a.el && g <= kDecodeMaxE; ++g) sy->gu_done[g] = 0;
             for (int rb = 0; rb < NDN; ++rb) sy->dn_done[rb] = 0;
             sy->exit_cnt = 0;

@@ -315,14 +315,24 @@ __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
                 failed = true;
                 break;
             }
+            // The tile's words into registers, then the slot goes back to the copy engine (the
+            // next copy overlaps this tile's conversion and MMAs).
             const uint8_t* tile = ww + slot * TB;
             uint32_t bx[2][2][2];
             x_frags<WT>(wx + slot * 1024 + 128 * tok_b, tok_b & 7, c, bx);
+            RawGroup<WT> raw[8];
+#pragma unroll
+            for (int g = 0; g < 8; ++g) tile_raw<WT>(tile, 16 * g + gq, c, raw[g]);
+            __syncwarp();  // every lane has read the slot
+            if (lane == 0) {
+                done = q + 1;
+                if (issued < total) issue(issued++);
+            }
 #pragma unroll
             for (int g = 0; g < 8; ++g) {
                 uint32_t a[2][2][4];
                 float d[2][2];
-                tile_frags<WT, false>(tile, 16 * g + gq, c, a, d);
+                raw_frags<WT>(raw[g], a, d);
 #pragma unroll
                 for (int b = 0; b < 2; ++b) {
                     float blk[4] = {0.f, 0.f, 0.f, 0.f};
@@ -333,11 +343,6 @@ __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
                     acc[g][2] = fmaf(d[b][1], blk[2], acc[g][2]);
                     acc[g][3] = fmaf(d[b][1], blk[3], acc[g][3]);
                 }
-            }
-            __syncwarp();  // every lane is done with the slot
-            if (lane == 0) {
-                done = q + 1;
-                if (issued < total) issue(issued++);
             }
         }
         if (failed && lane == 0) abort_flag = 1;

@@ -8,6 +8,8 @@
 // that the swizzled activation loads are free of bank conflicts too.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace hymoe {
@@ -112,6 +114,55 @@ __device__ __forceinline__ void tile_frags(const uint8_t* tile, int r0, int c, u
             d[0][1] = __low2float(s1); d[1][1] = __high2float(s1);
         }
     }
+}
+
+// The raw shared-memory words of one 16-row group of a Q4_0 / Q8_0 tile that tile_frags<WT, false>
+// reads (scales of rows r0 and r0 + 8, quants of both blocks), loaded first so that a caller can
+// hand the tile's buffer back to its copy engine before the conversion and the MMAs.
+template <int WT>
+struct RawGroup {
+    uint32_t s0, s1;                                            // block scales, rows r0 / r0 + 8
+    typename std::conditional<WT == W_Q8_0, uint2, uint32_t>::type v[2][2];  // [block][row r0 / r0 + 8]
+};
+
+template <int WT>
+__device__ __forceinline__ void tile_raw(const uint8_t* tile, int r0, int c, RawGroup<WT>& g) {
+    g.s0 = *reinterpret_cast<const uint32_t*>(tile + 4 * r0);
+    g.s1 = *reinterpret_cast<const uint32_t*>(tile + 4 * (r0 + 8));
+    const uint8_t* q = tile + 512;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        if constexpr (WT == W_Q8_0) {
+            g.v[b][0] = *reinterpret_cast<const uint2*>(q + 32 * (2 * r0 + b) + 8 * c);
+            g.v[b][1] = *reinterpret_cast<const uint2*>(q + 32 * (2 * (r0 + 8) + b) + 8 * c);
+        } else {
+            g.v[b][0] = *reinterpret_cast<const uint32_t*>(q + 16 * (2 * r0 + b) + 4 * c);
+            g.v[b][1] = *reinterpret_cast<const uint32_t*>(q + 16 * (2 * (r0 + 8) + b) + 4 * c);
+        }
+    }
+}
+
+// tile_frags<WT, false> from the raw words (the same fragments and scales).
+template <int WT>
+__device__ __forceinline__ void raw_frags(const RawGroup<WT>& g, uint32_t (&a)[2][2][4], float (&d)[2][2]) {
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        if constexpr (WT == W_Q8_0) {
+            q8x4_to_h2(g.v[b][0].x, a[b][0][0], a[b][0][2]);
+            q8x4_to_h2(g.v[b][0].y, a[b][1][0], a[b][1][2]);
+            q8x4_to_h2(g.v[b][1].x, a[b][0][1], a[b][0][3]);
+            q8x4_to_h2(g.v[b][1].y, a[b][1][1], a[b][1][3]);
+        } else {
+            uint32_t l0[2], h0[2], l1[2], h1[2];
+            q4x4_to_h2(g.v[b][0], l0, h0);
+            q4x4_to_h2(g.v[b][1], l1, h1);
+            a[b][0][0] = l0[0]; a[b][0][2] = l0[1]; a[b][0][1] = l1[0]; a[b][0][3] = l1[1];
+            a[b][1][0] = h0[0]; a[b][1][2] = h0[1]; a[b][1][1] = h1[0]; a[b][1][3] = h1[1];
+        }
+    }
+    const __half2 s0 = u2h(g.s0), s1 = u2h(g.s1);
+    d[0][0] = __low2float(s0); d[1][0] = __high2float(s0);
+    d[0][1] = __low2float(s1); d[1][1] = __high2float(s1);
 }
 
 // B fragments of one token row (128 bytes = 64 halves, 16-byte chunks swizzled by XOR with

@@ -1059,6 +1059,8 @@ hymoe_status hymoe_synchronize(hymoe_ctx* c) {
     if (word != 0) {
         cudaMemset(c->err_word, 0, sizeof(int));
         if (word & DEVERR_TIMEOUT_PEER) c->comm_broken = true;
+        if (word & DEVERR_SPEC_MISMATCH)
+            return c->fail(HYMOE_ERR_CUDA, "decode kernel: certified routing disagreed with the router (code 0x%x)", word);
         return c->fail(HYMOE_ERR_TIMEOUT, "device-side bounded wait expired (code 0x%x)", word);
     }
     return HYMOE_OK;

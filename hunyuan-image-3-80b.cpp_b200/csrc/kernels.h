@@ -238,11 +238,18 @@ struct DecodeSync {               // zero between calls (the kernel's last CTA r
     uint32_t n_act;               // routed slots hit by the call
     uint32_t exit_cnt;            // CTAs finished
     uint32_t ticket;              // next list position to hand out
-    uint32_t pad[2];
+    uint32_t plan_claim;          // who publishes the plan: 0 open, 1 the certified pass, 2 the chains
+    uint32_t weights_ready;       // the chains' top-K (weights, rank order) is published
+    uint32_t spec_cert;           // tokens the certified pass has decided
+    uint32_t spec_fail;           // a token whose selection it could not certify
+    uint32_t spec_tok[kDecodeMaxT];     // (token, expert) bounds done, per token
     uint32_t gu_done[kDecodeMaxE + 1];  // gate_up items done, per group (0: shared, 1 + j: routed)
     uint32_t dn_done[kDecodeMaxRb];     // groups done, per down row block
     int32_t act_slot[kDecodeMaxE];      // active routed index j -> placement slot
     int32_t j_of[kDecodeMaxE];          // placement slot -> j (-1: not hit)
+    uint64_t spec_mask[kDecodeMaxT];    // certified selection per token (bit = placement slot)
+    double spec_lb[kDecodeMaxT * kDecodeMaxE];  // fp64 logit + bias per (token, expert)
+    double spec_bd[kDecodeMaxT * kDecodeMaxE];  // bound on the chain's logit - spec_lb
 };
 struct DecodeMaps {
     CUtensorMap x;  // fp16 token rows (rows 0..7 used), box {64, 8}, SW128

@@ -15,8 +15,13 @@
 //     broadcast, router rows by conflict-free lane reads, 2 stages of 128 columns in shared
 //     memory (an earlier 16 x 32 tile with 4 chains per thread was shared-memory-latency
 //     bound: 163 us against 0.137 ms for this kernel plus the top-K at 4096 tokens).
-//   router_logits_small_kernel (8 < T <= 64): CTA = 8 tokens x 8 experts, one chain per
-//     thread, deeper ring: the latency-bound chains spread over many CTAs.
+//   router_logits_rows_kernel (8 < T <= 64): CTA = one warp owning 4 tokens x 8 experts, one
+//     chain per lane; its 12 rows are staged whole (4 column chunks of cp.async groups, the
+//     chains starting on the first), so only warp barriers interrupt the chains: the call is
+//     the chain's latency (~17 us at H = 4096) plus the first chunk's load.  An earlier
+//     8 x 8-thread CTA streaming 256-column stages through a 6-stage ring with a CTA barrier
+//     per stage took 40 us at 64 tokens.  router_logits_small_kernel keeps that form for
+//     hidden sizes whose rows do not fit in shared memory.
 //   router_logits_decode_kernel (T <= 8): CTA = one expert; its router row and the T
 //     token rows are staged in shared memory once, then T threads run their chains.
 // router_topk_kernel: one warp per token (16 tokens = one dispatch chunk per CTA): softmax
@@ -225,6 +230,69 @@ __global__ __launch_bounds__(64) void router_logits_small_kernel(
     }
 }
 
+// 8 < T <= 64: CTA = one warp, lane = 8 * token + expert over 4 tokens x 8 experts.  The warp's
+// 4 token rows and 8 router rows (rows padded by 4 floats: the 8 router rows' 16-byte lane reads
+// hit distinct banks) and the norm weights are staged whole in 4 column chunks, one cp.async
+// group each; each chunk is normalised (pre-norm calls) and chained as soon as it has landed.
+constexpr int kRowsTT = 4, kRowsTE = 8, kRowsChunks = 4;
+
+size_t rows_smem(int H) { return sizeof(float) * (static_cast<size_t>(kRowsTT + kRowsTE) * (H + 4) + H); }
+
+__global__ __launch_bounds__(32) void router_logits_rows_kernel(
+    const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
+    const float* __restrict__ bias, float* __restrict__ logits, RowNorm nrm) {
+    extern __shared__ float4 rsm4[];
+    const int ld = H + 4;
+    float* xs = reinterpret_cast<float*>(rsm4);  // [4][ld]
+    float* ws = xs + kRowsTT * ld;                // [8][ld]
+    float* ns = ws + kRowsTE * ld;                // [H]
+    __shared__ float rs[kRowsTT];
+    const int lane = threadIdx.x, tt = lane >> 3, ee = lane & 7;
+    const int t0 = blockIdx.x * kRowsTT, e0 = blockIdx.y * kRowsTE;
+    const int nt = min(kRowsTT, T - t0), ne = min(kRowsTE, E - e0);
+    const bool norm = nrm.rms != nullptr;
+    if (norm && lane < kRowsTT) rs[lane] = nrm.rms[min(t0 + lane, T - 1)];
+    const int cc = H / kRowsChunks;  // columns of a chunk
+#pragma unroll
+    for (int c = 0; c < kRowsChunks; ++c) {
+        const int c0 = c * cc;
+        for (int r = 0; r < nt; ++r) {
+            const float* src = x + static_cast<size_t>(t0 + r) * H;
+            for (int j = c0 + 4 * lane; j < c0 + cc; j += 128) cp_async16(xs + r * ld + j, src + j);
+        }
+        for (int r = 0; r < ne; ++r) {
+            const float* src = Wr + static_cast<size_t>(e0 + r) * H;
+            for (int j = c0 + 4 * lane; j < c0 + cc; j += 128) cp_async16(ws + r * ld + j, src + j);
+        }
+        if (norm)
+            for (int j = c0 + 4 * lane; j < c0 + cc; j += 128) cp_async16(ns + j, nrm.w + j);
+        cp_async_commit();
+    }
+    const float* xr = xs + tt * ld;
+    const float* wr = ws + ee * ld;
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < kRowsChunks; ++c) {
+        if (c == 0) cp_async_wait<kRowsChunks - 1>();
+        else if (c == 1) cp_async_wait<kRowsChunks - 2>();
+        else if (c == 2) cp_async_wait<kRowsChunks - 3>();
+        else cp_async_wait<0>();
+        __syncwarp();  // every lane's copies of chunk c are visible
+        const int c0 = c * cc;
+        if (norm) {
+            norm_slab(xs + c0, nt, cc, ld, rs, ns + c0, 32);
+            __syncwarp();
+        }
+#pragma unroll 8
+        for (int k = c0; k < c0 + cc; k += 4)
+            acc = chain4(acc, *reinterpret_cast<const float4*>(xr + k), *reinterpret_cast<const float4*>(wr + k));
+    }
+    if (tt < nt && ee < ne) {
+        const int t = t0 + tt, e = e0 + ee;
+        logits[static_cast<size_t>(t) * E + e] = bias != nullptr ? __fadd_rn(acc, bias[e]) : acc;
+    }
+}
+
 __global__ __launch_bounds__(32 * kRouterTok) void router_topk_kernel(
     const float* __restrict__ logits, int T, int E, int K, float* __restrict__ probs_out,
     float* __restrict__ topk_w, int* __restrict__ topk_idx, int* __restrict__ chunk_counts,
@@ -253,6 +321,13 @@ cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, 
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         router_logits_decode_kernel<<<E, 128, smem, st>>>(x, T, H, Wr, E, bias, logits, nrm);
+    } else if (T <= kSmallMaxT && H % (4 * kRowsChunks) == 0 && rows_smem(H) <= 227u * 1024u) {
+        const size_t smem = rows_smem(H);
+        e = cudaFuncSetAttribute(router_logits_rows_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        dim3 g((T + kRowsTT - 1) / kRowsTT, (E + kRowsTE - 1) / kRowsTE);
+        router_logits_rows_kernel<<<g, 32, smem, st>>>(x, T, H, Wr, E, bias, logits, nrm);
     } else if (T <= kSmallMaxT) {
         const size_t smem = sizeof(float) * kSmallStages * ((kSmallTT + kSmallTE) * kSmallLd + kSmallKC);
         e = cudaFuncSetAttribute(router_logits_small_kernel,

@@ -160,3 +160,24 @@ def test_full_shape_one_kernel_decode(orc, wt, T):
     bad, _ = topk_mismatches(got["idx"], o["idx"], logits, K)
     assert bad == 0
     assert rel_l2(got["out"], o["out"]) <= REL_L2_TOL
+
+
+def test_near_tie_falls_back_to_the_router_chains(orc):
+    """A router bias that puts the K-th and (K+1)-th logits of every token 1e-6 apart: the
+    one-kernel path's certified pass cannot decide those selections, so the plan comes from
+    the bit-exact chains; results still equal the multi-kernel path's bits.  A second call
+    without the bias (every token certified) gives the multi-kernel bits too."""
+    H, I, E, K, wt, T, seed = 512, 256, 64, 8, O.Q8_0, 1, 441
+    lay = host_layer(orc, seed, 0, H, I, E, wt)
+    x = O.synth_x(orc, seed, T, H)
+    logits = orc.router(x, lay["router"], K)[0][0].astype(np.float64)
+    order = np.argsort(-logits, kind="stable")
+    bias = np.zeros(E, np.float32)
+    bias[order[K]] = np.float32(logits[order[K - 1]] - logits[order[K]] - 1e-6)
+    fused, multi = _pair(H, I, E, K, T)
+    for m in (fused, multi):
+        _load(m, lay, wt)
+    _same(fused.forward_host(0, x, bias=bias, debug=True), multi.forward_host(0, x, bias=bias, debug=True))
+    _same(fused.forward_host(0, x, debug=True), multi.forward_host(0, x, debug=True))
+    fused.close()
+    multi.close()
