@@ -127,6 +127,11 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
     __shared__ float s_rs[kDecodeMaxT];
     __shared__ float s_pbuf[kDWarps][kMaxE];
     __shared__ float s_logit[kDecodeMaxT * kMaxE];
+    // The weight tile pointers of every slot and (per warp, once the plan is seen) the active
+    // slots: the issue path never waits on a global load for them.
+    __shared__ const uint8_t* s_wgu[kDecodeMaxE + 1];
+    __shared__ const uint8_t* s_wdn[kDecodeMaxE + 1];
+    __shared__ int s_act[kDWarps][kDecodeMaxE];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int gq = lane >> 2, c4 = lane & 3;
@@ -151,6 +156,10 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
         s_abort = 0;
         s_last = 0;
         s_comb = 0;
+    }
+    if (tid <= a.el) {
+        s_wgu[tid] = a.gu[tid];
+        s_wdn[tid] = a.dn[tid];
     }
     if (lane == 0)
         for (int r = 0; r < R; ++r) mbar_init(&wb[r], 1);
@@ -262,158 +271,182 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
     // long before the chains end; the chains then only supply the weights and their rank order
     // (and check the selection).  A warp per (token, expert) pair, lanes over 32 column chunks.
     if (cta >= spec0 && cta < router0) {
-        const int per = H / 32;  // columns per lane (H % 128 == 0)
+        // Unit = one token x 8 experts: the token row, the 8 router rows (and the norm weights)
+        // are staged in shared memory, then warp w takes expert e0 + w, lane l the columns
+        // [l * per, (l + 1) * per) in order.  Rows are padded by 4 floats after every per
+        // columns so that the lanes' chunk reads spread over the banks.
+        const int per = H / 32;                 // columns per lane (H % 128 == 0)
+        const int ldp = H + 128;                // padded row (floats)
         const bool norm = a.nrm.rms != nullptr;
-        const int n_pairs = T * E, n_w = n_spec * kDWarps;
-        for (int pr = (cta - spec0) * kDWarps + warp; pr < n_pairs; pr += n_w) {
-            const int t = pr / E, e = pr - t * E;
-            const int c0 = lane * per;
-            const float* xr = a.x + static_cast<size_t>(t) * H + c0;
-            const float* wr = a.Wr + static_cast<size_t>(e) * H + c0;
-            const float rms = norm ? __ldg(a.nrm.rms + t) : 1.f;
-            auto prod4 = [&](int k, float (&p)[4]) {
-                float4 xv = __ldg(reinterpret_cast<const float4*>(xr + k));
-                const float4 wv = __ldg(reinterpret_cast<const float4*>(wr + k));
-                if (norm) {
-                    const float4 g = __ldg(reinterpret_cast<const float4*>(a.nrm.w + c0 + k));
-                    xv = make_float4(__fmul_rn(__fmul_rn(xv.x, rms), g.x), __fmul_rn(__fmul_rn(xv.y, rms), g.y),
-                                     __fmul_rn(__fmul_rn(xv.z, rms), g.z), __fmul_rn(__fmul_rn(xv.w, rms), g.w));
-                }
-                p[0] = __fmul_rn(xv.x, wv.x);
-                p[1] = __fmul_rn(xv.y, wv.y);
-                p[2] = __fmul_rn(xv.z, wv.z);
-                p[3] = __fmul_rn(xv.w, wv.w);
-            };
-            double loc = 0.0, pabs = 0.0;
-            for (int k = 0; k < per; k += 4) {
-                float p[4];
-                prod4(k, p);
+        float* sx = reinterpret_cast<float*>(base);  // [ldp] token row
+        float* sw = sx + ldp;                        // [8][ldp] router rows
+        float* sn = sw + 8 * ldp;                    // [ldp] norm weights
+        const int egroups = (E + 7) / 8, n_units = T * egroups;
+        for (int un = cta - spec0; un < n_units; un += n_spec) {
+            const int t = un / egroups, e0 = (un - t * egroups) * 8, ne = min(8, E - e0);
+            for (int i = tid; i < H / 4; i += kDThreads) {
+                const int c = 4 * i, pc = c + 4 * (c / per);
+                cp_async16(sx + pc, a.x + static_cast<size_t>(t) * H + c);
+                if (norm) cp_async16(sn + pc, a.nrm.w + c);
+                for (int r = 0; r < ne; ++r) cp_async16(sw + r * ldp + pc, a.Wr + static_cast<size_t>(e0 + r) * H + c);
+            }
+            cp_async_commit();
+            cp_async_wait<0>();
+            __syncthreads();
+            if (warp < ne) {
+                const int e = e0 + warp;
+                const int cl = lane * (per + 4);  // this lane's chunk, padded
+                const float rms = norm ? __ldg(a.nrm.rms + t) : 1.f;
+                auto prod4 = [&](int k, float (&p)[4]) {
+                    float4 xv = *reinterpret_cast<const float4*>(sx + cl + k);
+                    const float4 wv = *reinterpret_cast<const float4*>(sw + warp * ldp + cl + k);
+                    if (norm) {
+                        const float4 g = *reinterpret_cast<const float4*>(sn + cl + k);
+                        xv = make_float4(__fmul_rn(__fmul_rn(xv.x, rms), g.x), __fmul_rn(__fmul_rn(xv.y, rms), g.y),
+                                         __fmul_rn(__fmul_rn(xv.z, rms), g.z), __fmul_rn(__fmul_rn(xv.w, rms), g.w));
+                    }
+                    p[0] = __fmul_rn(xv.x, wv.x);
+                    p[1] = __fmul_rn(xv.y, wv.y);
+                    p[2] = __fmul_rn(xv.z, wv.z);
+                    p[3] = __fmul_rn(xv.w, wv.w);
+                };
+                double loc = 0.0, pabs = 0.0;
+                for (int k = 0; k < per; k += 4) {
+                    float p[4];
+                    prod4(k, p);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    loc += static_cast<double>(p[i]);
-                    pabs += fabs(static_cast<double>(p[i]));
+                    for (int i = 0; i < 4; ++i) {
+                        loc += static_cast<double>(p[i]);
+                        pabs += fabs(static_cast<double>(p[i]));
+                    }
                 }
-            }
-            double inc = loc;  // inclusive prefix of the chunk sums over lanes (column order)
+                double inc = loc;  // inclusive prefix of the chunk sums over lanes (column order)
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const double v = __shfl_up_sync(0xffffffffu, inc, o);
-                if (lane >= o) inc += v;
-            }
-            double run = inc - loc, sabs = 0.0;
-            for (int k = 0; k < per; k += 4) {
-                float p[4];
-                prod4(k, p);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    run += static_cast<double>(p[i]);
-                    sabs += fabs(run);
+                for (int o = 1; o < 32; o <<= 1) {
+                    const double v = __shfl_up_sync(0xffffffffu, inc, o);
+                    if (lane >= o) inc += v;
                 }
-            }
+                double run = inc - loc, sabs = 0.0;
+                for (int k = 0; k < per; k += 4) {
+                    float p[4];
+                    prod4(k, p);
 #pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                pabs += __shfl_xor_sync(0xffffffffu, pabs, o);
-                sabs += __shfl_xor_sync(0xffffffffu, sabs, o);
-            }
-            const double L = __shfl_sync(0xffffffffu, inc, 31);
-            int last = 0;
-            if (lane == 0) {
-                const double u = 5.9604644775390625e-8;  // 2^-24
-                const double gH = H * u / (1.0 - H * u);
-                const double bc = u / (1.0 - u) * (sabs + H * gH * pabs) + 1e-9 * (pabs + fabs(L));
-                const double lb = L + (a.bias != nullptr ? static_cast<double>(a.bias[e]) : 0.0);
-                sy->spec_lb[t * E + e] = lb;
-                sy->spec_bd[t * E + e] = bc + u * (fabs(lb) + bc) + 1e-12 * (fabs(lb) + 1.0);
-                last = atom_acq_rel_gpu_add(sy->spec_tok + t, 1u) == static_cast<uint32_t>(E - 1);
-            }
-            if (!__shfl_sync(0xffffffffu, last, 0)) continue;
-            // This warp completed token t's bounds: certify its selection.
-            double lb0 = -1e300, lb1 = -1e300, bd0 = 0.0, bd1 = 0.0;
-            if (lane < E) {
-                lb0 = __ldcg(sy->spec_lb + t * E + lane);
-                bd0 = __ldcg(sy->spec_bd + t * E + lane);
-            }
-            if (lane + 32 < E) {
-                lb1 = __ldcg(sy->spec_lb + t * E + lane + 32);
-                bd1 = __ldcg(sy->spec_bd + t * E + lane + 32);
-            }
-            bool sel0 = false, sel1 = false;
-            for (int k = 0; k < a.K; ++k) {  // K rounds of arg-max, ties to the lower expert
-                double bv = -1e300;
-                int bi = 1 << 30;
-                if (!sel0 && lane < E) {
-                    bv = lb0;
-                    bi = lane;
-                }
-                if (!sel1 && lane + 32 < E && (lb1 > bv || bi == (1 << 30))) {
-                    bv = lb1;
-                    bi = lane + 32;
+                    for (int i = 0; i < 4; ++i) {
+                        run += static_cast<double>(p[i]);
+                        sabs += fabs(run);
+                    }
                 }
 #pragma unroll
                 for (int o = 16; o; o >>= 1) {
-                    const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    if (ov > bv || (ov == bv && oi < bi)) {
-                        bv = ov;
-                        bi = oi;
+                    pabs += __shfl_xor_sync(0xffffffffu, pabs, o);
+                    sabs += __shfl_xor_sync(0xffffffffu, sabs, o);
+                }
+                const double L = __shfl_sync(0xffffffffu, inc, 31);
+                int last = 0;
+                if (lane == 0) {
+                    const double u = 5.9604644775390625e-8;  // 2^-24
+                    const double gH = H * u / (1.0 - H * u);
+                    const double bc = u / (1.0 - u) * (sabs + H * gH * pabs) + 1e-9 * (pabs + fabs(L));
+                    const double lb = L + (a.bias != nullptr ? static_cast<double>(a.bias[e]) : 0.0);
+                    sy->spec_lb[t * E + e] = lb;
+                    sy->spec_bd[t * E + e] = bc + u * (fabs(lb) + bc) + 1e-12 * (fabs(lb) + 1.0);
+                    last = atom_acq_rel_gpu_add(sy->spec_tok + t, 1u) == static_cast<uint32_t>(E - 1);
+                }
+                if (__shfl_sync(0xffffffffu, last, 0)) {
+                    // This warp completed token t's bounds: certify its selection.
+                    double lb0 = -1e300, lb1 = -1e300, bd0 = 0.0, bd1 = 0.0;
+                    if (lane < E) {
+                        lb0 = __ldcg(sy->spec_lb + t * E + lane);
+                        bd0 = __ldcg(sy->spec_bd + t * E + lane);
+                    }
+                    if (lane + 32 < E) {
+                        lb1 = __ldcg(sy->spec_lb + t * E + lane + 32);
+                        bd1 = __ldcg(sy->spec_bd + t * E + lane + 32);
+                    }
+                    bool sel0 = false, sel1 = false;
+                    for (int k = 0; k < a.K; ++k) {  // K rounds of arg-max, ties to the lower expert
+                        double bv = -1e300;
+                        int bi = 1 << 30;
+                        if (!sel0 && lane < E) {
+                            bv = lb0;
+                            bi = lane;
+                        }
+                        if (!sel1 && lane + 32 < E && (lb1 > bv || bi == (1 << 30))) {
+                            bv = lb1;
+                            bi = lane + 32;
+                        }
+#pragma unroll
+                        for (int o = 16; o; o >>= 1) {
+                            const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                            if (ov > bv || (ov == bv && oi < bi)) {
+                                bv = ov;
+                                bi = oi;
+                            }
+                        }
+                        if (bi == lane) sel0 = true;
+                        if (bi == lane + 32) sel1 = true;
+                    }
+                    double lo = 1e300, hi = -1e300, top = -1e300;
+                    if (lane < E) {
+                        top = lb0 + bd0;
+                        if (sel0) lo = lb0 - bd0;
+                        else hi = lb0 + bd0;
+                    }
+                    if (lane + 32 < E) {
+                        top = fmax(top, lb1 + bd1);
+                        if (sel1) lo = fmin(lo, lb1 - bd1);
+                        else hi = fmax(hi, lb1 + bd1);
+                    }
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) {
+                        lo = fmin(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+                        hi = fmax(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+                        top = fmax(top, __shfl_xor_sync(0xffffffffu, top, o));
+                    }
+                    const bool ok = lo - hi > kSpecMargin && lo - top > -kSpecRange;
+                    uint64_t mask = 0;
+                    if (sel0) mask |= 1ull << (a.slot_of != nullptr ? __ldg(a.slot_of + lane) : lane);
+                    if (sel1) mask |= 1ull << (a.slot_of != nullptr ? __ldg(a.slot_of + lane + 32) : lane + 32);
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) mask |= __shfl_xor_sync(0xffffffffu, mask, o);
+                    int all = 0;
+                    if (lane == 0) {
+                        sy->spec_mask[t] = mask;
+                        if (!ok) atomicOr(&sy->spec_fail, 1u);
+                        all = atom_acq_rel_gpu_add(&sy->spec_cert, 1u) == static_cast<uint32_t>(T - 1);
+                        // every token decided, none failed, and the chains have not published yet
+                        if (all) all = __ldcg(&sy->spec_fail) == 0 && atomicCAS(&sy->plan_claim, 0u, 1u) == 0u;
+                    }
+                    if (__shfl_sync(0xffffffffu, all, 0)) {
+                        // Publish the plan: the union of the certified selections, in slot order.
+                        uint64_t uni = 0;
+                        for (int tt = 0; tt < T; ++tt)
+                            uni |= __ldcg(reinterpret_cast<const unsigned long long*>(sy->spec_mask + tt));
+                        int n = 0;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int sl = lane + 32 * h;
+                            const bool hit = sl < a.el && ((uni >> sl) & 1ull);
+                            const unsigned b = __ballot_sync(0xffffffffu, hit);
+                            const int rank = n + __popc(b & ((1u << lane) - 1u));
+                            if (sl < a.el) {
+                                sy->j_of[sl] = hit ? rank : -1;
+                                if (hit) sy->act_slot[rank] = sl;
+                            }
+                            n += __popc(b);
+                        }
+                        if (lane == 0) sy->n_act = static_cast<uint32_t>(n);
+                        __syncwarp();
+                        if (lane == 0) st_release_gpu_u32(&sy->plan_ready, 1u);
                     }
                 }
-                if (bi == lane) sel0 = true;
-                if (bi == lane + 32) sel1 = true;
             }
-            double lo = 1e300, hi = -1e300, top = -1e300;
-            if (lane < E) {
-                top = lb0 + bd0;
-                if (sel0) lo = lb0 - bd0;
-                else hi = lb0 + bd0;
-            }
-            if (lane + 32 < E) {
-                top = fmax(top, lb1 + bd1);
-                if (sel1) lo = fmin(lo, lb1 - bd1);
-                else hi = fmax(hi, lb1 + bd1);
-            }
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                lo = fmin(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-                hi = fmax(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-                top = fmax(top, __shfl_xor_sync(0xffffffffu, top, o));
-            }
-            const bool ok = lo - hi > kSpecMargin && lo - top > -kSpecRange;
-            uint64_t mask = 0;
-            if (sel0) mask |= 1ull << (a.slot_of != nullptr ? __ldg(a.slot_of + lane) : lane);
-            if (sel1) mask |= 1ull << (a.slot_of != nullptr ? __ldg(a.slot_of + lane + 32) : lane + 32);
-#pragma unroll
-            for (int o = 16; o; o >>= 1) mask |= __shfl_xor_sync(0xffffffffu, mask, o);
-            int all = 0;
-            if (lane == 0) {
-                sy->spec_mask[t] = mask;
-                if (!ok) atomicOr(&sy->spec_fail, 1u);
-                all = atom_acq_rel_gpu_add(&sy->spec_cert, 1u) == static_cast<uint32_t>(T - 1);
-                // every token decided, none failed, and the chains have not published yet
-                if (all) all = __ldcg(&sy->spec_fail) == 0 && atomicCAS(&sy->plan_claim, 0u, 1u) == 0u;
-            }
-            if (!__shfl_sync(0xffffffffu, all, 0)) continue;
-            // Publish the plan: the union of the certified selections, in slot order.
-            uint64_t uni = 0;
-            for (int tt = 0; tt < T; ++tt)
-                uni |= __ldcg(reinterpret_cast<const unsigned long long*>(sy->spec_mask + tt));
-            int n = 0;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int sl = lane + 32 * h;
-                const bool hit = sl < a.el && ((uni >> sl) & 1ull);
-                const unsigned b = __ballot_sync(0xffffffffu, hit);
-                const int rank = n + __popc(b & ((1u << lane) - 1u));
-                if (sl < a.el) {
-                    sy->j_of[sl] = hit ? rank : -1;
-                    if (hit) sy->act_slot[rank] = sl;
-                }
-                n += __popc(b);
-            }
-            if (lane == 0) sy->n_act = static_cast<uint32_t>(n);
-            __syncwarp();
-            if (lane == 0) st_release_gpu_u32(&sy->plan_ready, 1u);
+            __syncthreads();  // the staged rows are reused by the next unit
         }
+        // The staging area becomes the ring: order these generic accesses before the copies.
+        fence_proxy_async_smem();
+        __syncthreads();
     }
 
     // ---------------------------------------------------------------- fp16 token rows
@@ -455,7 +488,8 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
     };
     int n_act = -1;
     bool xp_ok = false;
-    int gu_ok_g = -1;
+    bool sh_ok = false;  // the shared expert's gate_up items are known to be done
+    uint64_t gu_ok = 0;  // routed groups known done: bit g - 1 for group g (1..64)
     int wq = 0, xq = 0, cq = 0;
     Cur wc{0, 0, 0, -1, {0, 0, 0}, nullptr};
     Cur xc = wc;
@@ -512,6 +546,7 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
     };
     auto take_plan = [&]() {
         n_act = static_cast<int>(__ldcg(reinterpret_cast<const int*>(&sy->n_act)));
+        for (int j = 0; j < n_act; ++j) s_act[warp][j] = __ldcg(sy->act_slot + j);
         if (wc.state < 0) resolve(wc);
         if (xc.state < 0) resolve(xc);
     };
@@ -524,9 +559,9 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
     // Weights of the weight cursor's tile into its slot (known item, free slot).
     auto issue_w = [&]() {
         if (wc.w == nullptr) {
-            const int slot = wc.it.g == 0 ? a.el : __ldcg(sy->act_slot + wc.it.g - 1);
+            const int slot = wc.it.g == 0 ? a.el : s_act[warp][wc.it.g - 1];
             const int nks = wc.it.kind ? ks_dn : ks_gu;
-            wc.w = (wc.it.kind ? a.dn[slot] : a.gu[slot]) + static_cast<size_t>(wc.it.rb) * nks * TB;
+            wc.w = (wc.it.kind ? s_wdn[slot] : s_wgu[slot]) + static_cast<size_t>(wc.it.rb) * nks * TB;
         }
         const int s = wq % R, k = warp + kDWarps * wc.m;
         mbar_arrive_expect_tx(&wb[s], TB + 1024u);
@@ -534,7 +569,9 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
         ++wq;
         advance(wc);
     };
-    auto x_ready = [&](const Item& it) { return it.kind == 0 ? xp_ok : gu_ok_g == it.g; };
+    auto x_ready = [&](const Item& it) {
+        return it.kind == 0 ? xp_ok : it.g == 0 ? sh_ok : ((gu_ok >> (it.g - 1)) & 1ull) != 0;
+    };
     // Activation box of the activation cursor's tile (its weights are issued: xq < wq): 1 issued,
     // 0 its producer has not published it yet (as far as this lane knows), -1 a blocking wait
     // failed.  force: issue without the check (only to let a barrier complete before an early
@@ -548,7 +585,8 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
                 xp_ok = true;
             } else {
                 if (!wait_geq(sy->gu_done + it.g, static_cast<uint32_t>(NGU), a.err)) return -1;
-                gu_ok_g = it.g;
+                if (it.g == 0) sh_ok = true;
+                else gu_ok |= 1ull << (it.g - 1);
             }
             fence_proxy_async_global();  // the producers' generic stores before this lane's TMA reads
         }
@@ -586,7 +624,8 @@ __global__ __launch_bounds__(kDThreads, 1) void decode_kernel(const __grid_const
             return;
         }
         if (p == &sy->xp_ready) xp_ok = true;
-        else gu_ok_g = static_cast<int>(p - sy->gu_done);
+        else if (p == sy->gu_done) sh_ok = true;
+        else gu_ok |= 1ull << static_cast<int>(p - sy->gu_done - 1);
         fence_proxy_async_global();  // the producers' generic stores before this lane's TMA reads
     };
 
@@ -825,7 +864,9 @@ size_t decode_smem(int wtype, int T, int H, int E) {
     const int n_router = E < kDRouterCtas ? E : kDRouterCtas;
     const int epc = (E + n_router - 1) / n_router;
     const size_t router = sizeof(float) * static_cast<size_t>(epc + T + 1) * H;
-    const size_t need = 1024 + (ring > router ? ring : router);
+    const size_t spec = sizeof(float) * 10u * static_cast<size_t>(H + 128);
+    size_t need = ring > router ? ring : router;
+    need = 1024 + (need > spec ? need : spec);
     return need <= 227u * 1024u ? need : 0;
 }
 
