@@ -510,8 +510,12 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
         }
     } else if (!EP || warp < 14) {
         // ------------------------------------------------------------ dequantisers
-        // Two groups of four warps take alternate stages, so two stages are converted
-        // concurrently; each thread converts entries e and e + 128 of its stage.
+        // Two groups of four warps take alternate stage slots (slot s to group s & 1), so two
+        // stages are converted concurrently; each thread converts entries e and e + 128 of its
+        // stage.  Each slot belongs to one group, which therefore waits for the slot's phases
+        // strictly in order (with an odd slot count, a split by iteration parity would let
+        // both groups use every slot, and a group two phases ahead would pass the parity wait
+        // of a phase that has not completed).
         const int dq = tid - 192;  // 0..255
         const uint32_t grp = static_cast<uint32_t>(dq >> 7);
         const int e = dq & 127;
@@ -521,7 +525,7 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
             const int4 item = a.items[w];
             const bool has_tile = 2 * item.y + static_cast<int>(rank) < a.n_rb;
             for (int ks = 0; ks < a.n_ks; ++ks, ++it) {
-                if ((it & 1u) != grp) continue;
+                if ((static_cast<uint32_t>(it % STAGES) & 1u) != grp) continue;
                 const int s = it % STAGES;
                 const uint32_t ph = (it / STAGES) & 1;
                 if (!mbar_wait(&full[s], ph, err, DEVERR_TIMEOUT_DEQUANT)) {

@@ -58,3 +58,4 @@ def test_items_cover_every_tile_once_and_each_pair_walks_forward(seed):
             _, seq = deal(len(items), ncl)
             for ws in seq.values():
                 assert ws == sorted(ws)
+
