@@ -311,16 +311,45 @@ __global__ void unmap_slots_kernel(int* __restrict__ idx, const int* __restrict_
 // k-major priorities (one CTA of 1024 threads).  For each choice k, tokens in blocks of 1024:
 // a lane's rank among its warp's lanes of the same slot (warp match), plus the counts of the
 // same slot in earlier warps of the block, plus the slot's running count over earlier blocks
-// and earlier choices.
+// and earlier choices.  Over an expert-parallel job (recs != nullptr) the running count of
+// choice k starts at the job's pairs of earlier choices plus earlier ranks' pairs of choice k
+// (the job's tokens are rank 0's, then rank 1's, ...), and the capacity comes from the job's
+// token count.
 __global__ __launch_bounds__(1024) void capacity_kernel(int* __restrict__ topk_idx, float* __restrict__ topk_w,
                                                         int* __restrict__ chunk_counts, int T, int K, int E,
-                                                        int capacity) {
+                                                        int capacity, const int* __restrict__ recs, int N, int me,
+                                                        float cf, int min_capacity) {
     __shared__ int run[kMaxE];
     __shared__ int wcnt[32][kMaxE];
+    __shared__ int cap_s;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rl = ep_choice_rec(E);
     if (tid < kMaxE) run[tid] = 0;
+    if (tid == 0) {
+        int cap = capacity;
+        if (recs != nullptr) {
+            int t_job = 0;
+            for (int r = 0; r < N; ++r) t_job += recs[r * rl + kEpMaxK * E];
+            const float f = __fdiv_rn(__fmul_rn(__fmul_rn(cf, static_cast<float>(K)), static_cast<float>(t_job)),
+                                      static_cast<float>(E));
+            const uint32_t fu = f >= 4294967296.f ? 0xffffffffu : static_cast<uint32_t>(f);
+            cap = max(max(static_cast<int>(min(fu, 1u << 30)), K), min_capacity);
+        }
+        cap_s = cap;
+    }
+    __syncthreads();
+    const int cap = cap_s;
     const unsigned lt = (1u << lane) - 1u;
     for (int k = 0; k < K; ++k) {
+        if (recs != nullptr && tid < E) {
+            int b = 0;
+            for (int r = 0; r < N; ++r) {
+                for (int k2 = 0; k2 < k; ++k2) b += recs[r * rl + k2 * E + tid];
+                if (r < me) b += recs[r * rl + k * E + tid];
+            }
+            run[tid] = b;
+        }
+        __syncthreads();
         for (int t0 = 0; t0 < T; t0 += 1024) {
             const int t = t0 + tid;
             const bool valid = t < T;
@@ -340,12 +369,12 @@ __global__ __launch_bounds__(1024) void capacity_kernel(int* __restrict__ topk_i
                 run[tid] = acc;
             }
             __syncthreads();
-            if (valid && wcnt[warp][slot] + __popc(peers & lt) >= capacity) {
+            if (valid && wcnt[warp][slot] + __popc(peers & lt) >= cap) {
                 topk_idx[t * K + k] = slot | kDroppedPair;
                 topk_w[t * K + k] = 0.f;
                 atomicSub(chunk_counts + static_cast<size_t>(t / kRouterTok) * E + slot, 1);
             }
-            __syncthreads();  // wcnt is rewritten by the next block
+            __syncthreads();  // wcnt (and run, next choice) are rewritten
         }
     }
 }
@@ -373,7 +402,15 @@ cudaError_t launch_capacity(int* topk_idx, float* topk_w, int* chunk_counts, int
                             cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
     if (E > kMaxE) return cudaErrorInvalidValue;
-    capacity_kernel<<<1, 1024, 0, st>>>(topk_idx, topk_w, chunk_counts, T, K, E, capacity);
+    capacity_kernel<<<1, 1024, 0, st>>>(topk_idx, topk_w, chunk_counts, T, K, E, capacity, nullptr, 1, 0, 0.f, 0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_capacity_job(int* topk_idx, float* topk_w, int* chunk_counts, int T, int K, int E,
+                                const int* recs, int N, int me, float cf, int min_capacity, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    if (E > kMaxE || K > kEpMaxK || N > kEpMaxRanks) return cudaErrorInvalidValue;
+    capacity_kernel<<<1, 1024, 0, st>>>(topk_idx, topk_w, chunk_counts, T, K, E, 0, recs, N, me, cf, min_capacity);
     return cudaGetLastError();
 }
 

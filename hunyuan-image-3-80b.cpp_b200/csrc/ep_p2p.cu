@@ -81,6 +81,45 @@ __global__ void ep_counts_kernel(EpPeers peers, int N, int me, int E, int T, con
     }
 }
 
+// This rank's choice record (pairs per (choice k, slot), then its token count) into `rec`
+// (one CTA; shared-memory counters).
+__device__ void choice_record(const int* __restrict__ topk_idx, int T, int K, int E, int* rec) {
+    __shared__ int cnt[kEpMaxK * 64];
+    for (int i = threadIdx.x; i < kEpMaxK * E; i += blockDim.x) cnt[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * K; i += blockDim.x) atomicAdd(&cnt[(i % K) * E + topk_idx[i]], 1);
+    __syncthreads();
+    for (int i = threadIdx.x; i < kEpMaxK * E; i += blockDim.x) rec[i] = cnt[i];
+    if (threadIdx.x == 0) rec[kEpMaxK * E] = T;
+}
+
+__global__ void choice_record_kernel(const int* __restrict__ topk_idx, int T, int K, int E, int* rec) {
+    choice_record(topk_idx, T, K, E, rec);
+}
+
+// Peer memory: the record goes to every rank's choice records (slot `me`), then this rank's
+// choice flag is raised on every rank and every rank's flag is awaited (bounded).
+__global__ void ep_choice_kernel(EpPeers peers, int N, int me, int E, int K, int T, const int* __restrict__ topk_idx,
+                                 uint32_t epoch, uint64_t budget_ns, int* err) {
+    const int rl = ep_choice_rec(E);
+    int* mine = peers.meta[me] + ep_choice_off(E) + me * rl;
+    choice_record(topk_idx, T, K, E, mine);
+    __syncthreads();
+    for (int d = 0; d < N; ++d) {
+        if (d == me) continue;
+        int* dst = peers.meta[d] + ep_choice_off(E) + me * rl;
+        for (int i = threadIdx.x; i < rl; i += blockDim.x) dst[i] = mine[i];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < N)
+        st_release_sys(reinterpret_cast<uint32_t*>(peers.meta[threadIdx.x]) + kEpFlagChoice + me, epoch);
+    if (threadIdx.x == 0) {
+        const uint32_t* flags = reinterpret_cast<const uint32_t*>(peers.meta[me]) + kEpFlagChoice;
+        wait_flags(flags, N, epoch, budget_ns, err);
+    }
+}
+
 // Grid (router chunk of 16 tokens, column slice of 256); 128 threads.  slot_pos[t, k]
 // receives the pair's expert-sorted position (its row in this rank's yret).
 constexpr int kEpCols = 256;
@@ -104,19 +143,24 @@ __global__ __launch_bounds__(128) void ep_scatter_kernel(
     }
     {
         const int tt = tid >> 3, k = tid & 7;
-        sidx[tt][k] = (tt < nt && k < K) ? topk_idx[(t0 + tt) * K + k] : -1;
+        const int v = (tt < nt && k < K) ? topk_idx[(t0 + tt) * K + k] : -1;
+        sidx[tt][k] = v >= 0 && (v & kDroppedPair) ? -1 : v;  // a dropped pair takes no row
     }
     __syncthreads();
     {
         const int tt = tid >> 3, k = tid & 7;
         if (tt < nt && k < K) {
             const int e = sidx[tt][k];
-            int rank = 0;
-            for (int p = 0; p < tt; ++p)
-                for (int kk = 0; kk < K; ++kk) rank += sidx[p][kk] == e;
-            const int d = e / el;
-            const int pos = chunk_base[c * E + e] + rank;  // expert-sorted position of the pair
-            srow[tt][k] = base[d] + pos - goff[d * el];
+            int pos = -1;
+            srow[tt][k] = -1;
+            if (e >= 0) {
+                int rank = 0;
+                for (int p = 0; p < tt; ++p)
+                    for (int kk = 0; kk < K; ++kk) rank += sidx[p][kk] == e;
+                const int d = e / el;
+                pos = chunk_base[c * E + e] + rank;  // expert-sorted position of the pair
+                srow[tt][k] = base[d] + pos - goff[d * el];
+            }
             if (blockIdx.y == 0) slot_pos[(t0 + tt) * K + k] = pos;
         }
     }
@@ -135,6 +179,7 @@ __global__ __launch_bounds__(128) void ep_scatter_kernel(
             v.z = *reinterpret_cast<const uint32_t*>(&h2);
             v.w = *reinterpret_cast<const uint32_t*>(&h3);
             for (int k = 0; k < K; ++k) {
+                if (sidx[tt][k] < 0) continue;
                 const int d = sidx[tt][k] / el;
                 *reinterpret_cast<uint4*>(peers.xp[d] + static_cast<size_t>(srow[tt][k]) * H + j) = v;
             }
@@ -177,18 +222,23 @@ __global__ __launch_bounds__(128) void ep_local_kernel(
     }
     {
         const int tt = tid >> 3, k = tid & 7;
-        sidx[tt][k] = (tt < nt && k < K) ? topk_idx[(t0 + tt) * K + k] : -1;
+        const int v = (tt < nt && k < K) ? topk_idx[(t0 + tt) * K + k] : -1;
+        sidx[tt][k] = v >= 0 && (v & kDroppedPair) ? -1 : v;  // a dropped pair takes no row
     }
     __syncthreads();
     {
         const int tt = tid >> 3, k = tid & 7;
         if (tt < nt && k < K) {
             const int e = sidx[tt][k];
-            int rank = 0;
-            for (int p = 0; p < tt; ++p)
-                for (int kk = 0; kk < K; ++kk) rank += sidx[p][kk] == e;
-            const int pos = chunk_base[c * E + e] + rank;
-            srow[tt][k] = e / el == me ? base + pos : -1;
+            int pos = -1;
+            srow[tt][k] = -1;
+            if (e >= 0) {
+                int rank = 0;
+                for (int p = 0; p < tt; ++p)
+                    for (int kk = 0; kk < K; ++kk) rank += sidx[p][kk] == e;
+                pos = chunk_base[c * E + e] + rank;
+                srow[tt][k] = e / el == me ? base + pos : -1;
+            }
             if (blockIdx.y == 0) slot_pos[(t0 + tt) * K + k] = pos;
         }
     }
@@ -263,6 +313,19 @@ cudaError_t launch_ep_counts(const EpPeers& p, int N, int me, int E, int T, cons
                              uint64_t budget_ns, int* err, cudaStream_t st) {
     if (N > kEpMaxRanks) return cudaErrorInvalidValue;
     ep_counts_kernel<<<1, 128, 0, st>>>(p, N, me, E, T, gcnt, epoch, budget_ns, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_choice_counts(const EpPeers& p, int N, int me, int E, int K, int T, const int* topk_idx,
+                                    uint32_t epoch, uint64_t budget_ns, int* err, cudaStream_t st) {
+    if (E > 64 || K > kEpMaxK || N > kEpMaxRanks) return cudaErrorInvalidValue;
+    ep_choice_kernel<<<1, 256, 0, st>>>(p, N, me, E, K, T, topk_idx, epoch, budget_ns, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_choice_record(const int* topk_idx, int T, int K, int E, int* rec, cudaStream_t st) {
+    if (E > 64 || K > kEpMaxK) return cudaErrorInvalidValue;
+    choice_record_kernel<<<1, 256, 0, st>>>(topk_idx, T, K, E, rec);
     return cudaGetLastError();
 }
 

@@ -237,7 +237,9 @@ __device__ void ep_send_rows(const EpFuse& f, int ct, int cta, int n_ctas, int* 
                 v.z = *reinterpret_cast<const uint32_t*>(&h2);
                 v.w = *reinterpret_cast<const uint32_t*>(&h3);
                 for (int k = 0; k < f.K; ++k) {
-                    const int d = __ldg(f.topk_idx + t * f.K + k) / f.el;
+                    const int sl = __ldg(f.topk_idx + t * f.K + k);
+                    if (sl & kDroppedPair) continue;  // a pair dropped by the capacity takes no row
+                    const int d = sl / f.el;
                     if (d == f.me) continue;
                     const int row = base_s[d] + __ldg(f.slot_pos + t * f.K + k);
                     *reinterpret_cast<uint4*>(f.peers.xp[d] + static_cast<size_t>(row) * f.H + j) = v;

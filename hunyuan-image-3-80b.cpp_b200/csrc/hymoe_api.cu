@@ -236,6 +236,7 @@ struct hymoe_ctx {
     __half* y_ret = nullptr;     // [T*K, H] routed results back from their ranks (fp16), in this
                                  // rank's expert-sorted pair order (peers write it directly)
     int* C_dev = nullptr;        // [N][E] gathered per-expert counts
+    int* choice_dev = nullptr;   // [N][ep_choice_rec(E)] gathered choice records (NCCL transport)
     int* C_host = nullptr;       // pinned copy
     cudaEvent_t ev_counts = nullptr;
     double ep_timeout_s = 60.0;
@@ -659,7 +660,7 @@ const char* hymoe_last_error(const hymoe_ctx* ctx) {
 // ranks agree on the outcome: either all use peer memory or all keep the NCCL exchange.
 hymoe_status ep_p2p_setup(hymoe_ctx* c) {
     const int N = c->cfg.ep_size, me = c->cfg.ep_rank;
-    const size_t meta_ints = kEpCountOff + static_cast<size_t>(kEpMaxRanks) * (c->E + 1);
+    const size_t meta_ints = static_cast<size_t>(ep_meta_ints(c->E));
     HY_CUDA(c, dalloc(&c->ep_meta, meta_ints));
     HY_CUDA(c, cudaMemset(c->ep_meta, 0, meta_ints * sizeof(int)));
     HY_CUDA(c, dalloc(&c->done_ctas, 1));
@@ -879,6 +880,7 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
         A(dalloc(&c->xp_send, T * K * H));
         A(dalloc(&c->y_ret, T * K * H));
         A(dalloc(&c->C_dev, static_cast<size_t>(N) * E));
+        A(dalloc(&c->choice_dev, static_cast<size_t>(N) * ep_choice_rec(E)));
         A(cudaMallocHost(reinterpret_cast<void**>(&c->C_host), sizeof(int) * N * E));
         A(cudaEventCreateWithFlags(&c->ev_counts, cudaEventDisableTiming));
     }
@@ -1008,6 +1010,7 @@ void hymoe_destroy(hymoe_ctx* c) {
     cudaFree(c->xp_send);
     cudaFree(c->y_ret);
     cudaFree(c->C_dev);
+    cudaFree(c->choice_dev);
     if (c->C_host) cudaFreeHost(c->C_host);
     if (c->ev_counts) cudaEventDestroy(c->ev_counts);
     cudaFree(c->gcnt);
@@ -1347,8 +1350,8 @@ hymoe_status hymoe_set_routing(hymoe_ctx* c, const hymoe_routing* r) {
     RouteMode m;  // NULL: moe_forward_cpu's routing
     if (r) {
         if (r->drop_tokens) {
-            if (c->cfg.ep_size > 1)
-                return c->fail(HYMOE_ERR_UNSUPPORTED, "capacity drops (drop_tokens) run on one GPU only");
+            if (c->K > kEpMaxK)
+                return c->fail(HYMOE_ERR_UNSUPPORTED, "capacity drops need moe_topk <= %d", kEpMaxK);
             if (!(r->capacity_factor >= 0.f) || !std::isfinite(r->capacity_factor))
                 return c->fail(HYMOE_ERR_INVALID_ARG, "capacity_factor %g", static_cast<double>(r->capacity_factor));
             m.drop = 1;
@@ -1611,6 +1614,24 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
     const bool p2p = ep && c->p2p;
     const uint32_t epoch = p2p ? ++c->epoch : 0;
     const uint64_t budget_ns = static_cast<uint64_t>(c->ep_timeout_s * 1e9);
+    // Capacity-limited routing over an expert-parallel job: every rank's choice record (pairs per
+    // (choice, slot) and its token count), by peer memory or an NCCL all-gather.
+    auto choice_recs = [&]() -> const int* {
+        return p2p ? c->ep_meta + ep_choice_off(E) : c->choice_dev;
+    };
+    auto exchange_choices = [&]() -> hymoe_status {
+        if (p2p) {
+            HY_CUDA(c, launch_ep_choice_counts(c->peers, N, rank, E, K, T, c->topk_idx, epoch, budget_ns, c->err_word, st));
+            return HYMOE_OK;
+        }
+        const int rl = ep_choice_rec(E);
+        HY_CUDA(c, launch_choice_record(c->topk_idx, T, K, E, c->choice_dev + static_cast<size_t>(rank) * rl, st));
+        ncclResult_t r = ncclAllGather(c->choice_dev + static_cast<size_t>(rank) * rl, c->choice_dev, rl, ncclInt32,
+                                       c->comm, st);
+        if (r != ncclSuccess && r != ncclInProgress)
+            return c->fail(HYMOE_ERR_NCCL, "ncclAllGather(choice counts): %s", ncclGetErrorString(r));
+        return ep_poll(c, "choice-count exchange");
+    };
     auto device_part = [&]() -> hymoe_status {
         // HYMOE_PRE_NORM: the layer's RMSNorm first; everything below reads the normalised rows
         // (the residual stays the caller's).  Timed with the router phase.
@@ -1740,13 +1761,21 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             if (c->route.drop) {
                 // topkgating_full's capacity with drop_tokens (src/hunyuan_moe_full.cpp:205-224):
                 // floor(capacity_factor * K * T / E) in single precision, at least K and
-                // min_capacity; pairs beyond it in k-major order are dropped
-                const uint32_t f = static_cast<uint32_t>(c->route.capacity_factor * static_cast<float>(K) *
-                                                         static_cast<float>(T) / static_cast<float>(E));
-                const int cap = std::max(std::max<int>(static_cast<int>(std::min<uint32_t>(f, 1u << 30)), K),
-                                         c->route.min_capacity);
+                // min_capacity; pairs beyond it in k-major order are dropped.  Expert parallel:
+                // over the job's tokens (rank 0's first), from every rank's choice counts.
                 c->phase_begin();
-                HY_CUDA(c, launch_capacity(c->topk_idx, c->topk_w, c->chunk_counts, T, K, E, cap, st));
+                if (ep) {
+                    hymoe_status sx = exchange_choices();
+                    if (sx != HYMOE_OK) return sx;
+                    HY_CUDA(c, launch_capacity_job(c->topk_idx, c->topk_w, c->chunk_counts, T, K, E, choice_recs(), N,
+                                                   rank, c->route.capacity_factor, c->route.min_capacity, st));
+                } else {
+                    const uint32_t f = static_cast<uint32_t>(c->route.capacity_factor * static_cast<float>(K) *
+                                                             static_cast<float>(T) / static_cast<float>(E));
+                    const int cap = std::max(std::max<int>(static_cast<int>(std::min<uint32_t>(f, 1u << 30)), K),
+                                             c->route.min_capacity);
+                    HY_CUDA(c, launch_capacity(c->topk_idx, c->topk_w, c->chunk_counts, T, K, E, cap, st));
+                }
                 c->phase_end(HYMOE_PHASE_ROUTER);
             }
             PlanArgs pa{};
@@ -1779,6 +1808,10 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             }
         } else {
             HY_CUDA(c, cudaMemsetAsync(c->gcnt, 0, sizeof(int) * E, st));
+            if (c->route.drop && ep) {  // a rank without tokens still takes part in the exchange
+                hymoe_status sx = exchange_choices();
+                if (sx != HYMOE_OK) return sx;
+            }
         }
 
         std::vector<size_t> send_cnt(N, 0), send_off(N, 0), recv_cnt(N, 0), recv_off(N, 0);

@@ -105,6 +105,12 @@ cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st);
 // topk_idx, weight 0, and leave their chunk's count.  One CTA.
 cudaError_t launch_capacity(int* topk_idx, float* topk_w, int* chunk_counts, int T, int K, int E, int capacity,
                             cudaStream_t st);
+// The same over an expert-parallel job: recs = every rank's choice record (stride
+// ep_choice_rec(E)), this rank's tokens come after those of ranks 0..me-1; the capacity is
+// computed on the device from the job's token count (floor(cf * K * T_job / E) in single
+// precision, at least K and min_capacity).
+cudaError_t launch_capacity_job(int* topk_idx, float* topk_w, int* chunk_counts, int T, int K, int E,
+                                const int* recs, int N, int me, float cf, int min_capacity, cudaStream_t st);
 // idx[i] = expert_of_slot[idx[i]] for i < n (top-K slots back to expert ids for the caller);
 // the dropped-pair bit is cleared; expert_of_slot == nullptr: identity (only the bit is cleared).
 cudaError_t launch_unmap_slots(int* idx, const int* expert_of_slot, int n, cudaStream_t st);
@@ -129,10 +135,17 @@ cudaError_t launch_ep_segments_fused(const int* C, int ld, int N, int rank, int 
 
 // ---- ep_p2p.cu (expert-parallel dispatch / combine over NVLink peer memory)
 constexpr int kEpMaxRanks = 8;
-// Metadata block of every rank (ints): flags [count | deliver | ready][kEpMaxRanks], then the
-// count matrix [kEpMaxRanks][E + 1] (E per-expert pair counts + the source's token count).
+constexpr int kEpMaxK = 8;
+// Metadata block of every rank (ints): flags [count | deliver | ready | choice][kEpMaxRanks],
+// then the count matrix [kEpMaxRanks][E + 1] (E per-expert pair counts + the source's token
+// count), then (capacity-limited routing) the choice-count records [kEpMaxRanks][ep_choice_rec]:
+// a rank's pairs per (choice k, slot) [kEpMaxK][E] and its token count.
 constexpr int kEpFlagCount = 0, kEpFlagDeliver = kEpMaxRanks, kEpFlagReady = 2 * kEpMaxRanks;
-constexpr int kEpCountOff = 3 * kEpMaxRanks;
+constexpr int kEpFlagChoice = 3 * kEpMaxRanks;
+constexpr int kEpCountOff = 4 * kEpMaxRanks;
+__host__ __device__ constexpr int ep_choice_off(int E) { return kEpCountOff + kEpMaxRanks * (E + 1); }
+__host__ __device__ constexpr int ep_choice_rec(int E) { return kEpMaxK * E + 1; }
+__host__ __device__ constexpr int ep_meta_ints(int E) { return ep_choice_off(E) + kEpMaxRanks * ep_choice_rec(E); }
 struct EpPeers {  // every rank's buffers as mapped in this process (own entry: local)
     __half* xp[kEpMaxRanks];   // activation matrices
     __half* yr[kEpMaxRanks];   // routed-result matrices (fp16, same rows as xp)
@@ -141,6 +154,13 @@ struct EpPeers {  // every rank's buffers as mapped in this process (own entry: 
 };
 cudaError_t launch_ep_counts(const EpPeers& p, int N, int me, int E, int T, const int* gcnt, uint32_t epoch,
                              uint64_t budget_ns, int* err, cudaStream_t st);
+// Capacity-limited routing across ranks: this rank's pairs per (choice, slot) and its token count
+// (one ep_choice_rec record) into every rank's choice records, then a bounded wait for every
+// rank's (peer memory).  The NCCL transport writes the record with launch_choice_record and
+// gathers the records with ncclAllGather.
+cudaError_t launch_ep_choice_counts(const EpPeers& p, int N, int me, int E, int K, int T, const int* topk_idx,
+                                    uint32_t epoch, uint64_t budget_ns, int* err, cudaStream_t st);
+cudaError_t launch_choice_record(const int* topk_idx, int T, int K, int E, int* rec, cudaStream_t st);
 // Decode-size calls: every pair's row (fp16) into its owner's xp and the token rows into rows
 // [0, T) of this rank's xp; slot_pos = expert-sorted positions; then this rank's delivery flag.
 cudaError_t launch_ep_scatter(const EpPeers& p, int N, int me, int E, int el, int T, int H, int K, const float* x,

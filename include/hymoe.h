@@ -197,12 +197,14 @@ hymoe_status hymoe_set_norm(hymoe_ctx* ctx, uint32_t layer, const float* weight,
  *     experts can be selected (ties: lower group);
  *   norm_topk_prob: weights = p / sum of the K selected p, the sum clamped below at 1e-8
  *     (with K > 1); otherwise weights = p * routed_scaling_factor;
- *   drop_tokens (capacity_factor, min_capacity): capacity-limited routing on one GPU
- *     (HYMOE_ERR_UNSUPPORTED with expert parallelism): capacity = floor(capacity_factor * K *
- *     T / E) in single precision, at least K and min_capacity; each expert keeps its first
- *     `capacity` pairs in k-major order (every token's first choice before any second choice,
- *     tokens in order) and the other pairs are dropped: they take no GEMM rows, add nothing
- *     to the output, and their debug weights read 0 (src/hunyuan_moe_full.cpp:205-305).
+ *   drop_tokens (capacity_factor, min_capacity): capacity-limited routing (moe_topk <= 8):
+ *     capacity = floor(capacity_factor * K * T / E) in single precision, at least K and
+ *     min_capacity; each expert keeps its first `capacity` pairs in k-major order (every
+ *     token's first choice before any second choice, tokens in order) and the other pairs are
+ *     dropped: they take no GEMM rows, add nothing to the output, and their debug weights
+ *     read 0 (src/hunyuan_moe_full.cpp:205-305).  With expert parallelism T is the job's token
+ *     count and the order runs over the job's tokens in rank order (rank 0's first), as one
+ *     call over the concatenated tokens would; every rank must set the same routing.
  *     Without drop_tokens topkgating_full's capacity keeps every pair.
  * The debug probabilities stay the unmasked softmax (the reference's router_probs).
  * NULL restores moe_forward_cpu's routing (the default). */

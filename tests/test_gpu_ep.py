@@ -45,7 +45,8 @@ def _placement(world):
 NORM_W = (1.0 + 0.05 * np.cos(np.arange(H))).astype(np.float32)
 
 
-def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p", place=None, pre_norm=False):
+def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p", place=None, pre_norm=False,
+               drop=None):
     import sys
     os.environ["HYMOE_EP_TRANSPORT"] = transport
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -68,6 +69,8 @@ def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p", pla
         m.load_layer(0, lay["router"], lay["sgu"], lay["sdn"], egu, edn, WT)
         if pre_norm:
             m.set_norm(0, NORM_W, 1e-5)
+        if drop is not None:
+            m.set_routing(drop=drop, min_capacity=1)
         outs = []
         for call, t in enumerate(tokens):
             x = O2.synth_x(orc, SEED + 100 * call + rank, t, H)
@@ -80,7 +83,7 @@ def _ep_worker(rank, world, nccl_id, tokens, max_tokens, q, transport="p2p", pla
         q.put((rank, f"error: {e!r}", None))
 
 
-def _run_ep(world, tokens_per_rank, transport="p2p", place=None, pre_norm=False, max_tokens=None):
+def _run_ep(world, tokens_per_rank, transport="p2p", place=None, pre_norm=False, max_tokens=None, drop=None):
     import hymoe
     nccl_id = hymoe.nccl_unique_id()
     ctx = mp.get_context("spawn")
@@ -89,7 +92,7 @@ def _run_ep(world, tokens_per_rank, transport="p2p", place=None, pre_norm=False,
         max_tokens = max(16, max(max(t) for t in tokens_per_rank))  # job-wide bound
     procs = [ctx.Process(target=_ep_worker,
                          args=(r, world, nccl_id, tokens_per_rank[r], max_tokens, q, transport, place,
-                               pre_norm))
+                               pre_norm, drop))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -196,6 +199,41 @@ def test_expert_parallel_pre_norm_matches_single_gpu(orc, transport):
         ref = single.forward_host(0, x, bias=bias, debug=True, resid="x", pre_norm=True)
         assert np.array_equal(res[rank][0]["idx"], ref["idx"])
         assert np.array_equal(res[rank][0]["out"], ref["out"]), f"rank {rank}"
+    single.close()
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
+def test_expert_parallel_capacity_drops_over_the_job(orc, transport):
+    """Capacity-limited routing (topkgating_full with drop_tokens, src/hunyuan_moe_full.cpp:205-305)
+    across ranks: the capacity comes from the job's token count and the k-major priority runs
+    over the job's tokens in rank order, so every rank's output equals the one-GPU call over the
+    concatenated tokens (rank 0's first) with the same routing — bit for bit on the tensor-core
+    path, with the same dropped pairs (weight 0).  The second call has a rank without tokens,
+    which still takes part in the count exchange."""
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    tokens = [[300, 0], [200, 180]]
+    cf = 0.5
+    res = _run_ep(2, tokens, transport, drop=cf)
+    import hymoe
+    lay = _layer(orc)
+    single = hymoe.MoE(H, I, E, K, 1, 520, device=0)
+    single.load_layer(0, lay["router"], lay["sgu"], lay["sdn"], lay["egu"], lay["edn"], WT)
+    single.set_routing(drop=cf, min_capacity=1)
+    dropped = 0
+    for call in range(2):
+        bias = O.zipf_bias(SEED + call, E)
+        xs = [O.synth_x(orc, SEED + 100 * call + r, tokens[r][call], H) for r in range(2)]
+        ref = single.forward_host(0, np.concatenate(xs), bias=bias, debug=True)
+        t0 = 0
+        for rank in range(2):
+            t = tokens[rank][call]
+            got = res[rank][call]
+            for k in ("idx", "w", "out"):
+                assert np.array_equal(got[k], ref[k][t0:t0 + t]), (rank, call, k)
+            dropped += int((got["w"] == 0).sum())
+            t0 += t
+    assert dropped > 0  # the capacity did bite
     single.close()
 
 
