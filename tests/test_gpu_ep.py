@@ -208,9 +208,9 @@ def test_expert_parallel_capacity_drops_over_the_job(orc, transport):
     """Capacity-limited routing (topkgating_full with drop_tokens, src/hunyuan_moe_full.cpp:205-305)
     across ranks: the capacity comes from the job's token count and the k-major priority runs
     over the job's tokens in rank order, so every rank's output equals the one-GPU call over the
-    concatenated tokens (rank 0's first) with the same routing — bit for bit on the tensor-core
-    path, with the same dropped pairs (weight 0).  The second call has a rank without tokens,
-    which still takes part in the count exchange."""
+    concatenated tokens (rank 0's first) with the same routing: the same selections and dropped
+    pairs (weight 0), the same output bits when every rank is on the tensor-core path.  The
+    second call has a rank without tokens, which still takes part in the count exchange."""
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     tokens = [[300, 0], [200, 180]]
     cf = 0.5
@@ -229,8 +229,14 @@ def test_expert_parallel_capacity_drops_over_the_job(orc, transport):
         for rank in range(2):
             t = tokens[rank][call]
             got = res[rank][call]
-            for k in ("idx", "w", "out"):
+            for k in ("idx", "w"):
                 assert np.array_equal(got[k], ref[k][t0:t0 + t]), (rank, call, k)
+            # Bits when every rank is on the tensor-core path; a rank without tokens computes
+            # the rows it receives on the decode kernels (another summation order): tolerance.
+            if all(tokens[r][call] > 64 for r in range(2)):
+                assert np.array_equal(got["out"], ref["out"][t0:t0 + t]), (rank, call)
+            elif t:
+                assert rel_l2(got["out"], ref["out"][t0:t0 + t]) <= REL_L2_TOL, (rank, call)
             dropped += int((got["w"] == 0).sum())
             t0 += t
     assert dropped > 0  # the capacity did bite
