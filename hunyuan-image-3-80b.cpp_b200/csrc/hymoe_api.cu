@@ -1874,7 +1874,8 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             }
             gemv = max_rows <= static_cast<size_t>(kGemvMaxRows);
             gemv_rows = max_rows;
-            if (total_sent != static_cast<size_t>(T) * K)
+            // every pair is sent once, except those a capacity dropped
+            if (c->route.drop ? total_sent > static_cast<size_t>(T) * K : total_sent != static_cast<size_t>(T) * K)
                 return c->fail(HYMOE_ERR_STATE, "count exchange inconsistent: %zu rows for %d pairs", total_sent, T * K);
             // Every rank checks every rank's receive size (all hold the full count matrix), so
             // either all ranks proceed to the exchange or all return this error.
