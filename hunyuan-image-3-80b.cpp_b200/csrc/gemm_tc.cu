@@ -17,7 +17,8 @@
 // on both CTAs' barriers.  Per SM this halves the token-operand traffic (L2 -> SMEM and
 // SMEM -> tensor core) of a 128 x N single-SM tile.
 //
-// Warp roles (448 threads per CTA, one CTA per SM, persistent over the work list):
+// Warp roles (512 threads per CTA, one CTA per SM, persistent over the work list; warp w
+// runs on SM sub-partition w % 4):
 //   warp 0      producer: TMA 2-D load of this CTA's B half (128B swizzle) + one bulk copy
 //               of its raw GGUF weight tile, both completing on the local full[s]
 //   warp 1      TMEM allocation for the pair; in the leader, the MMA issuer
@@ -26,10 +27,14 @@
 //               in the same warp (tile row order of glu_gate_row / glu_up_row) by one
 //               shuffle per token pair, SwiGLU -> fp16; down stores fp32 (shared expert) or
 //               fp16 (routed) rows; one coalesced segment per token, no shared memory
-//   warps 6..13 dequantisers, two groups of four on alternate stages: GGUF Q4_0/Q8_0/F16
-//               tile -> fp16 A half in the canonical K-major 128B-swizzled layout, two
-//               (row, GGUF block) entries per thread; then arrive on the leader's a_ready[s]
-//   warps 14..17 (fused expert parallel only, 576 threads) communication, beside the MMA
+//   warps 6-8, 10-12, 14, 15  dequantisers, two groups of four on alternate stages: GGUF
+//               Q4_0/Q8_0/F16 tile -> fp16 A half in the canonical K-major 128B-swizzled
+//               layout, two (row, GGUF block) entries per thread; then arrive on the leader's
+//               a_ready[s].  None runs on sub-partition 1: the MMA issuer (warp 1) shares it
+//               only with an epilogue warp and two idle warps (9, 13), because with two
+//               dequantisers beside it the issuer's instruction slots, not the tensor core,
+//               set the stage period of full tiles (0.448 against 0.352 us per stage)
+//   warps 16..19 (fused expert parallel only, 640 threads) communication, beside the MMA
 //               pipeline: in gate_up they store this rank's token rows owned by other ranks
 //               into the owners' activation matrices (NVLink peer stores), and the producer
 //               loads a remote source's rows only after that source's delivery flag; in down
@@ -68,13 +73,20 @@ namespace hymoe {
 
 namespace {
 
-constexpr int kThreads = 448;
-constexpr int kEpThreads = 576;    // + four communication warps (fused expert parallel)
+constexpr int kThreads = 512;
+constexpr int kEpThreads = 640;    // + four communication warps (fused expert parallel)
 constexpr int kEpSendCols = 1024;  // columns per send work unit: 128 threads x 8 fp16
 constexpr int kABytes = kTileRows * 128;        // 16 KB fp16 A half
 constexpr int kBBytes = kMaxBoxRows * 128;      // 16 KB fp16 B half (largest box)
 constexpr int kAccCols = 256;
 constexpr int kTmemCols = 512;
+
+// Dequantiser index 0..7 of warps 6, 7, 8, 10, 11, 12, 14, 15 (-1 for other warps): the
+// dequantisers keep off sub-partition 1, where the MMA issuer runs.
+__device__ __forceinline__ int dequant_index(int warp) {
+    const int d = warp - 6;
+    return (d < 0 || d > 9 || (warp & 3) == 1) ? -1 : d - d / 4;
+}
 
 __device__ __forceinline__ bool named_bar_and(int id, int n, bool p) {
     uint32_t r;
@@ -510,7 +522,7 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
                 }
             }
         }
-    } else if (!EP || warp < 14) {
+    } else if (dequant_index(warp) >= 0) {
         // ------------------------------------------------------------ dequantisers
         // Two groups of four warps take alternate stage slots (slot s to group s & 1), so two
         // stages are converted concurrently; each thread converts entries e and e + 128 of its
@@ -518,7 +530,7 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
         // strictly in order (with an odd slot count, a split by iteration parity would let
         // both groups use every slot, and a group two phases ahead would pass the parity wait
         // of a phase that has not completed).
-        const int dq = tid - 192;  // 0..255
+        const int dq = dequant_index(warp) * 32 + lane;  // 0..255
         const uint32_t grp = static_cast<uint32_t>(dq >> 7);
         const int e = dq & 127;
         uint32_t it = 0;
@@ -545,7 +557,7 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
                 if (lane == 0) mbar_arrive_cluster(mapa_shared(&aready[s], 0));
             }
         }
-    } else {
+    } else if (warp >= kThreads / 32) {
         // ------------------------------------------------------------ communication (EP)
         if constexpr (EP) {
             const int ct = tid - kThreads;  // 0..127
