@@ -63,9 +63,25 @@ __device__ unsigned long long g_trace[2][8][kTraceIters];
 extern "C" int hymoe_trace_read(void* host, size_t bytes) {
     return static_cast<int>(cudaMemcpyFromSymbol(host, g_trace, bytes < sizeof(g_trace) ? bytes : sizeof(g_trace)));
 }
+// Per-item stamps of every pair's MMA issuer in gate_up launches: [pair][item of the pair]
+// {first MMA issue, last commit issue, item token rows}.
+constexpr int kTracePairs = 80, kTraceItems = 256;
+__device__ unsigned long long g_trace_items[kTracePairs][kTraceItems][3];
+#define HY_ITEM(glu, cid, j, k, v)                                        \
+    do {                                                                 \
+        if ((glu) && (cid) < kTracePairs && (j) < kTraceItems)           \
+            g_trace_items[cid][j][k] = (v);                              \
+    } while (0)
+extern "C" int hymoe_trace_items_read(void* host, size_t bytes) {
+    return static_cast<int>(cudaMemcpyFromSymbol(host, g_trace_items,
+                                                 bytes < sizeof(g_trace_items) ? bytes : sizeof(g_trace_items)));
+}
 #else
 #define HY_TRACE(ev, it) \
     do {                 \
+    } while (0)
+#define HY_ITEM(glu, cid, j, k, v) \
+    do {                           \
     } while (0)
 #endif
 
@@ -431,6 +447,7 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
                         break;
                     }
                     HY_TRACE(3, it);
+                    if (ks == 0) HY_ITEM(a.glu, cid, tc, 0, globaltimer_ns());
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + s * kABytes);
                     const uint32_t b_addr = smem_u32(sB + s * kBBytes);
@@ -443,6 +460,8 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
                 }
                 if (!ok) break;
                 mma_commit_2sm_mc(&acc_full[ab], 0x3);
+                HY_ITEM(a.glu, cid, tc, 1, globaltimer_ns());
+                HY_ITEM(a.glu, cid, tc, 2, static_cast<unsigned long long>(item.w));
             }
             // All pair MMAs complete before either CTA releases tensor memory.
             mma_commit_2sm(mma_done);
