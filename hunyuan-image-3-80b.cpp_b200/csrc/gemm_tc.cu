@@ -34,7 +34,8 @@
 //               only with an epilogue warp and two idle warps (9, 13), because with two
 //               dequantisers beside it the issuer's instruction slots, not the tensor core,
 //               set the stage period of full tiles (0.448 against 0.352 us per stage)
-//   warps 16..19 (fused expert parallel only, 640 threads) communication, beside the MMA
+//   warps 16, 18, 19, 20 (fused expert parallel only, 672 threads; warp 17 idle, again to keep
+//               sub-partition 1 to the MMA issuer) communication, beside the MMA
 //               pipeline: in gate_up they store this rank's token rows owned by other ranks
 //               into the owners' activation matrices (NVLink peer stores), and the producer
 //               loads a remote source's rows only after that source's delivery flag; in down
@@ -90,7 +91,7 @@ namespace hymoe {
 namespace {
 
 constexpr int kThreads = 512;
-constexpr int kEpThreads = 640;    // + four communication warps (fused expert parallel)
+constexpr int kEpThreads = 672;    // + four communication warps (fused expert parallel) and an idle one
 constexpr int kEpSendCols = 1024;  // columns per send work unit: 128 threads x 8 fp16
 constexpr int kABytes = kTileRows * 128;        // 16 KB fp16 A half
 constexpr int kBBytes = kMaxBoxRows * 128;      // 16 KB fp16 B half (largest box)
@@ -102,6 +103,11 @@ constexpr int kTmemCols = 512;
 __device__ __forceinline__ int dequant_index(int warp) {
     const int d = warp - 6;
     return (d < 0 || d > 9 || (warp & 3) == 1) ? -1 : d - d / 4;
+}
+
+// Communication warp index 0..3 of warps 16, 18, 19, 20 (-1 for other warps).
+__device__ __forceinline__ int comm_index(int warp) {
+    return warp == 16 ? 0 : (warp >= 18 && warp <= 20) ? warp - 17 : -1;
 }
 
 __device__ __forceinline__ bool named_bar_and(int id, int n, bool p) {
@@ -576,10 +582,10 @@ __global__ void __launch_bounds__(EP ? kEpThreads : kThreads, 1)
                 if (lane == 0) mbar_arrive_cluster(mapa_shared(&aready[s], 0));
             }
         }
-    } else if (warp >= kThreads / 32) {
+    } else if (comm_index(warp) >= 0) {
         // ------------------------------------------------------------ communication (EP)
         if constexpr (EP) {
-            const int ct = tid - kThreads;  // 0..127
+            const int ct = comm_index(warp) * 32 + lane;  // 0..127
             if (a.ep_mode == 1) {
                 ep_send_rows(ep, ct, blockIdx.x, gridDim.x, comm_s);
                 ep_finish(ep, ct, gridDim.x, kEpFlagDeliver, comm_s + kEpMaxRanks);
