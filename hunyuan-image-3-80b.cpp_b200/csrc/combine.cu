@@ -21,6 +21,8 @@ __global__ __launch_bounds__(128, 10) void combine_kernel(const float* __restric
                                                       const float* __restrict__ topk_w,
                                                       const float* resid, float* out, int T,
                                                       int H, int K) {
+    griddep_wait();
+    griddep_launch_dependents();
     const int t = blockIdx.y;
     const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (j >= H) return;
@@ -69,11 +71,11 @@ __global__ __launch_bounds__(128, 10) void combine_kernel(const float* __restric
 
 cudaError_t launch_combine(const float* y_shared, const __half* y_routed, const int* slot_pos,
                            const float* topk_w, const float* resid, float* out, int T, int H,
-                           int K, cudaStream_t st) {
+                           int K, cudaStream_t st, bool pdl) {
     if (K > 8) return cudaErrorInvalidValue;
     dim3 grid((H / 8 + 127) / 128, T);
-    combine_kernel<<<grid, 128, 0, st>>>(y_shared, y_routed, slot_pos, topk_w, resid, out, T, H, K);
-    return cudaGetLastError();
+    return launch_kernel(pdl, combine_kernel, grid, dim3(128), 0, st, y_shared, y_routed, slot_pos, topk_w, resid,
+                         out, T, H, K);
 }
 
 }  // namespace hymoe

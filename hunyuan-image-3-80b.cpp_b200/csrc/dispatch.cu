@@ -153,6 +153,8 @@ __global__ __launch_bounds__(1024) void topk_plan_kernel(const float* __restrict
                                                          float* __restrict__ probs_out,
                                                          float* __restrict__ topk_w,
                                                          int* __restrict__ topk_idx, PlanArgs a) {
+    griddep_wait();
+    griddep_launch_dependents();
     __shared__ float pbuf[kRouterTok][kMaxE];
     __shared__ int gcnt_s[kMaxE], goff_s[kMaxSegs + 1];
     const int tid = threadIdx.x, warp = tid >> 5;
@@ -187,6 +189,8 @@ __global__ __launch_bounds__(128) void scatter_gather_kernel(
     const float* __restrict__ x, int T, int H, int E, int K, const int* __restrict__ topk_idx,
     const int* __restrict__ chunk_base, int* __restrict__ slot_pos, __half* __restrict__ xp_routed,
     __half* __restrict__ xp_shared, RowNorm nrm) {
+    griddep_wait();
+    griddep_launch_dependents();
     __shared__ int sidx[kRouterTok][8];
     __shared__ int spos[kRouterTok][8];
     const int c = blockIdx.x, t0 = c * kRouterTok, tid = threadIdx.x;
@@ -387,10 +391,9 @@ cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st) {
 }
 
 cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, float* topk_w,
-                             int* topk_idx, const PlanArgs& a, cudaStream_t st) {
+                             int* topk_idx, const PlanArgs& a, cudaStream_t st, bool pdl) {
     if (T > kRouterTok || a.n_chunks != 1) return cudaErrorInvalidValue;
-    topk_plan_kernel<<<1, 1024, 0, st>>>(logits, T, K, probs, topk_w, topk_idx, a);
-    return cudaGetLastError();
+    return launch_kernel(pdl, topk_plan_kernel, dim3(1), dim3(1024), 0, st, logits, T, K, probs, topk_w, topk_idx, a);
 }
 
 cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st) {
@@ -422,11 +425,10 @@ cudaError_t launch_unmap_slots(int* idx, const int* expert_of_slot, int n, cudaS
 
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
                                   const int* chunk_base, int* slot_pos, __half* xp_routed,
-                                  __half* xp_shared, cudaStream_t st, const RowNorm& nrm) {
+                                  __half* xp_shared, cudaStream_t st, const RowNorm& nrm, bool pdl) {
     dim3 grid((T + kRouterTok - 1) / kRouterTok, (H + kScatterCols - 1) / kScatterCols);
-    scatter_gather_kernel<<<grid, 128, 0, st>>>(x, T, H, E, K, topk_idx, chunk_base, slot_pos,
-                                                  xp_routed, xp_shared, nrm);
-    return cudaGetLastError();
+    return launch_kernel(pdl, scatter_gather_kernel, grid, dim3(128), 0, st, x, T, H, E, K, topk_idx, chunk_base,
+                         slot_pos, xp_routed, xp_shared, nrm);
 }
 
 cudaError_t launch_shared_prep(const float* x, int T, int H, __half* xp, int group, int n_rb_gu,

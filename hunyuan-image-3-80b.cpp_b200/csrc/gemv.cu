@@ -248,6 +248,9 @@ __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
     const __grid_constant__ GemvMaps maps, const int4* __restrict__ items, const int* __restrict__ n_items,
     const uint8_t* const* __restrict__ wtiles, int n_ks, int glu, void* __restrict__ out, int out_ld,
     __half* __restrict__ out_r, int shared_rows, int* err) {
+    // Programmatic dependent launch: everything up to griddep_wait reads only what was complete
+    // before this grid could be scheduled (the work list, written by the plan two or more
+    // launches back, and the weights); the activation rows come from the predecessor.
     constexpr int TB = tile_bytes(WT);
     extern __shared__ uint8_t gsm_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
@@ -283,18 +286,31 @@ __global__ __launch_bounds__(kGemvThreads, 1) void gemv_stream_kernel(
         return i < kStreamItems ? s_item[i] : items[blockIdx.x + i * G];
     };
 
-    auto issue = [&](int q) {  // lane 0: tile q of this warp's stream
+    auto issue_w = [&](int q) {  // lane 0: weights of tile q of this warp's stream
         const int i = q / per_item, m = q - i * per_item;
         const int4 it = item_at(i);
         const uint8_t* wt = i < kStreamItems ? s_wt[i] : wtiles[it.x] + static_cast<size_t>(it.y) * n_ks * TB;
         const int k = warp + kGemvWarps * m, slot = q % R;
         mbar_arrive_expect_tx(&wb[slot], TB + 1024u);
         bulk_load(ww + slot * TB, wt + static_cast<size_t>(k) * TB, TB, &wb[slot]);
-        tma_load_2d(wx + slot * 1024, &maps.x[0], &wb[slot], k * kTileK, it.z);
+    };
+    auto issue_x = [&](int q) {  // lane 0: the activation box of tile q (same barrier)
+        const int i = q / per_item, m = q - i * per_item;
+        const int k = warp + kGemvWarps * m, slot = q % R;
+        tma_load_2d(wx + slot * 1024, &maps.x[0], &wb[slot], k * kTileK, item_at(i).z);
+    };
+    auto issue = [&](int q) {
+        issue_w(q);
+        issue_x(q);
     };
     int issued = 0, done = 0;  // lane 0's stream positions
+    const int first = min(R, total);
     if (lane == 0)
-        for (; issued < min(R, total); ++issued) issue(issued);
+        for (int q = 0; q < first; ++q) issue_w(q);
+    griddep_wait();
+    griddep_launch_dependents();
+    if (lane == 0)
+        for (; issued < first; ++issued) issue_x(issued);
 
     const int tok_b = col_token<WT>(gq);
     const int t0 = col_token<WT>(2 * c), t1 = col_token<WT>(2 * c + 1);
@@ -403,14 +419,13 @@ size_t stream_smem() {
 template <int WT, int R>
 cudaError_t launch_stream(const GemvMaps& maps, const int4* items, const int* n_items, int n_sms,
                           const uint8_t* const* wtiles, int n_ks, int glu, void* out, int out_ld, __half* out_r,
-                          int shared_rows, int* err, cudaStream_t st) {
+                          int shared_rows, int* err, cudaStream_t st, bool pdl) {
     const size_t smem = stream_smem<WT, R>();
     cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<WT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    gemv_stream_kernel<WT, R><<<n_sms, kGemvThreads, smem, st>>>(maps, items, n_items, wtiles, n_ks, glu, out,
-                                                                 out_ld, out_r, shared_rows, err);
-    return cudaGetLastError();
+    return launch_kernel(pdl, gemv_stream_kernel<WT, R>, dim3(n_sms), dim3(kGemvThreads), smem, st, maps, items,
+                         n_items, wtiles, n_ks, glu, out, out_ld, out_r, shared_rows, err);
 }
 
 // Stages per CTA: as many as fit in ~72 KB (three CTAs per SM), at least 2 and at most 4;
@@ -447,13 +462,15 @@ cudaError_t launch_t(const GemvMaps& maps, const int4* items, const int* n_items
 cudaError_t launch_gemv(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
                         const uint8_t* const* wtiles, int wtype, int n_ks, int glu, int max_rows,
                         void* out, int out_ld, __half* out_r, int shared_rows, int* err, int n_sms,
-                        cudaStream_t st) {
+                        cudaStream_t st, bool pdl) {
     if (max_items <= 0) return cudaSuccess;
     if (max_rows < 1 || max_rows > kGemvMaxRows) return cudaErrorInvalidValue;
     if (max_rows <= 8 && wtype == W_Q8_0)
-        return launch_stream<W_Q8_0, 2>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, out_r, shared_rows, err, st);
+        return launch_stream<W_Q8_0, 2>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, out_r, shared_rows, err, st,
+                                        pdl);
     if (max_rows <= 8 && wtype == W_Q4_0)
-        return launch_stream<W_Q4_0, 3>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, out_r, shared_rows, err, st);
+        return launch_stream<W_Q4_0, 3>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, out_r, shared_rows, err, st,
+                                        pdl);
     switch (wtype) {
         case W_Q4_0: return launch_t<W_Q4_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st);
         case W_Q8_0: return launch_t<W_Q8_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st);

@@ -171,6 +171,7 @@ struct hymoe_ctx {
     cudaStream_t down_stream = nullptr;  // ... and chunk downloads
     cudaStream_t side_stream = nullptr;  // decode calls: the shared expert beside the router
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    bool pdl = true;  // decode chains with programmatic dependent launch (HYMOE_PDL=0 at create: off)
     int4 *items_sh_gu = nullptr, *items_sh_dn = nullptr;
     int* n_items_sh = nullptr;
     cudaStream_t stream = nullptr;
@@ -899,6 +900,8 @@ hymoe_status hymoe_create(const hymoe_config* cfg, hymoe_ctx** out) {
         // hidden).
         int coop = 0;
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, cfg->device);
+        const char* pd = getenv("HYMOE_PDL");
+        c->pdl = !(pd && strcmp(pd, "0") == 0);
         const char* df = getenv("HYMOE_DECODE_FUSED");
         const bool fused_on = df && strcmp(df, "1") == 0;
         if (N == 1 && coop && fused_on && E <= kDecodeMaxE && H / kTileRows <= kDecodeMaxRb) {
@@ -1736,6 +1739,12 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         // chains last long enough to hide it (measured: T=8 0.357 -> 0.351 ms; at T=1 the fork
         // outlasted the front end and delayed the routed launch, 0.105 -> 0.119 ms).
         const bool shared_apart = !ep && gemv && T >= 4 && T <= 8 && (L.wtype == W_Q4_0 || L.wtype == W_Q8_0);
+        // Decode chains on one GPU (1..8 tokens, weight-streaming kernels): router, top-K + plan,
+        // scatter, gate_up, down and combine are launched with programmatic dependent launch, so
+        // each is scheduled while its predecessor finishes (every one of these kernels waits for
+        // its predecessor's completion before it reads anything).
+        const bool pdl = c->pdl && !ep && gemv && T >= 1 && T <= kDecodeMaxT && !c->route.drop &&
+                         (L.wtype == W_Q4_0 || L.wtype == W_Q8_0);
         if (shared_apart) {
             cudaStream_t side = c->side_stream;
             HY_CUDA(c, cudaEventRecord(c->ev_fork, st));
@@ -1756,7 +1765,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             c->phase_begin();
             HY_CUDA(c, launch_router(dxn, T, H, L.router, E, K, dbias, dlog ? dlog : c->logits, dprob,
                                      c->topk_w, c->topk_idx, c->chunk_counts, slot_of, c->route, !fused, st,
-                                     nrm));
+                                     nrm, pdl));
             c->phase_end(HYMOE_PHASE_ROUTER, fused ? 1 : 2);
             if (c->route.drop) {
                 // topkgating_full's capacity with drop_tokens (src/hunyuan_moe_full.cpp:205-224):
@@ -1795,7 +1804,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             pa.items = items_args(gemv);
             c->phase_begin();
             if (fused)
-                HY_CUDA(c, launch_topk_plan(dlog ? dlog : c->logits, T, K, dprob, c->topk_w, c->topk_idx, pa, st));
+                HY_CUDA(c, launch_topk_plan(dlog ? dlog : c->logits, T, K, dprob, c->topk_w, c->topk_idx, pa, st, pdl));
             else
                 HY_CUDA(c, launch_plan(pa, st));
             c->phase_end(HYMOE_PHASE_PLAN);
@@ -1803,7 +1812,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
                 c->phase_begin();
                 HY_CUDA(c, launch_scatter_gather(dxn, T, H, E, K, c->topk_idx, c->chunk_base, c->slot_pos,
                                                  ep ? c->xp_send : c->xp + static_cast<size_t>(T) * H,
-                                                 shared_apart ? nullptr : c->xp, st, nrm));
+                                                 shared_apart ? nullptr : c->xp, st, nrm, pdl));
                 c->phase_end(HYMOE_PHASE_DISPATCH);
             }
         } else {
@@ -1938,11 +1947,11 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             c->phase_begin();
             const int mr = static_cast<int>(std::max<size_t>(1, gemv_rows));
             HY_CUDA(c, launch_gemv(c->gmaps_xp, c->items_gu, c->n_items, max_it, L.d_gu_ptrs, L.wtype, H / kTileK,
-                                   1, mr, c->hbuf, I, nullptr, 0, c->err_word, c->n_sms, st));
+                                   1, mr, c->hbuf, I, nullptr, 0, c->err_word, c->n_sms, st, pdl));
             c->phase_end(HYMOE_PHASE_GATE_UP);
             c->phase_begin();
             HY_CUDA(c, launch_gemv(c->gmaps_h, c->items_dn, c->n_items + 1, max_it, L.d_dn_ptrs, L.wtype,
-                                   I / kTileK, 0, mr, c->y, H, c->yr, T, c->err_word, c->n_sms, st));
+                                   I / kTileK, 0, mr, c->y, H, c->yr, T, c->err_word, c->n_sms, st, pdl));
             c->phase_end(HYMOE_PHASE_DOWN);
             if (p2p) {  // routed results back into their sources' return matrices, ready flags
                 c->phase_begin();
@@ -2014,7 +2023,8 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         if (shared_apart) HY_CUDA(c, cudaStreamWaitEvent(st, c->ev_join, 0));  // the shared expert's rows of y
         if (T > 0) {
             c->phase_begin();
-            HY_CUDA(c, launch_combine(c->y, y_routed, c->slot_pos, c->topk_w, dres, dout, T, H, K, st));
+            HY_CUDA(c, launch_combine(c->y, y_routed, c->slot_pos, c->topk_w, dres, dout, T, H, K, st,
+                                      pdl && !shared_apart));
             c->phase_end(HYMOE_PHASE_COMBINE);
             hymoe_status sd = debug_out();
             if (sd != HYMOE_OK) return sd;

@@ -62,7 +62,8 @@ constexpr int kGemvMaxRows = 64; // token rows per GEMV work item
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
                           int* topk_idx, int* chunk_counts, const int* slot_of,
-                          const RouteMode& mode, bool topk, cudaStream_t st, const RowNorm& nrm = {});
+                          const RouteMode& mode, bool topk, cudaStream_t st, const RowNorm& nrm = {},
+                          bool pdl = false);
 
 // ---- dispatch.cu
 constexpr int kMaxSegs = 80;  // >= E + 1 (E <= 64)
@@ -96,7 +97,7 @@ struct PlanArgs {
 cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
 // T <= kRouterTok (one chunk): top-K of every token and the plan in one launch.
 cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, float* topk_w,
-                             int* topk_idx, const PlanArgs& a, cudaStream_t st);
+                             int* topk_idx, const PlanArgs& a, cudaStream_t st, bool pdl = false);
 
 cudaError_t launch_items(const ItemsArgs& a, cudaStream_t st);
 // Capacity-limited routing (topkgating_full with drop_tokens, src/hunyuan_moe_full.cpp:205-305):
@@ -118,7 +119,8 @@ cudaError_t launch_unmap_slots(int* idx, const int* expert_of_slot, int n, cudaS
 // xp_shared == nullptr: the shared expert's rows are written elsewhere (launch_shared_prep).
 cudaError_t launch_scatter_gather(const float* x, int T, int H, int E, int K, const int* topk_idx,
                                   const int* chunk_base, int* slot_pos, __half* xp_routed,
-                                  __half* xp_shared, cudaStream_t st, const RowNorm& nrm = {});
+                                  __half* xp_shared, cudaStream_t st, const RowNorm& nrm = {},
+                                  bool pdl = false);
 // The shared expert as its own launch: its fp16 rows xp[0, T) and its work items (one per
 // 128-row block, all T rows) for gate_up and down; n_items[2].
 cudaError_t launch_shared_prep(const float* x, int T, int H, __half* xp, int group, int n_rb_gu,
@@ -242,7 +244,7 @@ struct GemvMaps {
 cudaError_t launch_gemv(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
                         const uint8_t* const* wtiles, int wtype, int n_ks, int glu, int max_rows,
                         void* out, int out_ld, __half* out_r, int shared_rows, int* err, int n_sms,
-                        cudaStream_t st);
+                        cudaStream_t st, bool pdl = false);
 
 // ---- decode.cu
 // The whole block for 1..8 tokens on one GPU (Q4_0 / Q8_0 weights) as one persistent
@@ -307,7 +309,7 @@ cudaError_t launch_decode(const DecodeMaps& maps, const DecodeArgs& a, int wtype
 // out[t] = resid[t] + y_shared[t] + sum_k w[t,k] * y_routed[slot_pos[t,k]] (routed rows fp16)
 cudaError_t launch_combine(const float* y_shared, const __half* y_routed, const int* slot_pos,
                            const float* topk_w, const float* resid, float* out, int T, int H,
-                           int K, cudaStream_t st);
+                           int K, cudaStream_t st, bool pdl = false);
 
 // ---- norm.cu
 // rms[t] = 1 / sqrt(sum of squares / H + eps) over T rows of H (H % 64 == 0), the reference's

@@ -135,8 +135,12 @@ __global__ __launch_bounds__(128) void router_logits_decode_kernel(
     __shared__ float rs[kDecodeMaxT];
     const int e = blockIdx.x;
     const bool norm = nrm.rms != nullptr;
+    // The router row before the programmatic-launch wait (it depends on no earlier launch); the
+    // token rows and the per-token norm factors after it.
     for (int i = threadIdx.x * 4; i < H; i += 128 * 4)
         cp_async16(ws + i, Wr + static_cast<size_t>(e) * H + i);
+    griddep_wait();
+    griddep_launch_dependents();
     for (int i = threadIdx.x * 4; i < T * H; i += 128 * 4) cp_async16(xs + i, x + i);
     if (norm) {
         for (int i = threadIdx.x * 4; i < H; i += 128 * 4) cp_async16(ns + i, nrm.w + i);
@@ -313,14 +317,16 @@ __global__ __launch_bounds__(32 * kRouterTok) void router_topk_kernel(
 cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, int K,
                           const float* bias, float* logits, float* probs, float* topk_w,
                           int* topk_idx, int* chunk_counts, const int* slot_of,
-                          const RouteMode& mode, bool topk, cudaStream_t st, const RowNorm& nrm) {
+                          const RouteMode& mode, bool topk, cudaStream_t st, const RowNorm& nrm, bool pdl) {
     cudaError_t e;
     if (T <= kDecodeMaxT) {
         const size_t smem = sizeof(float) * static_cast<size_t>(H) * (2 + T);
         e = cudaFuncSetAttribute(router_logits_decode_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
-        router_logits_decode_kernel<<<E, 128, smem, st>>>(x, T, H, Wr, E, bias, logits, nrm);
+        e = launch_kernel(pdl, router_logits_decode_kernel, dim3(E), dim3(128), smem, st, x, T, H, Wr, E, bias,
+                          logits, nrm);
+        if (e != cudaSuccess) return e;
     } else if (T <= kSmallMaxT && H % (4 * kRowsChunks) == 0 && rows_smem(H) <= 227u * 1024u) {
         const size_t smem = rows_smem(H);
         e = cudaFuncSetAttribute(router_logits_rows_kernel,
