@@ -103,6 +103,8 @@ __device__ void single_gpu_items(const PlanArgs& a, const int* goff_s, const int
 constexpr int kMaxChunksPerPart = 32;  // 16 parts x 32 chunks x 16 tokens = 8192 tokens
 
 __global__ __launch_bounds__(1024) void plan_kernel(PlanArgs a) {
+    griddep_wait();
+    griddep_launch_dependents();
     __shared__ int part_sum[64][17];
     __shared__ int gcnt_s[64], goff_s[kMaxSegs + 1];
     const int tid = threadIdx.x;
@@ -385,9 +387,8 @@ __global__ __launch_bounds__(1024) void capacity_kernel(int* __restrict__ topk_i
 
 }  // namespace
 
-cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st) {
-    plan_kernel<<<1, 1024, 0, st>>>(a);
-    return cudaGetLastError();
+cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st, bool pdl) {
+    return launch_kernel(pdl, plan_kernel, dim3(1), dim3(1024), 0, st, a);
 }
 
 cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, float* topk_w,

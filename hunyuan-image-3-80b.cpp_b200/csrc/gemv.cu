@@ -191,6 +191,8 @@ __global__ __launch_bounds__(kGemvThreads, 3) void gemv_kernel(const __grid_cons
                                                             void* __restrict__ out, int out_ld,
                                                             __half* __restrict__ out_r, int shared_rows,
                                                             int* err) {
+    griddep_wait();
+    griddep_launch_dependents();
     constexpr int TB = tile_bytes(WT);
     extern __shared__ uint8_t gsm_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
@@ -445,16 +447,15 @@ void gemv_smem(int max_box, int* slots, int* xb_max, size_t* smem) {
 template <int WT>
 cudaError_t launch_t(const GemvMaps& maps, const int4* items, const int* n_items, int max_items,
                      const uint8_t* const* wtiles, int n_ks, int glu, int max_rows, void* out,
-                     int out_ld, __half* out_r, int shared_rows, int* err, cudaStream_t st) {
+                     int out_ld, __half* out_r, int shared_rows, int* err, cudaStream_t st, bool pdl) {
     int slots = 0, xb_max = 0;
     size_t smem = 0;
     gemv_smem<WT>(box_index(max_rows), &slots, &xb_max, &smem);
     cudaError_t e = cudaFuncSetAttribute(gemv_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    gemv_kernel<WT><<<max_items, kGemvThreads, smem, st>>>(maps, items, n_items, wtiles, n_ks, glu, slots,
-                                                           xb_max, out, out_ld, out_r, shared_rows, err);
-    return cudaGetLastError();
+    return launch_kernel(pdl, gemv_kernel<WT>, dim3(max_items), dim3(kGemvThreads), smem, st, maps, items, n_items,
+                         wtiles, n_ks, glu, slots, xb_max, out, out_ld, out_r, shared_rows, err);
 }
 
 }  // namespace
@@ -472,9 +473,9 @@ cudaError_t launch_gemv(const GemvMaps& maps, const int4* items, const int* n_it
         return launch_stream<W_Q4_0, 3>(maps, items, n_items, n_sms, wtiles, n_ks, glu, out, out_ld, out_r, shared_rows, err, st,
                                         pdl);
     switch (wtype) {
-        case W_Q4_0: return launch_t<W_Q4_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st);
-        case W_Q8_0: return launch_t<W_Q8_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st);
-        default: return launch_t<W_F16>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st);
+        case W_Q4_0: return launch_t<W_Q4_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st, pdl);
+        case W_Q8_0: return launch_t<W_Q8_0>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st, pdl);
+        default: return launch_t<W_F16>(maps, items, n_items, max_items, wtiles, n_ks, glu, max_rows, out, out_ld, out_r, shared_rows, err, st, pdl);
     }
 }
 

@@ -1739,11 +1739,11 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
         // chains last long enough to hide it (measured: T=8 0.357 -> 0.351 ms; at T=1 the fork
         // outlasted the front end and delayed the routed launch, 0.105 -> 0.119 ms).
         const bool shared_apart = !ep && gemv && T >= 4 && T <= 8 && (L.wtype == W_Q4_0 || L.wtype == W_Q8_0);
-        // Decode chains on one GPU (1..8 tokens, weight-streaming kernels): router, top-K + plan,
-        // scatter, gate_up, down and combine are launched with programmatic dependent launch, so
-        // each is scheduled while its predecessor finishes (every one of these kernels waits for
-        // its predecessor's completion before it reads anything).
-        const bool pdl = c->pdl && !ep && gemv && T >= 1 && T <= kDecodeMaxT && !c->route.drop &&
+        // Decode-size chains on one GPU (1..64 tokens, weight-streaming kernels): router (and
+        // top-K), plan, scatter, gate_up, down and combine are launched with programmatic
+        // dependent launch, so each is scheduled while its predecessor finishes (every one of
+        // these kernels waits for its predecessor's completion before it reads anything).
+        const bool pdl = c->pdl && !ep && gemv && T >= 1 && T <= kGemvMaxRows && !c->route.drop &&
                          (L.wtype == W_Q4_0 || L.wtype == W_Q8_0);
         if (shared_apart) {
             cudaStream_t side = c->side_stream;
@@ -1806,7 +1806,7 @@ hymoe_status hymoe_forward(hymoe_ctx* c, uint32_t layer, const float* x, const f
             if (fused)
                 HY_CUDA(c, launch_topk_plan(dlog ? dlog : c->logits, T, K, dprob, c->topk_w, c->topk_idx, pa, st, pdl));
             else
-                HY_CUDA(c, launch_plan(pa, st));
+                HY_CUDA(c, launch_plan(pa, st, pdl));
             c->phase_end(HYMOE_PHASE_PLAN);
             if (!p2p) {  // peer-memory dispatch writes the rows straight to their owners
                 c->phase_begin();

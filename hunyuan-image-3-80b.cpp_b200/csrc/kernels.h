@@ -94,7 +94,7 @@ struct PlanArgs {
     RouteMode mode;           // fused top-K: routing variant
     ItemsArgs items;
 };
-cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st);
+cudaError_t launch_plan(const PlanArgs& a, cudaStream_t st, bool pdl = false);
 // T <= kRouterTok (one chunk): top-K of every token and the plan in one launch.
 cudaError_t launch_topk_plan(const float* logits, int T, int K, float* probs, float* topk_w,
                              int* topk_idx, const PlanArgs& a, cudaStream_t st, bool pdl = false);

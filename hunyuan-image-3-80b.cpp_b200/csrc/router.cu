@@ -245,6 +245,8 @@ size_t rows_smem(int H) { return sizeof(float) * (static_cast<size_t>(kRowsTT + 
 __global__ __launch_bounds__(32) void router_logits_rows_kernel(
     const float* __restrict__ x, int T, int H, const float* __restrict__ Wr, int E,
     const float* __restrict__ bias, float* __restrict__ logits, RowNorm nrm) {
+    griddep_wait();
+    griddep_launch_dependents();
     extern __shared__ float4 rsm4[];
     const int ld = H + 4;
     float* xs = reinterpret_cast<float*>(rsm4);  // [4][ld]
@@ -301,6 +303,8 @@ __global__ __launch_bounds__(32 * kRouterTok) void router_topk_kernel(
     const float* __restrict__ logits, int T, int E, int K, float* __restrict__ probs_out,
     float* __restrict__ topk_w, int* __restrict__ topk_idx, int* __restrict__ chunk_counts,
     const int* __restrict__ slot_of, RouteMode mode) {
+    griddep_wait();
+    griddep_launch_dependents();
     __shared__ float pbuf[kRouterTok][kMaxE];
     __shared__ int cnt[kMaxE];
     const int warp = threadIdx.x >> 5;
@@ -333,7 +337,8 @@ cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, 
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         dim3 g((T + kRowsTT - 1) / kRowsTT, (E + kRowsTE - 1) / kRowsTE);
-        router_logits_rows_kernel<<<g, 32, smem, st>>>(x, T, H, Wr, E, bias, logits, nrm);
+        e = launch_kernel(pdl, router_logits_rows_kernel, g, dim3(32), smem, st, x, T, H, Wr, E, bias, logits, nrm);
+        if (e != cudaSuccess) return e;
     } else if (T <= kSmallMaxT) {
         const size_t smem = sizeof(float) * kSmallStages * ((kSmallTT + kSmallTE) * kSmallLd + kSmallKC);
         e = cudaFuncSetAttribute(router_logits_small_kernel,
@@ -350,9 +355,9 @@ cudaError_t launch_router(const float* x, int T, int H, const float* Wr, int E, 
     }
     e = cudaGetLastError();
     if (e != cudaSuccess || !topk) return e;
-    router_topk_kernel<<<(T + kRouterTok - 1) / kRouterTok, 32 * kRouterTok, 0, st>>>(
-        logits, T, E, K, probs, topk_w, topk_idx, chunk_counts, slot_of, mode);
-    return cudaGetLastError();
+    // the top-K kernel waits for the logits kernel like every kernel of a programmatic chain
+    return launch_kernel(pdl, router_topk_kernel, dim3((T + kRouterTok - 1) / kRouterTok), dim3(32 * kRouterTok), 0,
+                         st, logits, T, E, K, probs, topk_w, topk_idx, chunk_counts, slot_of, mode);
 }
 
 }  // namespace hymoe
